@@ -1,0 +1,163 @@
+/*
+ * kvx -- B200-native KV-cache transfer for disaggregated prefill -> decode (C ABI).
+ *
+ * This library replaces the NIXL/UCX transport under lean-vLLM's NixlConnector
+ * (lean_vllm/kv_transfer/nixl_connector.py) on one NVSwitch node. Each entry point below names the NIXL agent call
+ * (or the reference code) it stands in for. All functions are plain C: pointers, sizes and int status codes; no
+ * exceptions cross the boundary. `stream` is a cudaStream_t passed as void* (0 is the legacy default stream).
+ *
+ * A transfer is described exactly as NixlConnectorWorker describes its READs:
+ *   - a cache is a list of regions, one per K, V or latent tensor of one layer (Region, nixl_connector.py:80-86);
+ *   - a job is one READ of one request: the blocks to take from one producer rank's cache (src) and where they
+ *     land in a consumer rank's cache (dst), and which heads (one Share of head_shares, nixl_connector.py:60-77);
+ *   - job j copies, for every region r and every i < n_blocks, num_heads*head_bytes bytes from
+ *       src.regions[r].addr + src_block_ids[i]*src.block_bytes + src_first_head*src.head_bytes
+ *     to
+ *       dst.regions[r].addr + dst_block_ids[i]*dst.block_bytes + dst_first_head*dst.head_bytes,
+ *     or whole blocks for latent regions (head_bytes == 0) when `latents` is set, nothing for them otherwise --
+ *     the byte map of block_descs (nixl_connector.py:89-108) applied to both sides of the READ (:404-417).
+ * Block ids and region tables are read from host memory at call time and travel inside the kernel launch, so no
+ * call here needs device scratch memory or a host-to-device copy of its own.
+ */
+#ifndef KVX_H
+#define KVX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVX_ABI_VERSION 1
+
+/* Status codes. Every entry point returns one; kvx_last_error() describes the last failure on this thread. */
+#define KVX_OK 0
+#define KVX_PENDING 1          /* kvx_check_xfer: still in flight (NIXL's "PROC", nixl_connector.py:434) */
+#define KVX_ERR_INVALID (-1)   /* a bad argument */
+#define KVX_ERR_CUDA (-2)      /* a CUDA call failed */
+#define KVX_ERR_RANGE (-3)     /* a block id or head range outside its cache (nixl_connector.py:398-399) */
+#define KVX_ERR_DEVICE (-4)    /* a kernel gave up a bounded wait; see kvx_device_error */
+
+/* Copy engines for kvx_copy/kvx_transfer flags (low byte). */
+#define KVX_ENGINE_AUTO 0      /* TMA bulk copies when every address and length is 16-byte aligned, else LSU */
+#define KVX_ENGINE_LSU 1       /* vectorised ld/st through the SMs' load/store units */
+#define KVX_ENGINE_TMA 2       /* cp.async.bulk global->smem->global, one issuing thread per CTA */
+
+/* One K, V or latent tensor of one layer. Mirrors Region (nixl_connector.py:80-86). */
+typedef struct kvx_region {
+    uint64_t addr;        /* device address of block 0 (this process's mapping; a peer's via kvx_ipc_open) */
+    uint64_t block_bytes; /* bytes between consecutive blocks */
+    uint64_t head_bytes;  /* bytes of one head's tokens in a block; 0 for latents */
+} kvx_region;
+
+/* One side of a transfer: a cache's regions, in model order. Mirrors the `regions` list a handshake carries
+ * (nixl_connector.py:360) and the local self.regions (:235). */
+typedef struct kvx_cache {
+    const kvx_region *regions; /* host array of n_regions */
+    int32_t n_regions;
+    int32_t num_blocks;        /* blocks per region; every block id must be below it (nixl_connector.py:398) */
+} kvx_cache;
+
+/* One READ: one request's blocks for one head share. Mirrors the arguments of the two block_descs calls and the
+ * READ posted in NixlConnectorWorker._start (nixl_connector.py:403-420). */
+typedef struct kvx_job {
+    int32_t src_cache;              /* index into the caches array */
+    int32_t dst_cache;
+    const int32_t *src_block_ids;   /* host array of n_blocks (remote_block_ids) */
+    const int32_t *dst_block_ids;   /* host array of n_blocks (local_block_ids) */
+    int32_t n_blocks;
+    int32_t src_first_head;         /* Share.remote_head */
+    int32_t dst_first_head;         /* Share.local_head */
+    int32_t num_heads;              /* Share.num_heads */
+    int32_t latents;                /* nonzero: whole latent blocks too (the first share, nixl_connector.py:403) */
+} kvx_job;
+
+/* CUDA IPC export of a device allocation, carried in the handshake reply in place of NIXL agent metadata. */
+typedef struct kvx_ipc_handle {
+    unsigned char handle[64]; /* cudaIpcMemHandle_t of the allocation holding the pointer */
+    uint64_t offset;          /* of the pointer within that allocation */
+    uint64_t alloc_bytes;     /* size of that allocation */
+    int32_t device;           /* exporting device ordinal, in the exporter's numbering */
+    int32_t pid;              /* exporting process; an importer in the same process uses the pointer directly */
+    uint64_t ptr;             /* the exported pointer, valid in the exporting process only */
+} kvx_ipc_handle;
+
+/* Opaque in-flight transfer: a launch plus the event recorded after it (a NIXL xfer handle, :411-418). */
+typedef struct kvx_xfer *kvx_xfer_t;
+
+/* ---- library ---- */
+int kvx_abi_version(void);
+/* The last failure's description on the calling thread (empty if none). */
+const char *kvx_last_error(void);
+
+/* ---- memory registration and the handshake ---- */
+
+/* Exports the allocation holding `ptr` for another process on this node.
+ * Replaces agent.get_reg_descs/register_memory/get_agent_metadata (nixl_connector.py:240-244). */
+int kvx_ipc_export(const void *ptr, kvx_ipc_handle *out);
+
+/* Maps a peer's exported allocation into this process on the current device and returns the exported pointer's
+ * address here. Reference-counted per allocation: a second open of the same allocation returns the same mapping.
+ * Replaces agent.add_remote_agent (nixl_connector.py:510). */
+int kvx_ipc_open(const kvx_ipc_handle *handle, void **out_ptr);
+
+/* Drops one reference taken by kvx_ipc_open; unmaps at zero. Replaces agent.remove_remote_agent (:337, :486). */
+int kvx_ipc_close(const kvx_ipc_handle *handle);
+
+/* Whether `device` can load and store `peer`'s memory directly (NVLink/NVSwitch); enables it if so. */
+int kvx_enable_peer_access(int device, int peer, int *out_can_access);
+
+/* ---- the three kernels ---- */
+
+/* Paged-block copy, one launch for all jobs, stream-ordered: gather from src blocks, head resharding, scatter into
+ * dst blocks. Either side may be another GPU's memory (a kvx_ipc_open mapping): a consumer-side launch pulls over
+ * NVLink, a producer-side launch pushes. This is the data movement of one or more NIXL READs (:411-420). */
+int kvx_copy(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags, void *stream);
+
+/* Gathers one job's chunks (region-major, then block) into the contiguous buffer `staging`, which must hold
+ * n_chunks*chunk_bytes bytes; `staging` may be a peer's mapping (pack-and-push in one pass).
+ * Chunk (region r, block i) lands at staging + (r*n_blocks + i)*chunk_bytes, the row order of block_descs. */
+int kvx_pack(const kvx_cache *src, const int32_t *src_block_ids, int n_blocks, int first_head, int num_heads,
+             int latents, void *staging, uint64_t staging_bytes, int flags, void *stream);
+
+/* Moves `bytes` contiguous bytes from `src` to `dst`, either of which may be a peer mapping (the push of a packed
+ * staging buffer over NVLink). */
+int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream);
+
+/* The inverse of kvx_pack: scatters a staging buffer in kvx_pack's order into dst blocks. */
+int kvx_scatter(const void *staging, uint64_t staging_bytes, const kvx_cache *dst, const int32_t *dst_block_ids,
+                int n_blocks, int first_head, int num_heads, int latents, int flags, void *stream);
+
+/* ---- transfers with completion (post, poll, release) ---- */
+
+/* kvx_copy after `wait_event` (a cudaEvent_t as void*, may be 0) has passed on `stream`, then records a completion
+ * event. Replaces initialize_xfer("READ") + transfer (nixl_connector.py:411-420); the wait replaces the host
+ * synchronisation on the ready event (:394-395) with a stream wait. */
+int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
+                 void *wait_event, void *stream, kvx_xfer_t *out);
+
+/* KVX_OK once the transfer's copies have landed, KVX_PENDING while in flight, <0 on failure.
+ * Replaces check_xfer_state (nixl_connector.py:431). */
+int kvx_check_xfer(kvx_xfer_t xfer);
+
+/* Frees the handle (waits for nothing). Replaces release_xfer_handle (nixl_connector.py:437). */
+int kvx_release_xfer(kvx_xfer_t xfer);
+
+/* ---- diagnostics ---- */
+
+/* Bytes kvx_copy would move for these jobs: the sum of descriptor lengths the reference counts
+ * (nixl_connector.py:421). Validates like kvx_copy; launches nothing. */
+int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, uint64_t *out_bytes);
+
+/* Reads and clears the device error word of the current device: 0, or the code of a bounded wait that ran out. */
+int kvx_device_error(int *out_code);
+
+/* Kernel launches issued by this process so far (all entry points), for launch accounting. */
+uint64_t kvx_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVX_H */

@@ -1,0 +1,808 @@
+// kvx: B200-native paged KV-cache transfer (the C ABI of include/kvx.h).
+//
+// One kernel family moves paged KV blocks: gather by source block table, head resharding, scatter by destination
+// block table, in a single pass over HBM or NVLink. A launch's whole description -- region tables of both caches,
+// block ids, head shares -- travels in the kernel's parameter space (up to 32 KB, CUDA >= 12.1), so a transfer needs
+// no device scratch memory and no host-to-device copy besides the launch itself.
+//
+// Work decomposition. Job j (one READ: one request x one head share) covers n_regions x n_blocks contiguous chunks
+// of chunk_bytes (HND caches keep a share's heads of one block contiguous). Chunks are cut into tiles of
+// tile_bytes; a launch numbers all tiles of all its jobs consecutively and a persistent grid of
+// (SM count x CTAs per SM) walks them with a grid stride. Two engines copy a tile:
+//   LSU -- every thread moves VEC-byte vectors (16 when all addresses and lengths allow) with streaming loads,
+//          UNROLL vectors in flight per thread;
+//   TMA -- one thread per CTA runs a STAGES-deep ring of cp.async.bulk global->shared loads (mbarrier completion)
+//          and cp.async.bulk shared->global stores (bulk-group completion); data never enters registers.
+// Either side may be another GPU's memory mapped with cudaIpcOpenMemHandle: a launch on the consumer pulls over
+// NVLink, a launch on the producer pushes. No TMA load here uses cluster multicast.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <unistd.h>
+
+#include "kvx.h"
+
+namespace {
+
+// ------------------------------------------------------------------------------------------------ errors
+
+thread_local std::string t_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_error = buf;
+    return code;
+}
+
+#define KVX_CUDA(call)                                                                                  \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess) return fail(KVX_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+std::atomic<uint64_t> g_launches{0};
+
+// ------------------------------------------------------------------------------------------------ launch params
+
+constexpr int kMaxRegions = 512;  // region slots per launch, over all caches it touches
+constexpr int kMaxCacheRegions = 256;
+constexpr int kMaxJobs = 96;      // job pieces per launch
+constexpr int kMaxIds = 3072;     // block ids per launch (source and destination)
+
+struct DevJob {
+    uint64_t tile_start;    // first tile of this job in the launch's numbering
+    uint64_t chunk_bytes;   // bytes per (region, block)
+    uint64_t src_head_off;  // src_first_head * head_bytes
+    uint64_t dst_head_off;
+    uint32_t src_region0;   // slot of this job's first source region
+    uint32_t dst_region0;
+    uint32_t n_regions;
+    uint32_t n_blocks;
+    uint32_t ids_off;       // source ids at ids[ids_off], destination ids at ids[ids_off + n_blocks]
+    uint32_t tiles_per_chunk;
+};
+
+struct Params {
+    uint64_t total_tiles;
+    uint32_t n_jobs;
+    uint32_t tile_bytes;
+    int32_t error_code;  // written to the device error word when a bounded wait runs out
+    uint32_t pad;
+    DevJob jobs[kMaxJobs];
+    uint64_t addr[kMaxRegions];         // region base (block 0)
+    uint64_t block_bytes[kMaxRegions];  // region block stride
+    int32_t ids[kMaxIds];
+};
+static_assert(sizeof(Params) <= 32764, "kernel parameter space is 32764 bytes");
+
+__device__ int g_device_error;  // first bounded-wait failure on this device, read by kvx_device_error
+
+struct Tile {
+    const char *src;
+    char *dst;
+    uint32_t len;
+};
+
+// Locates tile t of the launch. `j` is a cursor into the job list that only moves forward, since each CTA visits
+// tiles in increasing order.
+__device__ __forceinline__ Tile locate(const Params &p, uint64_t t, uint32_t &j) {
+    while (j + 1 < p.n_jobs && t >= p.jobs[j + 1].tile_start) ++j;
+    const DevJob &job = p.jobs[j];
+    const uint64_t lt = t - job.tile_start;
+    const uint64_t chunk = lt / job.tiles_per_chunk;
+    const uint64_t sub = lt - chunk * job.tiles_per_chunk;
+    const uint32_t r = (uint32_t)(chunk / job.n_blocks);
+    const uint32_t i = (uint32_t)(chunk - (uint64_t)r * job.n_blocks);
+    const int64_t sid = p.ids[job.ids_off + i];
+    const int64_t did = p.ids[job.ids_off + job.n_blocks + i];
+    const uint32_t sr = job.src_region0 + r, dr = job.dst_region0 + r;
+    const uint64_t off = sub * p.tile_bytes;
+    Tile tile;
+    tile.src = reinterpret_cast<const char *>(p.addr[sr] + (uint64_t)sid * p.block_bytes[sr] + job.src_head_off + off);
+    tile.dst = reinterpret_cast<char *>(p.addr[dr] + (uint64_t)did * p.block_bytes[dr] + job.dst_head_off + off);
+    const uint64_t rest = job.chunk_bytes - off;
+    tile.len = (uint32_t)(rest < p.tile_bytes ? rest : p.tile_bytes);
+    return tile;
+}
+
+// ------------------------------------------------------------------------------------------------ LSU engine
+
+template <int VEC>
+struct Vec;
+template <>
+struct Vec<16> {
+    using T = uint4;
+    static __device__ __forceinline__ T load(const void *p) {
+        T v;
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
+        return v;
+    }
+    static __device__ __forceinline__ void store(void *p, T v) {
+        asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+    }
+};
+template <>
+struct Vec<8> {
+    using T = uint2;
+    static __device__ __forceinline__ T load(const void *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+    static __device__ __forceinline__ void store(void *p, T v) { *reinterpret_cast<uint2 *>(p) = v; }
+};
+template <>
+struct Vec<4> {
+    using T = uint32_t;
+    static __device__ __forceinline__ T load(const void *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+    static __device__ __forceinline__ void store(void *p, T v) { *reinterpret_cast<uint32_t *>(p) = v; }
+};
+template <>
+struct Vec<2> {
+    using T = unsigned short;
+    static __device__ __forceinline__ T load(const void *p) {
+        return __ldg(reinterpret_cast<const unsigned short *>(p));
+    }
+    static __device__ __forceinline__ void store(void *p, T v) { *reinterpret_cast<unsigned short *>(p) = v; }
+};
+template <>
+struct Vec<1> {
+    using T = unsigned char;
+    static __device__ __forceinline__ T load(const void *p) { return __ldg(reinterpret_cast<const unsigned char *>(p)); }
+    static __device__ __forceinline__ void store(void *p, T v) { *reinterpret_cast<unsigned char *>(p) = v; }
+};
+
+constexpr int kLsuThreads = 512;
+constexpr int kLsuUnroll = 4;
+
+template <int VEC>
+__global__ void __launch_bounds__(kLsuThreads) kvx_copy_lsu(const __grid_constant__ Params p) {
+    using V = Vec<VEC>;
+    uint32_t j = 0;
+    for (uint64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+        const Tile tile = locate(p, t, j);
+        const uint32_t n = tile.len / VEC;
+        for (uint32_t base = threadIdx.x; base < n; base += kLsuThreads * kLsuUnroll) {
+            typename V::T r[kLsuUnroll];
+#pragma unroll
+            for (int u = 0; u < kLsuUnroll; ++u) {
+                const uint32_t k = base + u * kLsuThreads;
+                if (k < n) r[u] = V::load(tile.src + (uint64_t)k * VEC);
+            }
+#pragma unroll
+            for (int u = 0; u < kLsuUnroll; ++u) {
+                const uint32_t k = base + u * kLsuThreads;
+                if (k < n) V::store(tile.dst + (uint64_t)k * VEC, r[u]);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ TMA engine
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a bulk load that has not landed after 2 s is an error
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait on an mbarrier phase: false if it did not complete by `deadline` (globaltimer ns).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t deadline) {
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() > deadline) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t smem, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+constexpr int kTmaStages = 4;
+
+__global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Params p) {
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(8) uint64_t full[kTmaStages];
+    if (threadIdx.x != 0) return;  // one issuing thread; the rest of the warp has nothing to do
+
+    const uint64_t mine =
+        p.total_tiles > blockIdx.x ? (p.total_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    if (mine == 0) return;
+    for (int s = 0; s < kTmaStages; ++s)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+
+    char *dst_of[kTmaStages];
+    uint32_t len_of[kTmaStages];
+    uint32_t load_cursor = 0;
+    const uint32_t stage_bytes = p.tile_bytes;
+
+    auto issue = [&](uint64_t k) {
+        const int s = (int)(k % kTmaStages);
+        const Tile tile = locate(p, blockIdx.x + k * gridDim.x, load_cursor);
+        dst_of[s] = tile.dst;
+        len_of[s] = tile.len;
+        bulk_load(smem_u32(ring + (size_t)s * stage_bytes), tile.src, tile.len, smem_u32(&full[s]));
+    };
+
+    const uint64_t prologue = mine < kTmaStages ? mine : kTmaStages;
+    for (uint64_t k = 0; k < prologue; ++k) issue(k);
+
+    uint64_t landed = 0;  // loads waited for
+    bool ok = true;
+    for (uint64_t k = 0; k < mine; ++k) {
+        const int s = (int)(k % kTmaStages);
+        if (!mbar_wait(smem_u32(&full[s]), (uint32_t)((k / kTmaStages) & 1), globaltimer() + kWaitLimitNs)) {
+            ok = false;
+            break;
+        }
+        landed = k + 1;
+        bulk_store(dst_of[s], smem_u32(ring + (size_t)s * stage_bytes), len_of[s]);
+        // Refill the stage of tile k-1 once its store has read shared memory; tile k's store may still be reading.
+        if (k >= 1 && k - 1 + kTmaStages < mine) {
+            bulk_wait_read<1>();
+            issue(k - 1 + kTmaStages);
+        }
+    }
+    if (!ok) {
+        atomicCAS(&g_device_error, 0, p.error_code);
+        // Loads issued but not waited for may still be writing shared memory: give each a bounded wait.
+        const uint64_t issued = mine < landed + kTmaStages ? mine : landed + kTmaStages;
+        const uint64_t drain = globaltimer() + kWaitLimitNs;
+        for (uint64_t k = landed; k < issued; ++k)
+            if (!mbar_wait(smem_u32(&full[k % kTmaStages]), (uint32_t)((k / kTmaStages) & 1), drain)) break;
+    }
+    bulk_wait_all();
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+
+struct DeviceInfo {
+    int sms = 0;
+    size_t tma_smem_set = 0;
+};
+
+std::mutex g_mutex;
+std::map<int, DeviceInfo> g_devices;
+
+int device_info(DeviceInfo **out) {
+    int dev;
+    KVX_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_mutex);
+    DeviceInfo &info = g_devices[dev];
+    if (info.sms == 0) KVX_CUDA(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev));
+    *out = &info;
+    return KVX_OK;
+}
+
+// One contiguous run of a job's regions with a single chunk size, cut to the launch capacity.
+struct Piece {
+    int src_cache, dst_cache;
+    int r0, nr;
+    uint64_t chunk, src_head_off, dst_head_off;
+    const int32_t *src_ids, *dst_ids;
+    int nb;
+};
+
+uint64_t low_bit(uint64_t x) { return x & (~x + 1); }
+
+int plan(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, std::vector<Piece> &pieces,
+         uint64_t &bytes, uint64_t &align_bits) {
+    if (n_jobs < 0 || n_caches < 0) return fail(KVX_ERR_INVALID, "negative job or cache count");
+    if (n_jobs > 0 && (!jobs || !caches)) return fail(KVX_ERR_INVALID, "null jobs or caches");
+    for (int c = 0; c < n_caches; ++c) {
+        const kvx_cache &cache = caches[c];
+        if (cache.n_regions < 0 || cache.n_regions > kMaxCacheRegions)
+            return fail(KVX_ERR_INVALID, "cache %d has %d regions; at most %d", c, cache.n_regions, kMaxCacheRegions);
+        if (cache.n_regions > 0 && !cache.regions) return fail(KVX_ERR_INVALID, "cache %d has no region table", c);
+        if (cache.num_blocks < 0) return fail(KVX_ERR_INVALID, "cache %d has a negative block count", c);
+    }
+    bytes = 0;
+    align_bits = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+        const kvx_job &job = jobs[j];
+        if (job.src_cache < 0 || job.src_cache >= n_caches || job.dst_cache < 0 || job.dst_cache >= n_caches)
+            return fail(KVX_ERR_INVALID, "job %d names a cache outside the %d given", j, n_caches);
+        if (job.n_blocks < 0) return fail(KVX_ERR_INVALID, "job %d has a negative block count", j);
+        if (job.n_blocks == 0) continue;
+        if (!job.src_block_ids || !job.dst_block_ids) return fail(KVX_ERR_INVALID, "job %d has null block ids", j);
+        const kvx_cache &src = caches[job.src_cache], &dst = caches[job.dst_cache];
+        if (src.n_regions != dst.n_regions)
+            return fail(KVX_ERR_INVALID, "job %d pairs caches of %d and %d regions", j, src.n_regions, dst.n_regions);
+        for (int i = 0; i < job.n_blocks; ++i) {
+            if (job.src_block_ids[i] < 0 || job.src_block_ids[i] >= src.num_blocks)
+                return fail(KVX_ERR_RANGE, "job %d: source block id %d outside the cache's %d blocks", j,
+                            job.src_block_ids[i], src.num_blocks);
+            if (job.dst_block_ids[i] < 0 || job.dst_block_ids[i] >= dst.num_blocks)
+                return fail(KVX_ERR_RANGE, "job %d: destination block id %d outside the cache's %d blocks", j,
+                            job.dst_block_ids[i], dst.num_blocks);
+        }
+        int run_start = -1;
+        uint64_t run_chunk = 0, run_soff = 0, run_doff = 0;
+        auto close_run = [&](int end) {
+            if (run_start >= 0 && run_chunk > 0)
+                pieces.push_back(Piece{job.src_cache, job.dst_cache, run_start, end - run_start, run_chunk, run_soff,
+                                       run_doff, job.src_block_ids, job.dst_block_ids, job.n_blocks});
+            run_start = -1;
+        };
+        for (int r = 0; r < src.n_regions; ++r) {
+            const kvx_region &a = src.regions[r], &b = dst.regions[r];
+            if (!a.addr || !b.addr) return fail(KVX_ERR_INVALID, "job %d: region %d has a null address", j, r);
+            if ((a.head_bytes == 0) != (b.head_bytes == 0))
+                return fail(KVX_ERR_INVALID, "job %d: region %d is latent on one side only", j, r);
+            uint64_t chunk, soff = 0, doff = 0;
+            if (a.head_bytes) {
+                if (a.head_bytes != b.head_bytes)
+                    return fail(KVX_ERR_INVALID, "job %d: region %d heads are %llu and %llu bytes", j, r,
+                                (unsigned long long)a.head_bytes, (unsigned long long)b.head_bytes);
+                if (job.num_heads < 0 || job.src_first_head < 0 || job.dst_first_head < 0)
+                    return fail(KVX_ERR_INVALID, "job %d: negative head range", j);
+                if ((uint64_t)(job.src_first_head + job.num_heads) * a.head_bytes > a.block_bytes ||
+                    (uint64_t)(job.dst_first_head + job.num_heads) * b.head_bytes > b.block_bytes)
+                    return fail(KVX_ERR_RANGE, "job %d: heads [%d, +%d) / [%d, +%d) pass the end of a block", j,
+                                job.src_first_head, job.num_heads, job.dst_first_head, job.num_heads);
+                chunk = (uint64_t)job.num_heads * a.head_bytes;
+                soff = (uint64_t)job.src_first_head * a.head_bytes;
+                doff = (uint64_t)job.dst_first_head * b.head_bytes;
+            } else if (job.latents) {
+                if (a.block_bytes != b.block_bytes)
+                    return fail(KVX_ERR_INVALID, "job %d: latent region %d blocks are %llu and %llu bytes", j, r,
+                                (unsigned long long)a.block_bytes, (unsigned long long)b.block_bytes);
+                chunk = a.block_bytes;
+            } else {
+                chunk = 0;  // latents come from another share
+            }
+            if (chunk == 0) {
+                close_run(r);
+                continue;
+            }
+            align_bits |= a.addr | b.addr | a.block_bytes | b.block_bytes | soff | doff | chunk;
+            bytes += chunk * (uint64_t)job.n_blocks;
+            if (run_start >= 0 && (chunk != run_chunk || soff != run_soff || doff != run_doff)) close_run(r);
+            if (run_start < 0) {
+                run_start = r;
+                run_chunk = chunk;
+                run_soff = soff;
+                run_doff = doff;
+            }
+        }
+        close_run(src.n_regions);
+    }
+    return KVX_OK;
+}
+
+struct Config {
+    int engine;       // KVX_ENGINE_LSU or KVX_ENGINE_TMA
+    int vec;          // LSU vector bytes
+    uint32_t tile_bytes;
+    int ctas_per_sm;
+};
+
+// flags: bits 0-7 engine, bits 8-15 log2(tile bytes) (0: default), bits 16-23 CTAs per SM (0: default).
+int choose(int flags, uint64_t align_bits, Config &cfg) {
+    const int engine = flags & 0xff;
+    if (engine != KVX_ENGINE_AUTO && engine != KVX_ENGINE_LSU && engine != KVX_ENGINE_TMA)
+        return fail(KVX_ERR_INVALID, "unknown engine %d", engine);
+    const uint64_t lb = align_bits ? low_bit(align_bits) : 16;
+    cfg.vec = (int)std::min<uint64_t>(lb, 16);
+    const bool tma_ok = cfg.vec == 16;
+    if (engine == KVX_ENGINE_TMA && !tma_ok)
+        return fail(KVX_ERR_INVALID, "the TMA engine needs 16-byte aligned addresses and lengths");
+    cfg.engine = (engine == KVX_ENGINE_LSU || !tma_ok) ? KVX_ENGINE_LSU : KVX_ENGINE_TMA;
+    const int log_tile = (flags >> 8) & 0xff;
+    const int ctas = (flags >> 16) & 0xff;
+    if (cfg.engine == KVX_ENGINE_TMA) {
+        cfg.tile_bytes = log_tile ? (1u << log_tile) : (32u << 10);
+        cfg.ctas_per_sm = ctas ? ctas : 1;
+        if (cfg.tile_bytes < 16 || cfg.tile_bytes * kTmaStages > (200u << 10))
+            return fail(KVX_ERR_INVALID, "TMA tile of %u bytes does not fit %d stages", cfg.tile_bytes, kTmaStages);
+    } else {
+        cfg.tile_bytes = log_tile ? (1u << log_tile) : (32u << 10);
+        cfg.ctas_per_sm = ctas ? ctas : 2;
+        if (cfg.tile_bytes < (uint32_t)cfg.vec) return fail(KVX_ERR_INVALID, "tile smaller than a vector");
+    }
+    if (log_tile > 24) return fail(KVX_ERR_INVALID, "tile of 2^%d bytes", log_tile);
+    return KVX_OK;
+}
+
+int launch(Params &p, const Config &cfg, cudaStream_t stream) {
+    if (p.total_tiles == 0) return KVX_OK;
+    DeviceInfo *info;
+    if (int rc = device_info(&info)) return rc;
+    const uint64_t cap = (uint64_t)info->sms * cfg.ctas_per_sm;
+    const unsigned grid = (unsigned)std::min<uint64_t>(p.total_tiles, cap);
+    p.error_code = 1;
+    if (cfg.engine == KVX_ENGINE_TMA) {
+        const size_t smem = (size_t)cfg.tile_bytes * kTmaStages;
+        if (info->tma_smem_set < smem) {
+            KVX_CUDA(cudaFuncSetAttribute(kvx_copy_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            info->tma_smem_set = smem;
+        }
+        kvx_copy_tma<<<grid, 32, smem, stream>>>(p);
+    } else {
+        switch (cfg.vec) {
+            case 16: kvx_copy_lsu<16><<<grid, kLsuThreads, 0, stream>>>(p); break;
+            case 8: kvx_copy_lsu<8><<<grid, kLsuThreads, 0, stream>>>(p); break;
+            case 4: kvx_copy_lsu<4><<<grid, kLsuThreads, 0, stream>>>(p); break;
+            case 2: kvx_copy_lsu<2><<<grid, kLsuThreads, 0, stream>>>(p); break;
+            default: kvx_copy_lsu<1><<<grid, kLsuThreads, 0, stream>>>(p); break;
+        }
+    }
+    KVX_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return KVX_OK;
+}
+
+// Packs pieces into as few launches as the parameter space allows and launches them in order on `stream`.
+int run(const kvx_cache *caches, int n_caches, const std::vector<Piece> &pieces, const Config &cfg,
+        cudaStream_t stream) {
+    thread_local std::vector<Params> storage(1);
+    Params &p = storage[0];
+    std::vector<int> slot(n_caches, -1);
+    int n_regions = 0, n_ids = 0;
+    auto reset = [&] {
+        p.total_tiles = 0;
+        p.n_jobs = 0;
+        p.tile_bytes = cfg.tile_bytes;
+        std::fill(slot.begin(), slot.end(), -1);
+        n_regions = 0;
+        n_ids = 0;
+    };
+    reset();
+    auto region_slot = [&](int c) -> int {
+        if (slot[c] >= 0) return slot[c];
+        const kvx_cache &cache = caches[c];
+        if (n_regions + cache.n_regions > kMaxRegions) return -1;
+        for (int r = 0; r < cache.n_regions; ++r) {
+            p.addr[n_regions + r] = cache.regions[r].addr;
+            p.block_bytes[n_regions + r] = cache.regions[r].block_bytes;
+        }
+        slot[c] = n_regions;
+        n_regions += cache.n_regions;
+        return slot[c];
+    };
+    const int max_blocks = kMaxIds / 2;
+    for (const Piece &piece : pieces) {
+        for (int b0 = 0; b0 < piece.nb; b0 += max_blocks) {
+            const int nb = std::min(max_blocks, piece.nb - b0);
+            for (int attempt = 0; attempt < 2; ++attempt) {
+                int s = -1, d = -1;
+                const bool room = p.n_jobs < (uint32_t)kMaxJobs && n_ids + 2 * nb <= kMaxIds &&
+                                  (s = region_slot(piece.src_cache)) >= 0 && (d = region_slot(piece.dst_cache)) >= 0;
+                if (!room) {
+                    if (attempt == 1) return fail(KVX_ERR_INVALID, "a job piece does not fit one launch");
+                    if (int rc = launch(p, cfg, stream)) return rc;
+                    reset();
+                    continue;
+                }
+                DevJob &job = p.jobs[p.n_jobs++];
+                job.tile_start = p.total_tiles;
+                job.chunk_bytes = piece.chunk;
+                job.src_head_off = piece.src_head_off;
+                job.dst_head_off = piece.dst_head_off;
+                job.src_region0 = (uint32_t)(s + piece.r0);
+                job.dst_region0 = (uint32_t)(d + piece.r0);
+                job.n_regions = (uint32_t)piece.nr;
+                job.n_blocks = (uint32_t)nb;
+                job.ids_off = (uint32_t)n_ids;
+                job.tiles_per_chunk = (uint32_t)((piece.chunk + cfg.tile_bytes - 1) / cfg.tile_bytes);
+                std::memcpy(&p.ids[n_ids], piece.src_ids + b0, sizeof(int32_t) * nb);
+                std::memcpy(&p.ids[n_ids + nb], piece.dst_ids + b0, sizeof(int32_t) * nb);
+                n_ids += 2 * nb;
+                p.total_tiles += (uint64_t)piece.nr * nb * job.tiles_per_chunk;
+                break;
+            }
+        }
+    }
+    return launch(p, cfg, stream);
+}
+
+int copy_impl(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
+              cudaStream_t stream) {
+    std::vector<Piece> pieces;
+    uint64_t bytes, align_bits;
+    if (int rc = plan(caches, n_caches, jobs, n_jobs, pieces, bytes, align_bits)) return rc;
+    if (pieces.empty()) return KVX_OK;
+    Config cfg;
+    if (int rc = choose(flags, align_bits, cfg)) return rc;
+    return run(caches, n_caches, pieces, cfg, stream);
+}
+
+// A staging buffer in kvx_pack's order, as a cache of the same region count: region r starts where the rows of
+// regions before it end, and block i of it sits at i * chunk_bytes(r).
+int staging_cache(const kvx_cache *cache, int n_blocks, int num_heads, int latents, uint64_t staging,
+                  uint64_t staging_bytes, std::vector<kvx_region> &regions, std::vector<int32_t> &identity) {
+    if (!cache || cache->n_regions < 0 || (cache->n_regions > 0 && !cache->regions))
+        return fail(KVX_ERR_INVALID, "null cache");
+    if (n_blocks < 0 || num_heads < 0) return fail(KVX_ERR_INVALID, "negative block or head count");
+    if (!staging && n_blocks > 0) return fail(KVX_ERR_INVALID, "null staging buffer");
+    regions.resize(cache->n_regions);
+    uint64_t at = 0;
+    for (int r = 0; r < cache->n_regions; ++r) {
+        const kvx_region &a = cache->regions[r];
+        uint64_t chunk = a.head_bytes ? (uint64_t)num_heads * a.head_bytes : (latents ? a.block_bytes : 0);
+        regions[r].addr = staging + at;
+        regions[r].block_bytes = chunk ? chunk : 1;
+        regions[r].head_bytes = a.head_bytes;
+        at += chunk * (uint64_t)n_blocks;
+    }
+    if (at > staging_bytes)
+        return fail(KVX_ERR_RANGE, "staging needs %llu bytes, has %llu", (unsigned long long)at,
+                    (unsigned long long)staging_bytes);
+    identity.resize(n_blocks);
+    for (int i = 0; i < n_blocks; ++i) identity[i] = i;
+    return KVX_OK;
+}
+
+// Open IPC mappings in this process, by (device, allocation handle).
+struct Mapping {
+    void *base;
+    int refs;
+};
+std::map<std::pair<int, std::string>, Mapping> g_mappings;
+
+typedef int (*GetAddressRangeFn)(unsigned long long *, size_t *, unsigned long long);
+
+int allocation_of(const void *ptr, uint64_t *base, size_t *size) {
+    static GetAddressRangeFn fn = nullptr;
+    if (!fn) {
+        void *sym = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        KVX_CUDA(cudaGetDriverEntryPoint("cuMemGetAddressRange", &sym, cudaEnableDefault, &q));
+        if (!sym || q != cudaDriverEntryPointSuccess) return fail(KVX_ERR_CUDA, "cuMemGetAddressRange not found");
+        fn = reinterpret_cast<GetAddressRangeFn>(sym);
+    }
+    unsigned long long b = 0;
+    size_t s = 0;
+    const int rc = fn(&b, &s, (unsigned long long)(uintptr_t)ptr);
+    if (rc != 0) return fail(KVX_ERR_CUDA, "cuMemGetAddressRange failed with %d: not a device allocation", rc);
+    *base = b;
+    *size = s;
+    return KVX_OK;
+}
+
+struct Xfer {
+    cudaEvent_t done;
+    int device;
+};
+
+}  // namespace
+
+// ================================================================================================ C ABI
+
+extern "C" {
+
+int kvx_abi_version(void) { return KVX_ABI_VERSION; }
+
+const char *kvx_last_error(void) { return t_error.c_str(); }
+
+uint64_t kvx_launch_count(void) { return g_launches.load(); }
+
+int kvx_ipc_export(const void *ptr, kvx_ipc_handle *out) {
+    if (!ptr || !out) return fail(KVX_ERR_INVALID, "null pointer");
+    cudaPointerAttributes attr;
+    KVX_CUDA(cudaPointerGetAttributes(&attr, ptr));
+    if (attr.type != cudaMemoryTypeDevice) return fail(KVX_ERR_INVALID, "not device memory");
+    uint64_t base;
+    size_t size;
+    if (int rc = allocation_of(ptr, &base, &size)) return rc;
+    cudaIpcMemHandle_t handle;
+    KVX_CUDA(cudaIpcGetMemHandle(&handle, reinterpret_cast<void *>(base)));
+    std::memset(out, 0, sizeof *out);
+    static_assert(sizeof(handle) <= sizeof(out->handle), "handle size");
+    std::memcpy(out->handle, &handle, sizeof handle);
+    out->offset = (uint64_t)(uintptr_t)ptr - base;
+    out->alloc_bytes = size;
+    out->device = attr.device;
+    out->pid = (int32_t)getpid();
+    out->ptr = (uint64_t)(uintptr_t)ptr;
+    return KVX_OK;
+}
+
+int kvx_ipc_open(const kvx_ipc_handle *h, void **out_ptr) {
+    if (!h || !out_ptr) return fail(KVX_ERR_INVALID, "null pointer");
+    if (h->pid == (int32_t)getpid()) {  // our own allocation: CUDA IPC cannot reopen it, and need not
+        *out_ptr = reinterpret_cast<void *>(h->ptr);
+        return KVX_OK;
+    }
+    int dev;
+    KVX_CUDA(cudaGetDevice(&dev));
+    const auto key = std::make_pair(dev, std::string(reinterpret_cast<const char *>(h->handle), 64));
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_mappings.find(key);
+    if (it == g_mappings.end()) {
+        cudaIpcMemHandle_t handle;
+        std::memcpy(&handle, h->handle, sizeof handle);
+        void *base = nullptr;
+        KVX_CUDA(cudaIpcOpenMemHandle(&base, handle, cudaIpcMemLazyEnablePeerAccess));
+        it = g_mappings.emplace(key, Mapping{base, 0}).first;
+    }
+    it->second.refs += 1;
+    *out_ptr = static_cast<char *>(it->second.base) + h->offset;
+    return KVX_OK;
+}
+
+int kvx_ipc_close(const kvx_ipc_handle *h) {
+    if (!h) return fail(KVX_ERR_INVALID, "null pointer");
+    if (h->pid == (int32_t)getpid()) return KVX_OK;
+    int dev;
+    KVX_CUDA(cudaGetDevice(&dev));
+    const auto key = std::make_pair(dev, std::string(reinterpret_cast<const char *>(h->handle), 64));
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_mappings.find(key);
+    if (it == g_mappings.end()) return fail(KVX_ERR_INVALID, "handle not open on this device");
+    if (--it->second.refs == 0) {
+        void *base = it->second.base;
+        g_mappings.erase(it);
+        KVX_CUDA(cudaIpcCloseMemHandle(base));
+    }
+    return KVX_OK;
+}
+
+int kvx_enable_peer_access(int device, int peer, int *out_can_access) {
+    if (!out_can_access) return fail(KVX_ERR_INVALID, "null pointer");
+    *out_can_access = 0;
+    if (device == peer) {
+        *out_can_access = 1;
+        return KVX_OK;
+    }
+    int can = 0;
+    KVX_CUDA(cudaDeviceCanAccessPeer(&can, device, peer));
+    if (!can) return KVX_OK;
+    int prev;
+    KVX_CUDA(cudaGetDevice(&prev));
+    KVX_CUDA(cudaSetDevice(device));
+    cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        (void)cudaGetLastError();
+        e = cudaSuccess;
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "cudaDeviceEnablePeerAccess: %s", cudaGetErrorString(e));
+    *out_can_access = 1;
+    return KVX_OK;
+}
+
+int kvx_copy(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags, void *stream) {
+    return copy_impl(caches, n_caches, jobs, n_jobs, flags, static_cast<cudaStream_t>(stream));
+}
+
+int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, uint64_t *out_bytes) {
+    if (!out_bytes) return fail(KVX_ERR_INVALID, "null pointer");
+    std::vector<Piece> pieces;
+    uint64_t bytes, align_bits;
+    if (int rc = plan(caches, n_caches, jobs, n_jobs, pieces, bytes, align_bits)) return rc;
+    *out_bytes = bytes;
+    return KVX_OK;
+}
+
+int kvx_pack(const kvx_cache *src, const int32_t *src_block_ids, int n_blocks, int first_head, int num_heads,
+             int latents, void *staging, uint64_t staging_bytes, int flags, void *stream) {
+    std::vector<kvx_region> regions;
+    std::vector<int32_t> identity;
+    if (int rc = staging_cache(src, n_blocks, num_heads, latents, (uint64_t)(uintptr_t)staging, staging_bytes,
+                               regions, identity))
+        return rc;
+    const kvx_cache caches[2] = {*src, kvx_cache{regions.data(), src->n_regions, n_blocks}};
+    const kvx_job job = {0, 1, src_block_ids, identity.data(), n_blocks, first_head, 0, num_heads, latents};
+    return copy_impl(caches, 2, &job, 1, flags, static_cast<cudaStream_t>(stream));
+}
+
+int kvx_scatter(const void *staging, uint64_t staging_bytes, const kvx_cache *dst, const int32_t *dst_block_ids,
+                int n_blocks, int first_head, int num_heads, int latents, int flags, void *stream) {
+    std::vector<kvx_region> regions;
+    std::vector<int32_t> identity;
+    if (int rc = staging_cache(dst, n_blocks, num_heads, latents, (uint64_t)(uintptr_t)staging, staging_bytes,
+                               regions, identity))
+        return rc;
+    const kvx_cache caches[2] = {kvx_cache{regions.data(), dst->n_regions, n_blocks}, *dst};
+    const kvx_job job = {0, 1, identity.data(), dst_block_ids, n_blocks, 0, first_head, num_heads, latents};
+    return copy_impl(caches, 2, &job, 1, flags, static_cast<cudaStream_t>(stream));
+}
+
+int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream) {
+    if (bytes == 0) return KVX_OK;
+    if (!dst || !src) return fail(KVX_ERR_INVALID, "null pointer");
+    const kvx_region a = {(uint64_t)(uintptr_t)src, bytes, 0}, b = {(uint64_t)(uintptr_t)dst, bytes, 0};
+    const kvx_cache caches[2] = {{&a, 1, 1}, {&b, 1, 1}};
+    const int32_t zero = 0;
+    const kvx_job job = {0, 1, &zero, &zero, 1, 0, 0, 0, 1};
+    return copy_impl(caches, 2, &job, 1, flags, static_cast<cudaStream_t>(stream));
+}
+
+int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
+                 void *wait_event, void *stream, kvx_xfer_t *out) {
+    if (!out) return fail(KVX_ERR_INVALID, "null pointer");
+    *out = nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (wait_event) KVX_CUDA(cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_event), 0));
+    if (int rc = copy_impl(caches, n_caches, jobs, n_jobs, flags, s)) return rc;
+    Xfer *x = new Xfer{};
+    KVX_CUDA(cudaGetDevice(&x->device));
+    cudaError_t e = cudaEventCreateWithFlags(&x->done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(x->done, s);
+    if (e != cudaSuccess) {
+        delete x;
+        return fail(KVX_ERR_CUDA, "completion event: %s", cudaGetErrorString(e));
+    }
+    *out = reinterpret_cast<kvx_xfer_t>(x);
+    return KVX_OK;
+}
+
+int kvx_check_xfer(kvx_xfer_t xfer) {
+    if (!xfer) return fail(KVX_ERR_INVALID, "null transfer");
+    Xfer *x = reinterpret_cast<Xfer *>(xfer);
+    const cudaError_t e = cudaEventQuery(x->done);
+    if (e == cudaSuccess) return KVX_OK;
+    if (e == cudaErrorNotReady) {
+        (void)cudaGetLastError();
+        return KVX_PENDING;
+    }
+    return fail(KVX_ERR_CUDA, "transfer failed: %s", cudaGetErrorString(e));
+}
+
+int kvx_release_xfer(kvx_xfer_t xfer) {
+    if (!xfer) return KVX_OK;
+    Xfer *x = reinterpret_cast<Xfer *>(xfer);
+    const cudaError_t e = cudaEventDestroy(x->done);
+    delete x;
+    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "cudaEventDestroy: %s", cudaGetErrorString(e));
+    return KVX_OK;
+}
+
+int kvx_device_error(int *out_code) {
+    if (!out_code) return fail(KVX_ERR_INVALID, "null pointer");
+    int zero = 0;
+    KVX_CUDA(cudaMemcpyFromSymbol(out_code, g_device_error, sizeof(int)));
+    KVX_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+    return KVX_OK;
+}
+
+}  // extern "C"

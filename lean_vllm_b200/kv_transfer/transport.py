@@ -1,0 +1,204 @@
+"""The kvx transport: torch-facing wrappers over the C ABI (include/kvx.h).
+
+Stands where NixlConnector's NIXL agent stands (lean_vllm/kv_transfer/nixl_connector.py:50-57): it exports a rank's
+cache for peers (register_memory + agent metadata, :240-244), maps a peer's cache (add_remote_agent, :510), posts a
+block copy (initialize_xfer + transfer, :411-420), and polls it (check_xfer_state, :431). Every data-moving call is
+a CUDA kernel of libkvx.so; nothing here copies bytes on the host.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from lean_vllm_b200 import _native
+from lean_vllm_b200._native import Cache, IpcHandle, Job, Region, check, lib
+
+
+def _ids(block_ids) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+
+
+@dataclass
+class CacheTable:
+    """One rank's cache as kvx sees it: (addr, block_bytes, head_bytes) per K, V or latent region, in model order,
+    plus the block count every region shares. `addrs` are device addresses in this process (a peer's are its
+    kvx_ipc_open mapping)."""
+
+    regions: list[tuple[int, int, int]]
+    num_blocks: int
+    _struct: Cache | None = field(default=None, repr=False, compare=False)
+    _array: object = field(default=None, repr=False, compare=False)
+
+    @classmethod
+    def from_tensors(cls, kv_caches) -> "CacheTable":
+        """Regions of per-layer caches, as register_kv_caches derives them (nixl_connector.py:224-235): a key/value
+        layer is (2, blocks, heads, tokens, dim) HND, a latent layer (1, blocks, tokens, dim)."""
+        regions, num_blocks = [], None
+        for cache in kv_caches:
+            if cache.dim() not in (4, 5):
+                raise ValueError(f"a layer cache is 5-D (keys/values, HND) or 4-D (latents), not {cache.dim()}-D")
+            if not cache.is_cuda:
+                raise ValueError("kvx moves device memory; this cache is on the host")
+            itemsize = cache.element_size()
+            # What a share copies must be contiguous: a head's tokens (HND) or a whole latent block.
+            if cache.stride(-1) != 1 or cache.stride(-2) != cache.size(-1):
+                raise ValueError("each head's tokens (or each latent block) must be contiguous: an HND cache")
+            for part in cache:
+                head = part.stride(1) * itemsize if cache.dim() == 5 else 0
+                regions.append((part.data_ptr(), part.stride(0) * itemsize, head))
+            if num_blocks is None:
+                num_blocks = cache.size(1)
+            elif cache.size(1) != num_blocks:
+                raise ValueError("every layer must hold the same number of blocks")
+        return cls(regions, num_blocks or 0)
+
+    def rebased(self, mapping: dict[int, int]) -> "CacheTable":
+        """The same regions at other addresses: `mapping` takes each exporter address to its local mapping."""
+        return CacheTable([(mapping[a], b, h) for a, b, h in self.regions], self.num_blocks)
+
+    def struct(self) -> Cache:
+        if self._struct is None:
+            array = (Region * max(len(self.regions), 1))(*[Region(a, b, h) for a, b, h in self.regions])
+            self._array = array
+            self._struct = Cache(ctypes.cast(array, ctypes.POINTER(Region)), len(self.regions), self.num_blocks)
+        return self._struct
+
+
+@dataclass
+class CopyJob:
+    """One READ: blocks of one request for one head share (kvx_job)."""
+
+    src: int  # index of the source CacheTable in the call's list
+    dst: int
+    src_block_ids: object
+    dst_block_ids: object
+    src_first_head: int = 0
+    dst_first_head: int = 0
+    num_heads: int = 0
+    latents: bool = False
+
+
+def _marshal(caches: list[CacheTable], jobs: list[CopyJob]):
+    cache_array = (Cache * max(len(caches), 1))(*[c.struct() for c in caches])
+    keep = [cache_array]
+    job_array = (Job * max(len(jobs), 1))()
+    for k, job in enumerate(jobs):
+        src_ids, dst_ids = _ids(job.src_block_ids), _ids(job.dst_block_ids)
+        if len(src_ids) != len(dst_ids):
+            raise ValueError(f"job {k} pairs {len(src_ids)} source blocks with {len(dst_ids)} destination blocks")
+        keep += [src_ids, dst_ids]
+        ptr = ctypes.POINTER(ctypes.c_int32)
+        job_array[k] = Job(
+            job.src,
+            job.dst,
+            src_ids.ctypes.data_as(ptr),
+            dst_ids.ctypes.data_as(ptr),
+            len(src_ids),
+            job.src_first_head,
+            job.dst_first_head,
+            job.num_heads,
+            int(job.latents),
+        )
+    keep.append(job_array)
+    return cache_array, job_array, keep
+
+
+def copy(caches: list[CacheTable], jobs: list[CopyJob], stream: int = 0, flags: int = 0) -> None:
+    """Launches the paged-block copy of `jobs` on `stream` (a cudaStream_t as int)."""
+    if not jobs:
+        return
+    cache_array, job_array, _keep = _marshal(caches, jobs)
+    check(lib().kvx_copy(cache_array, len(caches), job_array, len(jobs), flags, stream))
+
+
+def job_bytes(caches: list[CacheTable], jobs: list[CopyJob]) -> int:
+    """Bytes the jobs move: the reference's descriptor-length sum (nixl_connector.py:421)."""
+    if not jobs:
+        return 0
+    cache_array, job_array, _keep = _marshal(caches, jobs)
+    out = ctypes.c_uint64()
+    check(lib().kvx_job_bytes(cache_array, len(caches), job_array, len(jobs), ctypes.byref(out)))
+    return out.value
+
+
+class Transfer:
+    """A posted copy and the event after it (a NIXL xfer handle)."""
+
+    def __init__(self, handle: int):
+        self._handle = ctypes.c_void_p(handle)
+
+    def done(self) -> bool:
+        """True once every byte has landed; raises if the transfer failed."""
+        return check(lib().kvx_check_xfer(self._handle)) == _native.KVX_OK
+
+    def release(self):
+        if self._handle:
+            check(lib().kvx_release_xfer(self._handle))
+            self._handle = ctypes.c_void_p(0)
+
+
+def transfer(caches: list[CacheTable], jobs: list[CopyJob], stream: int, wait_event: int = 0,
+             flags: int = 0) -> Transfer:
+    """Waits (on the stream) for `wait_event`, launches the copy, records completion."""
+    cache_array, job_array, _keep = _marshal(caches, jobs)
+    out = ctypes.c_void_p()
+    check(lib().kvx_transfer(cache_array, len(caches), job_array, len(jobs), flags, wait_event or None,
+                             stream or None, ctypes.byref(out)))
+    return Transfer(out.value)
+
+
+def pack(src: CacheTable, block_ids, first_head: int, num_heads: int, latents: bool, staging: int,
+         staging_bytes: int, stream: int = 0, flags: int = 0) -> None:
+    ids = _ids(block_ids)
+    check(lib().kvx_pack(ctypes.byref(src.struct()), ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(ids),
+                         first_head, num_heads, int(latents), staging, staging_bytes, flags, stream))
+
+
+def scatter(staging: int, staging_bytes: int, dst: CacheTable, block_ids, first_head: int, num_heads: int,
+            latents: bool, stream: int = 0, flags: int = 0) -> None:
+    ids = _ids(block_ids)
+    check(lib().kvx_scatter(staging, staging_bytes, ctypes.byref(dst.struct()),
+                            ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(ids), first_head, num_heads,
+                            int(latents), flags, stream))
+
+
+def push(dst: int, src: int, nbytes: int, stream: int = 0, flags: int = 0) -> None:
+    check(lib().kvx_push(dst, src, nbytes, flags, stream))
+
+
+def export(ptr: int) -> bytes:
+    """An IPC handle for the allocation holding device address `ptr`, as bytes for a handshake."""
+    handle = IpcHandle()
+    check(lib().kvx_ipc_export(ptr, ctypes.byref(handle)))
+    return handle.to_bytes()
+
+
+def open_mapping(blob: bytes) -> int:
+    """This process's address for a peer's exported pointer (on the current device)."""
+    handle = IpcHandle.from_bytes(blob)
+    out = ctypes.c_void_p()
+    check(lib().kvx_ipc_open(ctypes.byref(handle), ctypes.byref(out)))
+    return out.value or 0
+
+
+def close_mapping(blob: bytes) -> None:
+    check(lib().kvx_ipc_close(ctypes.byref(IpcHandle.from_bytes(blob))))
+
+
+def enable_peer_access(device: int, peer: int) -> bool:
+    out = ctypes.c_int()
+    check(lib().kvx_enable_peer_access(device, peer, ctypes.byref(out)))
+    return bool(out.value)
+
+
+def launch_count() -> int:
+    return int(lib().kvx_launch_count())
+
+
+def device_error() -> int:
+    out = ctypes.c_int()
+    check(lib().kvx_device_error(ctypes.byref(out)))
+    return out.value

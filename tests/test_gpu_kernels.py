@@ -1,0 +1,243 @@
+"""The kvx kernels through the C ABI, bit for bit against the reference's golden results and the CPU oracle.
+
+Every comparison here is exact (torch.equal on bf16 bit patterns): the path moves bytes and must not change one.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from lean_vllm_b200._native import ENGINE_LSU, ENGINE_TMA, KvxError, KvxRangeError, flags
+from lean_vllm_b200.kv_transfer import transport
+from lean_vllm_b200.kv_transfer.shares import head_shares, split_heads
+from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
+from oracle.kv_oracle import load_between
+from tests.helpers import bits, from_bits, full_of, rank_part, seeded, sha
+
+pytestmark = pytest.mark.gpu
+
+ENGINES = {"auto": 0, "lsu": flags(ENGINE_LSU), "tma": flags(ENGINE_TMA)}
+
+
+def load_on_gpu(prefill_layers, decode_layers, prefill_tp, decode_tp, local, remote, engine_flags, device="cuda"):
+    """Every decode rank pulls its shares from every prefill rank: one kvx_copy per decode rank, each job one
+    share (nixl_connector.py:396-421). All ranks' caches live on one GPU here."""
+    mla = prefill_layers[0].dim() == 4
+    heads = split_heads(0 if mla else prefill_layers[0].shape[2], decode_tp, prefill_tp)
+    producers = [[rank_part(layer, q, prefill_tp).to(device) for layer in prefill_layers] for q in range(prefill_tp)]
+    consumers = [[rank_part(layer, r, decode_tp).to(device) for layer in decode_layers] for r in range(decode_tp)]
+    tables = [CacheTable.from_tensors(p) for p in producers]
+    moved = []
+    for rank in range(decode_tp):
+        local_table = CacheTable.from_tensors(consumers[rank])
+        caches = [local_table] + tables
+        jobs = [
+            CopyJob(1 + s.remote_rank, 0, remote, local, s.remote_head, s.local_head, s.num_heads, latents=(i == 0))
+            for i, s in enumerate(head_shares(rank, decode_tp, prefill_tp, heads))
+        ]
+        moved.append(transport.job_bytes(caches, jobs))
+        transport.copy(caches, jobs, torch.cuda.current_stream().cuda_stream, engine_flags)
+    torch.cuda.synchronize()
+    return [[c.cpu() for c in layers] for layers in consumers], moved
+
+
+@pytest.mark.parametrize("engine", list(ENGINES))
+def test_every_small_case_matches_the_reference(golden, engine):
+    meta, arrays = golden
+    small = meta["small"]
+    for case in small["cases"]:
+        key = "lat" if case["mla"] else "kv"
+        prefill = from_bits(arrays[f"small_{key}_prefill"])
+        decode = from_bits(arrays[f"small_{key}_decode"])
+        local, remote = case.get("local", small["local"]), case.get("remote", small["remote"])
+        consumers, moved = load_on_gpu([prefill], [decode], case["prefill_tp"], case["decode_tp"], local, remote,
+                                       ENGINES[engine])
+        full = full_of([c[0] for c in consumers], case["mla"])
+        assert np.array_equal(bits(full), arrays[case["name"]]), case["name"]
+        assert moved == case["bytes_per_rank"], case["name"]
+
+
+@pytest.mark.parametrize("engine", list(ENGINES))
+@pytest.mark.parametrize("key", ["qwen_kv", "dsv2_lat"])
+def test_model_shaped_cases_match_the_reference_digests(golden, key, engine):
+    meta, _ = golden
+    spec = meta[key]
+    shape = tuple(spec["shape"])
+    prefill = [seeded(shape, s) for s in spec["prefill_seeds"]]
+    decode = [seeded(shape, s) for s in spec["decode_seeds"]]
+    assert [sha(t) for t in prefill] == spec["input_sha256"]["prefill"]
+    for case in spec["cases"]:
+        consumers, moved = load_on_gpu(prefill, decode, case["prefill_tp"], case["decode_tp"], spec["local"],
+                                       spec["remote"], ENGINES[engine])
+        assert moved == case["bytes_per_rank"], case["name"]
+        for layer in range(spec["layers"]):
+            assert sha(full_of([c[layer] for c in consumers], case["mla"])) == case["layer_sha256"][layer]
+
+
+def _odd_layers(mla, seed, blocks=9):
+    """Shapes whose heads or latent blocks are not 16-byte multiples, so the kernel falls back to narrow vectors."""
+    shape = (1, blocks, 5, 7) if mla else (2, blocks, 6, 5, 3)  # 70-byte latent blocks; 30-byte heads
+    return [seeded(shape, seed + i) for i in range(3)]
+
+
+@pytest.mark.parametrize("mla", [False, True], ids=["kv", "latents"])
+@pytest.mark.parametrize("prefill_tp, decode_tp", [(1, 1), (2, 3), (3, 2), (1, 6)])
+def test_unaligned_shapes_against_the_oracle(mla, prefill_tp, decode_tp):
+    prefill, decode = _odd_layers(mla, 0), _odd_layers(mla, 10)
+    local, remote = [8, 0, 4, 2], [1, 6, 0, 8]
+    consumers, moved = load_on_gpu(prefill, decode, prefill_tp, decode_tp, local, remote, 0)
+    expected, expected_moved = load_between([bits(t) for t in prefill], [bits(t) for t in decode], prefill_tp,
+                                            decode_tp, local, remote)
+    assert moved == expected_moved
+    for rank in range(decode_tp):
+        for layer in range(3):
+            assert np.array_equal(bits(consumers[rank][layer]), expected[rank][layer]), (rank, layer)
+
+
+def _qwen_like(num_blocks, layers, heads=8, seed=0, device="cuda"):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return [torch.randn(2, num_blocks, heads, 256, 128, generator=g, device=device).to(torch.bfloat16)
+            for _ in range(layers)]
+
+
+@pytest.mark.parametrize("engine", list(ENGINES))
+def test_a_many_request_batch_in_one_call_matches_torch_indexing(engine):
+    """64 requests of random lengths, one job each, shuffled block tables; the result must equal torch's own index
+    copy, and every block no request names must keep its bytes."""
+    rng = np.random.default_rng(0)
+    num_blocks, layers = 160, 3
+    src, dst = _qwen_like(num_blocks, layers, seed=1), _qwen_like(num_blocks, layers, seed=2)
+    before = [d.clone() for d in dst]
+    lengths = rng.integers(1, 5, size=64)
+    free_src, free_dst = rng.permutation(num_blocks), rng.permutation(num_blocks)
+    jobs, at = [], 0
+    for n in lengths:
+        if at + n > num_blocks:
+            break
+        jobs.append(CopyJob(0, 1, free_src[at : at + n], free_dst[at : at + n], 0, 0, 8))
+        at += n
+    caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
+    transport.copy(caches, jobs, torch.cuda.current_stream().cuda_stream, ENGINES[engine])
+    torch.cuda.synchronize()
+    s_ids = torch.tensor(np.concatenate([j.src_block_ids for j in jobs]), device="cuda", dtype=torch.long)
+    d_ids = torch.tensor(np.concatenate([j.dst_block_ids for j in jobs]), device="cuda", dtype=torch.long)
+    untouched = torch.ones(num_blocks, dtype=torch.bool, device="cuda")
+    untouched[d_ids] = False
+    for layer in range(layers):
+        assert torch.equal(dst[layer][:, d_ids], src[layer][:, s_ids])
+        assert torch.equal(dst[layer][:, untouched], before[layer][:, untouched])
+
+
+def test_more_jobs_and_blocks_than_one_launch_holds():
+    """Past the launch's capacity (96 job pieces, 1536 blocks a piece) the library splits into several launches."""
+    num_blocks, layers = 2000, 2
+    src = [torch.randn(2, num_blocks, 1, 16, 8, device="cuda").to(torch.bfloat16) for _ in range(layers)]
+    dst = [torch.zeros_like(s) for s in src]  # 150 small jobs land here, on disjoint blocks
+    big = [torch.zeros_like(s) for s in src]  # one 1700-block job lands here
+    perm = torch.randperm(num_blocks).numpy()
+    jobs = [CopyJob(0, 1, perm[k * 10 : (k + 1) * 10], np.arange(k * 10, (k + 1) * 10), 0, 0, 1) for k in range(150)]
+    jobs.append(CopyJob(0, 2, perm[:1700], perm[::-1][:1700].copy(), 0, 0, 1))
+    caches = [CacheTable.from_tensors(t) for t in (src, dst, big)]
+    before = transport.launch_count()
+    transport.copy(caches, jobs, 0, 0)
+    torch.cuda.synchronize()
+    assert transport.launch_count() - before >= 3
+    expect = {1: [torch.zeros_like(s) for s in src], 2: [torch.zeros_like(s) for s in src]}
+    for job in jobs:
+        for layer in range(layers):
+            expect[job.dst][layer][:, torch.as_tensor(job.dst_block_ids, dtype=torch.long)] = src[layer][
+                :, torch.as_tensor(job.src_block_ids, dtype=torch.long)]
+    for layer in range(layers):
+        assert torch.equal(dst[layer], expect[1][layer])
+        assert torch.equal(big[layer], expect[2][layer])
+
+
+def test_out_of_range_blocks_and_heads_raise_before_any_launch():
+    src = [torch.zeros(2, 4, 2, 16, 8, device="cuda", dtype=torch.bfloat16)]
+    dst = [torch.zeros(2, 4, 2, 16, 8, device="cuda", dtype=torch.bfloat16)]
+    caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
+    before = transport.launch_count()
+    with pytest.raises(KvxRangeError, match="outside the cache"):
+        transport.copy(caches, [CopyJob(0, 1, [4], [0], 0, 0, 2)])
+    with pytest.raises(KvxRangeError, match="outside the cache"):
+        transport.copy(caches, [CopyJob(0, 1, [0], [-1], 0, 0, 2)])
+    with pytest.raises(KvxRangeError, match="pass the end of a block"):
+        transport.copy(caches, [CopyJob(0, 1, [0], [0], 1, 0, 2)])
+    with pytest.raises(KvxError, match="latent on one side only"):
+        lat = CacheTable.from_tensors([torch.zeros(1, 4, 16, 16, device="cuda", dtype=torch.bfloat16)] * 2)
+        transport.copy([caches[0], lat], [CopyJob(0, 1, [0], [0], 0, 0, 1)])
+    assert transport.launch_count() == before
+
+
+def test_empty_jobs_launch_nothing():
+    src = [torch.zeros(2, 4, 2, 16, 8, device="cuda", dtype=torch.bfloat16)]
+    caches = [CacheTable.from_tensors(src), CacheTable.from_tensors([torch.ones_like(src[0])])]
+    before = transport.launch_count()
+    transport.copy(caches, [CopyJob(0, 1, [], [], 0, 0, 2), CopyJob(0, 1, [1], [2], 0, 0, 0)])
+    assert transport.launch_count() == before
+
+
+@pytest.mark.parametrize("engine", list(ENGINES))
+def test_pack_push_scatter_equals_the_direct_copy(engine):
+    """Gather into a staging buffer, push it to a second buffer, scatter: the same bytes as one direct copy, and the
+    staging buffer holds the rows in block_descs order."""
+    f = ENGINES[engine]
+    src = _qwen_like(24, 2, heads=4, seed=3)
+    dst = _qwen_like(24, 2, heads=4, seed=4)
+    direct = [d.clone() for d in dst]
+    s_ids, d_ids = [5, 17, 2, 9], [0, 23, 11, 6]
+    src_t, dst_t, direct_t = (CacheTable.from_tensors(x) for x in (src, dst, direct))
+    transport.copy([src_t, direct_t], [CopyJob(0, 1, s_ids, d_ids, 1, 2, 2)], 0, f)
+    chunk = 2 * 256 * 128 * 2
+    staging = torch.empty(4 * len(s_ids) * chunk, dtype=torch.uint8, device="cuda")
+    landing = torch.empty_like(staging)
+    transport.pack(src_t, s_ids, 1, 2, False, staging.data_ptr(), staging.numel(), 0, f)
+    transport.push(landing.data_ptr(), staging.data_ptr(), staging.numel(), 0, f)
+    transport.scatter(landing.data_ptr(), landing.numel(), dst_t, d_ids, 2, 2, False, 0, f)
+    torch.cuda.synchronize()
+    for layer in range(2):
+        assert torch.equal(dst[layer], direct[layer])
+    rows = landing.view(torch.bfloat16).view(4, len(s_ids), 2, 256, 128)  # (region, block, head, token, dim)
+    for r in range(4):
+        layer, part = divmod(r, 2)
+        assert torch.equal(rows[r], src[layer][part][s_ids, 1:3])
+
+
+def test_a_staging_buffer_too_small_is_refused():
+    src = CacheTable.from_tensors([torch.zeros(2, 4, 2, 16, 8, device="cuda", dtype=torch.bfloat16)])
+    staging = torch.empty(1024, dtype=torch.uint8, device="cuda")
+    with pytest.raises(KvxRangeError, match="staging needs"):
+        transport.pack(src, [0, 1, 2], 0, 2, False, staging.data_ptr(), staging.numel())
+
+
+def test_a_transfer_waits_for_its_ready_event_and_reports_completion():
+    """The load waits on the stream for the event recorded where the blocks were allocated (the reference's
+    ready.synchronize, nixl_connector.py:266, 394-395), then reports done through its own event."""
+    src = _qwen_like(8, 2, seed=5)
+    dst = [torch.zeros_like(s) for s in src]
+    side = torch.cuda.Stream()
+    main = torch.cuda.current_stream()
+    torch.cuda._sleep(20_000_000)  # the "step in flight" that still owns dst's blocks
+    for d in dst:
+        d.fill_(1.0)  # ... and writes them after the sleep
+    ready = main.record_event()
+    xfer = transport.transfer([CacheTable.from_tensors(src), CacheTable.from_tensors(dst)],
+                              [CopyJob(0, 1, [1, 2], [3, 4], 0, 0, 8)], side.cuda_stream, ready.cuda_event)
+    while not xfer.done():
+        pass
+    xfer.release()
+    for s, d in zip(src, dst):
+        assert torch.equal(d[:, [3, 4]], s[:, [1, 2]])
+        assert bool((d[:, [0, 1, 2, 5, 6, 7]] == 1.0).all())
+
+
+def test_ipc_export_and_open_in_the_same_process_is_the_pointer_itself():
+    t = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    view = t[4096:]
+    blob = transport.export(view.data_ptr())
+    assert transport.open_mapping(blob) == view.data_ptr()
+    transport.close_mapping(blob)
+
+
+def test_the_device_error_word_starts_clear():
+    assert transport.device_error() == 0
