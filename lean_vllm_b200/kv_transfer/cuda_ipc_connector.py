@@ -1,0 +1,463 @@
+"""CudaIpcConnector: the decode instance copies a finished prefill's blocks GPU to GPU over NVLink with kvx kernels.
+
+A drop-in for lean-vLLM's NixlConnector (lean_vllm/kv_transfer/nixl_connector.py) on one NVSwitch node. The scheduler
+half, the kv_transfer_params it returns, the handshake on kv_port + rank, the head shares between any two
+tensor-parallel sizes, reader counting and the release/expiry rules are the reference's. What changes is below the
+worker: instead of registering memory with a NIXL agent and posting one-sided READs, each rank exports its cache
+through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts ONE kvx kernel launch per load
+that gathers the shares' blocks from every producer rank's HBM over NVLink and scatters them into its own blocks.
+The launch waits on the stream for the load's ready event (no host synchronisation), completion is a CUDA event
+polled without blocking, and a consumer rank tells each producer rank it read from once its bytes have landed
+(the NIXL notification's role) over the same ZMQ channel as the handshake.
+"""
+
+from __future__ import annotations
+
+import json
+import logging
+import os
+import queue
+import threading
+from dataclasses import dataclass, field
+from time import monotonic
+
+import zmq
+
+from lean_vllm_b200 import envs
+from lean_vllm_b200.kv_transfer.base import (
+    KVConnectorMetadata,
+    KVConnectorOutput,
+    KVConnectorScheduler,
+    KVConnectorWorker,
+    KVTransferStats,
+    ReqToRecv,
+)
+from lean_vllm_b200.kv_transfer.shares import Share, head_shares, readers_of, split_heads
+
+logger = logging.getLogger(__name__)
+
+HANDSHAKE_TIMEOUT = 5.0  # ZMQ never refuses a connect; an absent producer is one that does not answer
+IDLE_WAIT = 0.01  # how often the transfer thread answers handshakes and counts notifications when idle
+BUSY_WAIT = 0.0002  # and how often it polls copies in flight
+
+
+def _cdiv(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+def node_id() -> str:
+    """Identifies this machine's boot: CUDA IPC mappings work only between processes of one node."""
+    try:
+        with open("/proc/sys/kernel/random/boot_id") as f:
+            return f.read().strip()
+    except OSError:
+        return os.uname().nodename
+
+
+def make_transport(kv_caches):
+    """The kvx transport for caches on a CUDA device (the reference's make_agent, nixl_connector.py:50-57)."""
+    from lean_vllm_b200.kv_transfer.kvx_transport import KvxTransport
+
+    return KvxTransport(kv_caches)
+
+
+class CudaIpcConnectorScheduler(KVConnectorScheduler):
+    """The engine's half, as NixlConnectorScheduler (nixl_connector.py:111-168)."""
+
+    def __init__(self, config):
+        self.kv_transfer = config.kv_transfer
+        self.block_size = config.kvcache_block_size
+        self.tp_size = config.tensor_parallel_size
+        self._reqs_to_recv: dict[str, ReqToRecv] = {}
+        self._reqs_to_send: dict[str, list[int]] = {}
+
+    def get_num_new_matched_tokens(self, seq, num_computed_tokens: int) -> tuple[int, bool]:
+        params = seq.kv_transfer_params
+        if not params or not params.get("do_remote_prefill"):
+            return 0, False
+        expected = _cdiv(seq.num_prompt_tokens, self.block_size)
+        given = len(params["remote_block_ids"])
+        if given != expected:
+            logger.warning("prefilling %s here instead: %d remote blocks for a %d-block prompt", seq.request_id,
+                           given, expected)
+            params["do_remote_prefill"] = False
+            return 0, False
+        return seq.num_prompt_tokens - num_computed_tokens, True  # any tp_size: shares cover every split
+
+    def update_state_after_alloc(self, seq, num_external_tokens: int):
+        params = seq.kv_transfer_params
+        params["do_remote_prefill"] = False  # one load per request; a preempted one recomputes
+        cached = seq.num_cached_tokens // self.block_size  # blocks this instance already holds are not read
+        self._reqs_to_recv[seq.request_id] = ReqToRecv(
+            local_block_ids=list(seq.block_table[cached:]),
+            remote_block_ids=list(params["remote_block_ids"][cached:]),
+            remote_request_id=params["remote_request_id"],
+            remote_engine_id=params["remote_engine_id"],
+            remote_host=params["remote_host"],
+            remote_port=params["remote_port"],
+            remote_tp_size=params.get("tp_size", 1),
+        )
+
+    def build_connector_meta(self) -> KVConnectorMetadata:
+        metadata = KVConnectorMetadata(self._reqs_to_recv, self._reqs_to_send)
+        self._reqs_to_recv, self._reqs_to_send = {}, {}
+        return metadata
+
+    def request_finished(self, seq) -> tuple[bool, dict | None]:
+        params = seq.kv_transfer_params
+        if not params or not params.get("do_remote_decode") or seq.finish_reason not in ("length", "stop"):
+            return False, None  # only a prefill that ran to its token hands over; an abort ends here
+        block_ids = list(seq.block_table[: _cdiv(seq.num_prompt_tokens, self.block_size)])
+        self._reqs_to_send[seq.request_id] = block_ids
+        kv = self.kv_transfer
+        return True, {
+            "do_remote_prefill": True,
+            "do_remote_decode": False,
+            "remote_request_id": seq.request_id,
+            "remote_engine_id": kv.engine_id,
+            "remote_block_ids": block_ids,
+            "remote_host": kv.kv_ip,
+            "remote_port": kv.kv_port,
+            "tp_size": self.tp_size,
+        }
+
+
+@dataclass(slots=True)
+class _Remote:
+    """A producer rank as its handshake described it, with its cache mapped here."""
+
+    engine_id: str
+    tp_size: int
+    num_blocks: int
+    exported: dict
+    table: object  # the transport's view of the producer rank's cache, mapped into this process
+    sock: object  # DEALER kept open for notifications
+
+
+@dataclass(slots=True)
+class _Load:
+    """One request's load: one kernel launch over every share."""
+
+    req: ReqToRecv
+    transfer: object = None
+    notify: list = field(default_factory=list)  # (remote key, message) to send once the bytes have landed
+    unnotified: set = field(default_factory=set)  # producer ranks no notification has reached
+    started: float = field(default_factory=monotonic)
+    num_bytes: int = 0
+    failed: bool = False
+
+
+class CudaIpcConnectorWorker(KVConnectorWorker):
+    """One rank's half, as NixlConnectorWorker (nixl_connector.py:195-520) with the kvx transport under it."""
+
+    def __init__(self, config, rank: int):
+        if config.kv_cache_layout != "HND":
+            raise AssertionError("CudaIpcConnector copies heads out of blocks, so needs HND caches")
+        self.kv_transfer = config.kv_transfer
+        self.rank = rank
+        self.tp_size = config.tensor_parallel_size
+        self.block_size = config.kvcache_block_size
+        self.kv_caches: list = []
+        self.num_heads = 0  # every rank's key heads together; 0 for a latent-only model
+        self.layout: dict = {}
+        self.transport = None
+        self.node = node_id()
+        self._lock = threading.Lock()  # guards the three maps below, shared with the transfer thread
+        self._reqs_to_send: dict[str, float] = {}  # request -> deadline for its readers
+        self._notified: dict[str, list] = {}  # request -> [notifications, readers, first seen]
+        self._finished = KVConnectorOutput()
+        self._queue: queue.Queue = queue.Queue()
+        self._context = zmq.Context()
+        self._context.setsockopt(zmq.LINGER, 0)
+        self._server = None
+        self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
+        self._loads: dict[str, _Load] = {}  # transfer thread only
+        self._thread: threading.Thread | None = None
+
+    # -------------------------------------------------------------------------------------------- engine thread
+
+    def register_kv_caches(self, kv_caches: list):
+        self.kv_caches = list(kv_caches)
+        layers = []
+        for cache in self.kv_caches:
+            if cache.dim() == 5:  # keys and values, (2, block, head, token, dim)
+                _, _, heads, tokens, dim = cache.shape
+                self.num_heads = heads * self.tp_size
+                layers.append(["kv", str(cache.dtype), self.num_heads, tokens, dim])
+            else:  # latents, (1, block, token, dim)
+                layers.append(["latent", str(cache.dtype), *cache.shape[2:]])
+        # What a peer must match: every rank's heads together, so the two sides may split them differently.
+        self.layout = {"block_size": self.block_size, "layers": layers}
+        self.transport = make_transport(self.kv_caches)
+        kv = self.kv_transfer
+        if kv.is_producer:
+            port = kv.kv_port + self.rank
+            server = self._context.socket(zmq.ROUTER)
+            try:
+                server.bind(f"tcp://{kv.kv_ip}:{port}")
+            except zmq.ZMQError as error:
+                server.close()
+                raise RuntimeError(f"cannot serve KV on {kv.kv_ip}:{port}: {error}; pick another kv_port") from error
+            self._server = server
+        self._thread = threading.Thread(target=self._run, name=f"kvx-ipc-{self.rank}", daemon=True)
+        self._thread.start()
+
+    def start_load_kv(self, metadata: KVConnectorMetadata):
+        if metadata.reqs_to_send:
+            deadline = monotonic() + envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+            with self._lock:
+                for request_id in metadata.reqs_to_send:
+                    self._reqs_to_send[request_id] = deadline
+                    self._release_if_read(request_id)
+        if metadata.reqs_to_recv:
+            # Freshly allocated blocks may still be written by a step in flight; the copy waits for it on the GPU.
+            ready = self.transport.ready_marker()
+            for request_id, req in metadata.reqs_to_recv.items():
+                self._queue.put((request_id, req, ready))
+
+    def get_finished(self) -> KVConnectorOutput:
+        now = monotonic()
+        timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+        with self._lock:
+            for request_id, deadline in list(self._reqs_to_send.items()):
+                if deadline < now:  # a copy is one-sided, so the producer cannot see one in flight: the timeout is long
+                    logger.warning("freeing the KV blocks of %s, which no decode instance read in %.0f s",
+                                   request_id, timeout)
+                    self._release(request_id)
+                    self._finished.expired_sending.add(request_id)
+            for request_id, (_, _, seen) in list(self._notified.items()):
+                if request_id not in self._reqs_to_send and seen + timeout < now:
+                    del self._notified[request_id]  # read here but never handed over: not this engine's
+            finished, self._finished = self._finished, KVConnectorOutput()
+        return finished
+
+    def shutdown(self):
+        if self._context.closed:
+            return
+        if self._thread is not None:
+            self._queue.put(None)
+            self._thread.join(timeout=10)
+        self._context.term()
+
+    def _release(self, request_id: str):
+        """Lock held. The engine frees the blocks once every rank reported them."""
+        if self._reqs_to_send.pop(request_id, None) is not None:
+            self._notified.pop(request_id, None)
+            self._finished.finished_sending.add(request_id)
+
+    def _release_if_read(self, request_id: str):
+        """Lock held."""
+        entry = self._notified.get(request_id)
+        if entry is not None and entry[0] >= entry[1]:
+            self._release(request_id)
+
+    # -------------------------------------------------------------------------------------------- transfer thread
+
+    def _run(self):
+        try:
+            self.transport.bind_thread()
+            while True:
+                wait = BUSY_WAIT if self._loads else IDLE_WAIT
+                try:
+                    items = [self._queue.get(timeout=wait)]
+                except queue.Empty:
+                    items = []
+                while not self._queue.empty():
+                    items.append(self._queue.get_nowait())
+                if None in items:
+                    return
+                for request_id, req, ready in items:
+                    self._start(request_id, req, ready)
+                if self._server is not None:
+                    self._serve()
+                self._poll()
+        except zmq.ContextTerminated:
+            pass
+        finally:
+            self._close()
+
+    def _close(self):
+        for load in self._loads.values():
+            if load.transfer is not None:
+                self.transport.wait(load.transfer)  # bytes still landing in blocks the engine would reuse
+                self.transport.release(load.transfer)
+        for remote in self._remotes.values():
+            self.transport.close(remote.exported)
+            remote.sock.close()
+        if self._server is not None:
+            self._server.close()
+
+    # Producer: answer handshakes, count the notifications that end each request's reads.
+
+    def _serve(self):
+        while True:
+            try:
+                identity, raw = self._server.recv_multipart(zmq.NOBLOCK)
+            except zmq.Again:
+                return
+            except ValueError:
+                continue
+            try:
+                message = json.loads(raw)
+                op = message.get("op")
+            except (ValueError, AttributeError):
+                message, op = {}, None
+            if op == "notify":
+                self._count(message.get("message", ""))
+                continue
+            if op == "handshake":
+                reply = {
+                    "ok": True,
+                    "engine_id": self.kv_transfer.engine_id,
+                    "tp_size": self.tp_size,
+                    "layout": self.layout,
+                    "num_blocks": int(self.kv_caches[0].size(1)),
+                    "exported": self.transport.exported,
+                    "node": self.node,
+                }
+            else:
+                reply = {"ok": False, "error": f"unknown op {op!r}"}
+            try:
+                self._server.send_multipart([identity, json.dumps(reply).encode()], zmq.NOBLOCK)
+            except zmq.Again:
+                logger.warning("a KV handshake went unanswered: its consumer is not reading")
+
+    def _count(self, message: str):
+        try:
+            request_id, readers = message.rsplit(":", 1)
+            readers = int(readers)
+        except ValueError:
+            logger.warning("ignoring a malformed KV notification %r", message)
+            return
+        with self._lock:
+            entry = self._notified.setdefault(request_id, [0, readers, monotonic()])
+            entry[0] += 1
+            self._release_if_read(request_id)
+
+    # Consumer: one launch per load, then poll it.
+
+    def _heads(self, req: ReqToRecv) -> int:
+        return split_heads(self.num_heads, self.tp_size, req.remote_tp_size)
+
+    def _start(self, request_id: str, req: ReqToRecv, ready):
+        load = self._loads[request_id] = _Load(req)
+        try:
+            heads = self._heads(req)
+            shares: list[Share] = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
+            load.unnotified = {share.remote_rank for share in shares}
+            jobs, tables = [], []
+            for i, share in enumerate(shares):
+                remote = self._handshake(req, share.remote_rank)
+                if max(req.remote_block_ids, default=-1) >= remote.num_blocks:
+                    raise RuntimeError(f"a block id past the producer's {remote.num_blocks} blocks")
+                readers = readers_of(share.remote_rank, req.remote_tp_size, self.tp_size, heads)
+                key = (req.remote_host, req.remote_port + share.remote_rank)
+                message = f"{req.remote_request_id}:{readers}"
+                job = (share, i == 0)  # latents come whole from the first producer rank only
+                nbytes = self.transport.job_bytes(remote.table, req, *job)
+                if nbytes == 0:
+                    self._notify(key, message)  # nothing to read from this rank, but it must count this reader
+                    load.unnotified.discard(share.remote_rank)
+                    continue
+                tables.append(remote.table)
+                jobs.append((len(tables) - 1, req, *job))
+                load.notify.append((key, message, share.remote_rank))
+                load.num_bytes += nbytes
+            load.started = monotonic()
+            if jobs:
+                load.transfer = self.transport.post(tables, jobs, ready)
+        except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
+            self._fail(load, error)
+
+    def _poll(self):
+        for request_id, load in list(self._loads.items()):
+            if load.transfer is not None:
+                try:
+                    if not self.transport.done(load.transfer):
+                        continue
+                except Exception as error:  # noqa: BLE001
+                    self._fail(load, RuntimeError(f"a kvx copy failed in flight: {error}"), in_flight=True)
+                self.transport.release(load.transfer)
+                load.transfer = None
+                if not load.failed:
+                    for key, message, remote_rank in load.notify:
+                        self._notify(key, message)
+                        load.unnotified.discard(remote_rank)
+            del self._loads[request_id]
+            with self._lock:
+                if load.failed:
+                    self._finished.failed_recving.add(request_id)
+                else:
+                    self._finished.finished_recving.add(request_id)
+                    self._finished.recv_stats[request_id] = KVTransferStats(monotonic() - load.started,
+                                                                           load.num_bytes)
+
+    def _notify(self, key, message: str):
+        remote = self._remotes.get(key)
+        if remote is None:
+            return
+        try:
+            remote.sock.send(json.dumps({"op": "notify", "message": message}).encode(), zmq.NOBLOCK)
+        except zmq.ZMQError as error:  # the producer frees at its timeout instead
+            logger.debug("notifying %s:%d failed: %s", key[0], key[1], error)
+
+    def _fail(self, load: _Load, error: Exception, in_flight: bool = False):
+        req = load.req
+        if not load.failed:
+            logger.warning("loading the KV of %s from %s:%d failed, so it prefills here: %s",
+                           req.remote_request_id, req.remote_host, req.remote_port, error)
+        load.failed = True
+        if in_flight:
+            return  # bytes may still be landing from those ranks: their blocks expire at the timeout instead
+        # Producer ranks no copy reached free their blocks now rather than at the timeout, where they are known.
+        for remote_rank in list(load.unnotified):
+            key = (req.remote_host, req.remote_port + remote_rank)
+            remote = self._remotes.get(key)
+            if remote is not None and remote.engine_id == req.remote_engine_id:
+                readers = readers_of(remote_rank, req.remote_tp_size, self.tp_size, self._heads(req))
+                self._notify(key, f"{req.remote_request_id}:{readers}")
+            load.unnotified.discard(remote_rank)
+        load.notify = []
+
+    def _handshake(self, req: ReqToRecv, remote_rank: int) -> _Remote:
+        """The producer rank's cache, asked for once per producer and mapped here, checked to match this engine."""
+        key = (req.remote_host, req.remote_port + remote_rank)
+        remote = self._remotes.get(key)
+        if remote is not None:
+            if remote.engine_id == req.remote_engine_id:
+                return remote
+            del self._remotes[key]  # restarted since: ask afresh
+            self.transport.close(remote.exported)
+            remote.sock.close()
+        sock = self._context.socket(zmq.DEALER)
+        keep = False
+        try:
+            sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
+            sock.connect(f"tcp://{key[0]}:{key[1]}")
+            sock.send(json.dumps({"op": "handshake"}).encode())
+            try:
+                raw = sock.recv()
+            except zmq.Again:
+                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake") from None
+            reply = json.loads(raw)
+            if not reply["ok"]:
+                raise RuntimeError(reply["error"])
+            if reply["engine_id"] != req.remote_engine_id:
+                raise RuntimeError(f"{key[0]}:{key[1]} is engine {reply['engine_id']}, not {req.remote_engine_id}")
+            if reply["tp_size"] != req.remote_tp_size:
+                raise RuntimeError(f"{key[0]}:{key[1]} runs tp_size {reply['tp_size']}, not {req.remote_tp_size}")
+            if reply["layout"] != json.loads(json.dumps(self.layout)):
+                raise RuntimeError(
+                    f"{key[0]}:{key[1]} lays its KV cache out as {reply['layout']}, this engine as {self.layout}; "
+                    "serve the same model, dtype and block size"
+                )
+            if reply.get("node") != self.node:
+                raise RuntimeError(f"{key[0]}:{key[1]} runs on another node; CUDA IPC needs both on one node")
+            table = self.transport.open(reply["exported"])
+            remote = _Remote(reply["engine_id"], reply["tp_size"], reply["num_blocks"], reply["exported"], table, sock)
+            self._remotes[key] = remote
+            keep = True
+            return remote
+        finally:
+            if not keep:
+                sock.close()

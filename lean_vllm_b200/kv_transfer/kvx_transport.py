@@ -1,0 +1,93 @@
+"""The connector's transport on CUDA devices: a rank's cache exported over CUDA IPC, peers' caches mapped, one kvx
+launch per load on a side stream, completion by event.
+
+It replaces the NIXL agent under NixlConnectorWorker call for call: register_memory/get_agent_metadata
+(nixl_connector.py:240-244) -> `exported`; add_remote_agent (:510) -> open; initialize_xfer + transfer (:411-420)
+-> post; check_xfer_state (:431) -> done; release_xfer_handle (:437) -> release; remove_remote_agent -> close.
+"""
+
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+
+from lean_vllm_b200 import _native, envs
+from lean_vllm_b200.kv_transfer import transport
+from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
+
+ENGINES = {"auto": _native.ENGINE_AUTO, "lsu": _native.ENGINE_LSU, "tma": _native.ENGINE_TMA}
+
+
+class KvxTransport:
+    def __init__(self, kv_caches: list[torch.Tensor]):
+        if not kv_caches or not all(c.is_cuda for c in kv_caches):
+            raise RuntimeError("CudaIpcConnector moves CUDA memory: every KV cache must be on a CUDA device")
+        self.device = kv_caches[0].device
+        if any(c.device != self.device for c in kv_caches):
+            raise RuntimeError("one rank's KV caches must share one device")
+        _native.lib()  # fail loudly here, at registration, if libkvx.so is missing
+        self.local = CacheTable.from_tensors(kv_caches)
+        self.flags = _native.flags(ENGINES.get(envs.LEAN_VLLM_KVX_ENGINE, _native.ENGINE_AUTO))
+        with torch.cuda.device(self.device):
+            self.stream = torch.cuda.Stream(device=self.device)
+        # One IPC handle per layer tensor; each region as (tensor, byte offset in it, block bytes, head bytes).
+        bases = [c.data_ptr() for c in kv_caches]
+        spans = [(c.data_ptr(), c.data_ptr() + c.numel() * c.element_size()) for c in kv_caches]
+        regions = []
+        for addr, block_bytes, head_bytes in self.local.regions:
+            index = next(i for i, (lo, hi) in enumerate(spans) if lo <= addr < hi)
+            regions.append([index, addr - bases[index], block_bytes, head_bytes])
+        with torch.cuda.device(self.device):
+            handles = [transport.export(base).hex() for base in bases]
+        self.exported = {
+            "handles": handles,
+            "regions": regions,
+            "num_blocks": self.local.num_blocks,
+            "device": self.device.index,
+            "pid": os.getpid(),
+        }
+
+    def bind_thread(self):
+        """CUDA's current device is per thread: the transfer thread works on the cache's device."""
+        torch.cuda.set_device(self.device)
+
+    def ready_marker(self):
+        """An event after everything queued so far on the engine's stream (the reference's ready event, :266)."""
+        return torch.cuda.current_stream(self.device).record_event()
+
+    def open(self, exported: dict) -> CacheTable:
+        bases = [transport.open_mapping(bytes.fromhex(h)) for h in exported["handles"]]
+        regions = [(bases[i] + offset, block_bytes, head_bytes) for i, offset, block_bytes, head_bytes in
+                   exported["regions"]]
+        return CacheTable(regions, exported["num_blocks"])
+
+    def close(self, exported: dict):
+        for h in exported["handles"]:
+            transport.close_mapping(bytes.fromhex(h))
+
+    def _job(self, src_index: int, req, share, latents: bool) -> CopyJob:
+        return CopyJob(src_index, 0, req.remote_block_ids, req.local_block_ids, share.remote_head, share.local_head,
+                       share.num_heads, latents)
+
+    def job_bytes(self, table: CacheTable, req, share, latents: bool) -> int:
+        """Bytes one share moves (validated like the launch), the reference's descriptor-length sum (:421)."""
+        return transport.job_bytes([self.local, table], [self._job(1, req, share, latents)])
+
+    def post(self, tables: list[CacheTable], jobs: list, ready) -> transport.Transfer:
+        """One launch for every share of a load, after `ready` on the side stream."""
+        caches = [self.local, *tables]
+        copy_jobs = [self._job(1 + index, req, share, latents) for index, req, share, latents in jobs]
+        event = ready.cuda_event if ready is not None else 0
+        return transport.transfer(caches, copy_jobs, self.stream.cuda_stream, event, self.flags)
+
+    def done(self, xfer: transport.Transfer) -> bool:
+        return xfer.done()
+
+    def wait(self, xfer: transport.Transfer):
+        while not xfer.done():
+            time.sleep(1e-4)
+
+    def release(self, xfer: transport.Transfer):
+        xfer.release()

@@ -1,0 +1,101 @@
+"""A host-memory stand-in for the kvx transport, for testing the connector's host logic on CPU. TEST ONLY.
+
+It implements the transport surface CudaIpcConnectorWorker calls, with kvx_copy's byte map (include/kvx.h)
+performed by memmove over CPU caches in this process, and it checks every range it touches against the registered
+caches, so a wrong offset, head or block id in what the connector asks for either lands the wrong bytes or raises.
+`fail` injects the two failures a transport can report: refused when posted, or failed in flight.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from itertools import count
+
+
+class HostTransport:
+    fail: str | None = None  # "posted" or "in flight"
+    instances: list["HostTransport"] = []
+
+    def __init__(self, kv_caches):
+        self.caches = list(kv_caches)
+        self.spans = [(c.data_ptr(), c.numel() * c.element_size()) for c in self.caches]
+        self.regions = []
+        for cache in self.caches:
+            itemsize = cache.element_size()
+            for part in cache:
+                head = part.stride(1) * itemsize if cache.dim() == 5 else 0
+                self.regions.append((part.data_ptr(), part.stride(0) * itemsize, head))
+        self.num_blocks = int(self.caches[0].size(1))
+        self.exported = {"regions": self.regions, "num_blocks": self.num_blocks, "spans": self.spans}
+        self.ids = count()
+        self.pending: dict[int, list] = {}
+        self.opened = 0
+        HostTransport.instances.append(self)
+
+    def bind_thread(self):
+        pass
+
+    def ready_marker(self):
+        return None
+
+    def open(self, exported):
+        self.opened += 1
+        return exported
+
+    def close(self, exported):
+        self.opened -= 1
+
+    @staticmethod
+    def _rows(table, block_ids, first_head, num_heads, latents):
+        rows = []
+        for addr, block_bytes, head_bytes in table["regions"]:
+            if head_bytes:
+                start, length = addr + first_head * head_bytes, num_heads * head_bytes
+            elif latents:
+                start, length = addr, block_bytes
+            else:
+                continue
+            rows += [(start + b * block_bytes, length) for b in block_ids]
+        return rows
+
+    def _check(self, table, block_ids, first_head, num_heads, rows):
+        if any(b < 0 or b >= table["num_blocks"] for b in block_ids):
+            raise RuntimeError("block id outside the cache")
+        for addr, length in rows:
+            if not any(lo <= addr and addr + length <= lo + n for lo, n in table["spans"]):
+                raise RuntimeError("a row outside registered memory")
+
+    def job_bytes(self, table, req, share, latents):
+        local = self._rows(self.exported, req.local_block_ids, share.local_head, share.num_heads, latents)
+        remote = self._rows(table, req.remote_block_ids, share.remote_head, share.num_heads, latents)
+        self._check(self.exported, req.local_block_ids, share.local_head, share.num_heads, local)
+        self._check(table, req.remote_block_ids, share.remote_head, share.num_heads, remote)
+        assert [n for _, n in local] == [n for _, n in remote]
+        return sum(n for _, n in local)
+
+    def post(self, tables, jobs, ready):
+        if HostTransport.fail == "posted":
+            raise RuntimeError("the transport refused the copy")
+        for index, req, share, latents in jobs:
+            local = self._rows(self.exported, req.local_block_ids, share.local_head, share.num_heads, latents)
+            remote = self._rows(tables[index], req.remote_block_ids, share.remote_head, share.num_heads, latents)
+            for (dst, n), (src, _) in zip(local, remote):
+                ctypes.memmove(dst, src, n)
+        handle = next(self.ids)
+        self.pending[handle] = [1]  # done on the second poll
+        return handle
+
+    def done(self, handle):
+        if HostTransport.fail == "in flight":
+            raise RuntimeError("copy failed in flight")
+        state = self.pending[handle]
+        if state[0]:
+            state[0] -= 1
+            return False
+        return True
+
+    def wait(self, handle):
+        pass
+
+    def release(self, handle):
+        self.pending.pop(handle, None)

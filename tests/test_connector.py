@@ -1,0 +1,262 @@
+"""CudaIpcConnector's worker halves on CPU caches over a host-memory transport: the reference connector's behaviour,
+case by case (tests/test_nixl_connector.py), with the results checked against the golden fixtures recorded from the
+reference connector itself."""
+
+import socket
+from time import sleep
+
+import numpy as np
+import pytest
+import torch
+
+from lean_vllm_b200.kv_transfer import (
+    KVConnectorMetadata,
+    KVConnectorOutput,
+    KVOutputAggregator,
+    ReqToRecv,
+    cuda_ipc_connector,
+)
+from lean_vllm_b200.kv_transfer.shares import Share, head_shares
+from tests.connector_cases import (
+    NUM_BLOCKS,
+    TP_PAIRS,
+    Sides,
+    free_port,
+    full_cache,
+    rank_cache,
+    recv,
+    wait_for,
+)
+from tests.helpers import bits, full_of
+from tests.host_transport import HostTransport
+
+
+@pytest.fixture(autouse=True)
+def host_transport(monkeypatch):
+    monkeypatch.setattr(cuda_ipc_connector, "make_transport", HostTransport)
+    monkeypatch.setattr(HostTransport, "fail", None)
+    monkeypatch.setattr(HostTransport, "instances", [])
+
+
+@pytest.fixture
+def sides():
+    s = Sides("cpu")
+    yield s
+    s.close()
+
+
+def test_each_rank_s_shares_are_the_overlap_of_its_heads_with_each_producer_rank_s():
+    assert head_shares(0, 1, 1, 8) == [Share(0, 0, 0, 8)]
+    assert head_shares(3, 4, 2, 8) == [Share(1, 2, 0, 2)]
+    assert head_shares(1, 2, 4, 8) == [Share(2, 0, 0, 2), Share(3, 0, 2, 2)]
+    assert head_shares(1, 6, 4, 12) == [Share(0, 2, 0, 1), Share(1, 0, 1, 1)]
+
+
+def test_shares_match_the_reference_on_every_split(golden):
+    meta, _ = golden
+    for rank, tp, rtp, heads, shares in meta["head_shares"]:
+        assert head_shares(rank, tp, rtp, heads) == [Share(*s) for s in shares]
+
+
+@pytest.mark.parametrize("mla", [False, True], ids=["kv", "latents"])
+@pytest.mark.parametrize("prefill_tp, decode_tp", TP_PAIRS)
+def test_each_decode_rank_gets_its_heads_whatever_the_two_sizes(sides, golden, prefill_tp, decode_tp, mla):
+    _, arrays = golden
+    prefill, decode = full_cache(0, mla), full_cache(1, mla)
+    key = "lat" if mla else "kv"
+    assert np.array_equal(bits(prefill), arrays[f"small_{key}_prefill"])  # the reference's inputs, bit for bit
+    producers = sides.make("kv_producer", prefill_tp, prefill)
+    consumers = sides.make("kv_consumer", decode_tp, decode, engine_id="decode")
+    for producer in producers:
+        producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [7, 2, 9]}))
+    for consumer in consumers:
+        consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0, 5, 3], [7, 2, 9])}))
+    outputs = [wait_for(c) for c in consumers]
+    assert KVOutputAggregator(decode_tp).aggregate(outputs).finished_recving == {"d-1"}
+    got = full_of([c.kv_caches[0] for c in consumers], mla)
+    assert np.array_equal(bits(got), arrays[f"small_{key}_tp{prefill_tp}to{decode_tp}"])
+    assert KVOutputAggregator(prefill_tp).aggregate([wait_for(p) for p in producers]).finished_sending == {"p-1"}
+
+
+def test_a_producer_rank_waits_for_every_decode_rank_that_reads_it(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 2, full_cache(1, False), engine_id="decode")
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    sleep(0.05)
+    assert not producers[0].get_finished(), "freed while decode rank 1 has yet to read"
+    consumers[1].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[1]).finished_recving == {"d-1"}
+    assert wait_for(producers[0]) == KVConnectorOutput(finished_sending={"p-1"})
+
+
+def test_a_copy_before_the_hand_over_frees_the_blocks_once_it_comes(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    sleep(0.05)
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    assert producers[0].get_finished() == KVConnectorOutput(finished_sending={"p-1"})
+
+
+def test_only_the_blocks_not_cached_here_are_copied(sides, golden):
+    _, arrays = golden
+    prefill, decode = full_cache(0, False), full_cache(1, False)
+    producers = sides.make("kv_producer", 2, prefill)
+    consumers = sides.make("kv_consumer", 1, decode, engine_id="decode")
+    for producer in producers:
+        producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [1, 2, 3]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [8], [3])}))
+    stats = wait_for(consumers[0]).recv_stats["d-1"]
+    assert stats.num_bytes == 2 * 12 * 4 * 8 * 2  # one block of keys and values, bf16 (the reference's answer)
+    assert np.array_equal(bits(consumers[0].kv_caches[0]), arrays["small_kv_prefix_hit"])
+
+
+def test_a_full_prefix_hit_copies_nothing_but_still_frees_the_producer_s_blocks(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    before = consumers[0].kv_caches[0].clone()
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [], [])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    assert wait_for(producers[0]).finished_sending == {"p-1"}
+    assert torch.equal(consumers[0].kv_caches[0], before)
+
+
+def test_an_absent_producer_fails_the_load(sides, monkeypatch):
+    monkeypatch.setattr(cuda_ipc_connector, "HANDSHAKE_TIMEOUT", 0.2)
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    req = ReqToRecv([0], [4], "p-1", "prefill", "127.0.0.1", free_port())
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": req}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+
+
+@pytest.mark.parametrize(
+    "overrides, message",
+    [
+        (dict(remote_engine_id="before-a-restart"), "is engine prefill, not before-a-restart"),
+        (dict(remote_tp_size=2), "runs tp_size 1, not 2"),
+        (dict(remote_block_ids=[NUM_BLOCKS]), "past the producer's"),
+    ],
+)
+def test_a_producer_that_does_not_match_the_request_fails_the_load(sides, caplog, overrides, message):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4], **overrides)}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    assert message in caplog.text
+
+
+def test_a_producer_of_another_model_fails_the_load(sides, caplog):
+    producers = sides.make("kv_producer", 1, full_cache(0, True))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    assert "serve the same model, dtype and block size" in caplog.text
+
+
+def test_a_producer_on_another_node_fails_the_load(sides, caplog):
+    """CUDA IPC mappings only work within one node, so a producer elsewhere is refused at the handshake."""
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    producers[0].node = "another-node"
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    assert "runs on another node" in caplog.text
+
+
+def test_a_copy_refused_when_posted_fails_the_load_and_tells_the_producer(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    HostTransport.fail = "posted"
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    assert wait_for(producers[0]) == KVConnectorOutput(finished_sending={"p-1"})
+
+
+def test_a_copy_failing_in_flight_fails_the_load_and_leaves_the_blocks_to_expire(sides, monkeypatch):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    HostTransport.fail = "in flight"
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    sleep(0.05)
+    assert not producers[0].get_finished()
+    monkeypatch.setenv("LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT", "0")
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))  # handed over again, to expire now
+    sleep(0.01)
+    assert producers[0].get_finished() == KVConnectorOutput(finished_sending={"p-1"}, expired_sending={"p-1"})
+
+
+def test_a_second_request_reuses_the_handshake(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    for request_id, block in (("p-1", 4), ("p-2", 5)):
+        producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={request_id: [block]}))
+        req = recv(producers, [block], [block], remote_request_id=request_id)
+        consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={request_id: req}))
+        assert wait_for(consumers[0]).finished_recving == {request_id}
+    assert len(consumers[0]._remotes) == 1 and consumers[0].transport.opened == 1
+
+
+def test_a_restarted_producer_is_asked_afresh_and_the_old_mapping_closed(sides):
+    first = sides.make("kv_producer", 1, full_cache(0, False), engine_id="prefill-a")
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(first, [0], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    first[0].shutdown()
+    sleep(0.05)
+    second = sides.make("kv_producer", 1, full_cache(2, False), port=first[0].kv_transfer.kv_port,
+                        engine_id="prefill-b")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-2": recv(second, [1], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-2"}
+    assert consumers[0].transport.opened == 1
+    assert torch.equal(consumers[0].kv_caches[0][:, 1], rank_cache(full_cache(2, False), 0, 1)[:, 4])
+
+
+def test_a_taken_port_is_named(sides):
+    with socket.socket() as taken:
+        taken.bind(("127.0.0.1", 0))
+        with pytest.raises(RuntimeError, match="pick another kv_port"):
+            sides.make("kv_producer", 1, full_cache(0, False), port=taken.getsockname()[1])
+
+
+def test_a_consumer_serves_nothing(sides):
+    assert sides.make("kv_consumer", 1, full_cache(1, False))[0]._server is None
+
+
+def test_an_nhd_cache_is_refused():
+    from lean_vllm_b200.kv_transfer import KVTransferConfig
+    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorWorker
+    from tests.connector_cases import WorkerConfig
+
+    with pytest.raises(AssertionError, match="needs HND caches"):
+        CudaIpcConnectorWorker(WorkerConfig(KVTransferConfig(), kv_cache_layout="NHD"), 0)
+
+
+def test_many_requests_in_one_step_each_finish(sides):
+    prefill, decode = full_cache(0, False), full_cache(1, False)
+    producers = sides.make("kv_producer", 2, prefill)
+    consumers = sides.make("kv_consumer", 2, decode, engine_id="decode")
+    pairs = {f"r{i}": ([i], [NUM_BLOCKS - 1 - i]) for i in range(6)}
+    for producer in producers:
+        producer.start_load_kv(KVConnectorMetadata(reqs_to_send={f"r{i}": [NUM_BLOCKS - 1 - i] for i in range(6)}))
+    for consumer in consumers:
+        consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={
+            rid: recv(producers, local, remote, remote_request_id=rid) for rid, (local, remote) in pairs.items()}))
+    done = set()
+    aggregator = KVOutputAggregator(2)
+    for _ in range(200):
+        done |= aggregator.aggregate([c.get_finished() for c in consumers]).finished_recving
+        if len(done) == 6:
+            break
+        sleep(0.005)
+    assert done == set(pairs)
+    expected = decode.clone()
+    for local, remote in pairs.values():
+        expected[:, local] = prefill[:, remote]
+    assert torch.equal(full_of([c.kv_caches[0] for c in consumers], False), expected)
