@@ -336,20 +336,11 @@ def run_gpu(args) -> None:
         dist.all_gather_object(digests, mine_digest, group=gloo)
         ok = digests[rank] == digests[rank ^ 1]
 
-    # e2e: through the transfer call with host block tables, completion polled (host clock).
-    e2e_ms = None
-    if args.steps:
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(max(args.steps // 2, 1)):
-            if jobs:
-                xfer = transport.transfer(caches, [CopyJob(0, 1, s.tolist(), d.tolist(), 0, 0, SHAPE["kv_heads"])
-                                                   for s, d in reqs], sid, 0, copy_flags)
-                while not xfer.done():
-                    time.sleep(20e-6)
-                xfer.release()
-        e2e_local = (time.perf_counter() - t0) * 1e3 / max(args.steps // 2, 1) if jobs else 0.0
-        e = torch.tensor([e2e_local], device=device, dtype=torch.float64)
+    # e2e: the same loads through the connector's public API (start_load_kv -> get_finished), host clock.
+    e2e_ms, e2e_bytes = None, 0
+    if args.steps and not args.no_e2e:
+        e2e_ms, e2e_bytes = e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device)
+        e = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(e, op=dist.ReduceOp.MAX)
         e2e_ms = float(e.item())
@@ -423,7 +414,10 @@ def run_gpu(args) -> None:
             line["e2e"] = {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                            "ms_per_step": round(e2e_ms, 4),
                            "h2d_bytes_per_step": ids_bytes * pairs, "d2h_bytes_per_step": 0,
-                           "path": "kvx_transfer from host block tables (carried in the launch), event polled"}
+                           "bytes_reported_by_connector": e2e_bytes,
+                           "path": ("CudaIpcConnectorWorker.start_load_kv(64 ReqToRecv from host lists) -> "
+                                    "get_finished() until all 64 finished_recving; one kvx launch per load, block "
+                                    "ids carried in the launch, completion by event query")}
         if loopback and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(lengths, reqs, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -433,6 +427,86 @@ def run_gpu(args) -> None:
             for blob in handles:
                 transport.close_mapping(blob)
         dist.destroy_process_group()
+
+
+def e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device):
+    """Times the step's loads through CudaIpcConnectorWorker (host clock, per step, consumer side): a producer
+    worker holds the source cache and a consumer worker loads every request. N=1 runs both in this process; a pair
+    runs the producer on rank 2p and the consumer on rank 2p+1. Returns (ms per step, bytes the connector counted)."""
+    import torch
+    import torch.distributed as dist
+    from dataclasses import dataclass
+
+    from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVTransferConfig, ReqToRecv
+    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorWorker
+
+    @dataclass
+    class WorkerConfig:
+        kv_transfer: KVTransferConfig
+        tensor_parallel_size: int = 1
+        kvcache_block_size: int = SHAPE["block"]
+        kv_cache_layout: str = "HND"
+
+    base_port = args.kv_port + 16 * (rank // 2)
+    loopback = world == 1
+    producer_worker = consumer_worker = None
+    if loopback or rank % 2 == 0:
+        kv = KVTransferConfig(kv_role="kv_producer", kv_port=base_port, engine_id="bench-prefill")
+        producer_worker = CudaIpcConnectorWorker(WorkerConfig(kv), 0)
+        producer_worker.register_kv_caches(src)
+    if loopback or rank % 2 == 1:
+        kv = KVTransferConfig(kv_role="kv_consumer", kv_port=base_port + 8, engine_id="bench-decode")
+        consumer_worker = CudaIpcConnectorWorker(WorkerConfig(kv), 0)
+        consumer_worker.register_kv_caches(dst)
+
+    def one_step(tag: str) -> tuple[float, int]:
+        sends = {f"{tag}-{i}": s.tolist() for i, (s, _) in enumerate(reqs)}
+        recvs = {f"{tag}-{i}": ReqToRecv(d.tolist(), s.tolist(), f"{tag}-{i}", "bench-prefill", "127.0.0.1",
+                                         base_port, 1) for i, (s, d) in enumerate(reqs)}
+        if world > 1:
+            dist.barrier(group=gloo)
+        torch.cuda.synchronize()
+        if producer_worker is not None:
+            producer_worker.start_load_kv(KVConnectorMetadata(reqs_to_send=sends))
+        t0 = time.perf_counter()
+        nbytes = 0
+        if consumer_worker is not None:
+            consumer_worker.start_load_kv(KVConnectorMetadata(reqs_to_recv=recvs))
+            pending = set(recvs)
+            deadline = time.monotonic() + 120
+            while pending and time.monotonic() < deadline:
+                out = consumer_worker.get_finished()
+                if out.failed_recving:
+                    raise RuntimeError(f"connector loads failed: {sorted(out.failed_recving)[:3]}")
+                for rid in out.finished_recving:
+                    nbytes += out.recv_stats[rid].num_bytes
+                pending -= out.finished_recving
+                if pending:
+                    time.sleep(50e-6)
+            if pending:
+                raise RuntimeError(f"{len(pending)} connector loads did not finish")
+        elapsed = (time.perf_counter() - t0) * 1e3
+        if producer_worker is not None:  # every held request is released once its reader has notified
+            left, deadline = set(sends), time.monotonic() + 60
+            while left and time.monotonic() < deadline:
+                left -= producer_worker.get_finished().finished_sending
+                if left:
+                    time.sleep(1e-3)
+            if left:
+                raise RuntimeError(f"{len(left)} held requests were never released")
+        return (elapsed if consumer_worker is not None else 0.0), nbytes
+
+    try:
+        one_step("warm")
+        times, nbytes = [], 0
+        for s in range(max(args.steps // 2, 2)):
+            ms, nbytes = one_step(f"s{s}")
+            times.append(ms)
+    finally:
+        for worker in (producer_worker, consumer_worker):
+            if worker is not None:
+                worker.shutdown()
+    return float(np.median(times)), nbytes
 
 
 def run_reference(args) -> None:
@@ -484,6 +558,8 @@ def main(argv=None):
     p.add_argument("--requests", type=int, default=64, help="a prefix of the 64 requests (small profiling cases)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true", help="skip the connector end-to-end timing")
+    p.add_argument("--kv-port", type=int, default=24600, help="first handshake port of the e2e connectors")
     args = p.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours" and args.steps > 0:
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
