@@ -1,22 +1,25 @@
 """Benchmark of the KV-cache transfer path: GB/s and ms per 8k-token request.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode pull|push] [--engine auto|lsu|tma]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload pair|hetero|mla] [--mode pull|push]
+                    [--engine auto|lsu|tma]
     python bench.py --impl reference ...      # the reference's CPU transfer path (restated in oracle/), host cores
 
-Workload: Qwen3-8B-shaped paged KV (36 layers x {K, V}, 8 KV heads x 128 dims, 256-token blocks, bf16, HND),
-64 requests with prompt lengths uniform in [1024, 8192], source and destination block ids drawn from seeded
-shuffled free lists, N(0,1) bf16 values. One step moves every block of every request once: one kvx_copy launch
-with one job per request.
+Workloads (seeded N(0,1) bf16 caches, block ids from seeded shuffled free lists):
+  pair    Qwen3-8B-shaped KV (36 layers x {K,V}, 8 KV heads x 128, 256-token blocks, HND), prefill TP1 -> decode TP1,
+          64 requests, prompt lengths uniform in [1024, 8192]. N=1: same-device loopback on cuda:0 (HBM-bound);
+          N even: N/2 independent pairs (ranks 2p -> 2p+1) over NVLink.
+  hetero  Qwen3-8B-shaped KV, prefill TP2 -> decode TP4 (head resharding), 128 requests, lengths log-uniform in
+          [512, 16384]; one group per 6 GPUs (prefill on the group's first 2 ranks, decode on its last 4).
+  mla     DeepSeek-V2-Lite-shaped latents (27 layers x 576, 64-token pages), prefill TP1 -> decode TP2 (each decode
+          rank takes a whole copy), 64 requests, lengths uniform in [2048, 16384]; one group per 3 GPUs.
 
-  N = 1   same-device loopback on cuda:0 (source and destination caches on one GPU): HBM-bound.
-  N even  N/2 prefill->decode pairs (ranks 2p -> 2p+1), one process per GPU, caches mapped over CUDA IPC; the
-          decode rank pulls (or, with --mode push, the prefill rank pushes) over NVLink. Pairs are independent
-          (weak scaling); no collective touches the data path.
+One step moves every block of every request once: on each launching rank one kvx_copy with one job per (request,
+head share). Groups are independent (weak scaling); no collective touches the data path.
 
-`value` is device-timed (CUDA events on the launching stream, max over ranks) with the caches resident in HBM;
-`e2e` times the same transfers through the public transport call (host block tables marshalled per step, launch,
-completion polled with the transfer's event) by the host clock. The caches exceed L2 many times over, so no flush
-is needed between steps.
+`value` is device-timed (CUDA events on the launching stream, max over ranks) with the caches resident in HBM:
+payload GB/s summed over decode ranks (the reference's byte count, nixl_connector.py:421 + base.py:106-108).
+`e2e` times the same loads through the connector's public API (CudaIpcConnectorWorker.start_load_kv ->
+get_finished) by the host clock. The caches exceed L2 by far, so no flush is needed between steps.
 """
 
 from __future__ import annotations
@@ -29,6 +32,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass
 
 import numpy as np
 
@@ -36,16 +40,54 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "KV transfer GB/s & ms per 8k-token request"
-SHAPE = dict(layers=36, kv_heads=8, head_dim=128, block=256, itemsize=2)
 BYTES_8K_REQUEST = 32 * 36 * 2 * 8 * 256 * 128 * 2  # 1,207,959,552: 32 blocks x 36 layers x K/V x 512 KiB
 NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
 
 
-def workload(seed: int = 0, n_requests: int = 64, lo: int = 1024, hi: int = 8192, block: int = 256):
-    """Prompt lengths and per-request (src, dst) block ids from seeded shuffled free lists."""
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    layers: int
+    kv_heads: int  # every rank's heads together; 0 for latents
+    head_dim: int  # latent width for latents
+    block: int
+    prefill_tp: int
+    decode_tp: int
+    n_requests: int
+    lengths: tuple  # (distribution, lo, hi)
+
+    @property
+    def mla(self) -> bool:
+        return self.kv_heads == 0
+
+    @property
+    def group_size(self) -> int:
+        return self.prefill_tp + self.decode_tp
+
+    def describe(self) -> str:
+        if self.mla:
+            return f"{self.layers} layers x latent {self.head_dim}, page {self.block} tokens, bf16"
+        return f"{self.layers} layers x {{K,V}}, {self.kv_heads} KV heads x {self.head_dim}, block {self.block} tokens, bf16, HND"
+
+
+WORKLOADS = {
+    "pair": Workload("qwen3-8b-kv", 36, 8, 128, 256, 1, 1, 64, ("uniform", 1024, 8192)),
+    "hetero": Workload("qwen3-8b-kv", 36, 8, 128, 256, 2, 4, 128, ("loguniform", 512, 16384)),
+    "mla": Workload("dsv2-lite-latent", 27, 0, 576, 64, 1, 2, 64, ("uniform", 2048, 16384)),
+}
+
+
+def workload(seed: int = 0, n_requests: int | None = None, spec: Workload = WORKLOADS["pair"]):
+    """Prompt lengths and per-request (src, dst) block ids from seeded shuffled free lists. A smaller n_requests
+    takes a prefix of the same draw."""
     rng = np.random.default_rng(seed)
-    lengths = rng.integers(lo, hi + 1, size=64)[:n_requests]  # a prefix of the same draw when fewer are asked
-    counts = [math.ceil(int(n) / block) for n in lengths]
+    dist, lo, hi = spec.lengths
+    if dist == "uniform":
+        lengths = rng.integers(lo, hi + 1, size=spec.n_requests)
+    else:
+        lengths = np.exp(rng.uniform(np.log(lo), np.log(hi), size=spec.n_requests)).astype(np.int64)
+    lengths = lengths[: n_requests or spec.n_requests]
+    counts = [math.ceil(int(n) / spec.block) for n in lengths]
     total = sum(counts)
     num_blocks = total + max(8, total // 16)  # slack, so ids are spread over a larger cache
     src_free, dst_free = rng.permutation(num_blocks), rng.permutation(num_blocks)
@@ -56,12 +98,16 @@ def workload(seed: int = 0, n_requests: int = 64, lo: int = 1024, hi: int = 8192
     return lengths, reqs, num_blocks
 
 
-def chunk_bytes(kv_heads: int) -> int:
-    return kv_heads * SHAPE["block"] * SHAPE["head_dim"] * SHAPE["itemsize"]
+def chunk_bytes(spec: Workload, heads: int) -> int:
+    if spec.mla:
+        return spec.block * spec.head_dim * 2
+    return heads * spec.block * spec.head_dim * 2
 
 
-def request_bytes(n_blocks: int, kv_heads: int = SHAPE["kv_heads"]) -> int:
-    return n_blocks * SHAPE["layers"] * 2 * chunk_bytes(kv_heads)
+def request_bytes(n_blocks: int, spec: Workload = WORKLOADS["pair"]) -> int:
+    """Payload of n_blocks for one decode rank holding every head (TP1)."""
+    parts = 1 if spec.mla else 2
+    return n_blocks * spec.layers * parts * chunk_bytes(spec, spec.kv_heads)
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -125,10 +171,11 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------ CPU baseline
 
 
-def cpu_baseline(lengths, reqs, seconds: float = 10.0, threads: int | None = None) -> dict:
+def cpu_baseline(reqs, spec: Workload = WORKLOADS["pair"], seconds: float = 10.0, threads: int | None = None) -> dict:
     """The reference's CPU transfer path, restated in C (oracle/kvx_oracle.c): per request, block_descs rows for
     both sides, then one memmove per row, rows spread over host threads. Timed on a bounded sample: the first
-    requests of the workload (at most 96 blocks) on host caches of the same shape, repeated for ~`seconds`."""
+    requests of the workload (at most 96 blocks) on host caches of the same shape (TP1 -> TP1), repeated for
+    ~`seconds`."""
     from oracle import c_oracle
     from oracle.kv_oracle import Region
 
@@ -140,63 +187,125 @@ def cpu_baseline(lengths, reqs, seconds: float = 10.0, threads: int | None = Non
         sample.append((src, dst))
         blocks += len(src)
     nb = blocks
-    layers = SHAPE["layers"]
-    shape = (2, nb, SHAPE["kv_heads"], SHAPE["block"], SHAPE["head_dim"])
-    src_caches = [np.full(shape, 0x3F80, dtype=np.uint16) for _ in range(layers)]
-    dst_caches = [np.zeros(shape, dtype=np.uint16) for _ in range(layers)]
+    if spec.mla:
+        shape = (1, nb, spec.block, spec.head_dim)
+    else:
+        shape = (2, nb, spec.kv_heads, spec.block, spec.head_dim)
+    src_caches = [np.full(shape, 0x3F80, dtype=np.uint16) for _ in range(spec.layers)]
+    dst_caches = [np.zeros(shape, dtype=np.uint16) for _ in range(spec.layers)]
     for a in dst_caches:
         a.fill(1)  # touch every page before timing
 
     def regions(caches):
-        return [Region(part.ctypes.data, part.strides[0], part.strides[1]) for c in caches for part in c]
+        return [Region(part.ctypes.data, part.strides[0], 0 if spec.mla else part.strides[1])
+                for c in caches for part in c]
 
     src_r, dst_r = regions(src_caches), regions(dst_caches)
-    # Remap the sample's ids onto the sample-sized caches, keeping the shuffled order.
     remap, at = [], 0
     rng = np.random.default_rng(1)
     src_perm, dst_perm = rng.permutation(nb), rng.permutation(nb)
-    for src, _ in sample:
+    for src, _ in sample:  # the sample's ids on sample-sized caches, still shuffled
         n = len(src)
         remap.append((src_perm[at : at + n], dst_perm[at : at + n]))
         at += n
     c_oracle.lib()
+    heads = spec.kv_heads
     moved, reps = 0, 0
     start = time.perf_counter()
     while True:
         for src_ids, dst_ids in remap:
-            d_addr, d_len = c_oracle.block_descs(dst_r, dst_ids, 0, SHAPE["kv_heads"], False)
-            s_addr, _ = c_oracle.block_descs(src_r, src_ids, 0, SHAPE["kv_heads"], False)
+            d_addr, d_len = c_oracle.block_descs(dst_r, dst_ids, 0, heads, spec.mla)
+            s_addr, _ = c_oracle.block_descs(src_r, src_ids, 0, heads, spec.mla)
             moved += c_oracle.read(d_addr, s_addr, d_len, threads)
         reps += 1
         elapsed = time.perf_counter() - start
         if elapsed >= seconds or reps >= 200:
             break
     gbs = moved / elapsed / 1e9
-    # Spot-check the copy: the first request's first destination chunk holds the source pattern.
-    assert int(dst_caches[0][0, remap[0][1][0], 0, 0, 0]) == 0x3F80
+    assert int(dst_caches[0][0, remap[0][1][0]].reshape(-1)[0]) == 0x3F80  # the copy happened
     return {
         "value": round(gbs, 3),
         "unit": "GB/s",
         "cores": threads,
         "kind": "port",
-        "sample": (f"first {len(sample)} requests of the workload ({nb} blocks, {request_bytes(nb) / 1e9:.2f} GB) on "
-                   f"host caches of the same shape, {reps} passes in {elapsed:.1f} s; C restatement of "
+        "sample": (f"first {len(sample)} requests of the workload ({nb} blocks, {request_bytes(nb, spec) / 1e9:.2f} GB)"
+                   f" on host caches of the same shape, {reps} passes in {elapsed:.1f} s; C restatement of "
                    "block_descs + one memmove per row, rows split over threads"),
         "ms_per_8k_request": round(BYTES_8K_REQUEST / (gbs * 1e9) * 1e3, 3),
         "host_cpus": os.cpu_count(),
     }
 
 
-# ------------------------------------------------------------------------------------------------ GPU arm
+# ------------------------------------------------------------------------------------------------ topology
 
 
-def alloc_cache(num_blocks: int, device, fill: bool, seed: int):
+@dataclass
+class Role:
+    group: int
+    side: str  # "prefill", "decode" or "idle" (or "both" for the 1-GPU loopback)
+    tp_rank: int
+
+
+def role_of(rank: int, world: int, spec: Workload) -> Role:
+    if world == 1:
+        if spec.group_size != 2:
+            raise SystemExit(f"the {spec.name} workload needs {spec.group_size} GPUs")
+        return Role(0, "both", 0)
+    groups = world // spec.group_size
+    if groups == 0:
+        raise SystemExit(f"the {spec.name} workload needs {spec.group_size} GPUs per group, got {world}")
+    group, index = divmod(rank, spec.group_size)
+    if group >= groups:
+        return Role(group, "idle", 0)
+    if index < spec.prefill_tp:
+        return Role(group, "prefill", index)
+    return Role(group, "decode", index - spec.prefill_tp)
+
+
+def plan(spec: Workload, role: Role, reqs, mode: str):
+    """What one rank launches: (peers, jobs). Cache 0 of every job list is this rank's own cache; cache k >= 1 is
+    peers[k-1] = (side, tp_rank) of the same group. Pull: a decode rank takes each of its shares from the prefill
+    rank holding it. Push: a prefill rank writes every share it holds into each decode rank that reads it. Latent
+    caches come whole from the first share only, as the reference reads them (nixl_connector.py:403)."""
+    from lean_vllm_b200.kv_transfer.shares import head_shares, split_heads
+    from lean_vllm_b200.kv_transfer.transport import CopyJob
+
+    heads = split_heads(spec.kv_heads, spec.decode_tp, spec.prefill_tp)
+    peers, jobs = [], []
+    if role.side == "both":  # loopback: cache 0 is the source, cache 1 the destination
+        shares = head_shares(0, 1, 1, heads)
+        peers = [("decode", 0)]
+        jobs = [CopyJob(0, 1, s, d, sh.remote_head, sh.local_head, sh.num_heads, i == 0)
+                for s, d in reqs for i, sh in enumerate(shares)]
+    elif role.side == "decode" and mode == "pull":
+        shares = head_shares(role.tp_rank, spec.decode_tp, spec.prefill_tp, heads)
+        for sh in shares:
+            if ("prefill", sh.remote_rank) not in peers:
+                peers.append(("prefill", sh.remote_rank))
+        jobs = [CopyJob(1 + peers.index(("prefill", sh.remote_rank)), 0, s, d, sh.remote_head, sh.local_head,
+                        sh.num_heads, i == 0) for s, d in reqs for i, sh in enumerate(shares)]
+    elif role.side == "prefill" and mode == "push":
+        for decode_rank in range(spec.decode_tp):
+            shares = head_shares(decode_rank, spec.decode_tp, spec.prefill_tp, heads)
+            mine = [(i, sh) for i, sh in enumerate(shares) if sh.remote_rank == role.tp_rank]
+            if not mine:
+                continue
+            peers.append(("decode", decode_rank))
+            jobs += [CopyJob(0, len(peers), s, d, sh.remote_head, sh.local_head, sh.num_heads, i == 0)
+                     for s, d in reqs for i, sh in mine]
+    return peers, jobs
+
+
+def alloc_cache(spec: Workload, tp: int, num_blocks: int, device, fill: bool, seed: int):
     import torch
 
-    shape = (2, num_blocks, SHAPE["kv_heads"], SHAPE["block"], SHAPE["head_dim"])
-    layers = []
+    if spec.mla:
+        shape = (1, num_blocks, spec.block, spec.head_dim)
+    else:
+        shape = (2, num_blocks, spec.kv_heads // tp, spec.block, spec.head_dim)
     g = torch.Generator(device=device).manual_seed(seed)
-    for _ in range(SHAPE["layers"]):
+    layers = []
+    for _ in range(spec.layers):
         t = torch.empty(shape, dtype=torch.bfloat16, device=device)
         if fill:
             t.normal_(generator=g)
@@ -214,72 +323,102 @@ def load_traffic() -> dict:
     return {}
 
 
+def digest(layers, ids, first_head: int, num_heads: int, mla: bool, device):
+    """Position-weighted digest of some blocks' heads (first and last layer): equal digests on both sides of a
+    copy mean the bytes landed."""
+    import torch
+
+    index = torch.as_tensor(ids, device=device, dtype=torch.long)
+    out = []
+    for layer in (0, len(layers) - 1):
+        part = layers[layer][:, index]
+        if not mla:
+            part = part[:, :, first_head : first_head + num_heads]
+        flat = part.contiguous().view(torch.int16).reshape(-1).to(torch.int64)
+        weights = torch.arange(flat.numel(), device=device, dtype=torch.int64) % 65521 + 1
+        out += [int(flat.sum().item()), int((flat * weights).sum().item())]
+    return out
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
 
     from lean_vllm_b200._native import ENGINE_AUTO, ENGINE_LSU, ENGINE_TMA, flags
     from lean_vllm_b200.kv_transfer import transport
+    from lean_vllm_b200.kv_transfer.shares import head_shares, split_heads
     from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
 
+    spec = WORKLOADS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}; launch N>1 with torchrun")
-    if world > 1 and world % 2:
-        raise SystemExit("N > 1 runs prefill->decode pairs, so N must be even")
+    role = role_of(rank, world, spec)
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     gloo = None
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
-        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=180))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
 
     engine = {"auto": ENGINE_AUTO, "lsu": ENGINE_LSU, "tma": ENGINE_TMA}[args.engine]
     copy_flags = flags(engine, args.tile_bytes, args.ctas_per_sm)
-    lengths, reqs, num_blocks = workload(args.seed, args.requests)
+    lengths, reqs, num_blocks = workload(args.seed, args.requests, spec)
     step_blocks = sum(len(s) for s, _ in reqs)
-    step_bytes = request_bytes(step_blocks)
-    pairs = max(world // 2, 1)
-    loopback = world == 1
-    producer = loopback or rank % 2 == 0
-    consumer = loopback or rank % 2 == 1
-    active = loopback or (consumer if args.mode == "pull" else producer)
+    heads = split_heads(spec.kv_heads, spec.decode_tp, spec.prefill_tp)
+    loopback = role.side == "both"
+    groups = 1 if loopback else world // spec.group_size
 
-    src = alloc_cache(num_blocks, device, fill=True, seed=1000 + rank) if producer else None
-    dst = alloc_cache(num_blocks, device, fill=False, seed=0) if consumer else None
+    src = dst = None
+    if role.side in ("prefill", "both"):
+        src = alloc_cache(spec, spec.prefill_tp, num_blocks, device, fill=True, seed=1000 + rank)
+    if role.side in ("decode", "both"):
+        dst = alloc_cache(spec, spec.decode_tp, num_blocks, device, fill=False, seed=0)
     torch.cuda.synchronize()
 
-    # Each side's cache as a CacheTable in the launching process: peers' caches through CUDA IPC.
-    mine = src if producer and not loopback else dst
-    handles = None
-    if not loopback:
-        exported = [transport.export(t.data_ptr()) for t in mine]
-        table = CacheTable.from_tensors(mine)
-        info = [None] * world
-        dist.all_gather_object(info, (exported, table.regions, table.num_blocks), group=gloo)
-        peer = rank ^ 1
-        handles = info[peer][0]
-        if active:
-            transport.enable_peer_access(local_rank, local_rank ^ 1)
-            peer_regions = []
-            for layer, blob in enumerate(handles):  # one exported tensor per layer: its K region, then V
-                k_addr = info[peer][1][2 * layer][0]
-                k_here = transport.open_mapping(blob)
-                for addr, bb, hb in info[peer][1][2 * layer : 2 * layer + 2]:
-                    peer_regions.append((k_here + (addr - k_addr), bb, hb))
-            peer_table = CacheTable(peer_regions, info[peer][2])
-            if producer:
-                caches = [CacheTable.from_tensors(src), peer_table]
-            else:
-                caches = [peer_table, CacheTable.from_tensors(dst)]
-    else:
-        caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
+    # Exchange every rank's cache description; map the peers this rank launches against.
+    mine = src if role.side == "prefill" else dst
+    info = [None] * world
+    if world > 1:
+        exported = [transport.export(t.data_ptr()) for t in mine] if mine is not None else []
+        table = CacheTable.from_tensors(mine) if mine is not None else None
+        dist.all_gather_object(info, (role.side, role.group, role.tp_rank, exported,
+                                      table.regions if table else None, table.num_blocks if table else 0),
+                               group=gloo)
 
-    jobs = [CopyJob(0, 1, s, d, 0, 0, SHAPE["kv_heads"]) for s, d in reqs] if active else []
+    def rank_of(group: int, side: str, tp_rank: int) -> int:
+        return group * spec.group_size + (tp_rank if side == "prefill" else spec.prefill_tp + tp_rank)
+
+    opened: list[bytes] = []
+
+    def peer_table(peer: int) -> CacheTable:
+        _, _, _, blobs, regions, nb = info[peer]
+        parts = 1 if spec.mla else 2
+        out = []
+        for layer, blob in enumerate(blobs):  # one exported tensor per layer: its K region, then V (or the latent)
+            first = regions[parts * layer][0]
+            here = transport.open_mapping(blob)
+            opened.append(blob)
+            for addr, bb, hb in regions[parts * layer : parts * layer + parts]:
+                out.append((here + (addr - first), bb, hb))
+        return CacheTable(out, nb)
+
+    # Jobs: one per (request, share) on the launching rank; its peers' caches mapped over CUDA IPC.
+    peers, jobs = plan(spec, role, reqs, args.mode)
+    launching = bool(jobs)
+    if loopback:
+        caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
+    elif launching:
+        own = dst if role.side == "decode" else src
+        caches = [CacheTable.from_tensors(own)] + [peer_table(rank_of(role.group, side, tp_rank))
+                                                   for side, tp_rank in peers]
+    else:
+        caches = []
+    my_bytes = transport.job_bytes(caches, jobs) if jobs else 0
     stream = torch.cuda.Stream(device=device)
     sid = stream.cuda_stream
 
@@ -306,44 +445,58 @@ def run_gpu(args) -> None:
         end.record(stream)
         barrier()
     launches = transport.launch_count() - launches0
-    elapsed_ms = start.elapsed_time(end) if active else 0.0
-    t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    elapsed_ms = start.elapsed_time(end) if launching else 0.0
+    stats = torch.tensor([elapsed_ms, float(launches), float(my_bytes)], device=device, dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    launch_total = torch.tensor([launches], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(launch_total)
-
-    # Correctness spot-check after timing: the first and last requests' blocks landed bit for bit (across a pair,
-    # by comparing position-weighted digests computed on each side).
-    def digest(layers, ids):
-        index = torch.as_tensor(ids, device=device, dtype=torch.long)
-        out = []
-        for layer in (0, SHAPE["layers"] - 1):
-            flat = layers[layer][:, index].contiguous().view(torch.int16).reshape(-1).to(torch.int64)
-            weights = torch.arange(flat.numel(), device=device, dtype=torch.int64) % 65521 + 1
-            out += [int(flat.sum().item()), int((flat * weights).sum().item())]
-        return out
-
-    ok = True
-    checks = [(reqs[0][0], reqs[0][1]), (reqs[-1][0], reqs[-1][1])]
-    if loopback:
-        ok = all(digest(dst, d) == digest(src, s) for s, d in checks)
+        gathered = [torch.zeros_like(stats) for _ in range(world)]
+        dist.all_gather(gathered, stats)
+        stats_all = torch.stack(gathered).cpu().numpy()
     else:
-        mine_digest = [digest(src, s) if producer else digest(dst, d) for s, d in checks]
-        digests = [None] * world
-        dist.all_gather_object(digests, mine_digest, group=gloo)
-        ok = digests[rank] == digests[rank ^ 1]
+        stats_all = stats.cpu().numpy()[None]
+    max_ms = float(stats_all[:, 0].max())
+    total_launches = int(stats_all[:, 1].sum())
+    step_bytes_total = float(stats_all[:, 2].sum())  # payload per step over all decode ranks of all groups
 
-    # e2e: the same loads through the connector's public API (start_load_kv -> get_finished), host clock.
+    # Correctness: for two requests, every decode rank's received heads equal the producer's, by digest.
+    ok = True
+    samples = [reqs[0], reqs[-1]]
+    if loopback:
+        ok = all(digest(dst, d, 0, heads, spec.mla, device) == digest(src, s, 0, heads, spec.mla, device)
+                 for s, d in samples)
+    elif world > 1:
+        mine_digests = {}
+        if role.side == "decode":
+            for i, sh in enumerate(head_shares(role.tp_rank, spec.decode_tp, spec.prefill_tp, heads)):
+                if spec.mla and i:
+                    continue
+                mine_digests[(role.tp_rank, i)] = [digest(dst, d, sh.local_head, sh.num_heads, spec.mla, device)
+                                                   for _, d in samples]
+        elif role.side == "prefill":
+            for decode_rank in range(spec.decode_tp):
+                for i, sh in enumerate(head_shares(decode_rank, spec.decode_tp, spec.prefill_tp, heads)):
+                    if sh.remote_rank != role.tp_rank or (spec.mla and i):
+                        continue
+                    mine_digests[(decode_rank, i)] = [digest(src, s, sh.remote_head, sh.num_heads, spec.mla, device)
+                                                      for s, _ in samples]
+        every = [None] * world
+        dist.all_gather_object(every, (role.group, role.side, mine_digests), group=gloo)
+        for group in range(groups):
+            got = {k: v for g, side, d in every if g == group and side == "decode" for k, v in d.items()}
+            want = {k: v for g, side, d in every if g == group and side == "prefill" for k, v in d.items()}
+            ok &= bool(got) and got == want
+
+    # e2e: the same loads through the connector's public API.
     e2e_ms, e2e_bytes = None, 0
     if args.steps and not args.no_e2e:
-        e2e_ms, e2e_bytes = e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device)
-        e = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        e2e_ms, e2e_bytes = e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo)
+        e = torch.tensor([e2e_ms, float(e2e_bytes)], device=device, dtype=torch.float64)
         if world > 1:
-            dist.all_reduce(e, op=dist.ReduceOp.MAX)
-        e2e_ms = float(e.item())
+            gathered = [torch.zeros_like(e) for _ in range(world)]
+            dist.all_gather(gathered, e)
+            e_all = torch.stack(gathered).cpu().numpy()
+        else:
+            e_all = e.cpu().numpy()[None]
+        e2e_ms, e2e_bytes = float(e_all[:, 0].max()), int(e_all[:, 1].sum())
 
     ok_t = torch.tensor([0.0 if ok else 1.0], device=device, dtype=torch.float64)
     if world > 1:
@@ -352,31 +505,39 @@ def run_gpu(args) -> None:
 
     if rank == 0:
         ms_per_step = max_ms / args.steps
-        total_bytes = step_bytes * pairs
-        gbs = total_bytes / (ms_per_step * 1e-3) / 1e9
-        per_pair_gbs = step_bytes / (ms_per_step * 1e-3) / 1e9
-        ms_8k = BYTES_8K_REQUEST / (per_pair_gbs * 1e9) * 1e3
+        gbs = step_bytes_total / (ms_per_step * 1e-3) / 1e9
+        per_group_bytes = step_bytes_total / groups
+        ms_8k = BYTES_8K_REQUEST / (per_group_bytes / (ms_per_step * 1e-3)) * 1e3
         peaks = {}
         peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
         if os.path.exists(peaks_path):
             with open(peaks_path) as f:
                 peaks = json.load(f)
-        traffic = load_traffic().get("loopback" if loopback else args.mode)
+        traffic = load_traffic().get("loopback" if loopback else f"{args.workload}-{args.mode}")
         if loopback:
             hbm = peaks.get("hbm_gbs", 6650.0)
-            achieved = 2 * step_bytes / (ms_per_step * 1e-3) / 1e9
+            achieved = 2 * step_bytes_total / (ms_per_step * 1e-3) / 1e9
             roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(achieved / hbm, 4),
-                        "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                        "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback",
                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                        "algorithmic_bytes_per_launch": 2 * step_bytes}
+                        "algorithmic_bytes_per_launch": int(2 * step_bytes_total)}
         else:
-            achieved = per_pair_gbs
+            # The busiest GPU's NVLink direction: each producer sends its decode ranks' shares of its heads.
+            per_group = step_bytes_total / groups
+            egress = per_group / spec.prefill_tp  # TP splits heads evenly; latents: each decode rank pulls whole
+            if spec.mla:
+                egress = per_group  # one producer feeds every decode rank a whole copy
+            ingress = per_group / spec.decode_tp
+            link_bytes = max(egress, ingress)
+            achieved = link_bytes / (ms_per_step * 1e-3) / 1e9
             roofline = {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
                         "frac": round(achieved / NVLINK_PEER_GBS, 4),
-                        "peak_source": "measured peer copy per direction (nominal 900)",
+                        "peak_source": "measured peer copy per direction on this pool (nominal 900 GB/s)",
+                        "link_bytes_per_step": int(link_bytes),
                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                        "algorithmic_bytes_per_launch": step_bytes}
+                        "algorithmic_bytes_per_launch": int(per_group / (spec.decode_tp if args.mode == "pull"
+                                                                         else spec.prefill_tp))}
         line = {
             "metric": METRIC,
             "value": round(gbs, 2),
@@ -392,50 +553,50 @@ def run_gpu(args) -> None:
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) bf16 caches, seeded shuffled block tables",
             "config": {
-                "workload": ("qwen3-8b-kv/loopback-1gpu" if loopback else f"qwen3-8b-kv/{pairs}x-pair-tp1to1"),
-                "shape": "36 layers x {K,V}, 8 KV heads x 128, block 256 tokens, bf16, HND",
+                "workload": (f"{spec.name}/loopback-1gpu" if loopback else
+                             f"{spec.name}/{groups}x-tp{spec.prefill_tp}to{spec.decode_tp}"),
+                "shape": spec.describe(),
                 "requests_per_step": len(reqs),
-                "prompt_lengths": f"uniform [1024, 8192], seed {args.seed}",
-                "blocks_per_step_per_pair": step_blocks,
-                "bytes_per_step_per_pair": step_bytes,
-                "pairs": pairs,
+                "prompt_lengths": f"{spec.lengths[0]} [{spec.lengths[1]}, {spec.lengths[2]}], seed {args.seed}",
+                "blocks_per_step_per_group": step_blocks,
+                "payload_bytes_per_step": int(step_bytes_total),
+                "groups": groups,
                 "mode": "loopback" if loopback else args.mode,
                 "engine": args.engine,
-                "parallelism": "1 GPU" if loopback else f"{pairs} independent prefill->decode pairs",
-                "l2": f"no flush: each step reads and writes {2 * step_bytes / 1e9:.1f} GB, far beyond the 126 MB L2",
+                "parallelism": ("1 GPU" if loopback else
+                                f"{groups} independent prefill TP{spec.prefill_tp} -> decode TP{spec.decode_tp} groups"),
+                "l2": f"no flush: each step moves {step_bytes_total / 1e9:.1f} GB, far beyond the 126 MB L2",
             },
             "roofline": roofline,
-            "gpu_launches": int(launch_total.item()),
+            "gpu_launches": total_launches,
             "clocks": clock_summary,
             "correct": bool(ok_t.item() == 0.0),
         }
         if e2e_ms is not None:
-            ids_bytes = 2 * 4 * step_blocks
-            line["e2e"] = {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            ids_bytes = 2 * 4 * step_blocks * spec.decode_tp * groups
+            line["e2e"] = {"value": round(e2e_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                            "ms_per_step": round(e2e_ms, 4),
-                           "h2d_bytes_per_step": ids_bytes * pairs, "d2h_bytes_per_step": 0,
+                           "h2d_bytes_per_step": ids_bytes, "d2h_bytes_per_step": 0,
                            "bytes_reported_by_connector": e2e_bytes,
-                           "path": ("CudaIpcConnectorWorker.start_load_kv(64 ReqToRecv from host lists) -> "
-                                    "get_finished() until all 64 finished_recving; one kvx launch per load, block "
-                                    "ids carried in the launch, completion by event query")}
+                           "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
+                                    "get_finished() until every load finished_recving; one kvx launch per load, "
+                                    "block ids carried in the launch, completion by event query")}
         if loopback and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(lengths, reqs, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(reqs, spec, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier()
-        if handles is not None and active:
-            for blob in handles:
-                transport.close_mapping(blob)
+        for blob in opened:
+            transport.close_mapping(blob)
         dist.destroy_process_group()
 
 
-def e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device):
-    """Times the step's loads through CudaIpcConnectorWorker (host clock, per step, consumer side): a producer
-    worker holds the source cache and a consumer worker loads every request. N=1 runs both in this process; a pair
-    runs the producer on rank 2p and the consumer on rank 2p+1. Returns (ms per step, bytes the connector counted)."""
+def e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo):
+    """Times a step's loads through CudaIpcConnectorWorker (host clock, consumer side, median over steps): each
+    group's prefill ranks hold the source cache and its decode ranks load every request, shares and all. The 1-GPU
+    loopback runs both workers in this process. Returns (ms per step, bytes the connector counted here)."""
     import torch
     import torch.distributed as dist
-    from dataclasses import dataclass
 
     from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVTransferConfig, ReqToRecv
     from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorWorker
@@ -444,25 +605,24 @@ def e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device):
     class WorkerConfig:
         kv_transfer: KVTransferConfig
         tensor_parallel_size: int = 1
-        kvcache_block_size: int = SHAPE["block"]
+        kvcache_block_size: int = spec.block
         kv_cache_layout: str = "HND"
 
-    base_port = args.kv_port + 16 * (rank // 2)
-    loopback = world == 1
+    base_port = args.kv_port + 16 * role.group
     producer_worker = consumer_worker = None
-    if loopback or rank % 2 == 0:
-        kv = KVTransferConfig(kv_role="kv_producer", kv_port=base_port, engine_id="bench-prefill")
-        producer_worker = CudaIpcConnectorWorker(WorkerConfig(kv), 0)
+    if role.side in ("prefill", "both"):
+        kv = KVTransferConfig(kv_role="kv_producer", kv_port=base_port, engine_id=f"bench-prefill-{role.group}")
+        producer_worker = CudaIpcConnectorWorker(WorkerConfig(kv, spec.prefill_tp), role.tp_rank)
         producer_worker.register_kv_caches(src)
-    if loopback or rank % 2 == 1:
-        kv = KVTransferConfig(kv_role="kv_consumer", kv_port=base_port + 8, engine_id="bench-decode")
-        consumer_worker = CudaIpcConnectorWorker(WorkerConfig(kv), 0)
+    if role.side in ("decode", "both"):
+        kv = KVTransferConfig(kv_role="kv_consumer", kv_port=base_port + 8, engine_id=f"bench-decode-{role.group}")
+        consumer_worker = CudaIpcConnectorWorker(WorkerConfig(kv, spec.decode_tp), role.tp_rank)
         consumer_worker.register_kv_caches(dst)
 
     def one_step(tag: str) -> tuple[float, int]:
         sends = {f"{tag}-{i}": s.tolist() for i, (s, _) in enumerate(reqs)}
-        recvs = {f"{tag}-{i}": ReqToRecv(d.tolist(), s.tolist(), f"{tag}-{i}", "bench-prefill", "127.0.0.1",
-                                         base_port, 1) for i, (s, d) in enumerate(reqs)}
+        recvs = {f"{tag}-{i}": ReqToRecv(d.tolist(), s.tolist(), f"{tag}-{i}", f"bench-prefill-{role.group}",
+                                         "127.0.0.1", base_port, spec.prefill_tp) for i, (s, d) in enumerate(reqs)}
         if world > 1:
             dist.barrier(group=gloo)
         torch.cuda.synchronize()
@@ -486,7 +646,7 @@ def e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device):
             if pending:
                 raise RuntimeError(f"{len(pending)} connector loads did not finish")
         elapsed = (time.perf_counter() - t0) * 1e3
-        if producer_worker is not None:  # every held request is released once its reader has notified
+        if producer_worker is not None:  # every held request is released once all its readers have notified
             left, deadline = set(sends), time.monotonic() + 60
             while left and time.monotonic() < deadline:
                 left -= producer_worker.get_finished().finished_sending
@@ -506,7 +666,7 @@ def e2e_connector(args, world, rank, src, dst, reqs, barrier, gloo, device):
         for worker in (producer_worker, consumer_worker):
             if worker is not None:
                 worker.shutdown()
-    return float(np.median(times)), nbytes
+    return (float(np.median(times)) if consumer_worker is not None else 0.0), nbytes
 
 
 def run_reference(args) -> None:
@@ -514,11 +674,12 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    lengths, reqs, num_blocks = workload(args.seed)
+    spec = WORKLOADS[args.workload]
+    lengths, reqs, num_blocks = workload(args.seed, args.requests, spec)
     cpu_seconds = max(2.0, min(args.cpu_seconds, 40.0 / max(args.steps + args.warmup, 1)))
     for _ in range(args.warmup):
-        cpu_baseline(lengths, reqs, seconds=0.5)
-    results = [cpu_baseline(lengths, reqs, seconds=cpu_seconds) for _ in range(max(args.steps, 1))]
+        cpu_baseline(reqs, spec, seconds=0.5)
+    results = [cpu_baseline(reqs, spec, seconds=cpu_seconds) for _ in range(max(args.steps, 1))]
     gbs = float(np.median([r["value"] for r in results]))
     base = results[0]
     line = {
@@ -535,8 +696,9 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: bf16-sized host caches, seeded shuffled block tables",
-        "config": {"workload": "qwen3-8b-kv (reference CPU transfer path)", "requests": "bounded sample per step",
-                   "prompt_lengths": f"uniform [1024, 8192], seed {args.seed}"},
+        "config": {"workload": f"{spec.name} (reference CPU transfer path, TP1 -> TP1)",
+                   "requests": "bounded sample per step",
+                   "prompt_lengths": f"{spec.lengths[0]} [{spec.lengths[1]}, {spec.lengths[2]}], seed {args.seed}"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": base["cores"], "kind": "port",
                          "sample": base["sample"]},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -550,19 +712,18 @@ def main(argv=None):
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="pair")
     p.add_argument("--mode", choices=["pull", "push"], default="pull")
     p.add_argument("--engine", choices=["auto", "lsu", "tma"], default="auto")
     p.add_argument("--tile-bytes", type=int, default=0)
     p.add_argument("--ctas-per-sm", type=int, default=0)
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--requests", type=int, default=64, help="a prefix of the 64 requests (small profiling cases)")
+    p.add_argument("--requests", type=int, default=0, help="a prefix of the workload's requests (small cases)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the connector end-to-end timing")
     p.add_argument("--kv-port", type=int, default=24600, help="first handshake port of the e2e connectors")
     args = p.parse_args(argv)
-    if args.warmup < 3 and args.impl == "ours" and args.steps > 0:
-        print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
     else:
