@@ -39,7 +39,10 @@ extern "C" {
 #define KVX_ERR_RANGE (-3)     /* a block id or head range outside its cache (nixl_connector.py:398-399) */
 #define KVX_ERR_DEVICE (-4)    /* a kernel gave up a bounded wait; see kvx_device_error */
 
-/* Copy engines for kvx_copy/kvx_transfer flags (low byte). */
+/* kvx_copy/kvx_transfer/kvx_pack/kvx_push/kvx_scatter flags word: bits 0-7 engine (below), bits 8-15 log2 of the
+ * tile size (0: 32 KiB), bits 16-23 CTAs per SM (0: 1 for TMA, 2 for LSU), bits 24-31 how many SMs the grid may
+ * cover (0: every SM; a copy that runs beside compute can be held to a few). */
+/* Copy engines (low byte of flags). */
 #define KVX_ENGINE_AUTO 0      /* TMA bulk copies when every address and length is 16-byte aligned, else LSU */
 #define KVX_ENGINE_LSU 1       /* vectorised ld/st through the SMs' load/store units */
 #define KVX_ENGINE_TMA 2       /* cp.async.bulk global->smem->global, one issuing thread per CTA */

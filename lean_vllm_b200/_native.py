@@ -142,11 +142,14 @@ def check(rc: int) -> int:
     raise (KvxRangeError if rc == KVX_ERR_RANGE else KvxError)(rc, message)
 
 
-def flags(engine: int = ENGINE_AUTO, tile_bytes: int = 0, ctas_per_sm: int = 0) -> int:
-    """kvx_copy's flags word: engine, tile size (a power of two, 0 for the default) and CTAs per SM."""
+def flags(engine: int = ENGINE_AUTO, tile_bytes: int = 0, ctas_per_sm: int = 0, sm_budget: int = 0) -> int:
+    """kvx_copy's flags word: engine, tile size (a power of two, 0 for the default), CTAs per SM, and how many SMs
+    the grid may cover (0 for all; a copy beside compute can be held to a few)."""
     log_tile = 0
     if tile_bytes:
         log_tile = tile_bytes.bit_length() - 1
         if 1 << log_tile != tile_bytes:
             raise ValueError(f"tile_bytes {tile_bytes} is not a power of two")
-    return engine | (log_tile << 8) | (ctas_per_sm << 16)
+    if not 0 <= ctas_per_sm < 256 or not 0 <= sm_budget < 256:
+        raise ValueError("ctas_per_sm and sm_budget are 0..255")
+    return engine | (log_tile << 8) | (ctas_per_sm << 16) | (sm_budget << 24)

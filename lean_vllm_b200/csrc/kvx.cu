@@ -423,9 +423,11 @@ struct Config {
     int vec;          // LSU vector bytes
     uint32_t tile_bytes;
     int ctas_per_sm;
+    int sm_budget;    // SMs the grid may cover (0: all)
 };
 
-// flags: bits 0-7 engine, bits 8-15 log2(tile bytes) (0: default), bits 16-23 CTAs per SM (0: default).
+// flags: bits 0-7 engine, bits 8-15 log2(tile bytes) (0: default), bits 16-23 CTAs per SM (0: default),
+// bits 24-31 SM budget (0: every SM) -- a copy that runs beside compute can be held to a few SMs.
 int choose(int flags, uint64_t align_bits, Config &cfg) {
     const int engine = flags & 0xff;
     if (engine != KVX_ENGINE_AUTO && engine != KVX_ENGINE_LSU && engine != KVX_ENGINE_TMA)
@@ -438,6 +440,7 @@ int choose(int flags, uint64_t align_bits, Config &cfg) {
     cfg.engine = (engine == KVX_ENGINE_LSU || !tma_ok) ? KVX_ENGINE_LSU : KVX_ENGINE_TMA;
     const int log_tile = (flags >> 8) & 0xff;
     const int ctas = (flags >> 16) & 0xff;
+    cfg.sm_budget = (flags >> 24) & 0xff;
     if (cfg.engine == KVX_ENGINE_TMA) {
         cfg.tile_bytes = log_tile ? (1u << log_tile) : (32u << 10);
         cfg.ctas_per_sm = ctas ? ctas : 1;
@@ -456,7 +459,8 @@ int launch(Params &p, const Config &cfg, cudaStream_t stream) {
     if (p.total_tiles == 0) return KVX_OK;
     DeviceInfo *info;
     if (int rc = device_info(&info)) return rc;
-    const uint64_t cap = (uint64_t)info->sms * cfg.ctas_per_sm;
+    const int sms = cfg.sm_budget > 0 && cfg.sm_budget < info->sms ? cfg.sm_budget : info->sms;
+    const uint64_t cap = (uint64_t)sms * cfg.ctas_per_sm;
     const unsigned grid = (unsigned)std::min<uint64_t>(p.total_tiles, cap);
     p.error_code = 1;
     if (cfg.engine == KVX_ENGINE_TMA) {

@@ -9,6 +9,11 @@ environment_variables: dict[str, Callable[[], Any]] = {
     "LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT": lambda: float(os.getenv("LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT", "480")),
     # kvx copy engine for connector transfers: "auto", "lsu" or "tma".
     "LEAN_VLLM_KVX_ENGINE": lambda: os.getenv("LEAN_VLLM_KVX_ENGINE", "auto").lower(),
+    # A decode (kv_consumer) rank also answers handshakes on kv_port + rank, so prefill ranks can push into it.
+    "LEAN_VLLM_KVX_ACCEPT_PUSH": lambda: os.getenv("LEAN_VLLM_KVX_ACCEPT_PUSH", "0").strip().lower()
+    not in ("", "0", "false"),
+    # SMs a per-layer save's copy may use while the prefill computes (0: every SM).
+    "LEAN_VLLM_KVX_SAVE_SMS": lambda: int(os.getenv("LEAN_VLLM_KVX_SAVE_SMS", "16")),
 }
 
 

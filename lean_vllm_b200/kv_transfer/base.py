@@ -86,7 +86,10 @@ def check_kv_transfer_params(params, kv_transfer: KVTransferConfig | None) -> st
 
 @dataclass(slots=True)
 class ReqToRecv:
-    """A remote prefill's blocks and the local blocks they land in, aligned (reference base.py:75-85)."""
+    """A remote prefill's blocks and the local blocks they land in, aligned (reference base.py:75-85).
+
+    `pushed` is this package's extension: the prefill instance writes the blocks itself, layer by layer as it
+    computes them (ReqToSave on its side), and this rank only waits for its word that they have landed."""
 
     local_block_ids: list[int]
     remote_block_ids: list[int]
@@ -95,17 +98,36 @@ class ReqToRecv:
     remote_host: str
     remote_port: int
     remote_tp_size: int = 1
+    pushed: bool = False
+
+
+@dataclass(slots=True)
+class ReqToSave:
+    """This package's extension (no counterpart in the reference): a request being prefilled here whose blocks are
+    pushed, layer by layer during the prefill, into a decode instance's already allocated blocks. `local_block_ids`
+    are this instance's, `remote_block_ids` the decode instance's, aligned; `remote_*` name the decode instance
+    (its kv_ip, kv_port, engine_id and tensor-parallel size)."""
+
+    local_block_ids: list[int]
+    remote_block_ids: list[int]
+    remote_engine_id: str
+    remote_host: str
+    remote_port: int
+    remote_tp_size: int = 1
 
 
 @dataclass(slots=True)
 class KVConnectorMetadata:
-    """One step's instructions for every worker half (reference base.py:88-96)."""
+    """One step's instructions for every worker half (reference base.py:88-96). `reqs_to_save` (requests this step
+    prefills whose KV is pushed layer by layer) is this package's extension; it defaults to empty, so metadata built
+    by the reference's scheduler half behaves exactly as there."""
 
     reqs_to_recv: dict[str, ReqToRecv] = field(default_factory=dict)
     reqs_to_send: dict[str, list[int]] = field(default_factory=dict)  # held blocks a decode instance may now read
+    reqs_to_save: dict[str, ReqToSave] = field(default_factory=dict)
 
     def __bool__(self):
-        return bool(self.reqs_to_recv) or bool(self.reqs_to_send)
+        return bool(self.reqs_to_recv) or bool(self.reqs_to_send) or bool(self.reqs_to_save)
 
 
 @dataclass(slots=True)

@@ -9,6 +9,10 @@ that gathers the shares' blocks from every producer rank's HBM over NVLink and s
 The launch waits on the stream for the load's ready event (no host synchronisation), completion is a CUDA event
 polled without blocking, and a consumer rank tells each producer rank it read from once its bytes have landed
 (the NIXL notification's role) over the same ZMQ channel as the handshake.
+
+It adds a layer-by-layer push the reference does not have (its docs list vLLM's save_kv_layer as unsupported,
+docs/disaggregated-prefill.md:29-30): given ReqToSave entries naming a decode instance's allocated blocks, a
+prefill rank copies each layer's blocks into them from save_kv_layer while later layers compute, on a few SMs.
 """
 
 from __future__ import annotations
@@ -31,8 +35,10 @@ from lean_vllm_b200.kv_transfer.base import (
     KVConnectorWorker,
     KVTransferStats,
     ReqToRecv,
+    ReqToSave,
 )
 from lean_vllm_b200.kv_transfer.shares import Share, head_shares, readers_of, split_heads
+from lean_vllm_b200.kv_transfer.transport import CopyJob
 
 logger = logging.getLogger(__name__)
 
@@ -124,31 +130,64 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
 
 @dataclass(slots=True)
 class _Remote:
-    """A producer rank as its handshake described it, with its cache mapped here."""
+    """A peer rank as its handshake described it, with its cache mapped here."""
 
     engine_id: str
     tp_size: int
     num_blocks: int
     exported: dict
-    table: object  # the transport's view of the producer rank's cache, mapped into this process
+    table: object  # the transport's view of the peer rank's cache, mapped into this process
     sock: object  # DEALER kept open for notifications
 
 
 @dataclass(slots=True)
 class _Load:
-    """One request's load: one kernel launch over every share."""
+    """One request's pull: one kernel launch over every share."""
 
     req: ReqToRecv
     transfer: object = None
-    notify: list = field(default_factory=list)  # (remote key, message) to send once the bytes have landed
+    notify: list = field(default_factory=list)  # (remote key, message, rank) to send once the bytes have landed
     unnotified: set = field(default_factory=set)  # producer ranks no notification has reached
     started: float = field(default_factory=monotonic)
     num_bytes: int = 0
     failed: bool = False
 
 
+@dataclass(slots=True)
+class _Save:
+    """A request this producer rank pushes, layer by layer, into a decode instance's blocks."""
+
+    req: ReqToSave
+    targets: list  # (remote key, decode rank, [(share index, Share)]): the decode ranks that take heads from here
+    tables: list = field(default_factory=list)  # their caches, mapped here, aligned with targets
+    ready: bool = False  # every target mapped
+    failed: bool = False
+    pushed: set = field(default_factory=set)  # layers launched
+    inflight: int = 0  # launches not yet landed
+    handed_over: bool = False  # the prefill is over (engine thread): no more per-layer pushes
+    finishing: bool = False  # what was left is queued (transfer thread): done once nothing is in flight
+    started: float = field(default_factory=monotonic)
+
+
+@dataclass(slots=True)
+class _Wait:
+    """A pushed load on a decode rank: it waits for every producer rank holding its heads to say they landed."""
+
+    req: ReqToRecv
+    expected: set
+    num_bytes: int
+    started: float = field(default_factory=monotonic)
+
+
 class CudaIpcConnectorWorker(KVConnectorWorker):
-    """One rank's half, as NixlConnectorWorker (nixl_connector.py:195-520) with the kvx transport under it."""
+    """One rank's half, as NixlConnectorWorker (nixl_connector.py:195-520) with the kvx transport under it.
+
+    Pull (the reference's contract): a decode rank copies its heads of a finished prefill's blocks from every
+    producer rank holding them, then notifies each. Push (this package's per-layer save): a prefill rank given
+    ReqToSave in its metadata copies each layer's blocks into the decode ranks' blocks from save_kv_layer, beside the
+    prefill's compute, and once the request is handed over and every copy has landed it tells each decode rank (which
+    holds a ReqToRecv with pushed=True) and frees the blocks.
+    """
 
     def __init__(self, config, rank: int):
         if config.kv_cache_layout != "HND":
@@ -157,14 +196,18 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self.rank = rank
         self.tp_size = config.tensor_parallel_size
         self.block_size = config.kvcache_block_size
+        self.accept_push = bool(getattr(config, "kvx_accept_push", False)) or envs.LEAN_VLLM_KVX_ACCEPT_PUSH
         self.kv_caches: list = []
         self.num_heads = 0  # every rank's key heads together; 0 for a latent-only model
         self.layout: dict = {}
+        self.layer_regions: list[tuple[int, int]] = []  # (first region, count) of each layer
         self.transport = None
         self.node = node_id()
-        self._lock = threading.Lock()  # guards the three maps below, shared with the transfer thread
+        self._lock = threading.Lock()  # guards the maps below that both threads touch
         self._reqs_to_send: dict[str, float] = {}  # request -> deadline for its readers
         self._notified: dict[str, list] = {}  # request -> [notifications, readers, first seen]
+        self._saves: dict[str, _Save] = {}  # producer: requests pushed layer by layer
+        self._saved: dict[str, dict] = {}  # decode: request -> {producer rank: landed ok}, may precede the wait
         self._finished = KVConnectorOutput()
         self._queue: queue.Queue = queue.Queue()
         self._context = zmq.Context()
@@ -172,13 +215,15 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._server = None
         self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
         self._loads: dict[str, _Load] = {}  # transfer thread only
+        self._waits: dict[str, _Wait] = {}  # transfer thread only
+        self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
         self._thread: threading.Thread | None = None
 
     # -------------------------------------------------------------------------------------------- engine thread
 
     def register_kv_caches(self, kv_caches: list):
         self.kv_caches = list(kv_caches)
-        layers = []
+        layers, at = [], 0
         for cache in self.kv_caches:
             if cache.dim() == 5:  # keys and values, (2, block, head, token, dim)
                 _, _, heads, tokens, dim = cache.shape
@@ -186,11 +231,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 layers.append(["kv", str(cache.dtype), self.num_heads, tokens, dim])
             else:  # latents, (1, block, token, dim)
                 layers.append(["latent", str(cache.dtype), *cache.shape[2:]])
+            self.layer_regions.append((at, cache.size(0)))
+            at += cache.size(0)
         # What a peer must match: every rank's heads together, so the two sides may split them differently.
         self.layout = {"block_size": self.block_size, "layers": layers}
         self.transport = make_transport(self.kv_caches)
         kv = self.kv_transfer
-        if kv.is_producer:
+        if kv.is_producer or self.accept_push:
             port = kv.kv_port + self.rank
             server = self._context.socket(zmq.ROUTER)
             try:
@@ -203,17 +250,63 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._thread.start()
 
     def start_load_kv(self, metadata: KVConnectorMetadata):
+        for request_id, req in getattr(metadata, "reqs_to_save", {}).items():
+            with self._lock:
+                known = request_id in self._saves
+                if not known:
+                    self._saves[request_id] = _Save(req, self._targets(req))
+            if not known:
+                self._queue.put(("connect", request_id))
         if metadata.reqs_to_send:
             deadline = monotonic() + envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+            finishing = []
             with self._lock:
                 for request_id in metadata.reqs_to_send:
+                    save = self._saves.get(request_id)
+                    if save is not None:
+                        save.handed_over = True
+                        finishing.append(request_id)
+                        continue
                     self._reqs_to_send[request_id] = deadline
                     self._release_if_read(request_id)
+            if finishing:
+                ready = self.transport.ready_marker()
+                for request_id in finishing:
+                    self._queue.put(("finish", request_id, ready))
         if metadata.reqs_to_recv:
             # Freshly allocated blocks may still be written by a step in flight; the copy waits for it on the GPU.
             ready = self.transport.ready_marker()
             for request_id, req in metadata.reqs_to_recv.items():
-                self._queue.put((request_id, req, ready))
+                self._queue.put(("load", request_id, req, ready))
+
+    def save_kv_layer(self, layer_index: int):
+        """Pushes layer `layer_index` of every request being saved whose decode ranks are mapped, in one launch on
+        the side stream after the layer's store (an event on the engine's stream), held to a few SMs."""
+        with self._lock:
+            active = [s for s in self._saves.values()
+                      if s.ready and not s.failed and not s.handed_over and layer_index not in s.pushed]
+            if not active:
+                return
+            for save in active:
+                save.pushed.add(layer_index)
+                save.inflight += 1
+        try:
+            tables, jobs = self._push_jobs(active)
+            ready = self.transport.ready_marker()
+            xfer = self.transport.post(tables, jobs, ready, layer=self.layer_regions[layer_index],
+                                       flags=self._save_flags())
+        except Exception as error:  # noqa: BLE001 - a failed save fails its loads, never the step
+            logger.warning("pushing layer %d failed: %s", layer_index, error)
+            with self._lock:
+                for save in active:
+                    save.inflight -= 1
+                    save.failed = True
+            return
+        with self._lock:
+            self._pushes.append((xfer, active))
+
+    def wait_for_save(self):
+        """Saves are ordered after their layers on the GPU and awaited on the transfer thread: nothing to do."""
 
     def get_finished(self) -> KVConnectorOutput:
         now = monotonic()
@@ -251,26 +344,61 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         if entry is not None and entry[0] >= entry[1]:
             self._release(request_id)
 
+    def _heads(self, req) -> int:
+        return split_heads(self.num_heads, self.tp_size, req.remote_tp_size)
+
+    def _targets(self, req: ReqToSave) -> list:
+        """The decode ranks that take heads from this rank, with those shares (seen from each decode rank)."""
+        heads = self._heads(req)
+        targets = []
+        for decode_rank in range(req.remote_tp_size):
+            shares = head_shares(decode_rank, req.remote_tp_size, self.tp_size, heads)
+            mine = [(i, share) for i, share in enumerate(shares) if share.remote_rank == self.rank]
+            if mine:
+                targets.append(((req.remote_host, req.remote_port + decode_rank), decode_rank, mine))
+        return targets
+
+    def _push_jobs(self, saves: list[_Save]) -> tuple[list, list]:
+        tables, jobs = [], []
+        for save in saves:
+            for (key, _, mine), table in zip(save.targets, save.tables):
+                tables.append(table)
+                k = len(tables)
+                for i, share in mine:
+                    jobs.append(CopyJob(0, k, save.req.local_block_ids, save.req.remote_block_ids, share.remote_head,
+                                        share.local_head, share.num_heads, i == 0))
+        return tables, jobs
+
+    def _save_flags(self):
+        return getattr(self.transport, "save_flags", None)
+
     # -------------------------------------------------------------------------------------------- transfer thread
 
     def _run(self):
         try:
             self.transport.bind_thread()
             while True:
-                wait = BUSY_WAIT if self._loads else IDLE_WAIT
+                busy = self._loads or self._waits or self._pushes or self._saves
                 try:
-                    items = [self._queue.get(timeout=wait)]
+                    items = [self._queue.get(timeout=BUSY_WAIT if busy else IDLE_WAIT)]
                 except queue.Empty:
                     items = []
                 while not self._queue.empty():
                     items.append(self._queue.get_nowait())
                 if None in items:
                     return
-                for request_id, req, ready in items:
-                    self._start(request_id, req, ready)
+                for item in items:
+                    if item[0] == "load":
+                        self._start(*item[1:])
+                    elif item[0] == "connect":
+                        self._connect(item[1])
+                    elif item[0] == "finish":
+                        self._finish(*item[1:])
                 if self._server is not None:
                     self._serve()
                 self._poll()
+                self._poll_pushes()
+                self._poll_waits()
         except zmq.ContextTerminated:
             pass
         finally:
@@ -281,13 +409,16 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if load.transfer is not None:
                 self.transport.wait(load.transfer)  # bytes still landing in blocks the engine would reuse
                 self.transport.release(load.transfer)
+        for xfer, _ in self._pushes:
+            self.transport.wait(xfer)
+            self.transport.release(xfer)
         for remote in self._remotes.values():
             self.transport.close(remote.exported)
             remote.sock.close()
         if self._server is not None:
             self._server.close()
 
-    # Producer: answer handshakes, count the notifications that end each request's reads.
+    # Serving: handshakes, and the notifications that end reads (producer) or pushes (decode).
 
     def _serve(self):
         while True:
@@ -305,6 +436,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if op == "notify":
                 self._count(message.get("message", ""))
                 continue
+            if op == "saved":
+                with self._lock:
+                    self._saved.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
+                        message.get("ok"))
+                continue
             if op == "handshake":
                 reply = {
                     "ok": True,
@@ -320,7 +456,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             try:
                 self._server.send_multipart([identity, json.dumps(reply).encode()], zmq.NOBLOCK)
             except zmq.Again:
-                logger.warning("a KV handshake went unanswered: its consumer is not reading")
+                logger.warning("a KV handshake went unanswered: its peer is not reading")
 
     def _count(self, message: str):
         try:
@@ -334,12 +470,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             entry[0] += 1
             self._release_if_read(request_id)
 
-    # Consumer: one launch per load, then poll it.
-
-    def _heads(self, req: ReqToRecv) -> int:
-        return split_heads(self.num_heads, self.tp_size, req.remote_tp_size)
+    # Pull: one launch per load, then poll it.
 
     def _start(self, request_id: str, req: ReqToRecv, ready):
+        if getattr(req, "pushed", False):
+            self._start_wait(request_id, req)
+            return
         load = self._loads[request_id] = _Load(req)
         try:
             heads = self._heads(req)
@@ -353,14 +489,17 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 readers = readers_of(share.remote_rank, req.remote_tp_size, self.tp_size, heads)
                 key = (req.remote_host, req.remote_port + share.remote_rank)
                 message = f"{req.remote_request_id}:{readers}"
-                job = (share, i == 0)  # latents come whole from the first producer rank only
-                nbytes = self.transport.job_bytes(remote.table, req, *job)
+                # Latents come whole from the first producer rank only (nixl_connector.py:403).
+                job = CopyJob(1, 0, req.remote_block_ids, req.local_block_ids, share.remote_head, share.local_head,
+                              share.num_heads, i == 0)
+                nbytes = self.transport.job_bytes([remote.table], [job])
                 if nbytes == 0:
                     self._notify(key, message)  # nothing to read from this rank, but it must count this reader
                     load.unnotified.discard(share.remote_rank)
                     continue
                 tables.append(remote.table)
-                jobs.append((len(tables) - 1, req, *job))
+                job.src = len(tables)
+                jobs.append(job)
                 load.notify.append((key, message, share.remote_rank))
                 load.num_bytes += nbytes
             load.started = monotonic()
@@ -392,14 +531,17 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     self._finished.recv_stats[request_id] = KVTransferStats(monotonic() - load.started,
                                                                            load.num_bytes)
 
-    def _notify(self, key, message: str):
+    def _send(self, key, message: dict):
         remote = self._remotes.get(key)
         if remote is None:
             return
         try:
-            remote.sock.send(json.dumps({"op": "notify", "message": message}).encode(), zmq.NOBLOCK)
-        except zmq.ZMQError as error:  # the producer frees at its timeout instead
+            remote.sock.send(json.dumps(message).encode(), zmq.NOBLOCK)
+        except zmq.ZMQError as error:  # the peer times out instead
             logger.debug("notifying %s:%d failed: %s", key[0], key[1], error)
+
+    def _notify(self, key, message: str):
+        self._send(key, {"op": "notify", "message": message})
 
     def _fail(self, load: _Load, error: Exception, in_flight: bool = False):
         req = load.req
@@ -419,8 +561,125 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             load.unnotified.discard(remote_rank)
         load.notify = []
 
-    def _handshake(self, req: ReqToRecv, remote_rank: int) -> _Remote:
-        """The producer rank's cache, asked for once per producer and mapped here, checked to match this engine."""
+    # Push, producer side: map the decode ranks, catch up on layers no save_kv_layer pushed, report landing.
+
+    def _connect(self, request_id: str):
+        with self._lock:
+            save = self._saves.get(request_id)
+        if save is None:
+            return
+        try:
+            tables = [self._handshake(save.req, decode_rank).table for _, decode_rank, _ in save.targets]
+            with self._lock:
+                save.tables = tables
+                save.ready = True
+        except Exception as error:  # noqa: BLE001
+            logger.warning("cannot push the KV of %s to %s:%d, so the decode instance prefills it: %s", request_id,
+                           save.req.remote_host, save.req.remote_port, error)
+            with self._lock:
+                save.failed = True
+
+    def _finish(self, request_id: str, ready):
+        with self._lock:
+            save = self._saves.get(request_id)
+            if save is None:
+                return
+            if not save.ready:
+                save.failed = True  # never mapped: nothing landed, nothing will
+            missing = [] if save.failed else [i for i in range(len(self.layer_regions)) if i not in save.pushed]
+            save.pushed.update(missing)
+        # The layers save_kv_layer did not reach (all of them for an engine without layer hooks).
+        posts = [None] if len(missing) == len(self.layer_regions) else missing
+        for layer in posts if missing else []:
+            with self._lock:
+                save.inflight += 1
+            try:
+                tables, jobs = self._push_jobs([save])
+                region = None if layer is None else self.layer_regions[layer]
+                xfer = self.transport.post(tables, jobs, ready, layer=region)
+            except Exception as error:  # noqa: BLE001
+                logger.warning("pushing the KV of %s failed: %s", request_id, error)
+                with self._lock:
+                    save.inflight -= 1
+                    save.failed = True
+                break
+            with self._lock:
+                self._pushes.append((xfer, [save]))
+        with self._lock:
+            save.finishing = True
+
+    def _poll_pushes(self):
+        with self._lock:
+            pushes = list(self._pushes)
+        for entry in pushes:
+            xfer, saves = entry
+            try:
+                if not self.transport.done(xfer):
+                    continue
+                failed = False
+            except Exception as error:  # noqa: BLE001
+                logger.warning("a kvx push failed in flight: %s", error)
+                failed = True
+            self.transport.release(xfer)
+            with self._lock:
+                self._pushes.remove(entry)
+                for save in saves:
+                    save.inflight -= 1
+                    save.failed |= failed
+        timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+        now = monotonic()
+        with self._lock:
+            done = [(rid, s) for rid, s in self._saves.items() if s.finishing and s.inflight == 0]
+            stale = [(rid, s) for rid, s in self._saves.items()
+                     if not s.handed_over and s.inflight == 0 and s.started + timeout < now]
+            for request_id, save in done:
+                del self._saves[request_id]
+                self._finished.finished_sending.add(request_id)  # every byte landed, or none will
+            for request_id, save in stale:  # never handed over (an aborted prefill): the decode side gives up
+                del self._saves[request_id]
+                save.failed = True
+        for request_id, save in done + stale:
+            for key, _, _ in save.targets:
+                self._send(key, {"op": "saved", "request": request_id, "rank": self.rank, "ok": not save.failed})
+
+    # Push, decode side: wait for every producer rank holding this rank's heads.
+
+    def _start_wait(self, request_id: str, req: ReqToRecv):
+        heads = self._heads(req)
+        shares = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
+        num_bytes = 0
+        for i, share in enumerate(shares):
+            for cache in self.kv_caches:
+                if cache.dim() == 5:
+                    num_bytes += 2 * len(req.local_block_ids) * share.num_heads * cache[0, 0, 0].numel() * \
+                        cache.element_size()
+                elif i == 0:
+                    num_bytes += len(req.local_block_ids) * cache[0, 0].numel() * cache.element_size()
+        self._waits[request_id] = _Wait(req, {share.remote_rank for share in shares}, num_bytes)
+
+    def _poll_waits(self):
+        timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+        now = monotonic()
+        for request_id, wait in list(self._waits.items()):
+            with self._lock:
+                saved = self._saved.get(wait.req.remote_request_id, {})
+                complete = wait.expected <= set(saved)
+                ok = complete and all(saved[rank] for rank in wait.expected)
+                if complete:
+                    self._saved.pop(wait.req.remote_request_id, None)
+            if not complete and wait.started + timeout >= now:
+                continue
+            del self._waits[request_id]
+            with self._lock:
+                if ok:
+                    self._finished.finished_recving.add(request_id)
+                    self._finished.recv_stats[request_id] = KVTransferStats(now - wait.started, wait.num_bytes)
+                else:
+                    logger.warning("the pushed KV of %s did not land, so it prefills here", wait.req.remote_request_id)
+                    self._finished.failed_recving.add(request_id)
+
+    def _handshake(self, req, remote_rank: int) -> _Remote:
+        """The peer rank's cache, asked for once per peer and mapped here, checked to match this engine."""
         key = (req.remote_host, req.remote_port + remote_rank)
         remote = self._remotes.get(key)
         if remote is not None:

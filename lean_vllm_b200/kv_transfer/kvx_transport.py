@@ -29,7 +29,10 @@ class KvxTransport:
             raise RuntimeError("one rank's KV caches must share one device")
         _native.lib()  # fail loudly here, at registration, if libkvx.so is missing
         self.local = CacheTable.from_tensors(kv_caches)
-        self.flags = _native.flags(ENGINES.get(envs.LEAN_VLLM_KVX_ENGINE, _native.ENGINE_AUTO))
+        engine = ENGINES.get(envs.LEAN_VLLM_KVX_ENGINE, _native.ENGINE_AUTO)
+        self.flags = _native.flags(engine)
+        # A per-layer save runs beside the prefill's kernels: hold it to a few SMs.
+        self.save_flags = _native.flags(engine, sm_budget=min(max(envs.LEAN_VLLM_KVX_SAVE_SMS, 0), 255))
         with torch.cuda.device(self.device):
             self.stream = torch.cuda.Stream(device=self.device)
         # One IPC handle per layer tensor; each region as (tensor, byte offset in it, block bytes, head bytes).
@@ -67,20 +70,26 @@ class KvxTransport:
         for h in exported["handles"]:
             transport.close_mapping(bytes.fromhex(h))
 
-    def _job(self, src_index: int, req, share, latents: bool) -> CopyJob:
-        return CopyJob(src_index, 0, req.remote_block_ids, req.local_block_ids, share.remote_head, share.local_head,
-                       share.num_heads, latents)
+    @staticmethod
+    def _caches(local: CacheTable, tables: list[CacheTable], layer) -> list[CacheTable]:
+        caches = [local, *tables]
+        if layer is None:
+            return caches
+        start, count = layer
+        return [CacheTable(c.regions[start : start + count], c.num_blocks) for c in caches]
 
-    def job_bytes(self, table: CacheTable, req, share, latents: bool) -> int:
-        """Bytes one share moves (validated like the launch), the reference's descriptor-length sum (:421)."""
-        return transport.job_bytes([self.local, table], [self._job(1, req, share, latents)])
+    def job_bytes(self, tables: list[CacheTable], jobs: list[CopyJob], layer=None) -> int:
+        """Bytes the jobs move (validated like the launch): the reference's descriptor-length sum (:421). Cache 0 of
+        every job is this rank's own; cache k is tables[k-1]."""
+        return transport.job_bytes(self._caches(self.local, tables, layer), jobs)
 
-    def post(self, tables: list[CacheTable], jobs: list, ready) -> transport.Transfer:
-        """One launch for every share of a load, after `ready` on the side stream."""
-        caches = [self.local, *tables]
-        copy_jobs = [self._job(1 + index, req, share, latents) for index, req, share, latents in jobs]
+    def post(self, tables: list[CacheTable], jobs: list[CopyJob], ready, layer=None,
+             flags: int | None = None) -> transport.Transfer:
+        """One launch for all jobs, after `ready` on the side stream. `layer` = (first region, region count)
+        restricts every cache to one layer's regions (a per-layer save)."""
         event = ready.cuda_event if ready is not None else 0
-        return transport.transfer(caches, copy_jobs, self.stream.cuda_stream, event, self.flags)
+        return transport.transfer(self._caches(self.local, tables, layer), jobs, self.stream.cuda_stream, event,
+                                  self.flags if flags is None else flags)
 
     def done(self, xfer: transport.Transfer) -> bool:
         return xfer.done()

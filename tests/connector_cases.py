@@ -28,12 +28,36 @@ class WorkerConfig:
     tensor_parallel_size: int = 1
     kvcache_block_size: int = BLOCK
     kv_cache_layout: str = "HND"
+    kvx_accept_push: bool = False
 
 
-def free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+_handed_out: set[int] = set()
+
+
+def free_port(span: int = 8) -> int:
+    """A port p with p .. p+span-1 free now and not handed out before in this process: an instance's ranks bind
+    kv_port + rank, so two instances need disjoint spans."""
+    for _ in range(200):
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            base = s.getsockname()[1]
+        ports = range(base, base + span)
+        if base + span > 65535 or any(p in _handed_out for p in ports):
+            continue
+        socks = []
+        try:
+            for p in ports:
+                sock = socket.socket()
+                socks.append(sock)
+                sock.bind(("127.0.0.1", p))
+        except OSError:
+            continue
+        finally:
+            for sock in socks:
+                sock.close()
+        _handed_out.update(ports)
+        return base
+    raise RuntimeError("no free port span")
 
 
 def full_cache(seed: int, mla: bool) -> torch.Tensor:
@@ -56,13 +80,17 @@ class Sides:
         self.device = device
         self.workers: list[CudaIpcConnectorWorker] = []
 
-    def make(self, role: str, tp_size: int, full: torch.Tensor, port: int = 0, engine_id: str = "prefill"):
+    def make(self, role: str, tp_size: int, full, port: int = 0, engine_id: str = "prefill",
+             accept_push: bool = False):
+        """An instance of tp_size ranks; `full` is one layer's cache (every rank's heads) or a list of layers."""
         port = port or free_port()
+        layers = full if isinstance(full, list) else [full]
         side = []
         for rank in range(tp_size):
             kv = KVTransferConfig(kv_connector="CudaIpcConnector", kv_role=role, kv_port=port, engine_id=engine_id)
-            worker = CudaIpcConnectorWorker(WorkerConfig(kv, tensor_parallel_size=tp_size), rank)
-            worker.register_kv_caches([rank_cache(full, rank, tp_size).to(self.device)])
+            config = WorkerConfig(kv, tensor_parallel_size=tp_size, kvx_accept_push=accept_push)
+            worker = CudaIpcConnectorWorker(config, rank)
+            worker.register_kv_caches([rank_cache(layer, rank, tp_size).to(self.device) for layer in layers])
             side.append(worker)
         self.workers.extend(side)
         return side

@@ -30,6 +30,7 @@ class HostTransport:
         self.ids = count()
         self.pending: dict[int, list] = {}
         self.opened = 0
+        self.posts: list[tuple] = []  # (layer, number of jobs) of every post, for tests to inspect
         HostTransport.instances.append(self)
 
     def bind_thread(self):
@@ -45,6 +46,13 @@ class HostTransport:
     def close(self, exported):
         self.opened -= 1
 
+    def _tables(self, tables, layer):
+        out = [self.exported, *tables]
+        if layer is None:
+            return out
+        start, n = layer
+        return [dict(t, regions=t["regions"][start : start + n]) for t in out]
+
     @staticmethod
     def _rows(table, block_ids, first_head, num_heads, latents):
         rows = []
@@ -58,29 +66,34 @@ class HostTransport:
             rows += [(start + b * block_bytes, length) for b in block_ids]
         return rows
 
-    def _check(self, table, block_ids, first_head, num_heads, rows):
+    @staticmethod
+    def _check(table, block_ids, rows):
         if any(b < 0 or b >= table["num_blocks"] for b in block_ids):
             raise RuntimeError("block id outside the cache")
         for addr, length in rows:
             if not any(lo <= addr and addr + length <= lo + n for lo, n in table["spans"]):
                 raise RuntimeError("a row outside registered memory")
 
-    def job_bytes(self, table, req, share, latents):
-        local = self._rows(self.exported, req.local_block_ids, share.local_head, share.num_heads, latents)
-        remote = self._rows(table, req.remote_block_ids, share.remote_head, share.num_heads, latents)
-        self._check(self.exported, req.local_block_ids, share.local_head, share.num_heads, local)
-        self._check(table, req.remote_block_ids, share.remote_head, share.num_heads, remote)
-        assert [n for _, n in local] == [n for _, n in remote]
-        return sum(n for _, n in local)
+    def _pairs(self, tables, jobs, layer):
+        caches = self._tables(tables, layer)
+        for job in jobs:
+            src, dst = caches[job.src], caches[job.dst]
+            s_rows = self._rows(src, job.src_block_ids, job.src_first_head, job.num_heads, job.latents)
+            d_rows = self._rows(dst, job.dst_block_ids, job.dst_first_head, job.num_heads, job.latents)
+            self._check(src, job.src_block_ids, s_rows)
+            self._check(dst, job.dst_block_ids, d_rows)
+            assert [n for _, n in s_rows] == [n for _, n in d_rows]
+            yield from zip(d_rows, s_rows)
 
-    def post(self, tables, jobs, ready):
+    def job_bytes(self, tables, jobs, layer=None):
+        return sum(n for (_, n), _ in self._pairs(tables, jobs, layer))
+
+    def post(self, tables, jobs, ready, layer=None, flags=None):
         if HostTransport.fail == "posted":
             raise RuntimeError("the transport refused the copy")
-        for index, req, share, latents in jobs:
-            local = self._rows(self.exported, req.local_block_ids, share.local_head, share.num_heads, latents)
-            remote = self._rows(tables[index], req.remote_block_ids, share.remote_head, share.num_heads, latents)
-            for (dst, n), (src, _) in zip(local, remote):
-                ctypes.memmove(dst, src, n)
+        for (dst, n), (src, _) in list(self._pairs(tables, jobs, layer)):
+            ctypes.memmove(dst, src, n)
+        self.posts.append((layer, len(jobs)))
         handle = next(self.ids)
         self.pending[handle] = [1]  # done on the second poll
         return handle

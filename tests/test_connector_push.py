@@ -1,0 +1,137 @@
+"""The per-layer save (push) on CPU caches over the host transport: protocol, catch-up of layers no hook pushed,
+failures, and bit-exact results against the reference's golden pulls."""
+
+import numpy as np
+import pytest
+import torch
+
+from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVConnectorOutput, cuda_ipc_connector
+from tests.connector_cases import TP_PAIRS, Sides, full_cache, wait_for
+from tests.helpers import bits, full_of
+from tests.host_transport import HostTransport
+from tests.push_cases import LOCAL, REMOTE, pushed_recv, run_push, save_req
+
+
+@pytest.fixture(autouse=True)
+def host_transport(monkeypatch):
+    monkeypatch.setattr(cuda_ipc_connector, "make_transport", HostTransport)
+    monkeypatch.setattr(HostTransport, "fail", None)
+
+
+@pytest.fixture
+def sides():
+    s = Sides("cpu")
+    yield s
+    s.close()
+
+
+@pytest.mark.parametrize("mla", [False, True], ids=["kv", "latents"])
+@pytest.mark.parametrize("prefill_tp, decode_tp", TP_PAIRS)
+def test_a_pushed_request_lands_what_the_reference_s_pull_lands(sides, golden, prefill_tp, decode_tp, mla):
+    _, arrays = golden
+    producers = sides.make("kv_producer", prefill_tp, full_cache(0, mla))
+    consumers = sides.make("kv_consumer", decode_tp, full_cache(1, mla), engine_id="decode", accept_push=True)
+    sent, recved = run_push(producers, consumers, layers_to_save=[0])
+    assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}
+    key = "lat" if mla else "kv"
+    got = full_of([c.kv_caches[0] for c in consumers], mla)
+    assert np.array_equal(bits(got), arrays[f"small_{key}_tp{prefill_tp}to{decode_tp}"])
+    # The decode side counts its own heads' bytes, as a pull would.
+    per_rank = 2 * 3 * (12 // decode_tp) * 4 * 8 * 2 if not mla else 3 * 4 * 6 * 2
+    assert all(stats.num_bytes == per_rank * decode_tp for stats in recved.recv_stats.values())
+
+
+def test_each_layer_is_pushed_by_its_own_hook_and_the_rest_at_hand_over(sides):
+    layers = [full_cache(10 + i, False) for i in range(3)]
+    producers = sides.make("kv_producer", 1, layers)
+    consumers = sides.make("kv_consumer", 2, [full_cache(20 + i, False) for i in range(3)], engine_id="decode",
+                           accept_push=True)
+    sent, recved = run_push(producers, consumers, layers_to_save=[0, 1])  # layer 2's hook never ran
+    assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}
+    posts = producers[0].transport.posts
+    assert [layer for layer, _ in posts] == [(0, 2), (2, 2), (4, 2)]  # one launch per layer: K and V regions
+    assert all(jobs == 2 for _, jobs in posts)  # one job per decode rank
+    for layer in range(3):
+        got = full_of([c.kv_caches[layer] for c in consumers], False)
+        want = full_cache(20 + layer, False)
+        want[:, LOCAL] = layers[layer][:, REMOTE]
+        assert torch.equal(got, want), layer
+
+
+def test_an_engine_without_layer_hooks_pushes_everything_in_one_launch_at_hand_over(sides):
+    layers = [full_cache(30 + i, False) for i in range(2)]
+    producers = sides.make("kv_producer", 2, layers)
+    consumers = sides.make("kv_consumer", 1, [full_cache(40 + i, False) for i in range(2)], engine_id="decode",
+                           accept_push=True)
+    sent, recved = run_push(producers, consumers, layers_to_save=[])
+    assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}
+    assert all([layer for layer, _ in p.transport.posts] == [None] for p in producers)
+    got = consumers[0].kv_caches
+    for layer in range(2):
+        want = full_cache(40 + layer, False)
+        want[:, LOCAL] = layers[layer][:, REMOTE]
+        assert torch.equal(got[layer], want)
+
+
+def test_the_landing_word_may_come_before_the_decode_side_waits(sides, golden):
+    _, arrays = golden
+    producers = sides.make("kv_producer", 2, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 4, full_cache(1, False), engine_id="decode", accept_push=True)
+    sent, recved = run_push(producers, consumers, layers_to_save=[0], decode_first=False)
+    assert recved.finished_recving == {"d-1"}
+    assert np.array_equal(bits(full_of([c.kv_caches[0] for c in consumers], False)), arrays["small_kv_tp2to4"])
+
+
+def test_a_decode_instance_that_does_not_answer_fails_the_push_and_its_wait(sides, monkeypatch):
+    monkeypatch.setattr(cuda_ipc_connector, "HANDSHAKE_TIMEOUT", 0.2)
+    monkeypatch.setenv("LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT", "0.5")
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")  # does not accept pushes
+    before = consumers[0].kv_caches[0].clone()
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
+    producers[0].save_kv_layer(0)
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(producers[0]) == KVConnectorOutput(finished_sending={"p-1"})  # the blocks are freed
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})  # and the decode side prefills
+    assert torch.equal(consumers[0].kv_caches[0], before)
+
+
+def test_a_push_refused_when_posted_tells_the_decode_side_it_failed(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    HostTransport.fail = "posted"
+    sent, recved = run_push(producers, consumers, layers_to_save=[0])
+    assert sent.finished_sending == {"p-1"}
+    assert recved.failed_recving == {"d-1"}
+
+
+def test_a_push_failing_in_flight_tells_the_decode_side_it_failed(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    HostTransport.fail = "in flight"
+    sent, recved = run_push(producers, consumers, layers_to_save=[0])
+    assert sent.finished_sending == {"p-1"}
+    assert recved.failed_recving == {"d-1"}
+
+
+def test_a_save_that_is_never_handed_over_expires(sides, monkeypatch):
+    monkeypatch.setenv("LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT", "0.3")
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
+    producers[0].save_kv_layer(0)  # the prefill is then aborted: no hand-over
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    assert not producers[0]._saves
+
+
+def test_hooks_without_saves_launch_nothing(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    producers[0].save_kv_layer(0)
+    producers[0].wait_for_save()
+    assert producers[0].transport.posts == []
+
+
+def test_a_consumer_that_accepts_pushes_serves_handshakes(sides):
+    assert sides.make("kv_consumer", 1, full_cache(1, False), accept_push=True)[0]._server is not None
