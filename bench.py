@@ -669,6 +669,198 @@ def e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo):
     return (float(np.median(times)) if consumer_worker is not None else 0.0), nbytes
 
 
+# Qwen3-8B per layer: q 4096x4096, k and v 4096x1024, o 4096x4096, MLP 3 x 4096x12288 = 193e6 weights, 2 FLOPs
+# each per token (attention scores left out, so the stand-in is, if anything, shorter than the real layer).
+LAYER_FLOPS_PER_TOKEN = 2 * 193e6
+
+
+def run_layerwise(args) -> None:
+    """Layer-by-layer push during a synthetic prefill, through the connector's per-layer save (save_kv_layer).
+
+    The prefill instance prefills the workload's first requests in steps of at most 8192 tokens; each layer of a
+    step is a bf16 GEMM with Qwen3-8B's per-layer FLOPs for the step's tokens (the calibrated stand-in for the real
+    layer), after which the engine calls save_kv_layer, which pushes that layer's blocks of the step's requests into
+    the decode instance's blocks on a high-priority stream held to a few SMs. The same prefill runs without saves.
+    Reported: compute time alone, with saves, until the last byte landed, and the exposed transfer time (the
+    latter minus compute alone) as a fraction of compute alone."""
+    import torch
+    import torch.distributed as dist
+
+    from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVTransferConfig, ReqToRecv
+    from lean_vllm_b200.kv_transfer.base import ReqToSave
+    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorWorker
+
+    spec = WORKLOADS["pair"]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    role = role_of(rank, world, spec)
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    gloo = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
+    lengths, reqs, num_blocks = workload(args.seed, args.requests or 16, spec)
+    steps, current, tokens = [], [], 0  # whole requests per step, at most 8192 tokens each
+    for i, n in enumerate(lengths):
+        if current and tokens + int(n) > 8192:
+            steps.append(current)
+            current, tokens = [], 0
+        current.append(i)
+        tokens += int(n)
+    steps.append(current)
+
+    @dataclass
+    class WorkerConfig:
+        kv_transfer: KVTransferConfig
+        tensor_parallel_size: int = 1
+        kvcache_block_size: int = spec.block
+        kv_cache_layout: str = "HND"
+        kvx_accept_push: bool = False
+
+    base_port = args.kv_port + 16 * role.group
+    src = dst = producer = consumer = None
+    if role.side in ("prefill", "both"):
+        src = alloc_cache(spec, 1, num_blocks, device, fill=True, seed=1000 + rank)
+        producer = CudaIpcConnectorWorker(WorkerConfig(KVTransferConfig(
+            kv_role="kv_producer", kv_port=base_port, engine_id=f"lw-prefill-{role.group}")), 0)
+        producer.register_kv_caches(src)
+    if role.side in ("decode", "both"):
+        dst = alloc_cache(spec, 1, num_blocks, device, fill=False, seed=0)
+        consumer = CudaIpcConnectorWorker(WorkerConfig(KVTransferConfig(
+            kv_role="kv_consumer", kv_port=base_port + 8, engine_id=f"lw-decode-{role.group}"),
+            kvx_accept_push=True), 0)
+        consumer.register_kv_caches(dst)
+    hidden, width = 4096, int(LAYER_FLOPS_PER_TOKEN / (2 * 4096))
+    if producer is not None:
+        a = torch.randn(8192, hidden, device=device, dtype=torch.bfloat16)
+        w = torch.randn(hidden, width, device=device, dtype=torch.bfloat16) * 0.01
+        out = torch.empty(8192, width, device=device, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(group=gloo)
+
+    def iteration(tag: str, saves: bool) -> tuple[float, float]:
+        """Returns (ms of compute, ms until the last push landed) on the prefill side (0 elsewhere)."""
+        ids = {i: f"{tag}-{i}" for i in range(len(reqs))}
+        if consumer is not None and saves:
+            consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={
+                ids[i]: ReqToRecv(reqs[i][1].tolist(), reqs[i][0].tolist(), ids[i], f"lw-prefill-{role.group}",
+                                  "127.0.0.1", base_port, 1, pushed=True) for i in range(len(reqs))}))
+        sync_all()
+        compute_ms = landed_ms = 0.0
+        if producer is not None:
+            stream = torch.cuda.current_stream()
+            start, compute_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            landed = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for step in steps:
+                n_tokens = int(sum(int(lengths[i]) for i in step))
+                if saves:
+                    producer.start_load_kv(KVConnectorMetadata(reqs_to_save={
+                        ids[i]: ReqToSave(reqs[i][0].tolist(), reqs[i][1].tolist(), f"lw-decode-{role.group}",
+                                          "127.0.0.1", base_port + 8, 1) for i in step}))
+                    if tag == "warm-b" and step is steps[0]:
+                        # First contact maps the decode cache on the transfer thread (once per decode instance);
+                        # every later save finds it mapped and is ready at once.
+                        deadline = time.monotonic() + 30
+                        for i in step:
+                            save = producer._saves[ids[i]]
+                            while not (save.ready or save.failed) and time.monotonic() < deadline:
+                                time.sleep(1e-4)
+                            if not save.ready:
+                                raise RuntimeError("the decode instance could not be mapped")
+                for layer in range(spec.layers):
+                    torch.matmul(a[:n_tokens], w, out=out[:n_tokens])
+                    if saves:
+                        producer.save_kv_layer(layer)
+                if saves:
+                    producer.wait_for_save()
+                    producer.start_load_kv(KVConnectorMetadata(reqs_to_send={ids[i]: reqs[i][0].tolist()
+                                                                              for i in step}))
+            compute_end.record(stream)
+            landed.record(producer.transport.save_stream)
+            landed.synchronize()
+            torch.cuda.synchronize()
+            compute_ms = start.elapsed_time(compute_end)
+            landed_ms = max(compute_ms, start.elapsed_time(landed))
+        if saves:
+            for worker, field_name in ((producer, "finished_sending"), (consumer, "finished_recving")):
+                if worker is None:
+                    continue
+                left, deadline = set(ids.values()), time.monotonic() + 120
+                while left and time.monotonic() < deadline:
+                    out_ = worker.get_finished()
+                    if out_.failed_recving:
+                        raise RuntimeError("a pushed load failed")
+                    left -= getattr(out_, field_name)
+                    time.sleep(1e-3)
+                if left:
+                    raise RuntimeError(f"{len(left)} pushed requests did not finish")
+        sync_all()
+        return compute_ms, landed_ms
+
+    try:
+        iteration("warm-a", False)
+        iteration("warm-b", True)
+        alone = [iteration(f"c{k}", False)[0] for k in range(args.steps)]
+        both = [iteration(f"s{k}", True) for k in range(args.steps)]
+        ok = True
+        samples = [reqs[0], reqs[-1]]
+        if world == 1:
+            ok = all(digest(dst, d, 0, 8, False, device) == digest(src, s, 0, 8, False, device) for s, d in samples)
+        else:
+            mine = [digest(src if src is not None else dst, s if src is not None else d, 0, 8, False, device)
+                    for s, d in samples] if role.side != "idle" else None
+            every = [None] * world
+            dist.all_gather_object(every, (role.group, role.side, mine), group=gloo)
+            for g in range(world // spec.group_size):
+                got = [m for gg, side, m in every if gg == g and side == "decode"]
+                want = [m for gg, side, m in every if gg == g and side == "prefill"]
+                ok &= got == want
+    finally:
+        for worker in (producer, consumer):
+            if worker is not None:
+                worker.shutdown()
+    stats = torch.tensor([float(np.median(alone)), float(np.median([c for c, _ in both])),
+                          float(np.median([ld for _, ld in both]))], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        t_alone, t_with, t_landed = (float(x) for x in stats.cpu())
+        payload = request_bytes(sum(len(s) for s, _ in reqs), spec)
+        flops = LAYER_FLOPS_PER_TOKEN * spec.layers * float(sum(int(x) for x in lengths))
+        line = {
+            "metric": "layerwise push during prefill: exposed transfer time",
+            "value": round((t_landed - t_alone) / t_alone, 5),
+            "unit": "fraction of prefill compute time",
+            "higher_is_better": False,
+            "n_gpus": world,
+            "steps": args.steps,
+            "ms_compute_alone": round(t_alone, 3),
+            "ms_compute_with_saves": round(t_with, 3),
+            "ms_until_last_byte_landed": round(t_landed, 3),
+            "exposed_ms": round(t_landed - t_alone, 3),
+            "compute_slowdown": round(t_with / t_alone - 1, 5),
+            "payload_bytes": payload,
+            "prefill_tflops": round(flops / (t_alone * 1e-3) / 1e12, 1),
+            "config": {"workload": f"{spec.name}/{'loopback-1gpu' if world == 1 else 'pair'} layerwise push",
+                       "requests": len(reqs), "prefill_steps": len(steps),
+                       "layer_stand_in": f"bf16 GEMM [tokens x 4096] @ [4096 x {width}] per layer",
+                       "save_sms": int(os.environ.get("LEAN_VLLM_KVX_SAVE_SMS", "16"))},
+            "correct": bool(ok),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -723,9 +915,13 @@ def main(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the connector end-to-end timing")
     p.add_argument("--kv-port", type=int, default=24600, help="first handshake port of the e2e connectors")
+    p.add_argument("--layerwise", action="store_true",
+                   help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
     args = p.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.layerwise:
+        run_layerwise(args)
     else:
         run_gpu(args)
 

@@ -214,6 +214,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._context.setsockopt(zmq.LINGER, 0)
         self._server = None
         self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
+        self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table) of _remotes; under the lock
         self._loads: dict[str, _Load] = {}  # transfer thread only
         self._waits: dict[str, _Wait] = {}  # transfer thread only
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
@@ -252,11 +253,17 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
     def start_load_kv(self, metadata: KVConnectorMetadata):
         for request_id, req in getattr(metadata, "reqs_to_save", {}).items():
             with self._lock:
-                known = request_id in self._saves
-                if not known:
-                    self._saves[request_id] = _Save(req, self._targets(req))
-            if not known:
-                self._queue.put(("connect", request_id))
+                if request_id in self._saves:
+                    continue
+                save = self._saves[request_id] = _Save(req, self._targets(req))
+                # Decode ranks mapped by an earlier handshake: ready now, so this step's first layer is pushed by
+                # its own hook. First contact goes to the transfer thread, never blocking this one on the network.
+                mapped = [self._mapped.get(key) for key, _, _ in save.targets]
+                if all(m is not None and m[0] == req.remote_engine_id for m in mapped):
+                    save.tables = [m[1] for m in mapped]
+                    save.ready = True
+                    continue
+            self._queue.put(("connect", request_id))
         if metadata.reqs_to_send:
             deadline = monotonic() + envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
             finishing = []
@@ -686,6 +693,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if remote.engine_id == req.remote_engine_id:
                 return remote
             del self._remotes[key]  # restarted since: ask afresh
+            with self._lock:
+                self._mapped.pop(key, None)
             self.transport.close(remote.exported)
             remote.sock.close()
         sock = self._context.socket(zmq.DEALER)
@@ -715,6 +724,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             table = self.transport.open(reply["exported"])
             remote = _Remote(reply["engine_id"], reply["tp_size"], reply["num_blocks"], reply["exported"], table, sock)
             self._remotes[key] = remote
+            with self._lock:
+                self._mapped[key] = (remote.engine_id, remote.table)
             keep = True
             return remote
         finally:

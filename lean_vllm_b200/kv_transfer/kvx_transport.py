@@ -35,6 +35,8 @@ class KvxTransport:
         self.save_flags = _native.flags(engine, sm_budget=min(max(envs.LEAN_VLLM_KVX_SAVE_SMS, 0), 255))
         with torch.cuda.device(self.device):
             self.stream = torch.cuda.Stream(device=self.device)
+            # Per-layer saves go first when SMs free up between the prefill's kernels.
+            self.save_stream = torch.cuda.Stream(device=self.device, priority=-10)
         # One IPC handle per layer tensor; each region as (tensor, byte offset in it, block bytes, head bytes).
         bases = [c.data_ptr() for c in kv_caches]
         spans = [(c.data_ptr(), c.data_ptr() + c.numel() * c.element_size()) for c in kv_caches]
@@ -85,10 +87,12 @@ class KvxTransport:
 
     def post(self, tables: list[CacheTable], jobs: list[CopyJob], ready, layer=None,
              flags: int | None = None) -> transport.Transfer:
-        """One launch for all jobs, after `ready` on the side stream. `layer` = (first region, region count)
-        restricts every cache to one layer's regions (a per-layer save)."""
+        """One launch for all jobs, after `ready`, on a side stream. `layer` = (first region, region count)
+        restricts every cache to one layer's regions; such a per-layer save runs on the high-priority stream
+        with `flags` (its SM budget)."""
         event = ready.cuda_event if ready is not None else 0
-        return transport.transfer(self._caches(self.local, tables, layer), jobs, self.stream.cuda_stream, event,
+        stream = self.save_stream if flags is not None else self.stream
+        return transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags)
 
     def done(self, xfer: transport.Transfer) -> bool:

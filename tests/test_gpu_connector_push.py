@@ -1,0 +1,80 @@
+"""The per-layer save (push) on CUDA devices with the kvx transport, in one process on one GPU: bit for bit against
+the reference's golden pulls, layer launches on the bounded SM budget, and the ordering after each layer's store."""
+
+import numpy as np
+import pytest
+import torch
+
+from lean_vllm_b200.kv_transfer import KVConnectorMetadata
+from tests.connector_cases import Sides, full_cache, wait_for
+from tests.helpers import bits, full_of
+from tests.push_cases import LOCAL, REMOTE, pushed_recv, run_push, save_req, wait_ready
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def sides():
+    s = Sides("cuda")
+    yield s
+    s.close()
+
+
+@pytest.mark.parametrize("mla", [False, True], ids=["kv", "latents"])
+@pytest.mark.parametrize("prefill_tp, decode_tp", [(1, 1), (2, 4), (4, 2), (4, 6), (1, 2)])
+def test_a_pushed_request_lands_what_the_reference_s_pull_lands_on_the_gpu(sides, golden, prefill_tp, decode_tp,
+                                                                           mla):
+    _, arrays = golden
+    producers = sides.make("kv_producer", prefill_tp, full_cache(0, mla))
+    consumers = sides.make("kv_consumer", decode_tp, full_cache(1, mla), engine_id="decode", accept_push=True)
+    sent, recved = run_push(producers, consumers, layers_to_save=[0])
+    assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}
+    key = "lat" if mla else "kv"
+    got = full_of([c.kv_caches[0].cpu() for c in consumers], mla)
+    assert np.array_equal(bits(got), arrays[f"small_{key}_tp{prefill_tp}to{decode_tp}"])
+
+
+@pytest.mark.parametrize("hooks", [[0, 1, 2], [0, 2], []], ids=["every-layer", "some-layers", "no-hooks"])
+def test_layers_pushed_by_hooks_and_at_hand_over_land_bit_for_bit(sides, hooks):
+    layers = [full_cache(10 + i, False) for i in range(3)]
+    producers = sides.make("kv_producer", 2, layers)
+    consumers = sides.make("kv_consumer", 1, [full_cache(20 + i, False) for i in range(3)], engine_id="decode",
+                           accept_push=True)
+    sent, recved = run_push(producers, consumers, layers_to_save=hooks)
+    assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}
+    for layer in range(3):
+        want = full_cache(20 + layer, False)
+        want[:, LOCAL] = layers[layer][:, REMOTE]
+        assert torch.equal(consumers[0].kv_caches[layer].cpu(), want), layer
+
+
+def test_a_layer_is_pushed_only_after_its_store_on_the_engine_stream(sides):
+    """save_kv_layer records an event on the engine's stream: a store still queued behind a long kernel is what
+    lands, not the bytes before it."""
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
+    assert wait_ready(producers[0])
+    cache = producers[0].kv_caches[0]
+    torch.cuda._sleep(50_000_000)  # the layer's attention, still running ...
+    cache[:, REMOTE] = 7.0  # ... before its store writes the blocks
+    producers[0].save_kv_layer(0)
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(producers[0]).finished_sending == {"p-1"}
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    assert bool((consumers[0].kv_caches[0][:, LOCAL] == 7.0).all())
+
+
+def test_a_per_layer_save_launch_is_held_to_its_sm_budget(sides, monkeypatch):
+    """The save's launch covers at most LEAN_VLLM_KVX_SAVE_SMS SMs (the grid is capped), and still lands every byte."""
+    monkeypatch.setenv("LEAN_VLLM_KVX_SAVE_SMS", "2")
+    big = torch.randn(2, 16, 12, 64, 128).to(torch.bfloat16)
+    producers = sides.make("kv_producer", 1, big)
+    consumers = sides.make("kv_consumer", 1, torch.zeros_like(big), engine_id="decode", accept_push=True)
+    assert producers[0].transport.save_flags >> 24 == 2
+    sent, recved = run_push(producers, consumers, layers_to_save=[0])
+    assert recved.finished_recving == {"d-1"}
+    want = torch.zeros_like(big)
+    want[:, LOCAL] = big[:, REMOTE]
+    assert torch.equal(consumers[0].kv_caches[0].cpu(), want)
