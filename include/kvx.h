@@ -132,6 +132,33 @@ int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream
 int kvx_scatter(const void *staging, uint64_t staging_bytes, const kvx_cache *dst, const int32_t *dst_block_ids,
                 int n_blocks, int first_head, int num_heads, int latents, int flags, void *stream);
 
+/* ---- the per-token cache store, alone or fused with the push ---- */
+
+/* One cache a store writes: the local paged cache, or a peer's (a decode rank's blocks, mapped with kvx_ipc_open).
+ * Strides are in bytes and address the cache as (block, token, head, dim), so NHD and HND caches both work, as the
+ * reference's store kernel reads them (attention/triton_cache.py:32-36, 66). */
+typedef struct kvx_store_dest {
+    uint64_t k_cache;            /* device address of block 0's keys (or latents) */
+    uint64_t v_cache;            /* device address of block 0's values; 0 for latents */
+    int64_t block_stride;        /* bytes between blocks */
+    int64_t token_stride;        /* bytes between a block's tokens */
+    int64_t head_stride;         /* bytes between heads (unused for latents) */
+    int32_t block_size;          /* tokens per block */
+    int32_t num_blocks;          /* slots at or past num_blocks*block_size are skipped and flagged (device error 2) */
+    const void *slot_mapping;    /* device array of num_tokens slots (block*block_size + offset); -1 skips */
+    int32_t slot_bytes;          /* 4 (int32) or 8 (int64) */
+    int32_t src_first_head;      /* this destination takes source heads [src_first_head, +num_heads) ... */
+    int32_t num_heads;
+    int32_t dst_first_head;      /* ... and stores them from its head dst_first_head */
+} kvx_store_dest;
+
+/* Scatters num_tokens rows of keys and values [token][head][head_bytes] (or latents, with value = NULL and
+ * num_heads = 1) into each destination's slots, one pass over the rows: destination 0 is the local cache
+ * (store_kvcache / store_latents, attention/triton_cache.py:9-91); destinations 1..3 may be peers' caches, which
+ * makes this the fused store-and-push of a layer-by-layer transfer. Strides of the rows are in bytes. */
+int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t value_stride, int num_tokens,
+              int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int flags, void *stream);
+
 /* ---- transfers with completion (post, poll, release) ---- */
 
 /* kvx_copy after `wait_event` (a cudaEvent_t as void*, may be 0) has passed on `stream`, then records a completion

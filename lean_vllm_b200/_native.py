@@ -82,6 +82,23 @@ class IpcHandle(ctypes.Structure):
         return cls.from_buffer_copy(data)
 
 
+class StoreDest(ctypes.Structure):
+    _fields_ = [
+        ("k_cache", ctypes.c_uint64),
+        ("v_cache", ctypes.c_uint64),
+        ("block_stride", ctypes.c_int64),
+        ("token_stride", ctypes.c_int64),
+        ("head_stride", ctypes.c_int64),
+        ("block_size", ctypes.c_int32),
+        ("num_blocks", ctypes.c_int32),
+        ("slot_mapping", ctypes.c_void_p),
+        ("slot_bytes", ctypes.c_int32),
+        ("src_first_head", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("dst_first_head", ctypes.c_int32),
+    ]
+
+
 # Every symbol include/kvx.h declares, with its argtypes and restype.
 _P = ctypes.c_void_p
 SIGNATURES: dict[str, tuple[list, object]] = {
@@ -98,6 +115,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kvx_push": ([_P, _P, ctypes.c_uint64, ctypes.c_int, _P], ctypes.c_int),
     "kvx_scatter": ([_P, ctypes.c_uint64, ctypes.POINTER(Cache), ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
+    "kvx_store": ([_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                   ctypes.POINTER(StoreDest), ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
     "kvx_transfer": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int, ctypes.c_int, _P, _P,
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "kvx_check_xfer": ([_P], ctypes.c_int),

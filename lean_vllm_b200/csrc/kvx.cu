@@ -302,6 +302,69 @@ __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Param
     bulk_wait_all();
 }
 
+// ------------------------------------------------------------------------------------------------ store kernel
+
+// The per-token cache store (the reference's store_kvcache/store_latents), optionally fused with the push: each
+// source row [token][head] is read once and written to every destination whose head range holds it. Thread t of
+// the flattened space (token, K|V, head, vector) moves one VEC-byte vector, so reads of a token's rows are
+// contiguous and each (token, head) row lands as one contiguous run of head_bytes in every cache.
+constexpr int kMaxStoreDests = 4;
+
+struct StoreDest {
+    uint64_t k, v;
+    int64_t block_stride, token_stride, head_stride;
+    const void *slots;
+    int32_t block_size, num_blocks, slot_bytes, src_first_head, num_heads, dst_first_head;
+};
+
+struct StoreParams {
+    uint64_t key, value;
+    int64_t key_stride, value_stride;
+    int32_t num_tokens, num_heads, head_bytes, n_dests;
+    StoreDest dests[kMaxStoreDests];
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(256) kvx_store_kernel(const __grid_constant__ StoreParams p) {
+    using V = Vec<VEC>;
+    const uint32_t vecs = (uint32_t)p.head_bytes / VEC;  // per (token, head) row
+    const uint32_t parts = p.value ? 2u : 1u;
+    const uint64_t total = (uint64_t)p.num_tokens * parts * p.num_heads * vecs;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t vec = (uint32_t)(i % vecs);
+        uint64_t rest = i / vecs;
+        const int32_t head = (int32_t)(rest % p.num_heads);
+        rest /= p.num_heads;
+        const uint32_t part = (uint32_t)(rest % parts);  // 0 keys (or latents), 1 values
+        const int32_t token = (int32_t)(rest / parts);
+        const uint64_t src_base = part ? p.value + (uint64_t)token * p.value_stride
+                                       : p.key + (uint64_t)token * p.key_stride;
+        const typename V::T data = V::load(reinterpret_cast<const char *>(src_base) +
+                                           (uint64_t)head * p.head_bytes + (uint64_t)vec * VEC);
+#pragma unroll
+        for (int d = 0; d < kMaxStoreDests; ++d) {
+            if (d >= p.n_dests) break;
+            const StoreDest &dst = p.dests[d];
+            if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
+            const int64_t slot = dst.slot_bytes == 8 ? static_cast<const int64_t *>(dst.slots)[token]
+                                                     : static_cast<const int32_t *>(dst.slots)[token];
+            if (slot < 0) continue;  // padding: no cache slot
+            if (slot >= (int64_t)dst.num_blocks * dst.block_size) {
+                atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
+                continue;
+            }
+            const int64_t block = slot / dst.block_size, offset = slot - block * dst.block_size;
+            const uint64_t base = part ? dst.v : dst.k;
+            char *out = reinterpret_cast<char *>(base + block * dst.block_stride + offset * dst.token_stride +
+                                                 (int64_t)(head - dst.src_first_head + dst.dst_first_head) *
+                                                     dst.head_stride) +
+                        (uint64_t)vec * VEC;
+            V::store(out, data);
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ host side
 
 struct DeviceInfo {
@@ -759,6 +822,64 @@ int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream
     const int32_t zero = 0;
     const kvx_job job = {0, 1, &zero, &zero, 1, 0, 0, 0, 1};
     return copy_impl(caches, 2, &job, 1, flags, static_cast<cudaStream_t>(stream));
+}
+
+int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t value_stride, int num_tokens,
+              int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int flags, void *stream) {
+    if (!key || !dests) return fail(KVX_ERR_INVALID, "null rows or destinations");
+    if (num_tokens < 0 || num_heads < 1 || head_bytes < 1)
+        return fail(KVX_ERR_INVALID, "bad row shape: %d tokens, %d heads of %d bytes", num_tokens, num_heads,
+                    head_bytes);
+    if (n_dests < 1 || n_dests > kMaxStoreDests)
+        return fail(KVX_ERR_INVALID, "%d destinations; 1 to %d", n_dests, kMaxStoreDests);
+    StoreParams p{};
+    p.key = (uint64_t)(uintptr_t)key;
+    p.value = (uint64_t)(uintptr_t)value;
+    p.key_stride = key_stride;
+    p.value_stride = value_stride;
+    p.num_tokens = num_tokens;
+    p.num_heads = num_heads;
+    p.head_bytes = head_bytes;
+    p.n_dests = n_dests;
+    uint64_t align_bits = p.key | p.value | (uint64_t)key_stride | (uint64_t)value_stride | (uint64_t)head_bytes;
+    for (int d = 0; d < n_dests; ++d) {
+        const kvx_store_dest &s = dests[d];
+        if (!s.k_cache || (!value) != (!s.v_cache))
+            return fail(KVX_ERR_INVALID, "destination %d: keys and values must match the rows given", d);
+        if (s.block_size < 1 || s.num_blocks < 0 || (s.slot_bytes != 4 && s.slot_bytes != 8))
+            return fail(KVX_ERR_INVALID, "destination %d: bad block size, block count or slot width", d);
+        if (num_tokens > 0 && !s.slot_mapping) return fail(KVX_ERR_INVALID, "destination %d: null slots", d);
+        if (s.src_first_head < 0 || s.num_heads < 0 || s.dst_first_head < 0 ||
+            s.src_first_head + s.num_heads > num_heads)
+            return fail(KVX_ERR_RANGE, "destination %d: heads [%d, +%d) of %d", d, s.src_first_head, s.num_heads,
+                        num_heads);
+        if (s.block_stride < 0 || s.token_stride < 0 || s.head_stride < 0)
+            return fail(KVX_ERR_INVALID, "destination %d: negative stride", d);
+        p.dests[d] = StoreDest{s.k_cache, s.v_cache, s.block_stride, s.token_stride, s.head_stride, s.slot_mapping,
+                               s.block_size, s.num_blocks, s.slot_bytes, s.src_first_head, s.num_heads,
+                               s.dst_first_head};
+        align_bits |= s.k_cache | s.v_cache | (uint64_t)s.block_stride | (uint64_t)s.token_stride |
+                      (uint64_t)s.head_stride;
+    }
+    if (num_tokens == 0) return KVX_OK;
+    const int vec = (int)std::min<uint64_t>(low_bit(align_bits), 16);
+    DeviceInfo *info;
+    if (int rc = device_info(&info)) return rc;
+    const uint64_t total = (uint64_t)num_tokens * (value ? 2 : 1) * num_heads * (head_bytes / vec);
+    const int sm_budget = (flags >> 24) & 0xff;
+    const int sms = sm_budget > 0 && sm_budget < info->sms ? sm_budget : info->sms;
+    const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 8);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (vec) {
+        case 16: kvx_store_kernel<16><<<grid, 256, 0, s>>>(p); break;
+        case 8: kvx_store_kernel<8><<<grid, 256, 0, s>>>(p); break;
+        case 4: kvx_store_kernel<4><<<grid, 256, 0, s>>>(p); break;
+        case 2: kvx_store_kernel<2><<<grid, 256, 0, s>>>(p); break;
+        default: kvx_store_kernel<1><<<grid, 256, 0, s>>>(p); break;
+    }
+    KVX_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return KVX_OK;
 }
 
 int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,

@@ -213,6 +213,29 @@ def load_between(
     return consumers, moved
 
 
+def store_kvcache(key: np.ndarray, value: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, slot_mapping) -> None:
+    """The per-token cache store, as TorchAttention.store_kvcache (attention/torch_backend.py:34-48): row t of
+    key/value [tokens, heads, dim] goes to block slot // block_size, token slot % block_size of the caches, given as
+    (blocks, block_size, heads, dim) views (an HND cache's transposed view works, the writes go through); slot -1
+    skips the row."""
+    block_size = k_cache.shape[1]
+    for t, slot in enumerate(np.asarray(slot_mapping).tolist()):
+        if slot < 0:
+            continue
+        block, offset = divmod(int(slot), block_size)
+        k_cache[block, offset] = key[t]
+        v_cache[block, offset] = value[t]
+
+
+def store_latents(latent: np.ndarray, latent_cache: np.ndarray, slot_mapping) -> None:
+    """TorchAttention.store_latents (attention/torch_backend.py:50-60): row t of latent [tokens, dim] goes to flat
+    slot t of the (blocks, block_size, dim) cache; slot -1 skips."""
+    flat = latent_cache.reshape(-1, latent_cache.shape[-1])
+    for t, slot in enumerate(np.asarray(slot_mapping).tolist()):
+        if slot >= 0:
+            flat[int(slot)] = latent[t]
+
+
 def expected_decode(prefill_full: np.ndarray, decode_full: np.ndarray, local_ids, remote_ids) -> np.ndarray:
     """The decode instance's full cache after the load: remote blocks copied onto local ones, all heads.
 

@@ -287,6 +287,36 @@ def descs_table(meta: dict):
                                block_ids=[3, 0, 11, 5], device_id=1, cases=cases)
 
 
+def store_cases(arrays: dict, meta: dict):
+    """The reference's per-token cache store (TorchAttention.store_kvcache / store_latents,
+    attention/torch_backend.py:34-60, the CPU path of the Triton kernels in triton_cache.py) on NHD and HND caches
+    and on latents, with padding slots (-1)."""
+    from lean_vllm.attention.torch_backend import TorchAttention
+
+    blocks, block, heads, dim, latent, tokens = 6, 4, 3, 8, 6, 10
+    g = torch.Generator().manual_seed(5)
+    slots = torch.randperm(blocks * block, generator=g)[:tokens].clone()
+    slots[[2, 7]] = -1
+    key = torch.randn(tokens, heads, dim, generator=g).to(torch.bfloat16)
+    value = torch.randn(tokens, heads, dim, generator=g).to(torch.bfloat16)
+    lat = torch.randn(tokens, latent, generator=g).to(torch.bfloat16)
+    arrays["store_slots"] = slots.numpy().astype(np.int64)
+    arrays["store_key"], arrays["store_value"], arrays["store_latent"] = as_bits(key), as_bits(value), as_bits(lat)
+    for layout in ("NHD", "HND"):
+        shape = (2, blocks, block, heads, dim) if layout == "NHD" else (2, blocks, heads, block, dim)
+        cache = seeded(shape, 6)
+        arrays[f"store_{layout}_before"] = as_bits(cache)
+        view = cache if layout == "NHD" else cache.transpose(2, 3)  # what bind_kv_cache hands the backend
+        TorchAttention.store_kvcache(None, key, value, view[0], view[1], slots)
+        arrays[f"store_{layout}_after"] = as_bits(cache)
+    cache = seeded((1, blocks, block, latent), 7)
+    arrays["store_latent_before"] = as_bits(cache)
+    TorchAttention.store_latents(None, lat, cache[0], slots)
+    arrays["store_latent_after"] = as_bits(cache)
+    meta["store"] = dict(blocks=blocks, block=block, heads=heads, dim=dim, latent=latent, tokens=tokens,
+                         reference="lean_vllm/attention/torch_backend.py:34-60")
+
+
 def main():
     arrays: dict = {}
     meta: dict = {"generator": "tests/golden/make_golden.py", "reference": "lean_vllm/kv_transfer/nixl_connector.py"}
@@ -294,6 +324,7 @@ def main():
     descs_table(meta)
     small_cases(arrays, meta)
     model_shaped_cases(meta)
+    store_cases(arrays, meta)
     np.savez_compressed(os.path.join(HERE, "kv_transfer_small.npz"), **arrays)
     with open(os.path.join(HERE, "kv_transfer_golden.json"), "w") as f:
         json.dump(meta, f, indent=1)

@@ -1,0 +1,133 @@
+"""kvx_store through the C ABI: the per-token cache store bit for bit against the reference's torch store (golden
+fixtures and the oracle), and the fused store-and-push into peers' caches with head resharding and latent
+replication."""
+
+import numpy as np
+import pytest
+import torch
+
+from lean_vllm_b200.attention.kvx_cache import PushTarget, store_kvcache, store_latents
+from lean_vllm_b200.kv_transfer import transport
+from oracle.kv_oracle import store_kvcache as oracle_store
+from tests.helpers import bits, from_bits
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
+@pytest.mark.parametrize("layout", ["NHD", "HND"])
+def test_the_store_matches_the_reference(golden, layout, slot_dtype):
+    _, arrays = golden
+    key = from_bits(arrays["store_key"]).cuda()
+    value = from_bits(arrays["store_value"]).cuda()
+    slots = torch.from_numpy(arrays["store_slots"]).to(slot_dtype).cuda()
+    cache = from_bits(arrays[f"store_{layout}_before"]).cuda()
+    view = cache if layout == "NHD" else cache.transpose(2, 3)
+    store_kvcache(key, value, view[0], view[1], slots)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(cache), arrays[f"store_{layout}_after"])
+
+
+def test_the_latent_store_matches_the_reference(golden):
+    _, arrays = golden
+    cache = from_bits(arrays["store_latent_before"]).cuda()
+    store_latents(from_bits(arrays["store_latent"]).cuda(), cache[0],
+                  torch.from_numpy(arrays["store_slots"]).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(cache), arrays["store_latent_after"])
+
+
+def _qwen_step(tokens=3000, blocks=40, heads=8, seed=0, hnd=True):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    key = torch.randn(tokens, heads, 128, generator=g, device="cuda").to(torch.bfloat16)
+    value = torch.randn(tokens, heads, 128, generator=g, device="cuda").to(torch.bfloat16)
+    shape = (2, blocks, heads, 256, 128) if hnd else (2, blocks, 256, heads, 128)
+    cache = torch.randn(*shape, generator=g, device="cuda").to(torch.bfloat16)
+    slots = torch.randperm(blocks * 256, generator=g, device="cuda")[:tokens]
+    slots[::97] = -1
+    return key, value, cache, slots
+
+
+@pytest.mark.parametrize("hnd", [True, False], ids=["HND", "NHD"])
+def test_a_model_sized_store_matches_the_oracle(hnd):
+    key, value, cache, slots = _qwen_step(hnd=hnd)
+    expected = bits(cache).copy()
+    e_view = expected if not hnd else expected.swapaxes(2, 3)
+    oracle_store(bits(key), bits(value), e_view[0], e_view[1], slots.cpu().numpy())
+    view = cache.transpose(2, 3) if hnd else cache
+    store_kvcache(key, value, view[0], view[1], slots)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(cache), expected)
+
+
+def test_the_fused_store_also_writes_each_peer_s_heads_into_its_own_slots():
+    """TP1 prefill -> TP2 decode: the store writes all 8 heads locally and heads 0-3 / 4-7 into two 4-head decode
+    caches at their own (shuffled) slots, in the same launch."""
+    key, value, cache, slots = _qwen_step(tokens=2000)
+    peers = [torch.zeros(2, 30, 4, 256, 128, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    peer_slots = [torch.randperm(30 * 256, device="cuda")[:2000] for _ in range(2)]
+    peer_slots[1][5] = -1
+    targets = [PushTarget.of(p.transpose(2, 3)[0], p.transpose(2, 3)[1], s, src_first_head=4 * r, num_heads=4)
+               for r, (p, s) in enumerate(zip(peers, peer_slots))]
+    expected_local = cache.clone()
+    view = expected_local.transpose(2, 3)
+    expected_peers = [p.clone() for p in peers]
+    store_kvcache(key, value, view[0], view[1], slots)  # the local store alone, as reference
+    for r, (p, s) in enumerate(zip(expected_peers, peer_slots)):
+        pv = p.transpose(2, 3)
+        store_kvcache(key[:, 4 * r : 4 * r + 4].contiguous(), value[:, 4 * r : 4 * r + 4].contiguous(), pv[0], pv[1],
+                      s)
+    before = transport.launch_count()
+    view = cache.transpose(2, 3)
+    store_kvcache(key, value, view[0], view[1], slots, push_to=targets)
+    torch.cuda.synchronize()
+    assert transport.launch_count() - before == 1
+    assert torch.equal(cache, expected_local)
+    for p, e in zip(peers, expected_peers):
+        assert torch.equal(p, e)
+
+
+def test_the_fused_latent_store_replicates_to_every_decode_rank():
+    g = torch.Generator(device="cuda").manual_seed(3)
+    latent = torch.randn(1000, 576, generator=g, device="cuda").to(torch.bfloat16)
+    local = torch.zeros(1, 40, 64, 576, device="cuda", dtype=torch.bfloat16)
+    slots = torch.randperm(40 * 64, device="cuda")[:1000]
+    peers = [torch.zeros(1, 50, 64, 576, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    peer_slots = [torch.randperm(50 * 64, device="cuda")[:1000].to(torch.int32) for _ in range(3)]
+    store_latents(latent, local[0], slots, push_to=[PushTarget.of(p[0], None, s) for p, s in zip(peers, peer_slots)])
+    torch.cuda.synchronize()
+    assert torch.equal(local[0].reshape(-1, 576)[slots], latent)
+    for p, s in zip(peers, peer_slots):
+        assert torch.equal(p[0].reshape(-1, 576)[s.long()], latent)
+
+
+def test_a_slot_past_the_cache_is_skipped_and_flagged():
+    key, value, cache, slots = _qwen_step(tokens=64, blocks=4)
+    slots[10] = 4 * 256  # one past the last slot
+    before = cache.clone()
+    assert transport.device_error() == 0
+    view = cache.transpose(2, 3)
+    store_kvcache(key, value, view[0], view[1], slots)
+    torch.cuda.synchronize()
+    assert transport.device_error() == 2
+    assert transport.device_error() == 0  # read and cleared
+    keep = slots.clone()
+    keep[10] = -1
+    e_view = before.transpose(2, 3)
+    store_kvcache(key, value, e_view[0], e_view[1], keep)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, before)
+
+
+def test_bad_arguments_raise_before_a_launch():
+    key, value, cache, slots = _qwen_step(tokens=16, blocks=2)
+    view = cache.transpose(2, 3)
+    with pytest.raises(ValueError, match="slots for"):
+        store_kvcache(key, value, view[0], view[1], slots[:5])
+    with pytest.raises(TypeError):
+        store_kvcache(key, value, view[0], view[1], slots.float())
+    bad = PushTarget.of(view[0], view[1], slots, src_first_head=6, num_heads=4)
+    from lean_vllm_b200._native import KvxRangeError
+
+    with pytest.raises(KvxRangeError, match="heads"):
+        store_kvcache(key, value, view[0], view[1], slots, push_to=[bad])
