@@ -328,6 +328,7 @@ def digest(layers, ids, first_head: int, num_heads: int, mla: bool, device):
     copy mean the bytes landed."""
     import torch
 
+    device = layers[0].device
     index = torch.as_tensor(ids, device=device, dtype=torch.long)
     out = []
     for layer in (0, len(layers) - 1):
@@ -372,13 +373,25 @@ def run_gpu(args) -> None:
     heads = split_heads(spec.kv_heads, spec.decode_tp, spec.prefill_tp)
     loopback = role.side == "both"
     groups = 1 if loopback else world // spec.group_size
+    # --peer-device: one process, the destination cache on another GPU, peer access instead of IPC (the NVLink
+    # path in a single process, for profilers that take one process).
+    peer_mode = loopback and args.peer_device is not None
+    dst_device = launch_device = device
+    if peer_mode:
+        dst_device = torch.device("cuda", args.peer_device)
+        launch_device = dst_device if args.mode == "pull" else device
+        other = device if args.mode == "pull" else dst_device
+        if not transport.enable_peer_access(launch_device.index, other.index):
+            raise SystemExit(f"cuda:{launch_device.index} cannot reach cuda:{other.index} directly")
 
     src = dst = None
     if role.side in ("prefill", "both"):
         src = alloc_cache(spec, spec.prefill_tp, num_blocks, device, fill=True, seed=1000 + rank)
     if role.side in ("decode", "both"):
-        dst = alloc_cache(spec, spec.decode_tp, num_blocks, device, fill=False, seed=0)
-    torch.cuda.synchronize()
+        dst = alloc_cache(spec, spec.decode_tp, num_blocks, dst_device, fill=False, seed=0)
+    torch.cuda.synchronize(device)
+    torch.cuda.synchronize(dst_device)
+    torch.cuda.set_device(launch_device)
 
     # Exchange every rank's cache description; map the peers this rank launches against.
     mine = src if role.side == "prefill" else dst
@@ -419,7 +432,7 @@ def run_gpu(args) -> None:
     else:
         caches = []
     my_bytes = transport.job_bytes(caches, jobs) if jobs else 0
-    stream = torch.cuda.Stream(device=device)
+    stream = torch.cuda.Stream(device=launch_device)
     sid = stream.cuda_stream
 
     def step():
@@ -438,7 +451,7 @@ def run_gpu(args) -> None:
 
     launches0 = transport.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
+    with ClockSampler(launch_device.index) as clocks:
         start.record(stream)
         for _ in range(args.steps):
             step()
@@ -487,7 +500,7 @@ def run_gpu(args) -> None:
 
     # e2e: the same loads through the connector's public API.
     e2e_ms, e2e_bytes = None, 0
-    if args.steps and not args.no_e2e:
+    if args.steps and not args.no_e2e and not peer_mode:
         e2e_ms, e2e_bytes = e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo)
         e = torch.tensor([e2e_ms, float(e2e_bytes)], device=device, dtype=torch.float64)
         if world > 1:
@@ -514,7 +527,7 @@ def run_gpu(args) -> None:
             with open(peaks_path) as f:
                 peaks = json.load(f)
         traffic = load_traffic().get("loopback" if loopback else f"{args.workload}-{args.mode}")
-        if loopback:
+        if loopback and not peer_mode:
             hbm = peaks.get("hbm_gbs", 6650.0)
             achieved = 2 * step_bytes_total / (ms_per_step * 1e-3) / 1e9
             roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -553,7 +566,8 @@ def run_gpu(args) -> None:
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) bf16 caches, seeded shuffled block tables",
             "config": {
-                "workload": (f"{spec.name}/loopback-1gpu" if loopback else
+                "workload": (f"{spec.name}/peer-1process-cuda0-to-cuda{args.peer_device}" if peer_mode else
+                             f"{spec.name}/loopback-1gpu" if loopback else
                              f"{spec.name}/{groups}x-tp{spec.prefill_tp}to{spec.decode_tp}"),
                 "shape": spec.describe(),
                 "requests_per_step": len(reqs),
@@ -581,7 +595,7 @@ def run_gpu(args) -> None:
                            "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
                                     "get_finished() until every load finished_recving; one kvx launch per load, "
                                     "block ids carried in the launch, completion by event query")}
-        if loopback and not args.no_cpu_baseline:
+        if loopback and not peer_mode and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(reqs, spec, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -734,7 +748,8 @@ def run_layerwise(args) -> None:
             kv_role="kv_consumer", kv_port=base_port + 8, engine_id=f"lw-decode-{role.group}"),
             kvx_accept_push=True), 0)
         consumer.register_kv_caches(dst)
-    hidden, width = 4096, int(LAYER_FLOPS_PER_TOKEN / (2 * 4096))
+    # A multiple of 128 wide, so the GEMM runs at tensor-core speed like the real layer's projections.
+    hidden, width = 4096, int(LAYER_FLOPS_PER_TOKEN / (2 * 4096)) // 128 * 128
     if producer is not None:
         a = torch.randn(8192, hidden, device=device, dtype=torch.bfloat16)
         w = torch.randn(hidden, width, device=device, dtype=torch.bfloat16) * 0.01
@@ -915,6 +930,8 @@ def main(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the connector end-to-end timing")
     p.add_argument("--kv-port", type=int, default=24600, help="first handshake port of the e2e connectors")
+    p.add_argument("--peer-device", type=int, default=None,
+                   help="N=1 only: put the destination cache on this GPU (one process, peer access over NVLink)")
     p.add_argument("--layerwise", action="store_true",
                    help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
     args = p.parse_args(argv)
