@@ -526,7 +526,7 @@ def run_gpu(args) -> None:
         if os.path.exists(peaks_path):
             with open(peaks_path) as f:
                 peaks = json.load(f)
-        traffic = load_traffic().get("loopback" if loopback else f"{args.workload}-{args.mode}")
+        traffic = load_traffic().get("loopback" if loopback and not peer_mode else f"{args.workload}-{args.mode}")
         if loopback and not peer_mode:
             hbm = peaks.get("hbm_gbs", 6650.0)
             achieved = 2 * step_bytes_total / (ms_per_step * 1e-3) / 1e9
@@ -549,6 +549,7 @@ def run_gpu(args) -> None:
                         "peak_source": "measured peer copy per direction on this pool (nominal 900 GB/s)",
                         "link_bytes_per_step": int(link_bytes),
                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                        "nvlink_rx_bytes_per_launch": traffic.get("nvlink_rx_bytes_per_launch") if traffic else None,
                         "algorithmic_bytes_per_launch": int(per_group / (spec.decode_tp if args.mode == "pull"
                                                                          else spec.prefill_tp))}
         line = {
@@ -876,6 +877,118 @@ def run_layerwise(args) -> None:
         dist.destroy_process_group()
 
 
+def run_store(args) -> None:
+    """The per-token cache store (store_kvcache, one kvx_store launch per layer) for one 8192-token prefill step of
+    a Qwen3-8B-shaped model: 36 layers, each with its own new keys/values [8192, 8, 128] bf16 and its own HND cache,
+    slots from a seeded shuffled block table. With --peer-device the same launches also push every row into a
+    decode cache on that GPU (the fused store-and-push). Beside it, the torch indexing store (the reference's
+    TorchAttention.store_kvcache, attention/torch_backend.py:34-48) on the same inputs."""
+    import torch
+
+    from lean_vllm_b200.attention.kvx_cache import PushTarget, store_kvcache
+    from lean_vllm_b200.kv_transfer import transport
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    tokens, heads, dim, block, layers, nb = 8192, 8, 128, 256, 36, 48
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    keys = [torch.randn(tokens, heads, dim, device=device, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    values = [torch.randn(tokens, heads, dim, device=device, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    caches = [torch.zeros(2, nb, heads, block, dim, device=device, dtype=torch.bfloat16) for _ in range(layers)]
+    blocks = torch.randperm(nb, device=device, generator=g)[: tokens // block]
+    slots = (blocks[:, None] * block + torch.arange(block, device=device)[None, :]).reshape(-1).contiguous()
+    targets = [[] for _ in range(layers)]
+    if args.peer_device is not None:
+        peer = torch.device("cuda", args.peer_device)
+        if not transport.enable_peer_access(0, peer.index):
+            raise SystemExit(f"cuda:0 cannot reach cuda:{peer.index} directly")
+        peer_caches = [torch.zeros(2, nb, heads, block, dim, device=peer, dtype=torch.bfloat16)
+                       for _ in range(layers)]
+        peer_slots = torch.flip(slots, [0]).contiguous()  # another block table on the decode side
+        targets = [[PushTarget.of(c.transpose(2, 3)[0], c.transpose(2, 3)[1], peer_slots)] for c in peer_caches]
+        torch.cuda.synchronize(peer)
+
+    def ours():
+        for layer in range(layers):
+            view = caches[layer].transpose(2, 3)
+            store_kvcache(keys[layer], values[layer], view[0], view[1], slots, push_to=targets[layer])
+
+    def torch_indexing():
+        b, o = slots // block, slots % block
+        for layer in range(layers):
+            view = caches[layer].transpose(2, 3)
+            view[0][b, o] = keys[layer]
+            view[1][b, o] = values[layer]
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / steps
+
+    launches0 = transport.launch_count()
+    with ClockSampler(0) as clocks:
+        ms = timed(ours, args.steps)
+    launches = transport.launch_count() - launches0
+    ms_torch = timed(torch_indexing, max(args.steps // 4, 2))
+    # Correctness: every layer's cache holds its rows at the slots (and the peer's at its slots).
+    ok = True
+    for layer in (0, layers - 1):
+        view = caches[layer].transpose(2, 3)
+        ok &= torch.equal(view[0][slots // block, slots % block], keys[layer])
+        ok &= torch.equal(view[1][slots // block, slots % block], values[layer])
+        if args.peer_device is not None:
+            pv = peer_caches[layer].transpose(2, 3)
+            ps = peer_slots.to(peer)
+            ok &= torch.equal(pv[0][ps // block, ps % block], keys[layer].to(peer))
+    rows = 2 * tokens * heads * dim * 2  # keys and values of one layer
+    hbm_bytes = layers * (2 * rows + tokens * 8)  # read rows and slots, write rows
+    peaks = {}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    if args.peer_device is None:
+        roofline = {"bound": "hbm", "achieved": round(hbm_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(hbm_bytes / (ms * 1e-3) / 1e9 / hbm, 4), "algorithmic_bytes_per_launch":
+                    hbm_bytes // layers, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"}
+    else:
+        link = layers * rows
+        roofline = {"bound": "nvlink", "achieved": round(link / (ms * 1e-3) / 1e9, 1), "peak": NVLINK_PEER_GBS,
+                    "unit": "GB/s", "frac": round(link / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4),
+                    "link_bytes_per_launch": link // layers, "hbm_bytes_per_launch": hbm_bytes // layers,
+                    "peak_source": "measured peer copy per direction on this pool (nominal 900 GB/s)"}
+    line = {
+        "metric": "KV cache store (store_kvcache) GB/s" + (" fused with push" if args.peer_device is not None else ""),
+        "value": round(hbm_bytes / (ms * 1e-3) / 1e9, 1),
+        "unit": "GB/s (HBM bytes read + written)",
+        "higher_is_better": True,
+        "n_gpus": 1 if args.peer_device is None else 2,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) bf16 rows, seeded shuffled block table",
+        "config": {"workload": "qwen3-8b-kv/store-8192-token-step", "layers": layers, "tokens": tokens,
+                   "shape": "8 KV heads x 128, block 256, HND",
+                   "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None},
+        "roofline": roofline,
+        "torch_indexing_ms_per_step": round(ms_torch, 4),
+        "speedup_vs_torch_indexing": round(ms_torch / ms, 2),
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "correct": bool(ok),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -934,9 +1047,12 @@ def main(argv=None):
                    help="N=1 only: put the destination cache on this GPU (one process, peer access over NVLink)")
     p.add_argument("--layerwise", action="store_true",
                    help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
+    p.add_argument("--store", action="store_true", help="measure the per-token cache store (and fused push)")
     args = p.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.store:
+        run_store(args)
     elif args.layerwise:
         run_layerwise(args)
     else:
