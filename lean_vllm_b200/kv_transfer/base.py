@@ -99,6 +99,7 @@ class ReqToRecv:
     remote_port: int
     remote_tp_size: int = 1
     pushed: bool = False
+    skip_blocks: int = 0  # pushed with no remote_block_ids: the prompt's leading blocks already cached here
 
 
 @dataclass(slots=True)
@@ -106,14 +107,16 @@ class ReqToSave:
     """This package's extension (no counterpart in the reference): a request being prefilled here whose blocks are
     pushed, layer by layer during the prefill, into a decode instance's already allocated blocks. `local_block_ids`
     are this instance's, `remote_block_ids` the decode instance's, aligned; `remote_*` name the decode instance
-    (its kv_ip, kv_port, engine_id and tensor-parallel size)."""
+    (its kv_ip, kv_port, engine_id and tensor-parallel size). With `push_id` and no remote_block_ids, the decode
+    instance is not known yet: its ranks announce themselves and their blocks under that id."""
 
     local_block_ids: list[int]
-    remote_block_ids: list[int]
-    remote_engine_id: str
-    remote_host: str
-    remote_port: int
+    remote_block_ids: list[int] | None = None
+    remote_engine_id: str = ""
+    remote_host: str = ""
+    remote_port: int = 0
     remote_tp_size: int = 1
+    push_id: str | None = None
 
 
 @dataclass(slots=True)

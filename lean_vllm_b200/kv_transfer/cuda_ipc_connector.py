@@ -68,7 +68,15 @@ def make_transport(kv_caches):
 
 
 class CudaIpcConnectorScheduler(KVConnectorScheduler):
-    """The engine's half, as NixlConnectorScheduler (nixl_connector.py:111-168)."""
+    """The engine's half, as NixlConnectorScheduler (nixl_connector.py:111-168).
+
+    Push mode adds two optional kv_transfer_params keys the reference does not have. A decode request sent before
+    its prefill carries "kv_push": true (with remote_block_ids empty): it is admitted, allocated and left waiting,
+    and its worker ranks announce its blocks to the prefill ranks. The prefill request carries "kv_push_id" (the
+    decode request's remote_request_id): at its admission -- the reference scheduler asks the connector about every
+    request right after allocating its blocks (engine/scheduler.py:193-196) -- this half hands the workers a
+    ReqToSave, and they push the blocks as they are computed.
+    """
 
     def __init__(self, config):
         self.kv_transfer = config.kv_transfer
@@ -76,11 +84,19 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
         self.tp_size = config.tensor_parallel_size
         self._reqs_to_recv: dict[str, ReqToRecv] = {}
         self._reqs_to_send: dict[str, list[int]] = {}
+        self._reqs_to_save: dict[str, ReqToSave] = {}
 
     def get_num_new_matched_tokens(self, seq, num_computed_tokens: int) -> tuple[int, bool]:
         params = seq.kv_transfer_params
+        if params and params.get("do_remote_decode") and params.get("kv_push_id"):
+            # A prefill whose decode instance waits for a push: its blocks are allocated now, so save them.
+            blocks = list(seq.block_table[: _cdiv(seq.num_prompt_tokens, self.block_size)])
+            self._reqs_to_save[seq.request_id] = ReqToSave(blocks, push_id=str(params["kv_push_id"]))
+            return 0, False
         if not params or not params.get("do_remote_prefill"):
             return 0, False
+        if params.get("kv_push"):  # the blocks will be pushed here: nothing to check against yet
+            return seq.num_prompt_tokens - num_computed_tokens, True
         expected = _cdiv(seq.num_prompt_tokens, self.block_size)
         given = len(params["remote_block_ids"])
         if given != expected:
@@ -94,19 +110,23 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
         params = seq.kv_transfer_params
         params["do_remote_prefill"] = False  # one load per request; a preempted one recomputes
         cached = seq.num_cached_tokens // self.block_size  # blocks this instance already holds are not read
+        pushed = bool(params.get("kv_push"))
+        prompt_blocks = _cdiv(seq.num_prompt_tokens, self.block_size)
         self._reqs_to_recv[seq.request_id] = ReqToRecv(
-            local_block_ids=list(seq.block_table[cached:]),
-            remote_block_ids=list(params["remote_block_ids"][cached:]),
+            local_block_ids=list(seq.block_table[cached:prompt_blocks] if pushed else seq.block_table[cached:]),
+            remote_block_ids=[] if pushed else list(params["remote_block_ids"][cached:]),
             remote_request_id=params["remote_request_id"],
             remote_engine_id=params["remote_engine_id"],
             remote_host=params["remote_host"],
             remote_port=params["remote_port"],
             remote_tp_size=params.get("tp_size", 1),
+            pushed=pushed,
+            skip_blocks=cached if pushed else 0,
         )
 
     def build_connector_meta(self) -> KVConnectorMetadata:
-        metadata = KVConnectorMetadata(self._reqs_to_recv, self._reqs_to_send)
-        self._reqs_to_recv, self._reqs_to_send = {}, {}
+        metadata = KVConnectorMetadata(self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save)
+        self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save = {}, {}, {}
         return metadata
 
     def request_finished(self, seq) -> tuple[bool, dict | None]:
@@ -167,6 +187,7 @@ class _Save:
     handed_over: bool = False  # the prefill is over (engine thread): no more per-layer pushes
     finishing: bool = False  # what was left is queued (transfer thread): done once nothing is in flight
     started: float = field(default_factory=monotonic)
+    ready_marker: object = None  # the engine stream's event at hand-over, which the catch-up pushes wait for
 
 
 @dataclass(slots=True)
@@ -208,6 +229,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._notified: dict[str, list] = {}  # request -> [notifications, readers, first seen]
         self._saves: dict[str, _Save] = {}  # producer: requests pushed layer by layer
         self._saved: dict[str, dict] = {}  # decode: request -> {producer rank: landed ok}, may precede the wait
+        self._push_ids: dict[str, str] = {}  # producer: push id -> request id, for saves awaiting their decode ranks
+        self._expects: dict[str, dict] = {}  # producer: push id -> a decode rank's announcement, may come first
         self._finished = KVConnectorOutput()
         self._queue: queue.Queue = queue.Queue()
         self._context = zmq.Context()
@@ -254,6 +277,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         for request_id, req in getattr(metadata, "reqs_to_save", {}).items():
             with self._lock:
                 if request_id in self._saves:
+                    continue
+                if req.remote_block_ids is None:  # its decode ranks announce themselves under req.push_id
+                    self._saves[request_id] = _Save(req, [])
+                    self._push_ids[str(req.push_id)] = request_id
+                    self._queue.put(("connect", request_id))
                     continue
                 save = self._saves[request_id] = _Save(req, self._targets(req))
                 # Decode ranks mapped by an earlier handshake: ready now, so this step's first layer is pushed by
@@ -443,6 +471,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if op == "notify":
                 self._count(message.get("message", ""))
                 continue
+            if op == "expect":
+                push_id = str(message.get("push_id"))
+                with self._lock:
+                    self._expects.setdefault(push_id, message)
+                    request_id = self._push_ids.get(push_id)
+                if request_id is not None:
+                    self._connect(request_id)
+                continue
             if op == "saved":
                 with self._lock:
                     self._saved.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
@@ -571,31 +607,59 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
     # Push, producer side: map the decode ranks, catch up on layers no save_kv_layer pushed, report landing.
 
     def _connect(self, request_id: str):
+        """Maps the decode ranks of a save (once its decode instance is known), then advances it."""
         with self._lock:
             save = self._saves.get(request_id)
-        if save is None:
-            return
+            if save is None or save.ready or save.failed:
+                return
+            if save.req.remote_block_ids is None:
+                expect = self._expects.pop(str(save.req.push_id), None)
+                if expect is None:
+                    return  # its decode ranks have not announced themselves yet
+                self._push_ids.pop(str(save.req.push_id), None)
+                skip = int(expect.get("skip", 0))
+                remote_ids = [int(b) for b in expect.get("block_ids", [])]
+                local_ids = list(save.req.local_block_ids)[skip:]
+                save.req = ReqToSave(local_ids, remote_ids, str(expect.get("engine_id", "")),
+                                     str(expect.get("host", "")), int(expect.get("port", 0)),
+                                     int(expect.get("tp_size", 1)), save.req.push_id)
+                save.targets = self._targets(save.req)
+                if len(local_ids) != len(remote_ids):
+                    save.failed = True  # still mapped below, so the decode ranks hear that nothing comes
+                    logger.warning("the decode instance announced %d blocks for %s, which has %d here",
+                                   len(remote_ids), request_id, len(local_ids))
         try:
             tables = [self._handshake(save.req, decode_rank).table for _, decode_rank, _ in save.targets]
             with self._lock:
                 save.tables = tables
-                save.ready = True
+                save.ready = not save.failed
         except Exception as error:  # noqa: BLE001
-            logger.warning("cannot push the KV of %s to %s:%d, so the decode instance prefills it: %s", request_id,
-                           save.req.remote_host, save.req.remote_port, error)
+            logger.warning("cannot push the KV of %s to %s:%d, so the decode instance prefills it: %s",
+                           request_id, save.req.remote_host, save.req.remote_port, error)
             with self._lock:
                 save.failed = True
+        self._advance(request_id)
 
     def _finish(self, request_id: str, ready):
         with self._lock:
             save = self._saves.get(request_id)
-            if save is None:
+            if save is not None:
+                save.ready_marker = ready
+        self._advance(request_id)
+
+    def _advance(self, request_id: str):
+        """A handed-over save whose decode ranks are mapped: push the layers no save_kv_layer reached (all of them
+        for an engine without layer hooks) and let it finish once they land. One whose mapping failed finishes at
+        once; one still waiting for its decode instance waits (and expires at the timeout)."""
+        with self._lock:
+            save = self._saves.get(request_id)
+            if save is None or not save.handed_over or save.finishing:
                 return
-            if not save.ready:
-                save.failed = True  # never mapped: nothing landed, nothing will
+            if not save.failed and not save.ready:
+                return
             missing = [] if save.failed else [i for i in range(len(self.layer_regions)) if i not in save.pushed]
             save.pushed.update(missing)
-        # The layers save_kv_layer did not reach (all of them for an engine without layer hooks).
+            ready = save.ready_marker
         posts = [None] if len(missing) == len(self.layer_regions) else missing
         for layer in posts if missing else []:
             with self._lock:
@@ -638,22 +702,49 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         with self._lock:
             done = [(rid, s) for rid, s in self._saves.items() if s.finishing and s.inflight == 0]
             stale = [(rid, s) for rid, s in self._saves.items()
-                     if not s.handed_over and s.inflight == 0 and s.started + timeout < now]
+                     if not s.finishing and s.inflight == 0 and s.started + timeout < now]
             for request_id, save in done:
                 del self._saves[request_id]
                 self._finished.finished_sending.add(request_id)  # every byte landed, or none will
-            for request_id, save in stale:  # never handed over (an aborted prefill): the decode side gives up
+            for request_id, save in stale:
+                # Never handed over (an aborted prefill), or handed over to a decode instance that never announced
+                # itself: the held blocks are freed as the reference frees unread ones.
                 del self._saves[request_id]
+                self._push_ids.pop(str(save.req.push_id), None)
                 save.failed = True
+                if save.handed_over:
+                    self._finished.finished_sending.add(request_id)
+                    self._finished.expired_sending.add(request_id)
+            for push_id, expect in list(self._expects.items()):
+                if expect.setdefault("_seen", now) + timeout < now:
+                    del self._expects[push_id]  # announced for a prefill that never came here
         for request_id, save in done + stale:
+            tag = save.req.push_id or request_id
             for key, _, _ in save.targets:
-                self._send(key, {"op": "saved", "request": request_id, "rank": self.rank, "ok": not save.failed})
+                self._send(key, {"op": "saved", "request": tag, "rank": self.rank, "ok": not save.failed})
 
     # Push, decode side: wait for every producer rank holding this rank's heads.
 
     def _start_wait(self, request_id: str, req: ReqToRecv):
         heads = self._heads(req)
         shares = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
+        if not req.remote_block_ids:
+            # The prefill instance does not know where to push yet: announce these blocks to every producer rank
+            # holding this rank's heads, under the push id (the load's remote_request_id).
+            kv = self.kv_transfer
+            announcement = {"op": "expect", "push_id": req.remote_request_id, "block_ids": list(req.local_block_ids),
+                            "skip": req.skip_blocks, "engine_id": kv.engine_id, "host": kv.kv_ip,
+                            "port": kv.kv_port, "tp_size": self.tp_size}
+            try:
+                for share in shares:
+                    self._handshake(req, share.remote_rank, fresh=True)
+                    self._send((req.remote_host, req.remote_port + share.remote_rank), announcement)
+            except Exception as error:  # noqa: BLE001
+                logger.warning("cannot announce %s to %s:%d, so it prefills here: %s", req.remote_request_id,
+                               req.remote_host, req.remote_port, error)
+                with self._lock:
+                    self._finished.failed_recving.add(request_id)
+                return
         num_bytes = 0
         for i, share in enumerate(shares):
             for cache in self.kv_caches:
@@ -685,13 +776,18 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     logger.warning("the pushed KV of %s did not land, so it prefills here", wait.req.remote_request_id)
                     self._finished.failed_recving.add(request_id)
 
-    def _handshake(self, req, remote_rank: int) -> _Remote:
-        """The peer rank's cache, asked for once per peer and mapped here, checked to match this engine."""
+    def _handshake(self, req, remote_rank: int, fresh: bool = False) -> _Remote:
+        """The peer rank's cache, asked for once per peer and mapped here, checked to match this engine. An empty
+        remote_engine_id accepts whichever engine answers; `fresh` asks again even if one is mapped, to see a
+        restart (for a load that names no engine id)."""
         key = (req.remote_host, req.remote_port + remote_rank)
         remote = self._remotes.get(key)
-        if remote is not None:
-            if remote.engine_id == req.remote_engine_id:
+        if remote is not None and fresh:
+            if self._ask(key)["engine_id"] == remote.engine_id:
                 return remote
+        elif remote is not None and (remote.engine_id == req.remote_engine_id or not req.remote_engine_id):
+            return remote
+        if remote is not None:
             del self._remotes[key]  # restarted since: ask afresh
             with self._lock:
                 self._mapped.pop(key, None)
@@ -710,7 +806,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             reply = json.loads(raw)
             if not reply["ok"]:
                 raise RuntimeError(reply["error"])
-            if reply["engine_id"] != req.remote_engine_id:
+            if req.remote_engine_id and reply["engine_id"] != req.remote_engine_id:
                 raise RuntimeError(f"{key[0]}:{key[1]} is engine {reply['engine_id']}, not {req.remote_engine_id}")
             if reply["tp_size"] != req.remote_tp_size:
                 raise RuntimeError(f"{key[0]}:{key[1]} runs tp_size {reply['tp_size']}, not {req.remote_tp_size}")
@@ -731,3 +827,20 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         finally:
             if not keep:
                 sock.close()
+
+    def _ask(self, key) -> dict:
+        """One handshake round trip on a socket of its own, for its reply only."""
+        sock = self._context.socket(zmq.DEALER)
+        try:
+            sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
+            sock.connect(f"tcp://{key[0]}:{key[1]}")
+            sock.send(json.dumps({"op": "handshake"}).encode())
+            try:
+                reply = json.loads(sock.recv())
+            except zmq.Again:
+                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake") from None
+        finally:
+            sock.close()
+        if not reply.get("ok"):
+            raise RuntimeError(reply.get("error", "handshake refused"))
+        return reply

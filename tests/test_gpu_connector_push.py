@@ -78,3 +78,23 @@ def test_a_per_layer_save_launch_is_held_to_its_sm_budget(sides, monkeypatch):
     want = torch.zeros_like(big)
     want[:, LOCAL] = big[:, REMOTE]
     assert torch.equal(consumers[0].kv_caches[0].cpu(), want)
+
+
+@pytest.mark.parametrize("prefill_tp, decode_tp, mla", [(1, 1, False), (2, 4, False), (1, 2, True)])
+def test_an_announced_push_through_both_halves_on_the_gpu(sides, golden, prefill_tp, decode_tp, mla):
+    """The decode request is admitted first and its ranks announce their blocks; the prefill's admission turns into
+    a ReqToSave; the bytes land as the reference's pull lands them."""
+    from time import sleep
+
+    from tests.push_cases import make_flow
+
+    _, arrays = golden
+    flow = make_flow(sides, prefill_tp, decode_tp, mla)
+    flow.decode_admits()
+    sleep(0.1)
+    flow.prefill_runs()
+    sent, recved = flow.results()
+    assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}
+    key = "lat" if mla else "kv"
+    got = full_of([c.kv_caches[0].cpu() for c in flow.consumers], mla)
+    assert np.array_equal(bits(got), arrays[f"small_{key}_tp{prefill_tp}to{decode_tp}"])
