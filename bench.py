@@ -689,6 +689,28 @@ def e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo):
 LAYER_FLOPS_PER_TOKEN = 2 * 193e6
 
 
+def token_slots(block_ids, length: int, block: int) -> np.ndarray:
+    """The cache slot of each of a request's tokens, given its block table."""
+    t = np.arange(int(length))
+    return np.asarray(block_ids, dtype=np.int64)[t // block] * block + t % block
+
+
+def row_digest(layers, slots):
+    """Position-weighted digest of the keys and values at the given slots (first and last layer)."""
+    import torch
+
+    device = layers[0].device
+    index = torch.as_tensor(slots, device=device, dtype=torch.long)
+    out = []
+    for layer in (0, len(layers) - 1):
+        view = layers[layer].transpose(2, 3)  # (2, blocks, tokens, heads, dim)
+        part = view[:, index // view.size(2), index % view.size(2)]
+        flat = part.contiguous().view(torch.int16).reshape(-1).to(torch.int64)
+        weights = torch.arange(flat.numel(), device=device, dtype=torch.int64) % 65521 + 1
+        out += [int(flat.sum().item()), int((flat * weights).sum().item())]
+    return out
+
+
 def run_layerwise(args) -> None:
     """Layer-by-layer push during a synthetic prefill, through the connector's per-layer save (save_kv_layer).
 
@@ -755,6 +777,11 @@ def run_layerwise(args) -> None:
         a = torch.randn(8192, hidden, device=device, dtype=torch.bfloat16)
         w = torch.randn(hidden, width, device=device, dtype=torch.bfloat16) * 0.01
         out = torch.empty(8192, width, device=device, dtype=torch.bfloat16)
+        if args.fused:  # each layer's new keys/values, stored through the connector (store_kv)
+            new_k = torch.randn(8192, spec.kv_heads, spec.head_dim, device=device).to(torch.bfloat16)
+            new_v = torch.randn(8192, spec.kv_heads, spec.head_dim, device=device).to(torch.bfloat16)
+            step_slots = [torch.as_tensor(np.concatenate([token_slots(reqs[i][0], lengths[i], spec.block)
+                                                          for i in step]), device=device) for step in steps]
     torch.cuda.synchronize()
 
     def sync_all():
@@ -776,7 +803,7 @@ def run_layerwise(args) -> None:
             start, compute_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             landed = torch.cuda.Event(enable_timing=True)
             start.record(stream)
-            for step in steps:
+            for si, step in enumerate(steps):
                 n_tokens = int(sum(int(lengths[i]) for i in step))
                 if saves:
                     producer.start_load_kv(KVConnectorMetadata(reqs_to_save={
@@ -794,7 +821,9 @@ def run_layerwise(args) -> None:
                                 raise RuntimeError("the decode instance could not be mapped")
                 for layer in range(spec.layers):
                     torch.matmul(a[:n_tokens], w, out=out[:n_tokens])
-                    if saves:
+                    if args.fused:  # the layer's store, which also pushes the rows of every mapped save
+                        producer.store_kv(layer, new_k[:n_tokens], new_v[:n_tokens], step_slots[si])
+                    elif saves:
                         producer.save_kv_layer(layer)
                 if saves:
                     producer.wait_for_save()
@@ -828,12 +857,18 @@ def run_layerwise(args) -> None:
         alone = [iteration(f"c{k}", False)[0] for k in range(args.steps)]
         both = [iteration(f"s{k}", True) for k in range(args.steps)]
         ok = True
-        samples = [reqs[0], reqs[-1]]
+        samples = [0, len(reqs) - 1]
+
+        def check(layers, ids, i):
+            if args.fused:  # the stored rows only: a last block's tail past the prompt is never written
+                return row_digest(layers, token_slots(ids, lengths[i], spec.block))
+            return digest(layers, ids, 0, 8, False, device)
+
         if world == 1:
-            ok = all(digest(dst, d, 0, 8, False, device) == digest(src, s, 0, 8, False, device) for s, d in samples)
+            ok = all(check(dst, reqs[i][1], i) == check(src, reqs[i][0], i) for i in samples)
         else:
-            mine = [digest(src if src is not None else dst, s if src is not None else d, 0, 8, False, device)
-                    for s, d in samples] if role.side != "idle" else None
+            mine = [check(src, reqs[i][0], i) if src is not None else check(dst, reqs[i][1], i)
+                    for i in samples] if role.side != "idle" else None
             every = [None] * world
             dist.all_gather_object(every, (role.group, role.side, mine), group=gloo)
             for g in range(world // spec.group_size):
@@ -868,6 +903,8 @@ def run_layerwise(args) -> None:
             "prefill_tflops": round(flops / (t_alone * 1e-3) / 1e12, 1),
             "config": {"workload": f"{spec.name}/{'loopback-1gpu' if world == 1 else 'pair'} layerwise push",
                        "requests": len(reqs), "prefill_steps": len(steps),
+                       "push": ("fused into each layer's store (store_kv)" if args.fused else
+                                "save_kv_layer after each layer"),
                        "layer_stand_in": f"bf16 GEMM [tokens x 4096] @ [4096 x {width}] per layer",
                        "save_sms": int(os.environ.get("LEAN_VLLM_KVX_SAVE_SMS", "16"))},
             "correct": bool(ok),
@@ -1048,6 +1085,8 @@ def main(argv=None):
     p.add_argument("--layerwise", action="store_true",
                    help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
     p.add_argument("--store", action="store_true", help="measure the per-token cache store (and fused push)")
+    p.add_argument("--fused", action="store_true",
+                   help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     args = p.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)

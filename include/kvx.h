@@ -150,11 +150,17 @@ typedef struct kvx_store_dest {
     int32_t src_first_head;      /* this destination takes source heads [src_first_head, +num_heads) ... */
     int32_t num_heads;
     int32_t dst_first_head;      /* ... and stores them from its head dst_first_head */
+    const int32_t *block_map;    /* destinations after the first: if set, a device array mapping destination 0's
+                                    block ids to this cache's (-1 skips), used instead of slot_mapping: the row of
+                                    destination-0 slot s lands at block_map[s / block_size] * block_size +
+                                    s % block_size (both caches then share block_size) */
+    int32_t block_map_len;       /* entries of block_map; a block id past it is skipped and flagged (error 2) */
+    int32_t pad_;
 } kvx_store_dest;
 
 /* Scatters num_tokens rows of keys and values [token][head][head_bytes] (or latents, with value = NULL and
  * num_heads = 1) into each destination's slots, one pass over the rows: destination 0 is the local cache
- * (store_kvcache / store_latents, attention/triton_cache.py:9-91); destinations 1..3 may be peers' caches, which
+ * (store_kvcache / store_latents, attention/triton_cache.py:9-91); destinations 1..8 may be peers' caches, which
  * makes this the fused store-and-push of a layer-by-layer transfer. Strides of the rows are in bytes. */
 int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t value_stride, int num_tokens,
               int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int flags, void *stream);

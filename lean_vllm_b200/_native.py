@@ -96,6 +96,9 @@ class StoreDest(ctypes.Structure):
         ("src_first_head", ctypes.c_int32),
         ("num_heads", ctypes.c_int32),
         ("dst_first_head", ctypes.c_int32),
+        ("block_map", ctypes.c_void_p),
+        ("block_map_len", ctypes.c_int32),
+        ("pad_", ctypes.c_int32),
     ]
 
 

@@ -4,7 +4,7 @@ store_kvcache / store_latents (lean_vllm/attention/triton_cache.py:58-91).
 Each call reads the step's new rows once and writes them into the local paged cache by slot mapping -- through the
 cache's own strides, so NHD caches and HND caches' transposed views both work, and slot -1 skips a row -- and, when
 `push_to` names peers' caches (a decode instance's blocks, mapped over CUDA IPC), into those too in the same pass,
-each with its own slot mapping and head range: the fused store-and-push of a layer-by-layer transfer, which needs no
+each with its own slot mapping (or a block map from the local block ids) and head range: the fused store-and-push of a layer-by-layer transfer, which needs no
 re-read of the cache. There is no fallback: without libkvx.so the call raises.
 """
 
@@ -21,9 +21,11 @@ from lean_vllm_b200._native import StoreDest, check, lib
 @dataclass
 class PushTarget:
     """A peer cache a store also writes. Addresses are device addresses in this process (a kvx_ipc_open mapping
-    for another GPU's memory); strides are in bytes over (block, token, head, dim). `slot_mapping` is a device
-    tensor on the storing GPU with the peer's slot for each row (-1 skips). Source heads [src_first_head,
-    +num_heads) land at the peer's heads from dst_first_head (head resharding); latents use the defaults."""
+    for another GPU's memory); strides are in bytes over (block, token, head, dim). Each row's slot there is either
+    given (`slot_mapping`, a device tensor on the storing GPU, -1 skips) or derived from the local slot through
+    `block_map` (a device int32 tensor: local block id -> peer block id, -1 skips; same block size on both sides).
+    Source heads [src_first_head, +num_heads) land at the peer's heads from dst_first_head (head resharding);
+    latents use the defaults."""
 
     k_cache: int
     v_cache: int
@@ -32,10 +34,11 @@ class PushTarget:
     head_stride: int
     block_size: int
     num_blocks: int
-    slot_mapping: torch.Tensor
+    slot_mapping: torch.Tensor | None
     src_first_head: int = 0
     num_heads: int | None = None
     dst_first_head: int = 0
+    block_map: torch.Tensor | None = None
 
     @classmethod
     def of(cls, k_cache: torch.Tensor, v_cache: torch.Tensor | None, slot_mapping: torch.Tensor, **heads):
@@ -69,19 +72,30 @@ def _slots(slot_mapping: torch.Tensor, num_tokens: int, device) -> torch.Tensor:
 
 
 def _dest(k_addr, v_addr, block_stride, token_stride, head_stride, block_size, num_blocks, slots, first, count,
-          dst_first) -> StoreDest:
+          dst_first, block_map=None) -> StoreDest:
+    if block_map is not None and (block_map.dtype != torch.int32 or not block_map.is_contiguous()):
+        raise ValueError("a block map is a contiguous int32 tensor")
     return StoreDest(k_addr, v_addr, block_stride, token_stride, head_stride, block_size, num_blocks,
-                     slots.data_ptr(), slots.element_size(), first, count, dst_first)
+                     slots.data_ptr() if slots is not None else None, slots.element_size() if slots is not None else 4,
+                     first, count, dst_first, block_map.data_ptr() if block_map is not None else None,
+                     block_map.numel() if block_map is not None else 0, 0)
 
 
-def _launch(key, value, num_heads, head_bytes, dests, keep, stream, flags):
+def _target_slots(target, num_tokens, device):
+    if target.block_map is not None:
+        if target.block_map.device != device:
+            raise ValueError("a block map must be on the storing device")
+        return None
+    return _slots(target.slot_mapping, num_tokens, device)
+
+
+def _launch(key, value, num_heads, head_bytes, dests, stream, flags):
     array = (StoreDest * len(dests))(*dests)
     s = stream if stream is not None else torch.cuda.current_stream(key.device).cuda_stream
     check(lib().kvx_store(key.data_ptr(), value.data_ptr() if value is not None else None,
                           key.stride(0) * key.element_size(),
                           value.stride(0) * value.element_size() if value is not None else 0,
                           key.size(0), num_heads, head_bytes, array, len(dests), flags, s))
-    del keep
 
 
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -93,22 +107,20 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
         raise ValueError("each token's heads must be contiguous rows of head_dim")
     if k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1:
         raise ValueError("key and value caches must share strides with contiguous head_dim")
-    if len(push_to) > 3:
-        raise ValueError("at most 3 peers per store")
+    if len(push_to) > 8:
+        raise ValueError("at most 8 peers per store")
     itemsize = key.element_size()
     slots = _slots(slot_mapping, num_tokens, key.device)
-    keep = [slots]
     dests = [_dest(k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0) * itemsize,
                    k_cache.stride(1) * itemsize, k_cache.stride(2) * itemsize, k_cache.size(1), k_cache.size(0),
                    slots, 0, num_heads, 0)]
     for target in push_to:
-        t_slots = _slots(target.slot_mapping, num_tokens, key.device)
-        keep.append(t_slots)
+        t_slots = _target_slots(target, num_tokens, key.device)
         count = num_heads - target.src_first_head if target.num_heads is None else target.num_heads
         dests.append(_dest(target.k_cache, target.v_cache, target.block_stride, target.token_stride,
                            target.head_stride, target.block_size, target.num_blocks, t_slots, target.src_first_head,
-                           count, target.dst_first_head))
-    _launch(key, value, num_heads, head_dim * itemsize, dests, keep, stream, flags)
+                           count, target.dst_first_head, target.block_map))
+    _launch(key, value, num_heads, head_dim * itemsize, dests, stream, flags)
 
 
 def store_latents(latent: torch.Tensor, latent_cache: torch.Tensor, slot_mapping: torch.Tensor, push_to=(),
@@ -118,19 +130,17 @@ def store_latents(latent: torch.Tensor, latent_cache: torch.Tensor, slot_mapping
     num_tokens, dim = latent.shape
     if latent.stride(-1) != 1 or latent_cache.stride(-2) != dim or latent_cache.stride(-1) != 1:
         raise ValueError("latent rows and cache tokens must be contiguous")
-    if len(push_to) > 3:
-        raise ValueError("at most 3 peers per store")
+    if len(push_to) > 8:
+        raise ValueError("at most 8 peers per store")
     itemsize = latent.element_size()
     slots = _slots(slot_mapping, num_tokens, latent.device)
-    keep = [slots]
     dests = [_dest(latent_cache.data_ptr(), 0, latent_cache.stride(0) * itemsize, latent_cache.stride(1) * itemsize,
                    0, latent_cache.size(1), latent_cache.size(0), slots, 0, 1, 0)]
     for target in push_to:
-        t_slots = _slots(target.slot_mapping, num_tokens, latent.device)
-        keep.append(t_slots)
+        t_slots = _target_slots(target, num_tokens, latent.device)
         dests.append(_dest(target.k_cache, 0, target.block_stride, target.token_stride, 0, target.block_size,
-                           target.num_blocks, t_slots, 0, 1, 0))
-    _launch(latent, None, 1, dim * itemsize, dests, keep, stream, flags)
+                           target.num_blocks, t_slots, 0, 1, 0, target.block_map))
+    _launch(latent, None, 1, dim * itemsize, dests, stream, flags)
 
 
 def launch_flags(sm_budget: int = 0) -> int:

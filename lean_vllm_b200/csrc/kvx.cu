@@ -308,13 +308,14 @@ __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Param
 // source row [token][head] is read once and written to every destination whose head range holds it. Thread t of
 // the flattened space (token, K|V, head, vector) moves one VEC-byte vector, so reads of a token's rows are
 // contiguous and each (token, head) row lands as one contiguous run of head_bytes in every cache.
-constexpr int kMaxStoreDests = 4;
+constexpr int kMaxStoreDests = 9;  // the local cache and up to 8 decode ranks
 
 struct StoreDest {
     uint64_t k, v;
     int64_t block_stride, token_stride, head_stride;
     const void *slots;
-    int32_t block_size, num_blocks, slot_bytes, src_first_head, num_heads, dst_first_head;
+    const int32_t *block_map;
+    int32_t block_size, num_blocks, slot_bytes, src_first_head, num_heads, dst_first_head, block_map_len, pad;
 };
 
 struct StoreParams {
@@ -342,13 +343,29 @@ __global__ void __launch_bounds__(256) kvx_store_kernel(const __grid_constant__ 
                                        : p.key + (uint64_t)token * p.key_stride;
         const typename V::T data = V::load(reinterpret_cast<const char *>(src_base) +
                                            (uint64_t)head * p.head_bytes + (uint64_t)vec * VEC);
-#pragma unroll
-        for (int d = 0; d < kMaxStoreDests; ++d) {
-            if (d >= p.n_dests) break;
+        const StoreDest &first = p.dests[0];
+        const int64_t first_slot = first.slot_bytes == 8 ? static_cast<const int64_t *>(first.slots)[token]
+                                                         : static_cast<const int32_t *>(first.slots)[token];
+        for (int d = 0; d < p.n_dests; ++d) {
             const StoreDest &dst = p.dests[d];
             if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
-            const int64_t slot = dst.slot_bytes == 8 ? static_cast<const int64_t *>(dst.slots)[token]
-                                                     : static_cast<const int32_t *>(dst.slots)[token];
+            int64_t slot;
+            if (d == 0) {
+                slot = first_slot;
+            } else if (dst.block_map) {  // this cache's block for destination 0's block
+                if (first_slot < 0) continue;
+                const int64_t b = first_slot / first.block_size;
+                if (b >= dst.block_map_len) {
+                    atomicCAS(&g_device_error, 0, 2);
+                    continue;
+                }
+                const int32_t mapped = dst.block_map[b];
+                if (mapped < 0) continue;  // a block no save covers
+                slot = (int64_t)mapped * dst.block_size + (first_slot - b * first.block_size);
+            } else {
+                slot = dst.slot_bytes == 8 ? static_cast<const int64_t *>(dst.slots)[token]
+                                           : static_cast<const int32_t *>(dst.slots)[token];
+            }
             if (slot < 0) continue;  // padding: no cache slot
             if (slot >= (int64_t)dst.num_blocks * dst.block_size) {
                 atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
@@ -848,7 +865,11 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
             return fail(KVX_ERR_INVALID, "destination %d: keys and values must match the rows given", d);
         if (s.block_size < 1 || s.num_blocks < 0 || (s.slot_bytes != 4 && s.slot_bytes != 8))
             return fail(KVX_ERR_INVALID, "destination %d: bad block size, block count or slot width", d);
-        if (num_tokens > 0 && !s.slot_mapping) return fail(KVX_ERR_INVALID, "destination %d: null slots", d);
+        if (s.block_map && (d == 0 || s.block_size != dests[0].block_size || s.block_map_len < 0))
+            return fail(KVX_ERR_INVALID, "destination %d: a block map needs a later destination of equal block size",
+                        d);
+        if (num_tokens > 0 && !s.slot_mapping && !s.block_map)
+            return fail(KVX_ERR_INVALID, "destination %d: null slots", d);
         if (s.src_first_head < 0 || s.num_heads < 0 || s.dst_first_head < 0 ||
             s.src_first_head + s.num_heads > num_heads)
             return fail(KVX_ERR_RANGE, "destination %d: heads [%d, +%d) of %d", d, s.src_first_head, s.num_heads,
@@ -856,8 +877,8 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
         if (s.block_stride < 0 || s.token_stride < 0 || s.head_stride < 0)
             return fail(KVX_ERR_INVALID, "destination %d: negative stride", d);
         p.dests[d] = StoreDest{s.k_cache, s.v_cache, s.block_stride, s.token_stride, s.head_stride, s.slot_mapping,
-                               s.block_size, s.num_blocks, s.slot_bytes, s.src_first_head, s.num_heads,
-                               s.dst_first_head};
+                               s.block_map, s.block_size, s.num_blocks, s.slot_bytes, s.src_first_head, s.num_heads,
+                               s.dst_first_head, s.block_map_len, 0};
         align_bits |= s.k_cache | s.v_cache | (uint64_t)s.block_stride | (uint64_t)s.token_stride |
                       (uint64_t)s.head_stride;
     }

@@ -91,7 +91,8 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
         if params and params.get("do_remote_decode") and params.get("kv_push_id"):
             # A prefill whose decode instance waits for a push: its blocks are allocated now, so save them.
             blocks = list(seq.block_table[: _cdiv(seq.num_prompt_tokens, self.block_size)])
-            self._reqs_to_save[seq.request_id] = ReqToSave(blocks, push_id=str(params["kv_push_id"]))
+            self._reqs_to_save[seq.request_id] = ReqToSave(blocks, push_id=str(params["kv_push_id"]),
+                                                           cached_blocks=num_computed_tokens // self.block_size)
             return 0, False
         if not params or not params.get("do_remote_prefill"):
             return 0, False
@@ -188,6 +189,9 @@ class _Save:
     finishing: bool = False  # what was left is queued (transfer thread): done once nothing is in flight
     started: float = field(default_factory=monotonic)
     ready_marker: object = None  # the engine stream's event at hand-over, which the catch-up pushes wait for
+    fused: bool | None = None  # decided at its first store_kv: its rows go to the decode ranks with every store
+    stored: set = field(default_factory=set)  # layers whose new rows store_kv pushed
+    mapped: bool = False  # its blocks are in its decode instance's block map
 
 
 @dataclass(slots=True)
@@ -241,6 +245,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._loads: dict[str, _Load] = {}  # transfer thread only
         self._waits: dict[str, _Wait] = {}  # transfer thread only
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
+        self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
+        self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
         self._thread: threading.Thread | None = None
 
     # -------------------------------------------------------------------------------------------- engine thread
@@ -276,8 +282,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
     def start_load_kv(self, metadata: KVConnectorMetadata):
         for request_id, req in getattr(metadata, "reqs_to_save", {}).items():
             with self._lock:
-                if request_id in self._saves:
+                old = self._saves.get(request_id)
+                if old is not None and list(old.req.local_block_ids) == list(req.local_block_ids):
                     continue
+                if old is not None:  # re-admitted after a preemption, in new blocks: start over
+                    self._forget_fused(old)
+                    self._saves.pop(request_id)
                 if req.remote_block_ids is None:  # its decode ranks announce themselves under req.push_id
                     self._saves[request_id] = _Save(req, [])
                     self._push_ids[str(req.push_id)] = request_id
@@ -319,7 +329,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         the side stream after the layer's store (an event on the engine's stream), held to a few SMs."""
         with self._lock:
             active = [s for s in self._saves.values()
-                      if s.ready and not s.failed and not s.handed_over and layer_index not in s.pushed]
+                      if s.ready and not s.failed and not s.handed_over and layer_index not in s.pushed
+                      and layer_index not in s.stored]
             if not active:
                 return
             for save in active:
@@ -393,16 +404,79 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 targets.append(((req.remote_host, req.remote_port + decode_rank), decode_rank, mine))
         return targets
 
-    def _push_jobs(self, saves: list[_Save]) -> tuple[list, list]:
+    def _push_jobs(self, saves: list[_Save], first_blocks: int | None = None) -> tuple[list, list]:
+        """Copy jobs for the saves' blocks (only their first `first_blocks` if given) to every target decode rank."""
         tables, jobs = [], []
         for save in saves:
+            local, remote = list(save.req.local_block_ids), list(save.req.remote_block_ids)
+            if first_blocks is not None:
+                local, remote = local[:first_blocks], remote[:first_blocks]
             for (key, _, mine), table in zip(save.targets, save.tables):
                 tables.append(table)
                 k = len(tables)
                 for i, share in mine:
-                    jobs.append(CopyJob(0, k, save.req.local_block_ids, save.req.remote_block_ids, share.remote_head,
-                                        share.local_head, share.num_heads, i == 0))
+                    jobs.append(CopyJob(0, k, local, remote, share.remote_head, share.local_head, share.num_heads,
+                                        i == 0))
         return tables, jobs
+
+    # Fused store-and-push: the attention layer's store writes the decode ranks' blocks too.
+
+    @staticmethod
+    def _instance(req) -> tuple:
+        return (req.remote_host, req.remote_port, req.remote_engine_id)
+
+    def _forget_fused(self, save: _Save):
+        """Lock held. Its blocks leave the block map before the engine can hand them to another request."""
+        if save.mapped:
+            self._map_updates.append((self._instance(save.req), list(save.req.local_block_ids), None))
+            save.mapped = False
+
+    def store_kv(self, layer_index: int, key, value, slot_mapping):
+        """Stores this step's keys/values [tokens, heads, dim] of layer `layer_index` into this rank's cache by
+        slot (the reference's store_kvcache, attention/triton_cache.py:58-81), and in the same pass into the decode
+        ranks' blocks of every request being saved whose decode instance was mapped at its first store. An engine
+        calls this in place of the backend's store; it then needs no save_kv_layer for those layers."""
+        targets = self._fused_targets(layer_index, latents=False)
+        self.transport.store(self.kv_caches[layer_index], key, value, slot_mapping, targets)
+
+    def store_latents(self, layer_index: int, latent, slot_mapping):
+        """store_kv for an MLA layer's latents [tokens, 576] (attention/triton_cache.py:84-91); every decode rank
+        takes a whole copy."""
+        targets = self._fused_targets(layer_index, latents=True)
+        self.transport.store(self.kv_caches[layer_index], latent, None, slot_mapping, targets)
+
+    def _fused_targets(self, layer_index: int, latents: bool) -> list:
+        with self._lock:
+            updates, self._map_updates = self._map_updates, []
+            groups: dict[tuple, _Save] = {}
+            for save in self._saves.values():
+                if save.failed or save.handed_over:
+                    continue
+                if save.fused is None:
+                    save.fused = save.ready  # mapped before its first store, or never fused
+                if not save.fused:
+                    continue
+                save.stored.add(layer_index)
+                if not save.mapped:
+                    updates.append((self._instance(save.req), list(save.req.local_block_ids),
+                                    list(save.req.remote_block_ids)))
+                    save.mapped = True
+                groups.setdefault(self._instance(save.req), save)
+        for instance, local_ids, remote_ids in updates:
+            block_map = self._block_maps.get(instance)
+            if block_map is None:
+                block_map = self._block_maps[instance] = self.transport.new_block_map()
+            self.transport.map_blocks(block_map, local_ids, remote_ids)
+        targets = []
+        start, _ = self.layer_regions[layer_index]
+        for instance, save in groups.items():
+            for (_, _, mine), table in zip(save.targets, save.tables):
+                for i, share in mine:
+                    if latents and i:
+                        continue  # latents come whole from the first producer rank only
+                    targets.append(self.transport.push_target(table, start, share, self._block_maps[instance],
+                                                              self.block_size))
+        return targets
 
     def _save_flags(self):
         return getattr(self.transport, "save_flags", None)
@@ -622,7 +696,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 local_ids = list(save.req.local_block_ids)[skip:]
                 save.req = ReqToSave(local_ids, remote_ids, str(expect.get("engine_id", "")),
                                      str(expect.get("host", "")), int(expect.get("port", 0)),
-                                     int(expect.get("tp_size", 1)), save.req.push_id)
+                                     int(expect.get("tp_size", 1)), save.req.push_id,
+                                     max(save.req.cached_blocks - skip, 0))
                 save.targets = self._targets(save.req)
                 if len(local_ids) != len(remote_ids):
                     save.failed = True  # still mapped below, so the decode ranks hear that nothing comes
@@ -657,15 +732,20 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 return
             if not save.failed and not save.ready:
                 return
-            missing = [] if save.failed else [i for i in range(len(self.layer_regions)) if i not in save.pushed]
+            layers = range(len(self.layer_regions))
+            missing = [] if save.failed else [i for i in layers if i not in save.pushed and i not in save.stored]
+            # Fused stores wrote only this prefill's new rows: prefix-cache hits need a copy of their own.
+            cached = 0 if save.failed or not save.stored else min(save.req.cached_blocks, len(save.req.local_block_ids))
             save.pushed.update(missing)
             ready = save.ready_marker
-        posts = [None] if len(missing) == len(self.layer_regions) else missing
-        for layer in posts if missing else []:
+        posts = [(None, None)] if len(missing) == len(self.layer_regions) else [(layer, None) for layer in missing]
+        if cached:
+            posts.append((None, cached))
+        for layer, first_blocks in posts if (missing or cached) else []:
             with self._lock:
                 save.inflight += 1
             try:
-                tables, jobs = self._push_jobs([save])
+                tables, jobs = self._push_jobs([save], first_blocks)
                 region = None if layer is None else self.layer_regions[layer]
                 xfer = self.transport.post(tables, jobs, ready, layer=region)
             except Exception as error:  # noqa: BLE001
@@ -705,11 +785,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                      if not s.finishing and s.inflight == 0 and s.started + timeout < now]
             for request_id, save in done:
                 del self._saves[request_id]
+                self._forget_fused(save)
                 self._finished.finished_sending.add(request_id)  # every byte landed, or none will
             for request_id, save in stale:
                 # Never handed over (an aborted prefill), or handed over to a decode instance that never announced
                 # itself: the held blocks are freed as the reference frees unread ones.
                 del self._saves[request_id]
+                self._forget_fused(save)
                 self._push_ids.pop(str(save.req.push_id), None)
                 save.failed = True
                 if save.handed_over:

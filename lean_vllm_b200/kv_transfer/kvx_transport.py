@@ -95,6 +95,42 @@ class KvxTransport:
         return transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags)
 
+    # The fused store-and-push (kvx_store), on the engine's stream.
+
+    def new_block_map(self) -> torch.Tensor:
+        """A device map from this cache's block ids to a decode instance's, all -1 (no block saved)."""
+        return torch.full((self.local.num_blocks,), -1, dtype=torch.int32, device=self.device)
+
+    def map_blocks(self, block_map: torch.Tensor, local_ids, remote_ids):
+        """Enter (or with remote_ids None, clear) blocks of a save, in order on the engine's stream."""
+        index = torch.as_tensor(list(local_ids), dtype=torch.long).to(self.device, non_blocking=True)
+        if remote_ids is None:
+            block_map.index_fill_(0, index, -1)
+        else:
+            block_map.index_copy_(0, index, torch.as_tensor(list(remote_ids), dtype=torch.int32).to(
+                self.device, non_blocking=True))
+
+    def push_target(self, table: CacheTable, first_region: int, share, block_map: torch.Tensor, block_size: int):
+        """One decode rank's cache for one layer (its regions from first_region) as a store destination."""
+        from lean_vllm_b200.attention.kvx_cache import PushTarget
+
+        k_region = table.regions[first_region]
+        v_region = table.regions[first_region + 1] if k_region[2] else None
+        return PushTarget.of_regions(k_region, v_region, block_size, table.num_blocks, None,
+                                     src_first_head=share.remote_head if k_region[2] else 0,
+                                     num_heads=share.num_heads if k_region[2] else 1,
+                                     dst_first_head=share.local_head if k_region[2] else 0, block_map=block_map)
+
+    def store(self, cache: torch.Tensor, key: torch.Tensor, value, slot_mapping: torch.Tensor, targets: list):
+        """The layer's store into `cache` (HND keys/values, or latents when value is None) and every target."""
+        from lean_vllm_b200.attention.kvx_cache import store_kvcache, store_latents
+
+        if value is None:
+            store_latents(key, cache[0], slot_mapping, push_to=targets)
+        else:
+            view = cache.transpose(2, 3)  # (2, blocks, tokens, heads, dim), as the attention backend sees it
+            store_kvcache(key, value, view[0], view[1], slot_mapping, push_to=targets)
+
     def done(self, xfer: transport.Transfer) -> bool:
         return xfer.done()
 

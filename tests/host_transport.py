@@ -31,6 +31,7 @@ class HostTransport:
         self.pending: dict[int, list] = {}
         self.opened = 0
         self.posts: list[tuple] = []  # (layer, number of jobs) of every post, for tests to inspect
+        self.stores: list[tuple] = []  # (number of peer targets, rows) of every store
         HostTransport.instances.append(self)
 
     def bind_thread(self):
@@ -97,6 +98,50 @@ class HostTransport:
         handle = next(self.ids)
         self.pending[handle] = [1]  # done on the second poll
         return handle
+
+    # The fused store-and-push, on host memory: kvx_store's byte map with slots and block maps.
+
+    def new_block_map(self):
+        import torch
+
+        return torch.full((self.num_blocks,), -1, dtype=torch.int32)
+
+    def map_blocks(self, block_map, local_ids, remote_ids):
+        for i, b in enumerate(local_ids):
+            block_map[b] = -1 if remote_ids is None else remote_ids[i]
+
+    def push_target(self, table, first_region, share, block_map, block_size):
+        k = table["regions"][first_region]
+        v = table["regions"][first_region + 1] if k[2] else None
+        heads = (share.remote_head, share.num_heads, share.local_head) if k[2] else (0, 1, 0)
+        return {"k": k, "v": v, "heads": heads, "block_map": block_map, "block_size": block_size, "table": table}
+
+    def store(self, cache, key, value, slot_mapping, targets):
+        self.stores.append((len(targets), key.shape[0]))
+        latents = value is None
+        block = cache.size(2) if latents else cache.size(3)
+        itemsize = key.element_size()
+        row = (key.size(-1) if latents else key.size(-1)) * itemsize  # one head's (or latent's) bytes
+        heads = 1 if latents else key.size(1)
+        parts = [(key, 0)] if latents else [(key, 0), (value, 1)]
+        for t, slot in enumerate(slot_mapping.tolist()):
+            if slot < 0:
+                continue
+            b, off = divmod(int(slot), block)
+            for rows, part in parts:
+                for h in range(heads):
+                    src = rows.data_ptr() + (t * heads + h) * row
+                    local = cache[part, b] if latents else cache[part, b, h]
+                    ctypes.memmove(local.data_ptr() + off * row, src, row)
+                    for target in targets:
+                        first, count, dst_first = target["heads"]
+                        mapped = int(target["block_map"][b])
+                        if mapped < 0 or not first <= h < first + count:
+                            continue
+                        addr, block_bytes, head_bytes = target["k"] if part == 0 else target["v"]
+                        dst = addr + mapped * block_bytes + (h - first + dst_first) * head_bytes + off * row
+                        self._check(target["table"], [mapped], [(dst, row)])
+                        ctypes.memmove(dst, src, row)
 
     def done(self, handle):
         if HostTransport.fail == "in flight":

@@ -98,3 +98,51 @@ def test_an_announced_push_through_both_halves_on_the_gpu(sides, golden, prefill
     key = "lat" if mla else "kv"
     got = full_of([c.kv_caches[0].cpu() for c in flow.consumers], mla)
     assert np.array_equal(bits(got), arrays[f"small_{key}_tp{prefill_tp}to{decode_tp}"])
+
+
+@pytest.mark.parametrize("prefill_tp, decode_tp, mla", [(1, 1, False), (2, 4, False), (4, 2, False),
+                                                        (1, 2, True)])
+def test_a_fused_store_lands_the_new_rows_in_the_decode_blocks_on_the_gpu(sides, prefill_tp, decode_tp, mla):
+    """store_kv writes each rank's new rows into its own cache and, through the block map, into every decode rank's
+    blocks in one kvx_store launch; hand-over then has nothing left to copy."""
+    from lean_vllm_b200.kv_transfer import ReqToRecv
+    from lean_vllm_b200.kv_transfer.base import ReqToSave
+    from tests.connector_cases import BLOCK, HEAD_DIM, LATENT_DIM, NUM_HEADS
+
+    prefill, decode = full_cache(0, mla), full_cache(1, mla)
+    producers = sides.make("kv_producer", prefill_tp, prefill)
+    consumers = sides.make("kv_consumer", decode_tp, decode, engine_id="decode", accept_push=True)
+    kv_d, kv_p = consumers[0].kv_transfer, producers[0].kv_transfer
+    local, remote = [7, 2, 9], [0, 5, 3]
+    for c in consumers:
+        c.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": ReqToRecv(
+            remote, local, "p-1", kv_p.engine_id, kv_p.kv_ip, kv_p.kv_port, prefill_tp, pushed=True)}))
+    for p in producers:
+        p.start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": ReqToSave(
+            local, remote, kv_d.engine_id, kv_d.kv_ip, kv_d.kv_port, decode_tp)}))
+        assert wait_ready(p)
+    g = torch.Generator().manual_seed(3)
+    shape = (3 * BLOCK, LATENT_DIM) if mla else (3 * BLOCK, NUM_HEADS, HEAD_DIM)
+    key = torch.randn(*shape, generator=g).to(torch.bfloat16).cuda()
+    value = torch.randn(*shape, generator=g).to(torch.bfloat16).cuda()
+    slots = torch.tensor([b * BLOCK + o for b in local for o in range(BLOCK)], device="cuda")
+    for rank, p in enumerate(producers):
+        if mla:
+            p.store_latents(0, key, slots)
+        else:
+            per = NUM_HEADS // prefill_tp
+            p.store_kv(0, key[:, rank * per : (rank + 1) * per].contiguous(),
+                       value[:, rank * per : (rank + 1) * per].contiguous(), slots)
+    for p in producers:
+        p.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": local}))
+    assert all(wait_for(p).finished_sending == {"p-1"} for p in producers)
+    assert all(wait_for(c).finished_recving == {"d-1"} for c in consumers)
+    have = full_of([p.kv_caches[0].cpu() for p in producers], mla)
+    got = full_of([c.kv_caches[0].cpu() for c in consumers], mla)
+    want = decode.clone()
+    want[:, remote] = have[:, local]
+    assert torch.equal(got, want)
+    if mla:
+        assert torch.equal(have[0].reshape(-1, LATENT_DIM)[slots.cpu()], key.cpu())
+    else:
+        assert torch.equal(have[0].transpose(1, 2).reshape(-1, NUM_HEADS, HEAD_DIM)[slots.cpu()], key.cpu())
