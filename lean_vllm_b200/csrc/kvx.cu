@@ -325,59 +325,91 @@ struct StoreParams {
     StoreDest dests[kMaxStoreDests];
 };
 
+struct StoreIndex {
+    int32_t token, head;
+    uint32_t part, vec;  // part 0 keys (or latents), 1 values
+};
+
+__device__ __forceinline__ StoreIndex store_index(uint64_t i, uint32_t vecs, uint32_t parts, int32_t num_heads) {
+    StoreIndex x;
+    x.vec = (uint32_t)(i % vecs);
+    uint64_t rest = i / vecs;
+    x.head = (int32_t)(rest % num_heads);
+    rest /= num_heads;
+    x.part = (uint32_t)(rest % parts);
+    x.token = (int32_t)(rest / parts);
+    return x;
+}
+
+// Writes one vector of row (token, part, head) into every destination whose head range holds it.
 template <int VEC>
-__global__ void __launch_bounds__(256) kvx_store_kernel(const __grid_constant__ StoreParams p) {
+__device__ __forceinline__ void store_vector(const StoreParams &p, const StoreIndex &x, typename Vec<VEC>::T data) {
+    const StoreDest &first = p.dests[0];
+    const int64_t first_slot = first.slot_bytes == 8 ? static_cast<const int64_t *>(first.slots)[x.token]
+                                                     : static_cast<const int32_t *>(first.slots)[x.token];
+    for (int d = 0; d < p.n_dests; ++d) {
+        const StoreDest &dst = p.dests[d];
+        if (x.head < dst.src_first_head || x.head >= dst.src_first_head + dst.num_heads) continue;
+        int64_t slot;
+        if (d == 0) {
+            slot = first_slot;
+        } else if (dst.block_map) {  // this cache's block for destination 0's block
+            if (first_slot < 0) continue;
+            const int64_t b = first_slot / first.block_size;
+            if (b >= dst.block_map_len) {
+                atomicCAS(&g_device_error, 0, 2);
+                continue;
+            }
+            const int32_t mapped = dst.block_map[b];
+            if (mapped < 0) continue;  // a block no save covers
+            slot = (int64_t)mapped * dst.block_size + (first_slot - b * first.block_size);
+        } else {
+            slot = dst.slot_bytes == 8 ? static_cast<const int64_t *>(dst.slots)[x.token]
+                                       : static_cast<const int32_t *>(dst.slots)[x.token];
+        }
+        if (slot < 0) continue;  // padding: no cache slot
+        if (slot >= (int64_t)dst.num_blocks * dst.block_size) {
+            atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
+            continue;
+        }
+        const int64_t block = slot / dst.block_size, offset = slot - block * dst.block_size;
+        const uint64_t base = x.part ? dst.v : dst.k;
+        char *out = reinterpret_cast<char *>(base + block * dst.block_stride + offset * dst.token_stride +
+                                             (int64_t)(x.head - dst.src_first_head + dst.dst_first_head) *
+                                                 dst.head_stride) +
+                    (uint64_t)x.vec * VEC;
+        Vec<VEC>::store(out, data);
+    }
+}
+
+constexpr int kStoreThreads = 256;
+constexpr int kStoreUnroll = 4;  // vectors each thread loads before it stores any: bytes in flight per SM
+
+template <int VEC>
+__global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
     const uint32_t vecs = (uint32_t)p.head_bytes / VEC;  // per (token, head) row
     const uint32_t parts = p.value ? 2u : 1u;
     const uint64_t total = (uint64_t)p.num_tokens * parts * p.num_heads * vecs;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint32_t vec = (uint32_t)(i % vecs);
-        uint64_t rest = i / vecs;
-        const int32_t head = (int32_t)(rest % p.num_heads);
-        rest /= p.num_heads;
-        const uint32_t part = (uint32_t)(rest % parts);  // 0 keys (or latents), 1 values
-        const int32_t token = (int32_t)(rest / parts);
-        const uint64_t src_base = part ? p.value + (uint64_t)token * p.value_stride
-                                       : p.key + (uint64_t)token * p.key_stride;
-        const typename V::T data = V::load(reinterpret_cast<const char *>(src_base) +
-                                           (uint64_t)head * p.head_bytes + (uint64_t)vec * VEC);
-        const StoreDest &first = p.dests[0];
-        const int64_t first_slot = first.slot_bytes == 8 ? static_cast<const int64_t *>(first.slots)[token]
-                                                         : static_cast<const int32_t *>(first.slots)[token];
-        for (int d = 0; d < p.n_dests; ++d) {
-            const StoreDest &dst = p.dests[d];
-            if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
-            int64_t slot;
-            if (d == 0) {
-                slot = first_slot;
-            } else if (dst.block_map) {  // this cache's block for destination 0's block
-                if (first_slot < 0) continue;
-                const int64_t b = first_slot / first.block_size;
-                if (b >= dst.block_map_len) {
-                    atomicCAS(&g_device_error, 0, 2);
-                    continue;
-                }
-                const int32_t mapped = dst.block_map[b];
-                if (mapped < 0) continue;  // a block no save covers
-                slot = (int64_t)mapped * dst.block_size + (first_slot - b * first.block_size);
-            } else {
-                slot = dst.slot_bytes == 8 ? static_cast<const int64_t *>(dst.slots)[token]
-                                           : static_cast<const int32_t *>(dst.slots)[token];
-            }
-            if (slot < 0) continue;  // padding: no cache slot
-            if (slot >= (int64_t)dst.num_blocks * dst.block_size) {
-                atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
-                continue;
-            }
-            const int64_t block = slot / dst.block_size, offset = slot - block * dst.block_size;
-            const uint64_t base = part ? dst.v : dst.k;
-            char *out = reinterpret_cast<char *>(base + block * dst.block_stride + offset * dst.token_stride +
-                                                 (int64_t)(head - dst.src_first_head + dst.dst_first_head) *
-                                                     dst.head_stride) +
-                        (uint64_t)vec * VEC;
-            V::store(out, data);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; base < total;
+         base += stride * kStoreUnroll) {
+        typename V::T data[kStoreUnroll];
+#pragma unroll
+        for (int u = 0; u < kStoreUnroll; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i >= total) break;
+            const StoreIndex x = store_index(i, vecs, parts, p.num_heads);
+            const uint64_t row = x.part ? p.value + (uint64_t)x.token * p.value_stride
+                                        : p.key + (uint64_t)x.token * p.key_stride;
+            data[u] = V::load(reinterpret_cast<const char *>(row) + (uint64_t)x.head * p.head_bytes +
+                              (uint64_t)x.vec * VEC);
+        }
+#pragma unroll
+        for (int u = 0; u < kStoreUnroll; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i >= total) break;
+            store_vector<VEC>(p, store_index(i, vecs, parts, p.num_heads), data[u]);
         }
     }
 }
@@ -889,14 +921,15 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     const uint64_t total = (uint64_t)num_tokens * (value ? 2 : 1) * num_heads * (head_bytes / vec);
     const int sm_budget = (flags >> 24) & 0xff;
     const int sms = sm_budget > 0 && sm_budget < info->sms ? sm_budget : info->sms;
-    const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 8);
+    const uint64_t per_cta = (uint64_t)kStoreThreads * kStoreUnroll;
+    const unsigned grid = (unsigned)std::min<uint64_t>((total + per_cta - 1) / per_cta, (uint64_t)sms * 8);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (vec) {
-        case 16: kvx_store_kernel<16><<<grid, 256, 0, s>>>(p); break;
-        case 8: kvx_store_kernel<8><<<grid, 256, 0, s>>>(p); break;
-        case 4: kvx_store_kernel<4><<<grid, 256, 0, s>>>(p); break;
-        case 2: kvx_store_kernel<2><<<grid, 256, 0, s>>>(p); break;
-        default: kvx_store_kernel<1><<<grid, 256, 0, s>>>(p); break;
+        case 16: kvx_store_kernel<16><<<grid, kStoreThreads, 0, s>>>(p); break;
+        case 8: kvx_store_kernel<8><<<grid, kStoreThreads, 0, s>>>(p); break;
+        case 4: kvx_store_kernel<4><<<grid, kStoreThreads, 0, s>>>(p); break;
+        case 2: kvx_store_kernel<2><<<grid, kStoreThreads, 0, s>>>(p); break;
+        default: kvx_store_kernel<1><<<grid, kStoreThreads, 0, s>>>(p); break;
     }
     KVX_CUDA(cudaGetLastError());
     g_launches.fetch_add(1, std::memory_order_relaxed);

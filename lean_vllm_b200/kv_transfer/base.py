@@ -117,7 +117,7 @@ class ReqToSave:
     remote_port: int = 0
     remote_tp_size: int = 1
     push_id: str | None = None
-    cached_blocks: int = 0  # leading local blocks that were prefix-cache hits here: no store of this prefill writes them
+    cached_blocks: int = 0  # leading local blocks that were prefix-cache hits: no store of this prefill writes them
 
 
 @dataclass(slots=True)

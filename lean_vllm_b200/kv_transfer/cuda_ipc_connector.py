@@ -4,8 +4,9 @@ A drop-in for lean-vLLM's NixlConnector (lean_vllm/kv_transfer/nixl_connector.py
 half, the kv_transfer_params it returns, the handshake on kv_port + rank, the head shares between any two
 tensor-parallel sizes, reader counting and the release/expiry rules are the reference's. What changes is below the
 worker: instead of registering memory with a NIXL agent and posting one-sided READs, each rank exports its cache
-through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts ONE kvx kernel launch per load
-that gathers the shares' blocks from every producer rank's HBM over NVLink and scatters them into its own blocks.
+through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts ONE kvx kernel launch for all
+loads a step starts, which gathers the shares' blocks from every producer rank's HBM over NVLink and scatters them
+into its own blocks.
 The launch waits on the stream for the load's ready event (no host synchronisation), completion is a CUDA event
 polled without blocking, and a consumer rank tells each producer rank it read from once its bytes have landed
 (the NIXL notification's role) over the same ZMQ channel as the handshake.
@@ -162,11 +163,21 @@ class _Remote:
 
 
 @dataclass(slots=True)
+class _Batch:
+    """One launch shared by the loads planned in one pass of the transfer thread."""
+
+    xfer: object
+    refs: int  # loads not yet finished with it; released at zero
+    done: bool = False
+    error: Exception | None = None
+
+
+@dataclass(slots=True)
 class _Load:
     """One request's pull: one kernel launch over every share."""
 
     req: ReqToRecv
-    transfer: object = None
+    transfer: _Batch | None = None
     notify: list = field(default_factory=list)  # (remote key, message, rank) to send once the bytes have landed
     unnotified: set = field(default_factory=set)  # producer ranks no notification has reached
     started: float = field(default_factory=monotonic)
@@ -496,13 +507,15 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     items.append(self._queue.get_nowait())
                 if None in items:
                     return
+                batch: list = []
                 for item in items:
                     if item[0] == "load":
-                        self._start(*item[1:])
+                        self._start(*item[1:], batch)
                     elif item[0] == "connect":
                         self._connect(item[1])
                     elif item[0] == "finish":
                         self._finish(*item[1:])
+                self._post_loads(batch)
                 if self._server is not None:
                     self._serve()
                 self._poll()
@@ -514,10 +527,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             self._close()
 
     def _close(self):
+        released = set()
         for load in self._loads.values():
-            if load.transfer is not None:
-                self.transport.wait(load.transfer)  # bytes still landing in blocks the engine would reuse
-                self.transport.release(load.transfer)
+            if load.transfer is not None and id(load.transfer) not in released:
+                released.add(id(load.transfer))
+                self.transport.wait(load.transfer.xfer)  # bytes still landing in blocks the engine would reuse
+                self.transport.release(load.transfer.xfer)
         for xfer, _ in self._pushes:
             self.transport.wait(xfer)
             self.transport.release(xfer)
@@ -589,7 +604,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
 
     # Pull: one launch per load, then poll it.
 
-    def _start(self, request_id: str, req: ReqToRecv, ready):
+    def _start(self, request_id: str, req: ReqToRecv, ready, batch: list):
+        """Plans one load (handshakes, shares, byte count); `_post_loads` launches the batch."""
         if getattr(req, "pushed", False):
             self._start_wait(request_id, req)
             return
@@ -621,19 +637,51 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 load.num_bytes += nbytes
             load.started = monotonic()
             if jobs:
-                load.transfer = self.transport.post(tables, jobs, ready)
+                batch.append((load, tables, jobs, ready))
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
             self._fail(load, error)
+
+    def _post_loads(self, batch: list):
+        """One launch for every load planned in this pass that waits on the same ready event: their jobs share one
+        kernel and one completion event, which each load polls."""
+        groups: dict[int, list] = {}
+        for entry in batch:
+            groups.setdefault(id(entry[3]), []).append(entry)
+        for entries in groups.values():
+            tables, jobs, index = [], [], {}
+            for _, load_tables, load_jobs, _ in entries:
+                for job in load_jobs:
+                    table = load_tables[job.src - 1]
+                    if id(table) not in index:
+                        tables.append(table)
+                        index[id(table)] = len(tables)
+                    jobs.append(CopyJob(index[id(table)], 0, job.src_block_ids, job.dst_block_ids, job.src_first_head,
+                                        job.dst_first_head, job.num_heads, job.latents))
+            try:
+                shared = _Batch(self.transport.post(tables, jobs, entries[0][3]), len(entries))
+            except Exception as error:  # noqa: BLE001 - refused when posted: these loads fail, producers hear now
+                for load, *_ in entries:
+                    self._fail(load, error)
+                continue
+            for load, *_ in entries:
+                load.transfer = shared
 
     def _poll(self):
         for request_id, load in list(self._loads.items()):
             if load.transfer is not None:
+                shared = load.transfer
                 try:
-                    if not self.transport.done(load.transfer):
+                    if not shared.done and not self.transport.done(shared.xfer):
                         continue
+                    shared.done = True
                 except Exception as error:  # noqa: BLE001
-                    self._fail(load, RuntimeError(f"a kvx copy failed in flight: {error}"), in_flight=True)
-                self.transport.release(load.transfer)
+                    shared.done = True
+                    shared.error = shared.error or error
+                if shared.error is not None:
+                    self._fail(load, RuntimeError(f"a kvx copy failed in flight: {shared.error}"), in_flight=True)
+                shared.refs -= 1
+                if shared.refs == 0:
+                    self.transport.release(shared.xfer)
                 load.transfer = None
                 if not load.failed:
                     for key, message, remote_rank in load.notify:
@@ -735,7 +783,9 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             layers = range(len(self.layer_regions))
             missing = [] if save.failed else [i for i in layers if i not in save.pushed and i not in save.stored]
             # Fused stores wrote only this prefill's new rows: prefix-cache hits need a copy of their own.
-            cached = 0 if save.failed or not save.stored else min(save.req.cached_blocks, len(save.req.local_block_ids))
+            cached = 0
+            if not save.failed and save.stored:
+                cached = min(save.req.cached_blocks, len(save.req.local_block_ids))
             save.pushed.update(missing)
             ready = save.ready_marker
         posts = [(None, None)] if len(missing) == len(self.layer_regions) else [(layer, None) for layer in missing]
