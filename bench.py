@@ -1026,6 +1026,132 @@ def run_store(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_poisson(args) -> None:
+    """BASELINE config 5's arrival sweep through the connector's public API: Qwen3-8B-shaped KV, prefill TP1 ->
+    decode TP1 (a pair over NVLink at N=2, the same GPU at N=1), requests arriving as a Poisson process at each rate
+    in --rates, prompt lengths log-normal with median 2048 and sigma 1.0 (a choice: BASELINE does not give sigma),
+    clipped to [128, 32768]. The decode side allocates each request's blocks from a free list and returns them when
+    its load finishes; the prefill side holds random source blocks. Per rate: p50/p99 of each load's latency (from
+    its start_load_kv to the get_finished that reports it, host clock) and the bytes moved over the wall time."""
+    import torch
+    import torch.distributed as dist
+
+    from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVTransferConfig, ReqToRecv
+    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorWorker
+
+    spec = WORKLOADS["pair"]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    role = role_of(rank, world, spec)
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    gloo = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=600))
+    pool = 1024  # blocks per side: 38.7 GB
+    rates = [float(r) for r in args.rates.split(",")]
+
+    @dataclass
+    class WorkerConfig:
+        kv_transfer: KVTransferConfig
+        tensor_parallel_size: int = 1
+        kvcache_block_size: int = spec.block
+        kv_cache_layout: str = "HND"
+
+    base_port = args.kv_port + 16 * role.group
+    producer = consumer = None
+    if role.side in ("prefill", "both"):
+        src = alloc_cache(spec, 1, pool, device, fill=True, seed=7)
+        producer = CudaIpcConnectorWorker(WorkerConfig(KVTransferConfig(
+            kv_role="kv_producer", kv_port=base_port, engine_id=f"ps-prefill-{role.group}")), 0)
+        producer.register_kv_caches(src)
+    if role.side in ("decode", "both"):
+        dst = alloc_cache(spec, 1, pool, device, fill=False, seed=0)
+        consumer = CudaIpcConnectorWorker(WorkerConfig(KVTransferConfig(
+            kv_role="kv_consumer", kv_port=base_port + 8, engine_id=f"ps-decode-{role.group}")), 0)
+        consumer.register_kv_caches(dst)
+    torch.cuda.synchronize()
+    results = []
+    try:
+        for rate in rates:
+            rng = np.random.default_rng(int(rate * 1000) + args.seed)
+            n = int(min(max(rate * args.poisson_seconds, 8), 400))
+            lengths = np.clip(np.exp(rng.normal(np.log(2048), 1.0, size=n)), 128, 32768).astype(np.int64)
+            arrivals = np.cumsum(rng.exponential(1.0 / rate, size=n))
+            blocks = [math.ceil(int(x) / spec.block) for x in lengths]
+            srcs = [rng.choice(pool, size=b, replace=False).astype(np.int32) for b in blocks]
+            ids = [f"r{rate}-{i}" for i in range(n)]
+            if producer is not None:
+                producer.start_load_kv(KVConnectorMetadata(reqs_to_send={ids[i]: srcs[i].tolist() for i in range(n)}))
+            if world > 1:
+                dist.barrier(group=gloo)
+            latency, moved = [], 0
+            if consumer is not None:
+                free = list(rng.permutation(pool))
+                pending, started, waiting = {}, {}, list(range(n))
+                t0 = time.perf_counter()
+                while waiting or pending:
+                    now = time.perf_counter() - t0
+                    due = [i for i in waiting if arrivals[i] <= now and len(free) >= blocks[i]]
+                    if due:
+                        reqs = {}
+                        for i in due:
+                            waiting.remove(i)
+                            local = [int(free.pop()) for _ in range(blocks[i])]
+                            pending[ids[i]] = (i, local)
+                            started[ids[i]] = time.perf_counter()
+                            reqs[ids[i]] = ReqToRecv(local, srcs[i].tolist(), ids[i], f"ps-prefill-{role.group}",
+                                                     "127.0.0.1", base_port, 1)
+                        consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv=reqs))
+                    out = consumer.get_finished()
+                    if out.failed_recving:
+                        raise RuntimeError(f"loads failed: {sorted(out.failed_recving)[:3]}")
+                    for rid in out.finished_recving:
+                        i, local = pending.pop(rid)
+                        latency.append((time.perf_counter() - started[rid]) * 1e3)
+                        moved += out.recv_stats[rid].num_bytes
+                        free.extend(local)
+                    time.sleep(50e-6)
+                wall = time.perf_counter() - t0
+                results.append({"rate_req_per_s": rate, "requests": n, "p50_ms": round(float(np.percentile(latency, 50)), 3),
+                                "p99_ms": round(float(np.percentile(latency, 99)), 3),
+                                "mean_ms": round(float(np.mean(latency)), 3),
+                                "offered_gb_per_s": round(moved / float(arrivals[-1]) / 1e9, 2),
+                                "moved_gb_per_s": round(moved / wall / 1e9, 2), "bytes": moved,
+                                "mean_prompt_tokens": int(lengths.mean())})
+            if world > 1:
+                dist.barrier(group=gloo)
+            if producer is not None:  # every held request released once read
+                left, deadline = set(ids), time.monotonic() + 60
+                while left and time.monotonic() < deadline:
+                    left -= producer.get_finished().finished_sending
+                    time.sleep(1e-3)
+    finally:
+        for worker in (producer, consumer):
+            if worker is not None:
+                worker.shutdown()
+    every = [None] * world
+    if world > 1:
+        dist.all_gather_object(every, results, group=gloo)
+    else:
+        every = [results]
+    if rank == 0:
+        rows = next(r for r in every if r)
+        line = {"metric": "KV transfer latency under Poisson arrivals (connector API)", "unit": "ms",
+                "higher_is_better": False, "n_gpus": world,
+                "config": {"workload": f"{spec.name}/{'loopback-1gpu' if world == 1 else 'pair'} poisson",
+                           "prompt_lengths": "log-normal, median 2048, sigma 1.0, clipped [128, 32768]",
+                           "decode_pool_blocks": pool},
+                "rates": rows}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -1087,9 +1213,14 @@ def main(argv=None):
     p.add_argument("--store", action="store_true", help="measure the per-token cache store (and fused push)")
     p.add_argument("--fused", action="store_true",
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
+    p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")
+    p.add_argument("--rates", default="1,4,16,64", help="arrival rates for --poisson, requests per second")
+    p.add_argument("--poisson-seconds", type=float, default=6.0, help="arrival window per rate")
     args = p.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.poisson:
+        run_poisson(args)
     elif args.store:
         run_store(args)
     elif args.layerwise:

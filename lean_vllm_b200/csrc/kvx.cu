@@ -325,91 +325,91 @@ struct StoreParams {
     StoreDest dests[kMaxStoreDests];
 };
 
-struct StoreIndex {
-    int32_t token, head;
-    uint32_t part, vec;  // part 0 keys (or latents), 1 values
-};
-
-__device__ __forceinline__ StoreIndex store_index(uint64_t i, uint32_t vecs, uint32_t parts, int32_t num_heads) {
-    StoreIndex x;
-    x.vec = (uint32_t)(i % vecs);
-    uint64_t rest = i / vecs;
-    x.head = (int32_t)(rest % num_heads);
-    rest /= num_heads;
-    x.part = (uint32_t)(rest % parts);
-    x.token = (int32_t)(rest / parts);
-    return x;
-}
-
-// Writes one vector of row (token, part, head) into every destination whose head range holds it.
+// Writes one vector of row (token, part, head) into every destination whose head range holds it. Slots are below
+// 2^31 (the host checks num_blocks * block_size), so the slot arithmetic runs in 32 bits.
 template <int VEC>
-__device__ __forceinline__ void store_vector(const StoreParams &p, const StoreIndex &x, typename Vec<VEC>::T data) {
+__device__ __forceinline__ void store_vector(const StoreParams &p, int32_t token, uint32_t part, int32_t head,
+                                             uint32_t byte_in_row, typename Vec<VEC>::T data) {
     const StoreDest &first = p.dests[0];
-    const int64_t first_slot = first.slot_bytes == 8 ? static_cast<const int64_t *>(first.slots)[x.token]
-                                                     : static_cast<const int32_t *>(first.slots)[x.token];
+    const int32_t first_slot = first.slot_bytes == 8 ? (int32_t) static_cast<const int64_t *>(first.slots)[token]
+                                                     : static_cast<const int32_t *>(first.slots)[token];
     for (int d = 0; d < p.n_dests; ++d) {
         const StoreDest &dst = p.dests[d];
-        if (x.head < dst.src_first_head || x.head >= dst.src_first_head + dst.num_heads) continue;
-        int64_t slot;
+        if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
+        int32_t slot;
         if (d == 0) {
             slot = first_slot;
         } else if (dst.block_map) {  // this cache's block for destination 0's block
             if (first_slot < 0) continue;
-            const int64_t b = first_slot / first.block_size;
-            if (b >= dst.block_map_len) {
+            const uint32_t b = (uint32_t)first_slot / (uint32_t)first.block_size;
+            if (b >= (uint32_t)dst.block_map_len) {
                 atomicCAS(&g_device_error, 0, 2);
                 continue;
             }
             const int32_t mapped = dst.block_map[b];
             if (mapped < 0) continue;  // a block no save covers
-            slot = (int64_t)mapped * dst.block_size + (first_slot - b * first.block_size);
+            slot = mapped * dst.block_size + (first_slot - (int32_t)b * first.block_size);
         } else {
-            slot = dst.slot_bytes == 8 ? static_cast<const int64_t *>(dst.slots)[x.token]
-                                       : static_cast<const int32_t *>(dst.slots)[x.token];
+            slot = dst.slot_bytes == 8 ? (int32_t) static_cast<const int64_t *>(dst.slots)[token]
+                                       : static_cast<const int32_t *>(dst.slots)[token];
         }
         if (slot < 0) continue;  // padding: no cache slot
-        if (slot >= (int64_t)dst.num_blocks * dst.block_size) {
+        if (slot >= dst.num_blocks * dst.block_size) {
             atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
             continue;
         }
-        const int64_t block = slot / dst.block_size, offset = slot - block * dst.block_size;
-        const uint64_t base = x.part ? dst.v : dst.k;
-        char *out = reinterpret_cast<char *>(base + block * dst.block_stride + offset * dst.token_stride +
-                                             (int64_t)(x.head - dst.src_first_head + dst.dst_first_head) *
+        const uint32_t block = (uint32_t)slot / (uint32_t)dst.block_size;
+        const uint32_t offset = (uint32_t)slot - block * (uint32_t)dst.block_size;
+        const uint64_t base = part ? dst.v : dst.k;
+        char *out = reinterpret_cast<char *>(base + (uint64_t)block * dst.block_stride +
+                                             (uint64_t)offset * dst.token_stride +
+                                             (int64_t)(head - dst.src_first_head + dst.dst_first_head) *
                                                  dst.head_stride) +
-                    (uint64_t)x.vec * VEC;
+                    byte_in_row;
         Vec<VEC>::store(out, data);
     }
 }
 
 constexpr int kStoreThreads = 256;
-constexpr int kStoreUnroll = 4;  // vectors each thread loads before it stores any: bytes in flight per SM
+constexpr int kStoreUnroll = 4;  // tokens each thread loads before it stores any: bytes in flight per SM
 
+// Each thread owns fixed positions within a token's rows -- (K|V, head, vector), decoded once -- and sweeps tokens:
+// a CTA covers `tpp` tokens per pass (one when a token's rows exceed the CTA), kStoreUnroll passes in flight.
 template <int VEC>
 __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
     const uint32_t vecs = (uint32_t)p.head_bytes / VEC;  // per (token, head) row
     const uint32_t parts = p.value ? 2u : 1u;
-    const uint64_t total = (uint64_t)p.num_tokens * parts * p.num_heads * vecs;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; base < total;
-         base += stride * kStoreUnroll) {
-        typename V::T data[kStoreUnroll];
+    const uint32_t per_token = parts * (uint32_t)p.num_heads * vecs;
+    const bool packed = per_token <= blockDim.x;
+    const uint32_t tpp = packed ? blockDim.x / per_token : 1;  // tokens per CTA pass
+    const uint32_t lane_token = packed ? threadIdx.x / per_token : 0;
+    if (lane_token >= tpp) return;  // threads past the last whole token of the pass
+    const uint32_t token_step = gridDim.x * tpp;
+    for (uint32_t w = packed ? threadIdx.x % per_token : threadIdx.x; w < per_token;
+         w += packed ? per_token : blockDim.x) {
+        const uint32_t vec = w % vecs;
+        const int32_t head = (int32_t)((w / vecs) % (uint32_t)p.num_heads);
+        const uint32_t part = w / (vecs * (uint32_t)p.num_heads);
+        const uint64_t row0 = part ? p.value : p.key;
+        const int64_t row_stride = part ? p.value_stride : p.key_stride;
+        const uint32_t byte_in_row = vec * VEC;
+        const uint64_t in_row = (uint64_t)head * p.head_bytes + byte_in_row;
+        for (uint32_t t0 = blockIdx.x * tpp + lane_token; t0 < (uint32_t)p.num_tokens;
+             t0 += token_step * kStoreUnroll) {
+            typename V::T data[kStoreUnroll];
 #pragma unroll
-        for (int u = 0; u < kStoreUnroll; ++u) {
-            const uint64_t i = base + u * stride;
-            if (i >= total) break;
-            const StoreIndex x = store_index(i, vecs, parts, p.num_heads);
-            const uint64_t row = x.part ? p.value + (uint64_t)x.token * p.value_stride
-                                        : p.key + (uint64_t)x.token * p.key_stride;
-            data[u] = V::load(reinterpret_cast<const char *>(row) + (uint64_t)x.head * p.head_bytes +
-                              (uint64_t)x.vec * VEC);
-        }
+            for (int u = 0; u < kStoreUnroll; ++u) {
+                const uint32_t t = t0 + u * token_step;
+                if (t >= (uint32_t)p.num_tokens) break;
+                data[u] = V::load(reinterpret_cast<const char *>(row0 + (uint64_t)t * row_stride + in_row));
+            }
 #pragma unroll
-        for (int u = 0; u < kStoreUnroll; ++u) {
-            const uint64_t i = base + u * stride;
-            if (i >= total) break;
-            store_vector<VEC>(p, store_index(i, vecs, parts, p.num_heads), data[u]);
+            for (int u = 0; u < kStoreUnroll; ++u) {
+                const uint32_t t = t0 + u * token_step;
+                if (t >= (uint32_t)p.num_tokens) break;
+                store_vector<VEC>(p, (int32_t)t, part, head, byte_in_row, data[u]);
+            }
         }
     }
 }
@@ -908,6 +908,8 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
                         num_heads);
         if (s.block_stride < 0 || s.token_stride < 0 || s.head_stride < 0)
             return fail(KVX_ERR_INVALID, "destination %d: negative stride", d);
+        if ((int64_t)s.num_blocks * s.block_size >= (int64_t)1 << 31)
+            return fail(KVX_ERR_INVALID, "destination %d: more than 2^31 slots", d);
         p.dests[d] = StoreDest{s.k_cache, s.v_cache, s.block_stride, s.token_stride, s.head_stride, s.slot_mapping,
                                s.block_map, s.block_size, s.num_blocks, s.slot_bytes, s.src_first_head, s.num_heads,
                                s.dst_first_head, s.block_map_len, 0};
@@ -918,11 +920,12 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     const int vec = (int)std::min<uint64_t>(low_bit(align_bits), 16);
     DeviceInfo *info;
     if (int rc = device_info(&info)) return rc;
-    const uint64_t total = (uint64_t)num_tokens * (value ? 2 : 1) * num_heads * (head_bytes / vec);
     const int sm_budget = (flags >> 24) & 0xff;
     const int sms = sm_budget > 0 && sm_budget < info->sms ? sm_budget : info->sms;
-    const uint64_t per_cta = (uint64_t)kStoreThreads * kStoreUnroll;
-    const unsigned grid = (unsigned)std::min<uint64_t>((total + per_cta - 1) / per_cta, (uint64_t)sms * 8);
+    const uint64_t per_token = (uint64_t)(value ? 2 : 1) * num_heads * (head_bytes / vec);
+    const uint64_t tpp = per_token <= kStoreThreads ? kStoreThreads / per_token : 1;
+    const uint64_t passes = ((uint64_t)num_tokens + tpp * kStoreUnroll - 1) / (tpp * kStoreUnroll);
+    const unsigned grid = (unsigned)std::min<uint64_t>(passes, (uint64_t)sms * 8);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (vec) {
         case 16: kvx_store_kernel<16><<<grid, kStoreThreads, 0, s>>>(p); break;

@@ -4,9 +4,9 @@ A drop-in for lean-vLLM's NixlConnector (lean_vllm/kv_transfer/nixl_connector.py
 half, the kv_transfer_params it returns, the handshake on kv_port + rank, the head shares between any two
 tensor-parallel sizes, reader counting and the release/expiry rules are the reference's. What changes is below the
 worker: instead of registering memory with a NIXL agent and posting one-sided READs, each rank exports its cache
-through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts ONE kvx kernel launch for all
-loads a step starts, which gathers the shares' blocks from every producer rank's HBM over NVLink and scatters them
-into its own blocks.
+through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts one kvx kernel launch per load
+(small loads started together share one), which gathers the shares' blocks from every producer rank's HBM over
+NVLink and scatters them into its own blocks.
 The launch waits on the stream for the load's ready event (no host synchronisation), completion is a CUDA event
 polled without blocking, and a consumer rank tells each producer rank it read from once its bytes have landed
 (the NIXL notification's role) over the same ZMQ channel as the handshake.
@@ -46,6 +46,7 @@ logger = logging.getLogger(__name__)
 HANDSHAKE_TIMEOUT = 5.0  # ZMQ never refuses a connect; an absent producer is one that does not answer
 IDLE_WAIT = 0.01  # how often the transfer thread answers handshakes and counts notifications when idle
 BUSY_WAIT = 0.0002  # and how often it polls copies in flight
+BATCH_BYTES = 64 << 20  # loads planned in one pass share a launch until they add up to this much
 
 
 def _cdiv(a: int, b: int) -> int:
@@ -251,6 +252,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._context = zmq.Context()
         self._context.setsockopt(zmq.LINGER, 0)
         self._server = None
+        self._deferred: list = []  # messages that came while a handshake wait answered handshakes only
         self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
         self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table) of _remotes; under the lock
         self._loads: dict[str, _Load] = {}  # transfer thread only
@@ -544,7 +546,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
 
     # Serving: handshakes, and the notifications that end reads (producer) or pushes (decode).
 
-    def _serve(self):
+    def _serve(self, answer_only: bool = False):
+        """Answers handshakes and takes notifications. While this thread waits for a peer's handshake reply it
+        calls this with answer_only: handshakes are answered (the peer may be waiting on this rank at the same time,
+        which would otherwise deadlock both until the timeout) and everything else is kept for later."""
+        if not answer_only and self._deferred:
+            deferred, self._deferred = self._deferred, []
+            for identity, message in deferred:
+                self._handle(identity, message)
         while True:
             try:
                 identity, raw = self._server.recv_multipart(zmq.NOBLOCK)
@@ -554,41 +563,59 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 continue
             try:
                 message = json.loads(raw)
-                op = message.get("op")
+                message.get("op")
             except (ValueError, AttributeError):
-                message, op = {}, None
-            if op == "notify":
-                self._count(message.get("message", ""))
+                message = {}
+            if answer_only and message.get("op") != "handshake":
+                self._deferred.append((identity, message))
                 continue
-            if op == "expect":
-                push_id = str(message.get("push_id"))
-                with self._lock:
-                    self._expects.setdefault(push_id, message)
-                    request_id = self._push_ids.get(push_id)
-                if request_id is not None:
-                    self._connect(request_id)
-                continue
-            if op == "saved":
-                with self._lock:
-                    self._saved.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
-                        message.get("ok"))
-                continue
-            if op == "handshake":
-                reply = {
-                    "ok": True,
-                    "engine_id": self.kv_transfer.engine_id,
-                    "tp_size": self.tp_size,
-                    "layout": self.layout,
-                    "num_blocks": int(self.kv_caches[0].size(1)),
-                    "exported": self.transport.exported,
-                    "node": self.node,
-                }
-            else:
-                reply = {"ok": False, "error": f"unknown op {op!r}"}
-            try:
-                self._server.send_multipart([identity, json.dumps(reply).encode()], zmq.NOBLOCK)
-            except zmq.Again:
-                logger.warning("a KV handshake went unanswered: its peer is not reading")
+            self._handle(identity, message)
+
+    def _handle(self, identity, message: dict):
+        op = message.get("op")
+        if op == "notify":
+            self._count(message.get("message", ""))
+            return
+        if op == "expect":
+            push_id = str(message.get("push_id"))
+            with self._lock:
+                self._expects.setdefault(push_id, message)
+                request_id = self._push_ids.get(push_id)
+            if request_id is not None:
+                self._connect(request_id)
+            return
+        if op == "saved":
+            with self._lock:
+                self._saved.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
+                    message.get("ok"))
+            return
+        if op == "handshake":
+            reply = {
+                "ok": True,
+                "engine_id": self.kv_transfer.engine_id,
+                "tp_size": self.tp_size,
+                "layout": self.layout,
+                "num_blocks": int(self.kv_caches[0].size(1)),
+                "exported": self.transport.exported,
+                "node": self.node,
+            }
+        else:
+            reply = {"ok": False, "error": f"unknown op {op!r}"}
+        try:
+            self._server.send_multipart([identity, json.dumps(reply).encode()], zmq.NOBLOCK)
+        except zmq.Again:
+            logger.warning("a KV handshake went unanswered: its peer is not reading")
+
+    def _reply(self, sock, key) -> bytes:
+        """A peer's handshake reply, answering handshakes addressed to this rank meanwhile."""
+        deadline = monotonic() + HANDSHAKE_TIMEOUT
+        while True:
+            if sock.poll(timeout=2):
+                return sock.recv()
+            if self._server is not None:
+                self._serve(answer_only=True)
+            if monotonic() > deadline:
+                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake")
 
     def _count(self, message: str):
         try:
@@ -638,6 +665,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             load.started = monotonic()
             if jobs:
                 batch.append((load, tables, jobs, ready))
+                # Launch as soon as the batch is big enough to keep the GPU busy while the next loads are planned;
+                # only small loads share a launch.
+                if sum(entry[0].num_bytes for entry in batch) >= BATCH_BYTES:
+                    self._post_loads(batch)
+                    batch.clear()
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
             self._fail(load, error)
 
@@ -931,11 +963,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
             sock.connect(f"tcp://{key[0]}:{key[1]}")
             sock.send(json.dumps({"op": "handshake"}).encode())
-            try:
-                raw = sock.recv()
-            except zmq.Again:
-                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake") from None
-            reply = json.loads(raw)
+            reply = json.loads(self._reply(sock, key))
             if not reply["ok"]:
                 raise RuntimeError(reply["error"])
             if req.remote_engine_id and reply["engine_id"] != req.remote_engine_id:
@@ -967,10 +995,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
             sock.connect(f"tcp://{key[0]}:{key[1]}")
             sock.send(json.dumps({"op": "handshake"}).encode())
-            try:
-                reply = json.loads(sock.recv())
-            except zmq.Again:
-                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake") from None
+            reply = json.loads(self._reply(sock, key))
         finally:
             sock.close()
         if not reply.get("ok"):

@@ -104,3 +104,15 @@ def test_a_pull_request_still_checks_its_block_count(sides):
                                               "remote_engine_id": "e", "remote_host": "h", "remote_port": 1,
                                               "remote_block_ids": [4, 5]})
     assert flow.decode_half.get_num_new_matched_tokens(seq, 0) == (0, False)
+
+
+def test_crossing_handshakes_do_not_deadlock(sides, monkeypatch):
+    """A decode rank handshakes a prefill rank (to announce) while that prefill rank handshakes it (to map it):
+    each must answer the other while it waits, or both stall until the timeout and the load fails."""
+    monkeypatch.setattr(cuda_ipc_connector, "HANDSHAKE_TIMEOUT", 0.5)
+    for attempt in range(4):
+        flow = make_flow(sides, 2, 4)
+        flow.prefill_runs(push_id=f"push-{attempt}")
+        flow.decode_admits(push_id=f"push-{attempt}")  # announcements race the prefill ranks' mapping
+        sent, recved = flow.results()
+        assert sent.finished_sending == {"p-1"} and recved.finished_recving == {"d-1"}, attempt
