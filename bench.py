@@ -1076,7 +1076,24 @@ def run_poisson(args) -> None:
         consumer.register_kv_caches(dst)
     torch.cuda.synchronize()
     results = []
+
+    def warm_up():
+        """One load before timing: the first handshake maps every layer of the producer's cache once."""
+        if producer is not None:
+            producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"warm": [0, 1]}))
+        if world > 1:
+            dist.barrier(group=gloo)
+        if consumer is not None:
+            consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={"warm": ReqToRecv(
+                [0, 1], [0, 1], "warm", f"ps-prefill-{role.group}", "127.0.0.1", base_port, 1)}))
+            deadline = time.monotonic() + 60
+            while not consumer.get_finished().finished_recving and time.monotonic() < deadline:
+                time.sleep(1e-3)
+        if world > 1:
+            dist.barrier(group=gloo)
+
     try:
+        warm_up()
         for rate in rates:
             rng = np.random.default_rng(int(rate * 1000) + args.seed)
             n = int(min(max(rate * args.poisson_seconds, 8), 400))

@@ -325,56 +325,53 @@ struct StoreParams {
     StoreDest dests[kMaxStoreDests];
 };
 
-// Writes one vector of row (token, part, head) into every destination whose head range holds it. Slots are below
-// 2^31 (the host checks num_blocks * block_size), so the slot arithmetic runs in 32 bits.
-template <int VEC>
-__device__ __forceinline__ void store_vector(const StoreParams &p, int32_t token, uint32_t part, int32_t head,
-                                             uint32_t byte_in_row, typename Vec<VEC>::T data) {
-    const StoreDest &first = p.dests[0];
-    const int32_t first_slot = first.slot_bytes == 8 ? (int32_t) static_cast<const int64_t *>(first.slots)[token]
-                                                     : static_cast<const int32_t *>(first.slots)[token];
-    for (int d = 0; d < p.n_dests; ++d) {
-        const StoreDest &dst = p.dests[d];
-        if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
-        int32_t slot;
-        if (d == 0) {
-            slot = first_slot;
-        } else if (dst.block_map) {  // this cache's block for destination 0's block
-            if (first_slot < 0) continue;
-            const uint32_t b = (uint32_t)first_slot / (uint32_t)first.block_size;
-            if (b >= (uint32_t)dst.block_map_len) {
-                atomicCAS(&g_device_error, 0, 2);
-                continue;
-            }
-            const int32_t mapped = dst.block_map[b];
-            if (mapped < 0) continue;  // a block no save covers
-            slot = mapped * dst.block_size + (first_slot - (int32_t)b * first.block_size);
-        } else {
-            slot = dst.slot_bytes == 8 ? (int32_t) static_cast<const int64_t *>(dst.slots)[token]
-                                       : static_cast<const int32_t *>(dst.slots)[token];
-        }
-        if (slot < 0) continue;  // padding: no cache slot
-        if (slot >= dst.num_blocks * dst.block_size) {
-            atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
-            continue;
-        }
-        const uint32_t block = (uint32_t)slot / (uint32_t)dst.block_size;
-        const uint32_t offset = (uint32_t)slot - block * (uint32_t)dst.block_size;
-        const uint64_t base = part ? dst.v : dst.k;
-        char *out = reinterpret_cast<char *>(base + (uint64_t)block * dst.block_stride +
-                                             (uint64_t)offset * dst.token_stride +
-                                             (int64_t)(head - dst.src_first_head + dst.dst_first_head) *
-                                                 dst.head_stride) +
-                    byte_in_row;
-        Vec<VEC>::store(out, data);
+__device__ __forceinline__ int32_t load_slot(const StoreDest &dst, uint32_t token) {
+    return dst.slot_bytes == 8 ? (int32_t) static_cast<const int64_t *>(dst.slots)[token]
+                               : static_cast<const int32_t *>(dst.slots)[token];
+}
+
+// Destination d's slot for a row whose destination-0 slot is first_slot (-1: no slot, skip). Slots are below 2^31
+// (the host checks num_blocks * block_size), so the arithmetic runs in 32 bits.
+__device__ __forceinline__ int32_t resolve_slot(const StoreParams &p, int d, uint32_t token, int32_t first_slot) {
+    const StoreDest &dst = p.dests[d];
+    if (d == 0) return first_slot;
+    if (!dst.block_map) return load_slot(dst, token);
+    if (first_slot < 0) return -1;
+    const uint32_t block_size0 = (uint32_t)p.dests[0].block_size;
+    const uint32_t b = (uint32_t)first_slot / block_size0;
+    if (b >= (uint32_t)dst.block_map_len) {
+        atomicCAS(&g_device_error, 0, 2);
+        return -1;
     }
+    const int32_t mapped = dst.block_map[b];  // a block no save covers maps to -1
+    return mapped < 0 ? -1 : mapped * dst.block_size + (first_slot - (int32_t)(b * block_size0));
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_row(const StoreParams &p, const StoreDest &dst, int32_t slot, uint32_t part,
+                                          int32_t head, uint32_t byte_in_row, typename Vec<VEC>::T data) {
+    if (slot < 0) return;  // padding: no cache slot
+    if (slot >= dst.num_blocks * dst.block_size) {
+        atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
+        return;
+    }
+    const uint32_t block = (uint32_t)slot / (uint32_t)dst.block_size;
+    const uint32_t offset = (uint32_t)slot - block * (uint32_t)dst.block_size;
+    const uint64_t base = part ? dst.v : dst.k;
+    char *out = reinterpret_cast<char *>(base + (uint64_t)block * dst.block_stride +
+                                         (uint64_t)offset * dst.token_stride +
+                                         (int64_t)(head - dst.src_first_head + dst.dst_first_head) * dst.head_stride) +
+                byte_in_row;
+    Vec<VEC>::store(out, data);
 }
 
 constexpr int kStoreThreads = 256;
 constexpr int kStoreUnroll = 4;  // tokens each thread loads before it stores any: bytes in flight per SM
 
 // Each thread owns fixed positions within a token's rows -- (K|V, head, vector), decoded once -- and sweeps tokens:
-// a CTA covers `tpp` tokens per pass (one when a token's rows exceed the CTA), kStoreUnroll passes in flight.
+// a CTA covers `tpp` tokens per pass (one when a token's rows exceed the CTA), kStoreUnroll passes in flight. The
+// rows and their destination-0 slots load together; each further destination resolves the slots of all tokens in
+// flight before it stores any, so every dependent load is one round trip per batch, not per token.
 template <int VEC>
 __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
@@ -386,6 +383,7 @@ __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_c
     const uint32_t lane_token = packed ? threadIdx.x / per_token : 0;
     if (lane_token >= tpp) return;  // threads past the last whole token of the pass
     const uint32_t token_step = gridDim.x * tpp;
+    const uint32_t n = (uint32_t)p.num_tokens;
     for (uint32_t w = packed ? threadIdx.x % per_token : threadIdx.x; w < per_token;
          w += packed ? per_token : blockDim.x) {
         const uint32_t vec = w % vecs;
@@ -395,20 +393,29 @@ __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_c
         const int64_t row_stride = part ? p.value_stride : p.key_stride;
         const uint32_t byte_in_row = vec * VEC;
         const uint64_t in_row = (uint64_t)head * p.head_bytes + byte_in_row;
-        for (uint32_t t0 = blockIdx.x * tpp + lane_token; t0 < (uint32_t)p.num_tokens;
-             t0 += token_step * kStoreUnroll) {
+        for (uint32_t t0 = blockIdx.x * tpp + lane_token; t0 < n; t0 += token_step * kStoreUnroll) {
             typename V::T data[kStoreUnroll];
+            int32_t first[kStoreUnroll];
 #pragma unroll
             for (int u = 0; u < kStoreUnroll; ++u) {
                 const uint32_t t = t0 + u * token_step;
-                if (t >= (uint32_t)p.num_tokens) break;
-                data[u] = V::load(reinterpret_cast<const char *>(row0 + (uint64_t)t * row_stride + in_row));
+                first[u] = -1;
+                if (t < n) {
+                    data[u] = V::load(reinterpret_cast<const char *>(row0 + (uint64_t)t * row_stride + in_row));
+                    first[u] = load_slot(p.dests[0], t);
+                }
             }
+            for (int d = 0; d < p.n_dests; ++d) {
+                const StoreDest &dst = p.dests[d];
+                if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
+                int32_t slot[kStoreUnroll];
 #pragma unroll
-            for (int u = 0; u < kStoreUnroll; ++u) {
-                const uint32_t t = t0 + u * token_step;
-                if (t >= (uint32_t)p.num_tokens) break;
-                store_vector<VEC>(p, (int32_t)t, part, head, byte_in_row, data[u]);
+                for (int u = 0; u < kStoreUnroll; ++u) {
+                    const uint32_t t = t0 + u * token_step;
+                    slot[u] = t < n ? resolve_slot(p, d, t, first[u]) : -1;
+                }
+#pragma unroll
+                for (int u = 0; u < kStoreUnroll; ++u) store_row<VEC>(p, dst, slot[u], part, head, byte_in_row, data[u]);
             }
         }
     }
