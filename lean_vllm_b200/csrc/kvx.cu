@@ -315,7 +315,8 @@ struct StoreDest {
     int64_t block_stride, token_stride, head_stride;
     const void *slots;
     const int32_t *block_map;
-    int32_t block_size, num_blocks, slot_bytes, src_first_head, num_heads, dst_first_head, block_map_len, pad;
+    int32_t block_size, num_blocks, slot_bytes, src_first_head, num_heads, dst_first_head, block_map_len;
+    int32_t block_shift;  // log2(block_size) when it is a power of two (the usual 16, 64, 256), else -1
 };
 
 struct StoreParams {
@@ -338,7 +339,8 @@ __device__ __forceinline__ int32_t resolve_slot(const StoreParams &p, int d, uin
     if (!dst.block_map) return load_slot(dst, token);
     if (first_slot < 0) return -1;
     const uint32_t block_size0 = (uint32_t)p.dests[0].block_size;
-    const uint32_t b = (uint32_t)first_slot / block_size0;
+    const int32_t shift0 = p.dests[0].block_shift;
+    const uint32_t b = shift0 >= 0 ? (uint32_t)first_slot >> shift0 : (uint32_t)first_slot / block_size0;
     if (b >= (uint32_t)dst.block_map_len) {
         atomicCAS(&g_device_error, 0, 2);
         return -1;
@@ -355,7 +357,8 @@ __device__ __forceinline__ void store_row(const StoreParams &p, const StoreDest 
         atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
         return;
     }
-    const uint32_t block = (uint32_t)slot / (uint32_t)dst.block_size;
+    const uint32_t block = dst.block_shift >= 0 ? (uint32_t)slot >> dst.block_shift
+                                                : (uint32_t)slot / (uint32_t)dst.block_size;
     const uint32_t offset = (uint32_t)slot - block * (uint32_t)dst.block_size;
     const uint64_t base = part ? dst.v : dst.k;
     char *out = reinterpret_cast<char *>(base + (uint64_t)block * dst.block_stride +
@@ -917,9 +920,12 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
             return fail(KVX_ERR_INVALID, "destination %d: negative stride", d);
         if ((int64_t)s.num_blocks * s.block_size >= (int64_t)1 << 31)
             return fail(KVX_ERR_INVALID, "destination %d: more than 2^31 slots", d);
+        int32_t shift = -1;
+        for (int k = 0; k < 31; ++k)
+            if (s.block_size == (1 << k)) shift = k;
         p.dests[d] = StoreDest{s.k_cache, s.v_cache, s.block_stride, s.token_stride, s.head_stride, s.slot_mapping,
                                s.block_map, s.block_size, s.num_blocks, s.slot_bytes, s.src_first_head, s.num_heads,
-                               s.dst_first_head, s.block_map_len, 0};
+                               s.dst_first_head, s.block_map_len, shift};
         align_bits |= s.k_cache | s.v_cache | (uint64_t)s.block_stride | (uint64_t)s.token_stride |
                       (uint64_t)s.head_stride;
     }
