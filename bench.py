@@ -969,10 +969,21 @@ def run_store(args) -> None:
         torch.cuda.synchronize()
         return start.elapsed_time(end) / steps
 
-    launches0 = transport.launch_count()
+    ms_eager = timed(ours, args.steps)  # one Python call and launch per layer, as an eager engine issues them
+    # The same 36 launches captured once and replayed: the kernels' own time, as a graph-captured engine runs them.
+    graph = torch.cuda.CUDAGraph()
+    capture = torch.cuda.Stream()
+    capture.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(capture):
+        ours()
+        torch.cuda.synchronize()
+        captured0 = transport.launch_count()
+        with torch.cuda.graph(graph, stream=capture):
+            ours()
+        per_replay = transport.launch_count() - captured0  # kvx_store launches each replay runs
+    torch.cuda.synchronize()
     with ClockSampler(0) as clocks:
-        ms = timed(ours, args.steps)
-    launches = transport.launch_count() - launches0
+        ms = timed(graph.replay, args.steps)
     ms_torch = timed(torch_indexing, max(args.steps // 4, 2))
     # Correctness: every layer's cache holds its rows at the slots (and the peer's at its slots).
     ok = True
@@ -1017,9 +1028,11 @@ def run_store(args) -> None:
                    "shape": "8 KV heads x 128, block 256, HND",
                    "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None},
         "roofline": roofline,
+        "ms_per_step_eager": round(ms_eager, 4),
+        "timing": "CUDA graph of the step's 36 store launches, replayed; ms_per_step_eager issues them one by one",
         "torch_indexing_ms_per_step": round(ms_torch, 4),
-        "speedup_vs_torch_indexing": round(ms_torch / ms, 2),
-        "gpu_launches": launches,
+        "speedup_vs_torch_indexing": round(ms_torch / ms_eager, 2),
+        "gpu_launches": per_replay * args.steps,
         "clocks": clocks.summary(),
         "correct": bool(ok),
     }
@@ -1169,6 +1182,97 @@ def run_poisson(args) -> None:
         dist.destroy_process_group()
 
 
+def run_staged(args) -> None:
+    """The three-kernel path the north star names, stage by stage: kvx_pack gathers each request's blocks into a
+    contiguous staging buffer (block_descs row order), kvx_push moves the buffer to a staging buffer on the decode
+    GPU (--peer-device; the same GPU otherwise), kvx_scatter writes it into the decode cache's blocks. Qwen3-8B
+    shape, the workload's first --requests requests (16 by default, so that both caches and both buffers fit). Each
+    stage is timed with CUDA events over --steps repetitions; pack and scatter are HBM-bound (read + write), the push
+    NVLink-bound (or HBM-bound on one GPU)."""
+    import torch
+
+    from lean_vllm_b200._native import ENGINE_AUTO, ENGINE_LSU, ENGINE_TMA, flags
+    from lean_vllm_b200.kv_transfer import transport
+    from lean_vllm_b200.kv_transfer.transport import CacheTable
+
+    spec = WORKLOADS["pair"]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peer = torch.device("cuda", args.peer_device) if args.peer_device is not None else device
+    if peer != device and not transport.enable_peer_access(0, peer.index):
+        raise SystemExit(f"cuda:0 cannot reach cuda:{peer.index} directly")
+    engine = {"auto": ENGINE_AUTO, "lsu": ENGINE_LSU, "tma": ENGINE_TMA}[args.engine]
+    copy_flags = flags(engine, args.tile_bytes, args.ctas_per_sm)
+    lengths, reqs, num_blocks = workload(args.seed, args.requests or 16, spec)
+    src = alloc_cache(spec, 1, num_blocks, device, fill=True, seed=3)
+    dst = alloc_cache(spec, 1, num_blocks, peer, fill=False, seed=0)
+    per_request = [request_bytes(len(s), spec) for s, _ in reqs]
+    total = sum(per_request)
+    offsets = np.concatenate([[0], np.cumsum(per_request)]).astype(np.int64)
+    staging = torch.empty(total, dtype=torch.uint8, device=device)
+    landing = torch.empty(total, dtype=torch.uint8, device=peer)
+    src_t, dst_t = CacheTable.from_tensors(src), CacheTable.from_tensors(dst)
+    heads = spec.kv_heads
+
+    def pack():
+        for (s, _), off, n in zip(reqs, offsets, per_request):
+            transport.pack(src_t, s, 0, heads, False, staging.data_ptr() + int(off), n, 0, copy_flags)
+
+    def push():
+        transport.push(landing.data_ptr(), staging.data_ptr(), total, 0, copy_flags)
+
+    def scatter():
+        for (_, d), off, n in zip(reqs, offsets, per_request):
+            transport.scatter(landing.data_ptr() + int(off), n, dst_t, d, 0, heads, False, 0, copy_flags)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(end) / args.steps
+
+    with ClockSampler(0) as clocks:
+        ms = {"pack": timed(pack), "push": timed(push), "scatter": timed(scatter)}
+    torch.cuda.synchronize(peer)
+    ok = all(digest(dst, d, 0, heads, False, peer) == digest(src, s, 0, heads, False, device)
+             for s, d in (reqs[0], reqs[-1]))
+    peaks = {}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    stages = {}
+    for name, t in ms.items():
+        moved = 2 * total if name != "push" or peer == device else total
+        bound, peak = ("nvlink", NVLINK_PEER_GBS) if name == "push" and peer != device else ("hbm", hbm)
+        achieved = moved / (t * 1e-3) / 1e9
+        stages[name] = {"ms": round(t, 4), "payload_gb_per_s": round(total / (t * 1e-3) / 1e9, 1),
+                        "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                     "frac": round(achieved / peak, 4), "algorithmic_bytes": moved}}
+    line = {
+        "metric": "staged KV transfer (pack -> push -> scatter) GB/s",
+        "value": round(total / (sum(ms.values()) * 1e-3) / 1e9, 1),
+        "unit": "GB/s payload through all three stages",
+        "higher_is_better": True,
+        "n_gpus": 1 if peer == device else 2,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "config": {"workload": f"{spec.name}/staged-{len(reqs)}-requests", "payload_bytes": total,
+                   "requests": len(reqs), "decode_device": f"cuda:{peer.index}", "engine": args.engine},
+        "stages": stages,
+        "clocks": clocks.summary(),
+        "correct": bool(ok),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -1231,6 +1335,7 @@ def main(argv=None):
     p.add_argument("--fused", action="store_true",
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")
+    p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
     p.add_argument("--rates", default="1,4,16,64", help="arrival rates for --poisson, requests per second")
     p.add_argument("--poisson-seconds", type=float, default=6.0, help="arrival window per rate")
     args = p.parse_args(argv)
@@ -1238,6 +1343,8 @@ def main(argv=None):
         run_reference(args)
     elif args.poisson:
         run_poisson(args)
+    elif args.staged:
+        run_staged(args)
     elif args.store:
         run_store(args)
     elif args.layerwise:
