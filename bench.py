@@ -1221,24 +1221,25 @@ def run_staged(args) -> None:
     def push():
         transport.push(landing.data_ptr(), staging.data_ptr(), total, 0, copy_flags)
 
-    def scatter():
+    def scatter():  # on the decode GPU, which owns both the landing buffer and the cache
         for (_, d), off, n in zip(reqs, offsets, per_request):
             transport.scatter(landing.data_ptr() + int(off), n, dst_t, d, 0, heads, False, 0, copy_flags)
 
-    def timed(fn):
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize(device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(args.steps):
-            fn()
-        end.record()
-        torch.cuda.synchronize(device)
-        return start.elapsed_time(end) / args.steps
+    def timed(fn, on):
+        with torch.cuda.device(on):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(on)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            for _ in range(args.steps):
+                fn()
+            end.record()
+            torch.cuda.synchronize(on)
+            return start.elapsed_time(end) / args.steps
 
     with ClockSampler(0) as clocks:
-        ms = {"pack": timed(pack), "push": timed(push), "scatter": timed(scatter)}
+        ms = {"pack": timed(pack, device), "push": timed(push, device), "scatter": timed(scatter, peer)}
     torch.cuda.synchronize(peer)
     ok = all(digest(dst, d, 0, heads, False, peer) == digest(src, s, 0, heads, False, device)
              for s, d in (reqs[0], reqs[-1]))

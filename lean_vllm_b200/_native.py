@@ -124,6 +124,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "kvx_check_xfer": ([_P], ctypes.c_int),
     "kvx_release_xfer": ([_P], ctypes.c_int),
+    "kvx_doorbell_open": ([ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "kvx_doorbell_ring_after": ([ctypes.c_int, _P], ctypes.c_int),
+    "kvx_doorbell_close": ([ctypes.c_int], ctypes.c_int),
     "kvx_job_bytes": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int,
                        ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "kvx_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),

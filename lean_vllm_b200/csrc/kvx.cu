@@ -20,6 +20,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cerrno>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -28,6 +29,7 @@
 #include <string>
 #include <vector>
 
+#include <sys/eventfd.h>
 #include <unistd.h>
 
 #include "kvx.h"
@@ -739,6 +741,52 @@ struct Xfer {
     int device;
 };
 
+// ------------------------------------------------------------------------------------------------ doorbells
+
+// A ring is an event recorded on the caller's stream, waited for on the doorbell's own stream, then a host callback
+// there: the caller's stream never stalls behind a callback, so back-to-back copies keep the link busy.
+struct Bell {
+    int fd;
+    cudaStream_t stream;  // made at the first ring, on the device current then
+};
+
+// Open doorbells by id. Ids are never reused, so a ring that outlives its doorbell finds no entry and writes
+// nothing; the lock orders that lookup against kvx_doorbell_close's close().
+std::mutex g_bells_mu;
+std::map<int, Bell> g_bells;
+int g_next_bell = 1;
+
+void CUDART_CB ring_bell(void *arg) {  // a CUDA host callback: no CUDA calls in here
+    const int id = (int)(intptr_t)arg;
+    std::lock_guard<std::mutex> lock(g_bells_mu);
+    auto it = g_bells.find(id);
+    if (it == g_bells.end()) return;
+    const uint64_t one = 1;
+    (void)!write(it->second.fd, &one, sizeof one);  // non-blocking; a full counter (2^64 - 2 rings) stays rung
+}
+
+// The doorbell's stream, made on first use (outside the lock: the callback above takes it).
+int bell_stream(int id, cudaStream_t *out) {
+    {
+        std::lock_guard<std::mutex> lock(g_bells_mu);
+        auto it = g_bells.find(id);
+        if (it == g_bells.end()) return fail(KVX_ERR_INVALID, "no open doorbell %d", id);
+        *out = it->second.stream;
+    }
+    if (*out) return KVX_OK;
+    cudaStream_t fresh;
+    KVX_CUDA(cudaStreamCreateWithFlags(&fresh, cudaStreamNonBlocking));
+    std::lock_guard<std::mutex> lock(g_bells_mu);
+    auto it = g_bells.find(id);
+    if (it == g_bells.end()) {
+        cudaStreamDestroy(fresh);
+        return fail(KVX_ERR_INVALID, "no open doorbell %d", id);
+    }
+    it->second.stream = fresh;
+    *out = fresh;
+    return KVX_OK;
+}
+
 }  // namespace
 
 // ================================================================================================ C ABI
@@ -989,6 +1037,45 @@ int kvx_release_xfer(kvx_xfer_t xfer) {
     const cudaError_t e = cudaEventDestroy(x->done);
     delete x;
     if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "cudaEventDestroy: %s", cudaGetErrorString(e));
+    return KVX_OK;
+}
+
+int kvx_doorbell_open(int *out_id, int *out_fd) {
+    if (!out_id || !out_fd) return fail(KVX_ERR_INVALID, "null pointer");
+    const int fd = eventfd(0, EFD_NONBLOCK | EFD_CLOEXEC);
+    if (fd < 0) return fail(KVX_ERR_INVALID, "eventfd: %s", strerror(errno));
+    std::lock_guard<std::mutex> lock(g_bells_mu);
+    const int id = g_next_bell++;
+    g_bells[id] = Bell{fd, nullptr};
+    *out_id = id;
+    *out_fd = fd;
+    return KVX_OK;
+}
+
+int kvx_doorbell_ring_after(int id, void *stream) {
+    cudaStream_t ring;
+    if (int rc = bell_stream(id, &ring)) return rc;
+    cudaEvent_t mark;
+    KVX_CUDA(cudaEventCreateWithFlags(&mark, cudaEventDisableTiming));
+    cudaError_t e = cudaEventRecord(mark, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ring, mark, 0);
+    if (e == cudaSuccess) e = cudaLaunchHostFunc(ring, ring_bell, (void *)(intptr_t)id);
+    cudaEventDestroy(mark);  // the wait keeps what it needs
+    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "doorbell ring: %s", cudaGetErrorString(e));
+    return KVX_OK;
+}
+
+int kvx_doorbell_close(int id) {
+    cudaStream_t ring;
+    {
+        std::lock_guard<std::mutex> lock(g_bells_mu);
+        auto it = g_bells.find(id);
+        if (it == g_bells.end()) return fail(KVX_ERR_INVALID, "no open doorbell %d", id);
+        close(it->second.fd);
+        ring = it->second.stream;
+        g_bells.erase(it);
+    }
+    if (ring) KVX_CUDA(cudaStreamDestroy(ring));  // rings still queued on it run and find no doorbell
     return KVX_OK;
 }
 

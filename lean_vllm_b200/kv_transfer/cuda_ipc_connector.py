@@ -7,9 +7,10 @@ worker: instead of registering memory with a NIXL agent and posting one-sided RE
 through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts one kvx kernel launch per load
 (small loads started together share one), which gathers the shares' blocks from every producer rank's HBM over
 NVLink and scatters them into its own blocks.
-The launch waits on the stream for the load's ready event (no host synchronisation), completion is a CUDA event
-polled without blocking, and a consumer rank tells each producer rank it read from once its bytes have landed
-(the NIXL notification's role) over the same ZMQ channel as the handshake.
+The launch waits on the stream for the load's ready event (no host synchronisation); a host callback after it rings
+an eventfd the transfer thread sleeps on beside its ZMQ socket and work queue, so it wakes when a copy lands or a
+message or a load arrives rather than polling on a timer; and a consumer rank tells each producer rank it read from
+once its bytes have landed (the NIXL notification's role) over the same ZMQ channel as the handshake.
 
 It adds a layer-by-layer push the reference does not have (its docs list vLLM's save_kv_layer as unsupported,
 docs/disaggregated-prefill.md:29-30): given ReqToSave entries naming a decode instance's allocated blocks, a
@@ -44,8 +45,9 @@ from lean_vllm_b200.kv_transfer.transport import CopyJob
 logger = logging.getLogger(__name__)
 
 HANDSHAKE_TIMEOUT = 5.0  # ZMQ never refuses a connect; an absent producer is one that does not answer
-IDLE_WAIT = 0.01  # how often the transfer thread answers handshakes and counts notifications when idle
-BUSY_WAIT = 0.0002  # and how often it polls copies in flight
+IDLE_WAIT = 0.01  # the transfer thread's longest sleep: deadlines are checked at least this often
+BELL_WAIT = 0.001  # its sleep with copies in flight whose completion rings its doorbell (a safety net only)
+BUSY_WAIT = 0.0002  # and with copies in flight on a transport without a doorbell, which it must poll
 BATCH_BYTES = 64 << 20  # loads planned in one pass share a launch until they add up to this much
 
 
@@ -201,6 +203,7 @@ class _Save:
     finishing: bool = False  # what was left is queued (transfer thread): done once nothing is in flight
     started: float = field(default_factory=monotonic)
     ready_marker: object = None  # the engine stream's event at hand-over, which the catch-up pushes wait for
+    finish_seen: bool = False  # the transfer thread took the hand-over (and its ready_marker)
     fused: bool | None = None  # decided at its first store_kv: its rows go to the decode ranks with every store
     stored: set = field(default_factory=set)  # layers whose new rows store_kv pushed
     mapped: bool = False  # its blocks are in its decode instance's block map
@@ -249,6 +252,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._expects: dict[str, dict] = {}  # producer: push id -> a decode rank's announcement, may come first
         self._finished = KVConnectorOutput()
         self._queue: queue.Queue = queue.Queue()
+        self._wake = os.eventfd(0, os.EFD_NONBLOCK | os.EFD_CLOEXEC)  # written after every put: wakes the thread
         self._context = zmq.Context()
         self._context.setsockopt(zmq.LINGER, 0)
         self._server = None
@@ -304,7 +308,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 if req.remote_block_ids is None:  # its decode ranks announce themselves under req.push_id
                     self._saves[request_id] = _Save(req, [])
                     self._push_ids[str(req.push_id)] = request_id
-                    self._queue.put(("connect", request_id))
+                    self._put(("connect", request_id))
                     continue
                 save = self._saves[request_id] = _Save(req, self._targets(req))
                 # Decode ranks mapped by an earlier handshake: ready now, so this step's first layer is pushed by
@@ -314,7 +318,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     save.tables = [m[1] for m in mapped]
                     save.ready = True
                     continue
-            self._queue.put(("connect", request_id))
+            self._put(("connect", request_id))
         if metadata.reqs_to_send:
             deadline = monotonic() + envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
             finishing = []
@@ -330,12 +334,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if finishing:
                 ready = self.transport.ready_marker()
                 for request_id in finishing:
-                    self._queue.put(("finish", request_id, ready))
+                    self._put(("finish", request_id, ready))
         if metadata.reqs_to_recv:
             # Freshly allocated blocks may still be written by a step in flight; the copy waits for it on the GPU.
             ready = self.transport.ready_marker()
             for request_id, req in metadata.reqs_to_recv.items():
-                self._queue.put(("load", request_id, req, ready))
+                self._put(("load", request_id, req, ready))
 
     def save_kv_layer(self, layer_index: int):
         """Pushes layer `layer_index` of every request being saved whose decode ranks are mapped, in one launch on
@@ -387,8 +391,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         if self._context.closed:
             return
         if self._thread is not None:
-            self._queue.put(None)
+            self._put(None)
             self._thread.join(timeout=10)
+        wake, self._wake = self._wake, -1
+        os.close(wake)
         self._context.term()
 
     def _release(self, request_id: str):
@@ -496,17 +502,39 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
 
     # -------------------------------------------------------------------------------------------- transfer thread
 
+    def _put(self, item):
+        self._queue.put(item)
+        if self._wake >= 0:  # closed at shutdown
+            os.eventfd_write(self._wake, 1)
+
     def _run(self):
         try:
             self.transport.bind_thread()
+            bell = getattr(self.transport, "doorbell", None)
+            poller = zmq.Poller()
+            poller.register(self._wake, zmq.POLLIN)
+            if bell is not None:
+                poller.register(bell.fd, zmq.POLLIN)
+            if self._server is not None:
+                poller.register(self._server, zmq.POLLIN)
             while True:
-                busy = self._loads or self._waits or self._pushes or self._saves
+                busy = self._loads or self._pushes
+                if self._queue.empty():
+                    # Sleep until a load is queued, a message comes, or (doorbell) a copy lands.
+                    wait = (BELL_WAIT if bell is not None else BUSY_WAIT) if busy else IDLE_WAIT
+                    poller.poll(wait * 1000)
                 try:
-                    items = [self._queue.get(timeout=BUSY_WAIT if busy else IDLE_WAIT)]
-                except queue.Empty:
-                    items = []
-                while not self._queue.empty():
-                    items.append(self._queue.get_nowait())
+                    os.eventfd_read(self._wake)  # before the queue is read: a put after this wakes the next poll
+                except BlockingIOError:
+                    pass
+                if bell is not None:
+                    bell.clear()  # before the copies are queried: a ring after this wakes the next poll
+                items = []
+                while True:
+                    try:
+                        items.append(self._queue.get_nowait())
+                    except queue.Empty:
+                        break
                 if None in items:
                     return
                 batch: list = []
@@ -543,6 +571,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             remote.sock.close()
         if self._server is not None:
             self._server.close()
+        if hasattr(self.transport, "shutdown"):
+            self.transport.shutdown()
 
     # Serving: handshakes, and the notifications that end reads (producer) or pushes (decode).
 
@@ -800,6 +830,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             save = self._saves.get(request_id)
             if save is not None:
                 save.ready_marker = ready
+                save.finish_seen = True
         self._advance(request_id)
 
     def _advance(self, request_id: str):
@@ -808,7 +839,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         once; one still waiting for its decode instance waits (and expires at the timeout)."""
         with self._lock:
             save = self._saves.get(request_id)
-            if save is None or not save.handed_over or save.finishing:
+            if save is None or not save.finish_seen or save.finishing:
                 return
             if not save.failed and not save.ready:
                 return
@@ -838,6 +869,18 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 break
             with self._lock:
                 self._pushes.append((xfer, [save]))
+        if save.stored and not (missing or cached) and not save.failed:
+            # Every layer was stored fused, on the engine's stream: the decode ranks hear once those stores landed.
+            try:
+                xfer = self.transport.fence(ready)
+            except Exception as error:  # noqa: BLE001
+                logger.warning("waiting for the stores of %s failed: %s", request_id, error)
+                with self._lock:
+                    save.failed = True
+            else:
+                with self._lock:
+                    save.inflight += 1
+                    self._pushes.append((xfer, [save]))
         with self._lock:
             save.finishing = True
 

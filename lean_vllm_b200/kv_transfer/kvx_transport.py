@@ -37,6 +37,8 @@ class KvxTransport:
             self.stream = torch.cuda.Stream(device=self.device)
             # Per-layer saves go first when SMs free up between the prefill's kernels.
             self.save_stream = torch.cuda.Stream(device=self.device, priority=-10)
+        # Rung after every post: the transfer thread sleeps on it instead of polling copies in flight.
+        self.doorbell = transport.Doorbell()
         # One IPC handle per layer tensor; each region as (tensor, byte offset in it, block bytes, head bytes).
         bases = [c.data_ptr() for c in kv_caches]
         spans = [(c.data_ptr(), c.data_ptr() + c.numel() * c.element_size()) for c in kv_caches]
@@ -92,8 +94,15 @@ class KvxTransport:
         with `flags` (its SM budget)."""
         event = ready.cuda_event if ready is not None else 0
         stream = self.save_stream if flags is not None else self.stream
-        return transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
+        xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags)
+        self.doorbell.ring_after(stream.cuda_stream)
+        return xfer
+
+    def fence(self, ready) -> transport.Transfer:
+        """A transfer of nothing that completes once `ready` has: what a save whose layers were all stored fused
+        (on the engine's stream) waits for before its decode instance hears that every byte landed."""
+        return self.post([], [], ready)
 
     # The fused store-and-push (kvx_store), on the engine's stream.
 
@@ -140,3 +149,7 @@ class KvxTransport:
 
     def release(self, xfer: transport.Transfer):
         xfer.release()
+
+    def shutdown(self):
+        """After every transfer was waited for: rings still queued then find the doorbell closed."""
+        self.doorbell.close()

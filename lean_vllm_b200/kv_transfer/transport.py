@@ -9,6 +9,7 @@ a CUDA kernel of libkvx.so; nothing here copies bytes on the host.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -148,6 +149,31 @@ def transfer(caches: list[CacheTable], jobs: list[CopyJob], stream: int, wait_ev
     check(lib().kvx_transfer(cache_array, len(caches), job_array, len(jobs), flags, wait_event or None,
                              stream or None, ctypes.byref(out)))
     return Transfer(out.value)
+
+
+class Doorbell:
+    """An eventfd rung from a stream once the work queued before each ring has ended (kvx_doorbell_*): a thread
+    polls `fd` beside its sockets and sleeps until a transfer lands."""
+
+    def __init__(self):
+        bell, fd = ctypes.c_int(), ctypes.c_int()
+        check(lib().kvx_doorbell_open(ctypes.byref(bell), ctypes.byref(fd)))
+        self.id, self.fd = bell.value, fd.value
+
+    def ring_after(self, stream: int):
+        check(lib().kvx_doorbell_ring_after(self.id, stream or None))
+
+    def clear(self):
+        """Takes the rings so far; the fd polls readable again at the next one."""
+        try:
+            os.eventfd_read(self.fd)
+        except BlockingIOError:
+            pass
+
+    def close(self):
+        if self.id:
+            check(lib().kvx_doorbell_close(self.id))
+            self.id = self.fd = 0
 
 
 def pack(src: CacheTable, block_ids, first_head: int, num_heads: int, latents: bool, staging: int,

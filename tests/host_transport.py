@@ -99,6 +99,12 @@ class HostTransport:
         self.pending[handle] = [1]  # done on the second poll
         return handle
 
+    def fence(self, ready):
+        """Host stores are synchronous: a handle that completes like a post's, copying nothing."""
+        handle = next(self.ids)
+        self.pending[handle] = [1]
+        return handle
+
     # The fused store-and-push, on host memory: kvx_store's byte map with slots and block maps.
 
     def new_block_map(self):

@@ -69,3 +69,25 @@ def test_ipc_handle_round_trips_as_bytes():
     back = _native.IpcHandle.from_bytes(h.to_bytes())
     assert (back.offset, back.device, back.pid, back.ptr) == (4096, 3, 77, 1 << 40)
     assert ctypes.sizeof(h) == 64 + 8 + 8 + 4 + 4 + 8
+
+
+def test_a_doorbell_opens_and_closes_without_a_device():
+    """Doorbells are host objects: opening gives a quiet non-blocking eventfd; a closed one refuses rings."""
+    if not os.path.exists(_native.LIB_PATH):
+        pytest.skip("libkvx.so is not built here")
+    import select
+
+    from lean_vllm_b200.kv_transfer.transport import Doorbell
+
+    a, b = Doorbell(), Doorbell()
+    assert a.id != b.id and a.fd != b.fd
+    assert select.select([a.fd], [], [], 0)[0] == []  # not rung
+    a.clear()  # nothing to take: no error, no block
+    bell = a.id
+    a.close()
+    assert a.id == 0
+    with pytest.raises(_native.KvxError, match="no open doorbell"):
+        _native.check(_native.lib().kvx_doorbell_ring_after(bell, None))
+    with pytest.raises(_native.KvxError, match="no open doorbell"):
+        _native.check(_native.lib().kvx_doorbell_close(bell))
+    b.close()

@@ -184,3 +184,32 @@ def test_a_re_admitted_prefill_starts_its_save_over(sides):
 def test_rank_cache_helper_slices_heads():
     full = full_cache(0, False)
     assert torch.equal(torch.cat([rank_cache(full, r, 3) for r in range(3)], dim=2), full)
+
+
+def test_a_fully_fused_save_is_reported_only_after_its_stores_land(sides):
+    """Every layer stored fused: nothing is copied at hand-over, but the decode ranks hear of the request only once
+    the engine stream's stores have landed (a fence on the hand-over's ready marker)."""
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    save_and_recv(producers, consumers)
+    key, value = rows(5, 3 * BLOCK, NUM_HEADS, False)
+    producers[0].store_kv(0, key, value, slots_of(LOCAL))
+    held = []
+    transport = producers[0].transport
+    real_fence = transport.fence
+
+    def slow_fence(ready):
+        handle = real_fence(ready)
+        transport.pending[handle] = [10**9]  # the stores are still running
+        held.append(handle)
+        return handle
+
+    transport.fence = slow_fence
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(LOCAL)}))
+    sleep(0.3)
+    assert len(held) == 1 and transport.posts == []
+    assert consumers[0].get_finished().finished_recving == set()
+    assert producers[0].get_finished().finished_sending == set()
+    transport.pending[held[0]] = [0]  # landed
+    assert wait_for(producers[0]).finished_sending == {"p-1"}
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}

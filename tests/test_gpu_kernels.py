@@ -231,6 +231,30 @@ def test_a_transfer_waits_for_its_ready_event_and_reports_completion():
         assert bool((d[:, [0, 1, 2, 5, 6, 7]] == 1.0).all())
 
 
+def test_a_doorbell_rings_once_the_stream_work_before_it_ends():
+    """kvx_doorbell_ring_after: the eventfd turns readable only after the copy queued before the ring landed."""
+    import select
+
+    src = _qwen_like(8, 2, seed=6)
+    dst = [torch.zeros_like(s) for s in src]
+    bell = transport.Doorbell()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(50_000_000)  # tens of ms at B200 clocks
+    xfer = transport.transfer([CacheTable.from_tensors(src), CacheTable.from_tensors(dst)],
+                              [CopyJob(0, 1, [1, 2], [3, 4], 0, 0, 8)], stream.cuda_stream)
+    bell.ring_after(stream.cuda_stream)
+    assert select.select([bell.fd], [], [], 0)[0] == []  # the sleep still runs
+    assert select.select([bell.fd], [], [], 10.0)[0] == [bell.fd]
+    assert xfer.done()  # the ring came after the copy's completion event
+    bell.clear()
+    assert select.select([bell.fd], [], [], 0)[0] == []
+    xfer.release()
+    bell.close()
+    for s, d in zip(src, dst):
+        assert torch.equal(d[:, [3, 4]], s[:, [1, 2]])
+
+
 def test_ipc_export_and_open_in_the_same_process_is_the_pointer_itself():
     t = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
     view = t[4096:]
