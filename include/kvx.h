@@ -182,19 +182,17 @@ int kvx_release_xfer(kvx_xfer_t xfer);
 
 /* ---- completion doorbells ---- */
 
-/* A doorbell: a non-blocking eventfd (`out_fd`, readable while rung) that kvx_doorbell_ring_after rings from a
- * host callback once a stream's work before the ring has ended. A transfer thread sleeps in poll() on it, on its
- * sockets and on its work queue together, and wakes when a copy lands, instead of querying every transfer on a
- * timer (the reference polls check_xfer_state every 1 ms, nixl_connector.py:43, :431). */
+/* A doorbell: a non-blocking eventfd (`out_fd`, readable while rung) and a native watcher thread that rings it when
+ * the stream work before a kvx_doorbell_ring_after has ended. A transfer thread sleeps in poll() on it, on its
+ * sockets and on its work queue together, and wakes within microseconds of a copy landing, instead of querying
+ * every transfer on a timer (the reference polls check_xfer_state every 1 ms, nixl_connector.py:43, :431). */
 int kvx_doorbell_open(int *out_id, int *out_fd);
 
-/* Rings doorbell `id` (adds 1 to its eventfd) once the work queued on `stream` so far has ended. `stream` itself
- * never waits for the ring: an event on it releases a host callback on the doorbell's own stream. Rings and the
- * close of one doorbell come from one thread. */
+/* Rings doorbell `id` (adds 1 to its eventfd) once the work queued on `stream` so far has ended: records an event
+ * there, which the watcher queries every few microseconds. `stream` never waits for anything. */
 int kvx_doorbell_ring_after(int id, void *stream);
 
-/* Closes the doorbell's eventfd. Rings still queued on streams then do nothing: the fd number is never written
- * after this returns, even if the process reuses it. */
+/* Stops the watcher (rings not yet due are dropped) and closes the eventfd. */
 int kvx_doorbell_close(int id);
 
 /* ---- diagnostics ---- */

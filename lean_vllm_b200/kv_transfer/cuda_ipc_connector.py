@@ -7,10 +7,11 @@ worker: instead of registering memory with a NIXL agent and posting one-sided RE
 through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts one kvx kernel launch per load
 (small loads started together share one), which gathers the shares' blocks from every producer rank's HBM over
 NVLink and scatters them into its own blocks.
-The launch waits on the stream for the load's ready event (no host synchronisation); a host callback after it rings
-an eventfd the transfer thread sleeps on beside its ZMQ socket and work queue, so it wakes when a copy lands or a
-message or a load arrives rather than polling on a timer; and a consumer rank tells each producer rank it read from
-once its bytes have landed (the NIXL notification's role) over the same ZMQ channel as the handshake.
+The launch waits on the stream for the load's ready event (no host synchronisation); a native watcher rings an
+eventfd once the copy's event completes, and the transfer thread sleeps on that, its ZMQ socket and its work queue
+together, so it wakes when a copy lands or a message or a load arrives rather than polling on a timer; and a
+consumer rank tells each producer rank it read from once its bytes have landed (the NIXL notification's role) over
+the same ZMQ channel as the handshake.
 
 It adds a layer-by-layer push the reference does not have (its docs list vLLM's save_kv_layer as unsupported,
 docs/disaggregated-prefill.md:29-30): given ReqToSave entries naming a decode instance's allocated blocks, a

@@ -1,6 +1,8 @@
 """The per-layer save (push) on CPU caches over the host transport: protocol, catch-up of layers no hook pushed,
 failures, and bit-exact results against the reference's golden pulls."""
 
+from time import monotonic, sleep
+
 import numpy as np
 import pytest
 import torch
@@ -123,6 +125,9 @@ def test_a_save_that_is_never_handed_over_expires(sides, monkeypatch):
     producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
     producers[0].save_kv_layer(0)  # the prefill is then aborted: no hand-over
     assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    deadline = monotonic() + 2.0  # the producer checks its deadlines at least every IDLE_WAIT
+    while producers[0]._saves and monotonic() < deadline:
+        sleep(0.005)
     assert not producers[0]._saves
 
 
