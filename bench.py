@@ -1274,6 +1274,60 @@ def run_staged(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_step_exchange(args) -> None:
+    """ModelRunner.kv_connector_step's per-step exchange of connector outputs between one instance's tensor-parallel
+    ranks (engine/model_runner.py:637-649), host only: every rank runs --steps steps with a stub connector, rank 0
+    times each step (start to its aggregated output). Two exchanges: the reference's gloo gather_object, and the
+    shared-memory step mailbox; two loads: quiet steps (nothing finished anywhere, the common case) and busy steps
+    (every rank reports 4 finished loads each step). Launch under torchrun with --gpus N for N ranks."""
+    import torch.distributed as dist
+
+    from lean_vllm_b200.kv_transfer.base import KVConnectorOutput, KVTransferStats
+    from lean_vllm_b200.kv_transfer.step import KVConnectorStep
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world < 2:
+        raise SystemExit("--step-exchange needs torchrun with 2 or more ranks")
+    dist.init_process_group("gloo")
+
+    class Stub:
+        def __init__(self, busy):
+            self.busy, self.n = busy, 0
+
+        def start_load_kv(self, metadata):
+            pass
+
+        def get_finished(self):
+            if not self.busy:
+                return KVConnectorOutput()
+            self.n += 1
+            ids = {f"req-{self.n}-{i}" for i in range(4)}
+            return KVConnectorOutput(finished_recving=ids, recv_stats={r: KVTransferStats(1e-3, 1 << 28) for r in ids})
+
+    results = {}
+    for exchange in ("gather", "mailbox"):
+        for load in ("quiet", "busy"):
+            step = KVConnectorStep(Stub(load == "busy"), rank, world, exchange=exchange)
+            times = []
+            for i in range(args.warmup + args.steps):
+                t0 = time.perf_counter()
+                step(None)
+                if i >= args.warmup:
+                    times.append((time.perf_counter() - t0) * 1e6)
+            step.close()
+            dist.barrier()
+            results[f"{exchange}/{load}"] = {"p50_us": round(float(np.median(times)), 1),
+                                             "p99_us": round(float(np.percentile(times, 99)), 1)}
+    if rank == 0:
+        print(json.dumps({"metric": "kv_connector_step exchange latency (rank 0, per step)", "unit": "us",
+                          "higher_is_better": False, "ranks": world, "steps": args.steps, "warmup": args.warmup,
+                          "config": {"workload": "stub connector; quiet = nothing finished, busy = 4 loads per rank "
+                                                 "per step", "host_cores": os.cpu_count()},
+                          "results": results}), flush=True)
+    dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -1337,11 +1391,15 @@ def main(argv=None):
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")
     p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
+    p.add_argument("--step-exchange", action="store_true",
+                   help="host only: kv_connector_step's per-step output exchange, gloo gather vs step mailbox")
     p.add_argument("--rates", default="1,4,16,64", help="arrival rates for --poisson, requests per second")
     p.add_argument("--poisson-seconds", type=float, default=6.0, help="arrival window per rate")
     args = p.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.step_exchange:
+        run_step_exchange(args)
     elif args.poisson:
         run_poisson(args)
     elif args.staged:

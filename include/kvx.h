@@ -38,6 +38,7 @@ extern "C" {
 #define KVX_ERR_CUDA (-2)      /* a CUDA call failed */
 #define KVX_ERR_RANGE (-3)     /* a block id or head range outside its cache (nixl_connector.py:398-399) */
 #define KVX_ERR_DEVICE (-4)    /* a kernel gave up a bounded wait; see kvx_device_error */
+#define KVX_ERR_TIMEOUT (-5)   /* a host wait ran out (a rank that never posted its step) */
 
 /* kvx_copy/kvx_transfer/kvx_pack/kvx_push/kvx_scatter flags word: bits 0-7 engine (below), bits 8-15 log2 of the
  * tile size (0: 32 KiB), bits 16-23 CTAs per SM (0: 1 for TMA, 2 for LSU), bits 24-31 how many SMs the grid may
@@ -194,6 +195,29 @@ int kvx_doorbell_ring_after(int id, void *stream);
 
 /* Stops the watcher (rings not yet due are dropped) and closes the eventfd. */
 int kvx_doorbell_close(int id);
+
+/* ---- the per-step exchange of connector outputs between one instance's ranks ---- */
+
+/* A step mailbox: host shared memory (a file every rank of one engine instance maps) through which each rank hands
+ * rank 0 its KVConnectorOutput every step, replacing the gloo gather_object of ModelRunner.kv_connector_step
+ * (engine/model_runner.py:637-649). Layout, all little-endian uint64 words: at 0 `consumed` (the last step rank 0
+ * has read); rank r's slot at 64 + r * kvx_mailbox_stride(slot_bytes): `seq` (the last step it posted), `len`, then
+ * `len` payload bytes (at most slot_bytes). A rank with nothing to report posts len 0. Waits spin, then sleep, and
+ * give up with KVX_ERR_TIMEOUT after timeout_s seconds. */
+uint64_t kvx_mailbox_stride(uint64_t slot_bytes);
+uint64_t kvx_mailbox_bytes(int world, uint64_t slot_bytes);
+
+/* Rank `rank` (1 <= rank < world) posts step `seq` (1, 2, ...): waits until rank 0 has read step seq - 1, copies
+ * `len` bytes of `data` into its slot, then publishes seq (release). */
+int kvx_mailbox_post(void *box, int world, int rank, uint64_t slot_bytes, uint64_t seq, const void *data,
+                     uint64_t len, double timeout_s);
+
+/* Rank 0 waits until every other rank has posted step `seq` (acquire) and writes each slot's length to lens[rank]
+ * (lens[0] = 0); the payloads are then readable in place until kvx_mailbox_release. */
+int kvx_mailbox_collect(void *box, int world, uint64_t slot_bytes, uint64_t seq, uint64_t *lens, double timeout_s);
+
+/* Rank 0 is done reading step `seq`: the other ranks may post seq + 1. */
+int kvx_mailbox_release(void *box, uint64_t seq);
 
 /* ---- diagnostics ---- */
 

@@ -18,6 +18,7 @@ KVX_ERR_INVALID = -1
 KVX_ERR_CUDA = -2
 KVX_ERR_RANGE = -3
 KVX_ERR_DEVICE = -4
+KVX_ERR_TIMEOUT = -5
 
 ENGINE_AUTO = 0
 ENGINE_LSU = 1
@@ -34,6 +35,10 @@ class KvxError(RuntimeError):
 
 class KvxRangeError(KvxError):
     """A block id or head range outside its cache (nixl_connector.py:398-399)."""
+
+
+class KvxTimeout(KvxError):
+    """A host wait ran out: a rank that never posted its step to the mailbox."""
 
 
 class KvxUnavailable(RuntimeError):
@@ -127,6 +132,13 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kvx_doorbell_open": ([ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "kvx_doorbell_ring_after": ([ctypes.c_int, _P], ctypes.c_int),
     "kvx_doorbell_close": ([ctypes.c_int], ctypes.c_int),
+    "kvx_mailbox_stride": ([ctypes.c_uint64], ctypes.c_uint64),
+    "kvx_mailbox_bytes": ([ctypes.c_int, ctypes.c_uint64], ctypes.c_uint64),
+    "kvx_mailbox_post": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, _P, ctypes.c_uint64,
+                          ctypes.c_double], ctypes.c_int),
+    "kvx_mailbox_collect": ([_P, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
+                             ctypes.c_double], ctypes.c_int),
+    "kvx_mailbox_release": ([_P, ctypes.c_uint64], ctypes.c_int),
     "kvx_job_bytes": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int,
                        ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "kvx_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
@@ -164,7 +176,7 @@ def check(rc: int) -> int:
     if rc >= 0:
         return rc
     message = lib().kvx_last_error().decode(errors="replace")
-    raise (KvxRangeError if rc == KVX_ERR_RANGE else KvxError)(rc, message)
+    raise {KVX_ERR_RANGE: KvxRangeError, KVX_ERR_TIMEOUT: KvxTimeout}.get(rc, KvxError)(rc, message)
 
 
 def flags(engine: int = ENGINE_AUTO, tile_bytes: int = 0, ctas_per_sm: int = 0, sm_budget: int = 0) -> int:

@@ -32,6 +32,7 @@
 #include <thread>
 #include <vector>
 
+#include <sched.h>
 #include <sys/eventfd.h>
 #include <sys/prctl.h>
 #include <time.h>
@@ -796,6 +797,39 @@ void watch(Bell *bell) {
     }
 }
 
+// ------------------------------------------------------------------------------------------------ step mailbox
+
+constexpr uint64_t kMailboxHeader = 64;
+
+uint64_t *mailbox_word(void *box, uint64_t offset) {
+    return reinterpret_cast<uint64_t *>(static_cast<char *>(box) + offset);
+}
+
+uint64_t slot_offset(int rank, uint64_t slot_bytes) {
+    return kMailboxHeader + (uint64_t)rank * ((16 + slot_bytes + 63) / 64 * 64);
+}
+
+double seconds_now() {
+    timespec t;
+    clock_gettime(CLOCK_MONOTONIC, &t);
+    return t.tv_sec + t.tv_nsec * 1e-9;
+}
+
+// Waits until *word >= want (acquire): spins with yields for ~50 us, then sleeps 20 us at a time.
+bool wait_word(const uint64_t *word, uint64_t want, double timeout_s) {
+    const double deadline = seconds_now() + timeout_s;
+    for (int spin = 0;; ++spin) {
+        if (__atomic_load_n(word, __ATOMIC_ACQUIRE) >= want) return true;
+        if (spin < 2000) {
+            sched_yield();
+            continue;
+        }
+        if (seconds_now() > deadline) return false;
+        const timespec pause{0, 20000};
+        nanosleep(&pause, nullptr);
+    }
+}
+
 std::mutex g_bells_mu;
 std::map<int, std::shared_ptr<Bell>> g_bells;  // open doorbells by id; ids are never reused
 int g_next_bell = 1;
@@ -1116,6 +1150,49 @@ int kvx_doorbell_close(int id) {
     for (const auto &item : bell->pending) cudaEventDestroy(item.first);  // rings that never came
     bell->pending.clear();
     close(bell->fd);
+    return KVX_OK;
+}
+
+uint64_t kvx_mailbox_stride(uint64_t slot_bytes) { return (16 + slot_bytes + 63) / 64 * 64; }
+
+uint64_t kvx_mailbox_bytes(int world, uint64_t slot_bytes) {
+    return world < 1 ? 0 : slot_offset(world, slot_bytes);
+}
+
+int kvx_mailbox_post(void *box, int world, int rank, uint64_t slot_bytes, uint64_t seq, const void *data,
+                     uint64_t len, double timeout_s) {
+    if (!box || rank < 1 || rank >= world || seq < 1 || (len && !data))
+        return fail(KVX_ERR_INVALID, "mailbox post: rank %d of %d, step %llu", rank, world, (unsigned long long)seq);
+    if (len > slot_bytes)
+        return fail(KVX_ERR_RANGE, "a step output of %llu bytes does not fit a %llu-byte mailbox slot",
+                    (unsigned long long)len, (unsigned long long)slot_bytes);
+    if (!wait_word(mailbox_word(box, 0), seq - 1, timeout_s))
+        return fail(KVX_ERR_TIMEOUT, "rank 0 did not read step %llu within %.1f s", (unsigned long long)(seq - 1),
+                    timeout_s);
+    const uint64_t at = slot_offset(rank, slot_bytes);
+    if (len) memcpy(static_cast<char *>(box) + at + 16, data, len);
+    __atomic_store_n(mailbox_word(box, at + 8), len, __ATOMIC_RELAXED);
+    __atomic_store_n(mailbox_word(box, at), seq, __ATOMIC_RELEASE);
+    return KVX_OK;
+}
+
+int kvx_mailbox_collect(void *box, int world, uint64_t slot_bytes, uint64_t seq, uint64_t *lens, double timeout_s) {
+    if (!box || !lens || world < 1 || seq < 1) return fail(KVX_ERR_INVALID, "mailbox collect: bad arguments");
+    lens[0] = 0;
+    for (int rank = 1; rank < world; ++rank) {
+        const uint64_t at = slot_offset(rank, slot_bytes);
+        if (!wait_word(mailbox_word(box, at), seq, timeout_s))
+            return fail(KVX_ERR_TIMEOUT, "rank %d did not post step %llu within %.1f s", rank,
+                        (unsigned long long)seq, timeout_s);
+        lens[rank] = __atomic_load_n(mailbox_word(box, at + 8), __ATOMIC_RELAXED);
+        if (lens[rank] > slot_bytes) return fail(KVX_ERR_RANGE, "rank %d posted a corrupt length", rank);
+    }
+    return KVX_OK;
+}
+
+int kvx_mailbox_release(void *box, uint64_t seq) {
+    if (!box) return fail(KVX_ERR_INVALID, "null mailbox");
+    __atomic_store_n(mailbox_word(box, 0), seq, __ATOMIC_RELEASE);
     return KVX_OK;
 }
 

@@ -16,12 +16,14 @@ from lean_vllm_b200.kv_transfer.base import (
     check_kv_transfer_params,
 )
 from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorScheduler, CudaIpcConnectorWorker
+from lean_vllm_b200.kv_transfer.step import KVConnectorStep
 
 __all__ = [
     "CONNECTORS",
     "KVConnectorMetadata",
     "KVConnectorOutput",
     "KVConnectorScheduler",
+    "KVConnectorStep",
     "KVConnectorWorker",
     "KVOutputAggregator",
     "KVTransferConfig",
