@@ -1119,7 +1119,7 @@ def run_poisson(args) -> None:
                 producer.start_load_kv(KVConnectorMetadata(reqs_to_send={ids[i]: srcs[i].tolist() for i in range(n)}))
             if world > 1:
                 dist.barrier(group=gloo)
-            latency, moved = [], 0
+            latency, in_flight, moved = [], [], 0
             if consumer is not None:
                 free = list(rng.permutation(pool))
                 pending, started, waiting = {}, {}, list(range(n))
@@ -1143,6 +1143,7 @@ def run_poisson(args) -> None:
                     for rid in out.finished_recving:
                         i, local = pending.pop(rid)
                         latency.append((time.perf_counter() - started[rid]) * 1e3)
+                        in_flight.append(out.recv_stats[rid].seconds * 1e3)
                         moved += out.recv_stats[rid].num_bytes
                         free.extend(local)
                     time.sleep(50e-6)
@@ -1150,6 +1151,8 @@ def run_poisson(args) -> None:
                 results.append({"rate_req_per_s": rate, "requests": n, "p50_ms": round(float(np.percentile(latency, 50)), 3),
                                 "p99_ms": round(float(np.percentile(latency, 99)), 3),
                                 "mean_ms": round(float(np.mean(latency)), 3),
+                                # the connector's own stats: from posting the copy to seeing it landed
+                                "p50_posted_to_landed_ms": round(float(np.percentile(in_flight, 50)), 3),
                                 "offered_gb_per_s": round(moved / float(arrivals[-1]) / 1e9, 2),
                                 "moved_gb_per_s": round(moved / wall / 1e9, 2), "bytes": moved,
                                 "mean_prompt_tokens": int(lengths.mean())})
