@@ -8,6 +8,7 @@ a CUDA kernel of libkvx.so; nothing here copies bytes on the host.
 
 from __future__ import annotations
 
+import array
 import ctypes
 import os
 from dataclasses import dataclass, field
@@ -18,8 +19,19 @@ from lean_vllm_b200 import _native
 from lean_vllm_b200._native import Cache, IpcHandle, Job, Region, check, lib
 
 
-def _ids(block_ids) -> np.ndarray:
-    return np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+_I32P = ctypes.POINTER(ctypes.c_int32)
+assert array.array("i").itemsize == 4
+
+
+def _ids(block_ids):
+    """Block ids as (keep-alive buffer, int32* for the ABI, count). A list goes through array.array (a few us for
+    hundreds of ids; numpy's ctypes accessor costs more than the rest of a launch's marshalling)."""
+    if isinstance(block_ids, np.ndarray):
+        a = np.ascontiguousarray(block_ids.reshape(-1), dtype=np.int32)
+        return a, a.ctypes.data_as(_I32P), int(a.size)
+    buf = array.array("i", block_ids)
+    n = len(buf)
+    return buf, ((ctypes.c_int32 * n).from_buffer(buf) if n else None), n
 
 
 @dataclass
@@ -87,17 +99,17 @@ def _marshal(caches: list[CacheTable], jobs: list[CopyJob]):
     keep = [cache_array]
     job_array = (Job * max(len(jobs), 1))()
     for k, job in enumerate(jobs):
-        src_ids, dst_ids = _ids(job.src_block_ids), _ids(job.dst_block_ids)
-        if len(src_ids) != len(dst_ids):
-            raise ValueError(f"job {k} pairs {len(src_ids)} source blocks with {len(dst_ids)} destination blocks")
-        keep += [src_ids, dst_ids]
-        ptr = ctypes.POINTER(ctypes.c_int32)
+        src_buf, src_ptr, n_src = _ids(job.src_block_ids)
+        dst_buf, dst_ptr, n_dst = _ids(job.dst_block_ids)
+        if n_src != n_dst:
+            raise ValueError(f"job {k} pairs {n_src} source blocks with {n_dst} destination blocks")
+        keep += [src_buf, dst_buf, src_ptr, dst_ptr]
         job_array[k] = Job(
             job.src,
             job.dst,
-            src_ids.ctypes.data_as(ptr),
-            dst_ids.ctypes.data_as(ptr),
-            len(src_ids),
+            src_ptr,
+            dst_ptr,
+            n_src,
             job.src_first_head,
             job.dst_first_head,
             job.num_heads,
@@ -178,16 +190,15 @@ class Doorbell:
 
 def pack(src: CacheTable, block_ids, first_head: int, num_heads: int, latents: bool, staging: int,
          staging_bytes: int, stream: int = 0, flags: int = 0) -> None:
-    ids = _ids(block_ids)
-    check(lib().kvx_pack(ctypes.byref(src.struct()), ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(ids),
+    _keep, ids, n = _ids(block_ids)
+    check(lib().kvx_pack(ctypes.byref(src.struct()), ids, n,
                          first_head, num_heads, int(latents), staging, staging_bytes, flags, stream))
 
 
 def scatter(staging: int, staging_bytes: int, dst: CacheTable, block_ids, first_head: int, num_heads: int,
             latents: bool, stream: int = 0, flags: int = 0) -> None:
-    ids = _ids(block_ids)
-    check(lib().kvx_scatter(staging, staging_bytes, ctypes.byref(dst.struct()),
-                            ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(ids), first_head, num_heads,
+    _keep, ids, n = _ids(block_ids)
+    check(lib().kvx_scatter(staging, staging_bytes, ctypes.byref(dst.struct()), ids, n, first_head, num_heads,
                             int(latents), flags, stream))
 
 
