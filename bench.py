@@ -945,10 +945,15 @@ def run_store(args) -> None:
         targets = [[PushTarget.of(c.transpose(2, 3)[0], c.transpose(2, 3)[1], peer_slots)] for c in peer_caches]
         torch.cuda.synchronize(peer)
 
+    from lean_vllm_b200._native import STORE_SERIAL
+
+    store_flags = STORE_SERIAL if args.serial else 0
+
     def ours():
         for layer in range(layers):
             view = caches[layer].transpose(2, 3)
-            store_kvcache(keys[layer], values[layer], view[0], view[1], slots, push_to=targets[layer])
+            store_kvcache(keys[layer], values[layer], view[0], view[1], slots, push_to=targets[layer],
+                          flags=store_flags)
 
     def torch_indexing():
         b, o = slots // block, slots % block
@@ -1026,7 +1031,8 @@ def run_store(args) -> None:
         "data": "synthetic: seeded N(0,1) bf16 rows, seeded shuffled block table",
         "config": {"workload": "qwen3-8b-kv/store-8192-token-step", "layers": layers, "tokens": tokens,
                    "shape": "8 KV heads x 128, block 256, HND",
-                   "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None},
+                   "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None,
+                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)"},
         "roofline": roofline,
         "ms_per_step_eager": round(ms_eager, 4),
         "timing": "CUDA graph of the step's 36 store launches, replayed; ms_per_step_eager issues them one by one",
@@ -1390,6 +1396,7 @@ def main(argv=None):
     p.add_argument("--layerwise", action="store_true",
                    help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
     p.add_argument("--store", action="store_true", help="measure the per-token cache store (and fused push)")
+    p.add_argument("--serial", action="store_true", help="with --store: plain launches (KVX_STORE_SERIAL)")
     p.add_argument("--fused", action="store_true",
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")

@@ -20,6 +20,8 @@ KVX_ERR_RANGE = -3
 KVX_ERR_DEVICE = -4
 KVX_ERR_TIMEOUT = -5
 
+STORE_SERIAL = 1  # kvx_store flag: a plain launch, no overlap with the kernel before it
+
 ENGINE_AUTO = 0
 ENGINE_LSU = 1
 ENGINE_TMA = 2

@@ -383,9 +383,16 @@ constexpr int kStoreUnroll = 4;  // tokens each thread loads before it stores an
 // a CTA covers `tpp` tokens per pass (one when a token's rows exceed the CTA), kStoreUnroll passes in flight. The
 // rows and their destination-0 slots load together; each further destination resolves the slots of all tokens in
 // flight before it stores any, so every dependent load is one round trip per batch, not per token.
+//
+// Launched with programmatic stream serialization (unless flags ask for a plain launch): the grid may be scheduled
+// while the kernel before it on the stream drains, waits for that kernel's completion and memory (griddepcontrol.
+// wait) before reading anything, then lets the next such launch start (launch_dependents). Per-layer stores thus
+// overlap each other's launch and ramp; with an ordinary kernel before or after, ordering is the plain stream's.
 template <int VEC>
 __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t vecs = (uint32_t)p.head_bytes / VEC;  // per (token, head) row
     const uint32_t parts = p.value ? 2u : 1u;
     const uint32_t per_token = parts * (uint32_t)p.num_heads * vecs;
@@ -437,6 +444,7 @@ __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_c
 struct DeviceInfo {
     int sms = 0;
     size_t tma_smem_set = 0;
+    int store_ctas_per_sm[5] = {0, 0, 0, 0, 0};  // resident kvx_store_kernel<16, 8, 4, 2, 1> CTAs per SM
 };
 
 std::mutex g_mutex;
@@ -1034,21 +1042,36 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     const int vec = (int)std::min<uint64_t>(low_bit(align_bits), 16);
     DeviceInfo *info;
     if (int rc = device_info(&info)) return rc;
+    int vi = 0;
+    while ((16 >> vi) != vec) ++vi;
+    void (*kernel)(StoreParams) = vec == 16 ? kvx_store_kernel<16>
+                                  : vec == 8 ? kvx_store_kernel<8>
+                                  : vec == 4 ? kvx_store_kernel<4>
+                                  : vec == 2 ? kvx_store_kernel<2>
+                                             : kvx_store_kernel<1>;
+    if (info->store_ctas_per_sm[vi] == 0) {
+        int occ = 0;
+        KVX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kStoreThreads, 0));
+        info->store_ctas_per_sm[vi] = occ > 0 ? occ : 1;
+    }
     const int sm_budget = (flags >> 24) & 0xff;
     const int sms = sm_budget > 0 && sm_budget < info->sms ? sm_budget : info->sms;
+    const int ctas_per_sm = ((flags >> 16) & 0xff) ? ((flags >> 16) & 0xff) : info->store_ctas_per_sm[vi];
     const uint64_t per_token = (uint64_t)(value ? 2 : 1) * num_heads * (head_bytes / vec);
     const uint64_t tpp = per_token <= kStoreThreads ? kStoreThreads / per_token : 1;
-    const uint64_t passes = ((uint64_t)num_tokens + tpp * kStoreUnroll - 1) / (tpp * kStoreUnroll);
-    const unsigned grid = (unsigned)std::min<uint64_t>(passes, (uint64_t)sms * 8);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    switch (vec) {
-        case 16: kvx_store_kernel<16><<<grid, kStoreThreads, 0, s>>>(p); break;
-        case 8: kvx_store_kernel<8><<<grid, kStoreThreads, 0, s>>>(p); break;
-        case 4: kvx_store_kernel<4><<<grid, kStoreThreads, 0, s>>>(p); break;
-        case 2: kvx_store_kernel<2><<<grid, kStoreThreads, 0, s>>>(p); break;
-        default: kvx_store_kernel<1><<<grid, kStoreThreads, 0, s>>>(p); break;
-    }
-    KVX_CUDA(cudaGetLastError());
+    const uint64_t passes = ((uint64_t)num_tokens + tpp - 1) / tpp;
+    // One resident wave: every CTA is on an SM from the start and sweeps its tokens; none waits for a second wave.
+    const unsigned grid = (unsigned)std::min<uint64_t>(passes, (uint64_t)sms * ctas_per_sm);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kStoreThreads);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = (flags & KVX_STORE_SERIAL) ? 0 : 1;
+    KVX_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return KVX_OK;
 }

@@ -131,3 +131,34 @@ def test_bad_arguments_raise_before_a_launch():
 
     with pytest.raises(KvxRangeError, match="heads"):
         store_kvcache(key, value, view[0], view[1], slots, push_to=[bad])
+
+
+@pytest.mark.parametrize("serial", [False, True], ids=["programmatic", "plain"])
+def test_chained_stores_see_what_the_kernels_before_them_wrote(serial):
+    """Stores launch with programmatic stream serialization: each may be scheduled while the kernel before it
+    drains, but reads nothing before that kernel has completed. A chain where every store reads the cache the
+    previous store (or a torch kernel) just wrote must equal the same chain run one launch at a time."""
+    from lean_vllm_b200._native import STORE_SERIAL
+
+    flags = STORE_SERIAL if serial else 0
+    g = torch.Generator(device="cuda").manual_seed(3)
+    blocks, block, heads, dim, hops = 24, 16, 4, 128, 12
+    tokens = blocks * block
+    caches = [torch.zeros(2, blocks, block, heads, dim, dtype=torch.bfloat16, device="cuda") for _ in range(hops)]
+    perms = [torch.randperm(tokens, device="cuda", generator=g) for _ in range(hops)]
+    rows = torch.randn(tokens, heads, dim, device="cuda", generator=g).to(torch.bfloat16)
+    key, value = rows * 2, rows - 1  # torch kernels right before the first store
+    for hop in range(hops):
+        store_kvcache(key, value, caches[hop][0], caches[hop][1], perms[hop], flags=flags)
+        # The next hop's rows are this cache, as stored: token i of the flat (blocks * block) view.
+        key, value = caches[hop][0].reshape(tokens, heads, dim), caches[hop][1].reshape(tokens, heads, dim)
+    torch.cuda.synchronize()
+    want_k, want_v = rows * 2, rows - 1
+    for hop in range(hops):
+        k = torch.empty_like(want_k)
+        k[perms[hop]] = want_k
+        v = torch.empty_like(want_v)
+        v[perms[hop]] = want_v
+        assert torch.equal(caches[hop][0].reshape(tokens, heads, dim), k), hop
+        assert torch.equal(caches[hop][1].reshape(tokens, heads, dim), v), hop
+        want_k, want_v = k, v
