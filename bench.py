@@ -945,9 +945,9 @@ def run_store(args) -> None:
         targets = [[PushTarget.of(c.transpose(2, 3)[0], c.transpose(2, 3)[1], peer_slots)] for c in peer_caches]
         torch.cuda.synchronize(peer)
 
-    from lean_vllm_b200._native import STORE_SERIAL
+    from lean_vllm_b200._native import STORE_LSU, STORE_SERIAL
 
-    store_flags = STORE_SERIAL if args.serial else 0
+    store_flags = (STORE_SERIAL if args.serial else 0) | (STORE_LSU if args.engine == "lsu" else 0)
 
     def ours():
         for layer in range(layers):
@@ -1032,7 +1032,9 @@ def run_store(args) -> None:
         "config": {"workload": "qwen3-8b-kv/store-8192-token-step", "layers": layers, "tokens": tokens,
                    "shape": "8 KV heads x 128, block 256, HND",
                    "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None,
-                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)"},
+                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)",
+                   "rows": "read by the threads (KVX_STORE_LSU)" if args.engine == "lsu" else
+                           "staged in shared memory by the TMA"},
         "roofline": roofline,
         "ms_per_step_eager": round(ms_eager, 4),
         "timing": "CUDA graph of the step's 36 store launches, replayed; ms_per_step_eager issues them one by one",
