@@ -1220,8 +1220,8 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
 
     // Rows on the TMA when every address is 16-byte aligned and two stages of a token group fit.
     const uint32_t parts = value ? 2u : 1u;
-    const uint64_t per_token16 = (uint64_t)parts * num_heads * (head_bytes / 16);
-    const uint64_t tpp16 = per_token16 <= kStoreTmaConsumers ? kStoreTmaConsumers / per_token16 : 1;
+    const uint64_t per_token16 = vec == 16 ? (uint64_t)parts * num_heads * (head_bytes / 16) : 0;  // >= 1 if 16
+    const uint64_t tpp16 = per_token16 && per_token16 <= kStoreTmaConsumers ? kStoreTmaConsumers / per_token16 : 1;
     const uint64_t stage_bytes = (uint64_t)parts * tpp16 * kStoreTmaTokens * num_heads * head_bytes;
     if (vec == 16 && !(flags & KVX_STORE_LSU) && 2 * stage_bytes <= kStoreTmaSmem) {
         if (info->store_tma_smem_set == 0) {
