@@ -357,6 +357,45 @@ __device__ __forceinline__ int32_t resolve_slot(const StoreParams &p, int d, uin
     return mapped < 0 ? -1 : mapped * dst.block_size + (first_slot - (int32_t)(b * block_size0));
 }
 
+// One destination as one thread sees it from its fixed (K|V, head, vector) position, computed once per thread so
+// that storing a vector costs a slot check, a shift and one address multiply-add: the kernels are bound by issue
+// rate, not bytes, when every field is re-read per token.
+struct StoreLane {
+    uint64_t base;  // the position's address at block 0, token 0; 0 when the head is not this destination's
+    int64_t block_stride, token_stride;
+    int32_t limit;  // num_blocks * block_size
+    int32_t shift;  // log2(block_size), or -1
+    uint32_t block_size;
+};
+
+__device__ __forceinline__ StoreLane lane_of(const StoreDest &dst, uint32_t part, int32_t head, uint32_t byte_in_row) {
+    StoreLane l;
+    const bool mine = head >= dst.src_first_head && head < dst.src_first_head + dst.num_heads;
+    l.base = mine ? (part ? dst.v : dst.k) + (int64_t)(head - dst.src_first_head + dst.dst_first_head) * dst.head_stride +
+                        byte_in_row
+                  : 0;
+    l.block_stride = dst.block_stride;
+    l.token_stride = dst.token_stride;
+    l.limit = dst.num_blocks * dst.block_size;
+    l.shift = dst.block_shift;
+    l.block_size = (uint32_t)dst.block_size;
+    return l;
+}
+
+template <int VEC>
+__device__ __forceinline__ void put(const StoreLane &l, int32_t slot, typename Vec<VEC>::T data) {
+    if (slot < 0) return;  // padding: no cache slot
+    if (slot >= l.limit) {
+        atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
+        return;
+    }
+    const uint32_t block = l.shift >= 0 ? (uint32_t)slot >> l.shift : (uint32_t)slot / l.block_size;
+    const uint32_t offset = (uint32_t)slot - block * l.block_size;
+    Vec<VEC>::store(reinterpret_cast<char *>(l.base + (uint64_t)block * l.block_stride +
+                                             (uint64_t)offset * l.token_stride),
+                    data);
+}
+
 template <int VEC>
 __device__ __forceinline__ void store_row(const StoreParams &p, const StoreDest &dst, int32_t slot, uint32_t part,
                                           int32_t head, uint32_t byte_in_row, typename Vec<VEC>::T data) {
@@ -389,7 +428,7 @@ constexpr int kStoreUnroll = 4;  // tokens each thread loads before it stores an
 // wait) before reading anything, then lets the next such launch start (launch_dependents). Per-layer stores thus
 // overlap each other's launch and ramp; with an ordinary kernel before or after, ordering is the plain stream's.
 template <int VEC>
-__global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_constant__ StoreParams p) {
+__global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -410,7 +449,10 @@ __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_c
         const uint64_t row0 = part ? p.value : p.key;
         const int64_t row_stride = part ? p.value_stride : p.key_stride;
         const uint32_t byte_in_row = vec * VEC;
-        const uint64_t in_row = (uint64_t)head * p.head_bytes + byte_in_row;
+        const char *in_row = reinterpret_cast<const char *>(row0 + (uint64_t)head * p.head_bytes + byte_in_row);
+        const StoreLane lane0 = lane_of(p.dests[0], part, head, byte_in_row);
+        const void *slots0 = p.dests[0].slots;
+        const bool wide0 = p.dests[0].slot_bytes == 8;
         for (uint32_t t0 = blockIdx.x * tpp + lane_token; t0 < n; t0 += token_step * kStoreUnroll) {
             typename V::T data[kStoreUnroll];
             int32_t first[kStoreUnroll];
@@ -419,11 +461,16 @@ __global__ void __launch_bounds__(kStoreThreads) kvx_store_kernel(const __grid_c
                 const uint32_t t = t0 + u * token_step;
                 first[u] = -1;
                 if (t < n) {
-                    data[u] = V::load(reinterpret_cast<const char *>(row0 + (uint64_t)t * row_stride + in_row));
-                    first[u] = load_slot(p.dests[0], t);
+                    data[u] = V::load(in_row + (int64_t)t * row_stride);
+                    first[u] = wide0 ? (int32_t) static_cast<const int64_t *>(slots0)[t]
+                                     : static_cast<const int32_t *>(slots0)[t];
                 }
             }
-            for (int d = 0; d < p.n_dests; ++d) {
+            if (lane0.base) {
+#pragma unroll
+                for (int u = 0; u < kStoreUnroll; ++u) put<VEC>(lane0, first[u], data[u]);
+            }
+            for (int d = 1; d < p.n_dests; ++d) {
                 const StoreDest &dst = p.dests[d];
                 if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
                 int32_t slot[kStoreUnroll];
@@ -581,7 +628,13 @@ __global__ void __launch_bounds__(kStoreTmaThreads, 1)
                     const uint32_t u = lane_token + (uint32_t)i * tpp;
                     if (t0 + u < n) data[i] = *reinterpret_cast<const uint4 *>(src + u * row_bytes);
                 }
-                for (int d = 0; d < p.n_dests; ++d) {
+                const StoreLane lane0 = lane_of(p.dests[0], part, head, byte_in_row);
+                if (lane0.base) {
+#pragma unroll
+                    for (int i = 0; i < kStoreTmaTokens; ++i)
+                        put<16>(lane0, t0 + lane_token + (uint32_t)i * tpp < n ? slots_now[i] : -1, data[i]);
+                }
+                for (int d = 1; d < p.n_dests; ++d) {
                     const StoreDest &dst = p.dests[d];
                     if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
                     int32_t slot[kStoreTmaTokens];
