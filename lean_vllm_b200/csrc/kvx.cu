@@ -382,18 +382,26 @@ __device__ __forceinline__ StoreLane lane_of(const StoreDest &dst, uint32_t part
     return l;
 }
 
-template <int VEC>
+// FAST: the destination's block size is a power of two and its block and token strides are below 2^32, so a slot
+// becomes an address with a shift, a mask and two 32x32->64-bit multiply-adds (the usual paged cache).
+template <int VEC, bool FAST>
 __device__ __forceinline__ void put(const StoreLane &l, int32_t slot, typename Vec<VEC>::T data) {
     if (slot < 0) return;  // padding: no cache slot
     if (slot >= l.limit) {
         atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
         return;
     }
-    const uint32_t block = l.shift >= 0 ? (uint32_t)slot >> l.shift : (uint32_t)slot / l.block_size;
-    const uint32_t offset = (uint32_t)slot - block * l.block_size;
-    Vec<VEC>::store(reinterpret_cast<char *>(l.base + (uint64_t)block * l.block_stride +
-                                             (uint64_t)offset * l.token_stride),
-                    data);
+    uint64_t at;
+    if (FAST) {
+        const uint32_t block = (uint32_t)slot >> l.shift;
+        const uint32_t offset = (uint32_t)slot & (l.block_size - 1);
+        at = l.base + (uint64_t)block * (uint32_t)l.block_stride + (uint64_t)offset * (uint32_t)l.token_stride;
+    } else {
+        const uint32_t block = l.shift >= 0 ? (uint32_t)slot >> l.shift : (uint32_t)slot / l.block_size;
+        const uint32_t offset = (uint32_t)slot - block * l.block_size;
+        at = l.base + (uint64_t)block * l.block_stride + (uint64_t)offset * l.token_stride;
+    }
+    Vec<VEC>::store(reinterpret_cast<char *>(at), data);
 }
 
 template <int VEC>
@@ -427,7 +435,7 @@ constexpr int kStoreUnroll = 4;  // tokens each thread loads before it stores an
 // while the kernel before it on the stream drains, waits for that kernel's completion and memory (griddepcontrol.
 // wait) before reading anything, then lets the next such launch start (launch_dependents). Per-layer stores thus
 // overlap each other's launch and ramp; with an ordinary kernel before or after, ordering is the plain stream's.
-template <int VEC>
+template <int VEC, bool FAST>
 __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -461,14 +469,14 @@ __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __gri
                 const uint32_t t = t0 + u * token_step;
                 first[u] = -1;
                 if (t < n) {
-                    data[u] = V::load(in_row + (int64_t)t * row_stride);
+                    data[u] = V::load(FAST ? in_row + (uint64_t)t * (uint32_t)row_stride : in_row + (int64_t)t * row_stride);
                     first[u] = wide0 ? (int32_t) static_cast<const int64_t *>(slots0)[t]
                                      : static_cast<const int32_t *>(slots0)[t];
                 }
             }
             if (lane0.base) {
 #pragma unroll
-                for (int u = 0; u < kStoreUnroll; ++u) put<VEC>(lane0, first[u], data[u]);
+                for (int u = 0; u < kStoreUnroll; ++u) put<VEC, FAST>(lane0, first[u], data[u]);
             }
             for (int d = 1; d < p.n_dests; ++d) {
                 const StoreDest &dst = p.dests[d];
@@ -502,6 +510,7 @@ constexpr uint32_t kStoreTmaSmem = 200 * 1024;             // ring bytes at most
 // store each 16-byte vector to every destination as kvx_store_kernel does. Every wait is bounded (2 s): a stuck
 // stage records error 3 in the device word, and the producer waits (bounded) for its loads in flight before the
 // CTA exits.
+template <bool FAST>
 __global__ void __launch_bounds__(kStoreTmaThreads, 1)
     kvx_store_tma(const __grid_constant__ StoreParams p, const uint32_t stages) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -632,7 +641,7 @@ __global__ void __launch_bounds__(kStoreTmaThreads, 1)
                 if (lane0.base) {
 #pragma unroll
                     for (int i = 0; i < kStoreTmaTokens; ++i)
-                        put<16>(lane0, t0 + lane_token + (uint32_t)i * tpp < n ? slots_now[i] : -1, data[i]);
+                        put<16, FAST>(lane0, t0 + lane_token + (uint32_t)i * tpp < n ? slots_now[i] : -1, data[i]);
                 }
                 for (int d = 1; d < p.n_dests; ++d) {
                     const StoreDest &dst = p.dests[d];
@@ -662,7 +671,7 @@ __global__ void __launch_bounds__(kStoreTmaThreads, 1)
 struct DeviceInfo {
     int sms = 0;
     size_t tma_smem_set = 0;
-    int store_ctas_per_sm[5] = {0, 0, 0, 0, 0};  // resident kvx_store_kernel<16, 8, 4, 2, 1> CTAs per SM
+    int store_ctas_per_sm[5][2] = {};  // resident kvx_store_kernel<16, 8, 4, 2, 1; FAST> CTAs per SM
     int store_tma_smem_set = 0;
 };
 
@@ -1271,6 +1280,12 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     cfg.attrs = &attr;
     cfg.numAttrs = (flags & KVX_STORE_SERIAL) ? 0 : 1;
 
+    // Destination 0 with a power-of-two block size and strides below 2^32, and row strides below 2^32: the kernels'
+    // address arithmetic then stays in 32-bit multiplies.
+    const kvx_store_dest &d0 = dests[0];
+    auto small = [](int64_t v) { return v >= 0 && v < ((int64_t)1 << 32); };
+    const bool fast = p.dests[0].block_shift >= 0 && small(d0.block_stride) && small(d0.token_stride) &&
+                      small(key_stride) && small(value_stride);
     // Rows on the TMA when every address is 16-byte aligned and two stages of a token group fit.
     const uint32_t parts = value ? 2u : 1u;
     const uint64_t per_token16 = vec == 16 ? (uint64_t)parts * num_heads * (head_bytes / 16) : 0;  // >= 1 if 16
@@ -1278,7 +1293,9 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     const uint64_t stage_bytes = (uint64_t)parts * tpp16 * kStoreTmaTokens * num_heads * head_bytes;
     if (vec == 16 && !(flags & KVX_STORE_LSU) && 2 * stage_bytes <= kStoreTmaSmem) {
         if (info->store_tma_smem_set == 0) {
-            KVX_CUDA(cudaFuncSetAttribute(kvx_store_tma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            KVX_CUDA(cudaFuncSetAttribute(kvx_store_tma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)kStoreTmaSmem));
+            KVX_CUDA(cudaFuncSetAttribute(kvx_store_tma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)kStoreTmaSmem));
             info->store_tma_smem_set = 1;
         }
@@ -1287,24 +1304,31 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
         cfg.gridDim = dim3((unsigned)std::min<uint64_t>(groups, (uint64_t)sms));
         cfg.blockDim = dim3(kStoreTmaThreads);
         cfg.dynamicSmemBytes = stages * stage_bytes;
-        KVX_CUDA(cudaLaunchKernelEx(&cfg, kvx_store_tma, p, stages));
+        KVX_CUDA(cudaLaunchKernelEx(&cfg, fast ? kvx_store_tma<true> : kvx_store_tma<false>, p, stages));
         g_launches.fetch_add(1, std::memory_order_relaxed);
         return KVX_OK;
     }
 
     int vi = 0;
     while ((16 >> vi) != vec) ++vi;
-    void (*kernel)(StoreParams) = vec == 16 ? kvx_store_kernel<16>
-                                  : vec == 8 ? kvx_store_kernel<8>
-                                  : vec == 4 ? kvx_store_kernel<4>
-                                  : vec == 2 ? kvx_store_kernel<2>
-                                             : kvx_store_kernel<1>;
-    if (info->store_ctas_per_sm[vi] == 0) {
+    void (*kernel)(StoreParams) =
+        fast ? (vec == 16 ? kvx_store_kernel<16, true>
+                : vec == 8 ? kvx_store_kernel<8, true>
+                : vec == 4 ? kvx_store_kernel<4, true>
+                : vec == 2 ? kvx_store_kernel<2, true>
+                           : kvx_store_kernel<1, true>)
+             : (vec == 16 ? kvx_store_kernel<16, false>
+                : vec == 8 ? kvx_store_kernel<8, false>
+                : vec == 4 ? kvx_store_kernel<4, false>
+                : vec == 2 ? kvx_store_kernel<2, false>
+                           : kvx_store_kernel<1, false>);
+    int &occupancy = info->store_ctas_per_sm[vi][fast ? 1 : 0];
+    if (occupancy == 0) {
         int occ = 0;
         KVX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kStoreThreads, 0));
-        info->store_ctas_per_sm[vi] = occ > 0 ? occ : 1;
+        occupancy = occ > 0 ? occ : 1;
     }
-    const int ctas_per_sm = ((flags >> 16) & 0xff) ? ((flags >> 16) & 0xff) : info->store_ctas_per_sm[vi];
+    const int ctas_per_sm = ((flags >> 16) & 0xff) ? ((flags >> 16) & 0xff) : occupancy;
     const uint64_t per_token = (uint64_t)parts * num_heads * (head_bytes / vec);
     const uint64_t tpp = per_token <= kStoreThreads ? kStoreThreads / per_token : 1;
     const uint64_t passes = ((uint64_t)num_tokens + tpp - 1) / tpp;

@@ -197,3 +197,22 @@ def test_rows_strided_across_tokens_store_like_contiguous_ones(head_dim):
     store_kvcache(key, value, view[0], view[1], slots)
     torch.cuda.synchronize()
     assert np.array_equal(bits(cache), expected)
+
+
+@pytest.mark.parametrize("block", [24, 64], ids=["block24", "block64"])
+def test_block_sizes_that_are_not_powers_of_two_divide(block):
+    """A 24-token block takes the general slot arithmetic (divide), a 64-token block the shift-and-mask one."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    tokens, heads, dim, blocks = 500, 2, 64, 30
+    key = torch.randn(tokens, heads, dim, generator=g, device="cuda").to(torch.bfloat16)
+    value = torch.randn(tokens, heads, dim, generator=g, device="cuda").to(torch.bfloat16)
+    cache = torch.randn(2, blocks, heads, block, dim, generator=g, device="cuda").to(torch.bfloat16)
+    slots = torch.randperm(blocks * block, generator=g, device="cuda")[:tokens]
+    slots[::31] = -1
+    expected = bits(cache).copy()
+    e_view = expected.swapaxes(2, 3)
+    oracle_store(bits(key), bits(value), e_view[0], e_view[1], slots.cpu().numpy())
+    view = cache.transpose(2, 3)
+    store_kvcache(key, value, view[0], view[1], slots)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(cache), expected)
