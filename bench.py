@@ -945,9 +945,9 @@ def run_store(args) -> None:
         targets = [[PushTarget.of(c.transpose(2, 3)[0], c.transpose(2, 3)[1], peer_slots)] for c in peer_caches]
         torch.cuda.synchronize(peer)
 
-    from lean_vllm_b200._native import STORE_LSU, STORE_SERIAL
+    from lean_vllm_b200._native import STORE_SERIAL
 
-    store_flags = (STORE_SERIAL if args.serial else 0) | (STORE_LSU if args.engine == "lsu" else 0)
+    store_flags = STORE_SERIAL if args.serial else 0
 
     def ours():
         for layer in range(layers):
@@ -990,6 +990,22 @@ def run_store(args) -> None:
     with ClockSampler(0) as clocks:
         ms = timed(graph.replay, args.steps)
     ms_torch = timed(torch_indexing, max(args.steps // 4, 2))
+    # Calibration: the same bytes per launch as a plain device copy (cudaMemcpyAsync of each layer's keys and values,
+    # 33.5 MB read + 33.5 MB written), 36 launches replayed from a graph the same way: what a launch of this size
+    # reaches at best, ramp and drain included.
+    flat_src = [torch.cat([k.reshape(-1), v.reshape(-1)]) for k, v in zip(keys, values)]
+    flat_dst = [torch.empty_like(f) for f in flat_src]
+    copy_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(capture):
+        for d, f in zip(flat_dst, flat_src):
+            d.copy_(f)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(copy_graph, stream=capture):
+            for d, f in zip(flat_dst, flat_src):
+                d.copy_(f)
+    torch.cuda.synchronize()
+    ms_copy = timed(copy_graph.replay, args.steps)
+    del flat_src, flat_dst, copy_graph
     # Correctness: every layer's cache holds its rows at the slots (and the peer's at its slots).
     ok = True
     for layer in (0, layers - 1):
@@ -1032,12 +1048,12 @@ def run_store(args) -> None:
         "config": {"workload": "qwen3-8b-kv/store-8192-token-step", "layers": layers, "tokens": tokens,
                    "shape": "8 KV heads x 128, block 256, HND",
                    "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None,
-                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)",
-                   "rows": "read by the threads (KVX_STORE_LSU)" if args.engine == "lsu" else
-                           "staged in shared memory by the TMA"},
+                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)"},
         "roofline": roofline,
         "ms_per_step_eager": round(ms_eager, 4),
         "timing": "CUDA graph of the step's 36 store launches, replayed; ms_per_step_eager issues them one by one",
+        "same_bytes_device_copy_ms_per_step": round(ms_copy, 4),
+        "frac_of_same_bytes_copy": round(ms_copy / ms, 4),
         "torch_indexing_ms_per_step": round(ms_torch, 4),
         "speedup_vs_torch_indexing": round(ms_torch / ms_eager, 2),
         "gpu_launches": per_replay * args.steps,

@@ -161,7 +161,6 @@ typedef struct kvx_store_dest {
 
 /* kvx_store flags: bits 16-23 CTAs per SM (0: as many as fit), bits 24-31 SM budget, as for copies; and */
 #define KVX_STORE_SERIAL 1     /* a plain launch: no overlap with the kernel before it on the stream */
-#define KVX_STORE_LSU 2        /* rows read by the threads themselves, never staged by the TMA */
 
 /* Scatters num_tokens rows of keys and values [token][head][head_bytes] (or latents, with value = NULL and
  * num_heads = 1) into each destination's slots, one pass over the rows: destination 0 is the local cache
@@ -230,8 +229,7 @@ int kvx_mailbox_release(void *box, uint64_t seq);
 int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, uint64_t *out_bytes);
 
 /* Reads and clears the device error word of the current device: 0, or the first error a kernel recorded -- 1 a copy's
- * bounded TMA wait ran out, 2 a store slot or block id past its cache (skipped), 3 a store's bounded TMA wait ran
- * out. */
+ * bounded TMA wait ran out, 2 a store slot or block id past its cache (skipped). */
 int kvx_device_error(int *out_code);
 
 /* Kernel launches issued by this process so far (all entry points), for launch accounting. */

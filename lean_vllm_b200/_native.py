@@ -21,7 +21,6 @@ KVX_ERR_DEVICE = -4
 KVX_ERR_TIMEOUT = -5
 
 STORE_SERIAL = 1  # kvx_store flag: a plain launch, no overlap with the kernel before it
-STORE_LSU = 2  # kvx_store flag: rows read by the threads, not staged through shared memory by the TMA
 
 ENGINE_AUTO = 0
 ENGINE_LSU = 1

@@ -494,185 +494,12 @@ __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __gri
     }
 }
 
-// ------------------------------------------------------------------------------------------------ store kernel, TMA reads
-
-constexpr int kStoreTmaConsumers = 256;                    // 8 consumer warps
-constexpr int kStoreTmaThreads = 32 + kStoreTmaConsumers;  // + the producer warp
-constexpr int kStoreTmaMaxStages = 6;
-constexpr int kStoreTmaTokens = 8;                         // tokens per consumer thread per stage
-constexpr uint32_t kStoreTmaSmem = 200 * 1024;             // ring bytes at most
-
-// The store with its row reads on the TMA, for 16-byte-aligned rows: one persistent CTA per SM takes a contiguous
-// range of token groups. Lane 0 of warp 0 streams each group's rows (keys, then values) into a ring of shared-memory
-// stages with cp.async.bulk -- one copy per part when a part's rows are contiguous across tokens, else one per
-// token -- running up to `stages` groups ahead of the consumers, so the read stream never waits on the writes. The 8
-// consumer warps take a stage, load its tokens' slots (the next stage's while this one's rows are written), and
-// store each 16-byte vector to every destination as kvx_store_kernel does. Every wait is bounded (2 s): a stuck
-// stage records error 3 in the device word, and the producer waits (bounded) for its loads in flight before the
-// CTA exits.
-template <bool FAST>
-__global__ void __launch_bounds__(kStoreTmaThreads, 1)
-    kvx_store_tma(const __grid_constant__ StoreParams p, const uint32_t stages) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    extern __shared__ __align__(128) unsigned char ring[];
-    __shared__ __align__(8) uint64_t full[kStoreTmaMaxStages], empty[kStoreTmaMaxStages];
-    __shared__ int failed;
-
-    const uint32_t parts = p.value ? 2u : 1u;
-    const uint32_t vecs = (uint32_t)p.head_bytes / 16;
-    const uint32_t heads = (uint32_t)p.num_heads;
-    const uint32_t row_bytes = heads * (uint32_t)p.head_bytes;
-    const uint32_t per_token = parts * heads * vecs;
-    const bool packed = per_token <= (uint32_t)kStoreTmaConsumers;
-    const uint32_t tpp = packed ? kStoreTmaConsumers / per_token : 1;  // tokens side by side in a pass
-    const uint32_t group = tpp * kStoreTmaTokens;                         // tokens per stage
-    const uint32_t part_bytes = group * row_bytes;
-    const uint32_t stage_bytes = parts * part_bytes;
-    const uint32_t n = (uint32_t)p.num_tokens;
-    const uint32_t groups = (n + group - 1) / group;
-    const uint32_t g_begin = (uint32_t)((uint64_t)groups * blockIdx.x / gridDim.x);
-    const uint32_t mine = (uint32_t)((uint64_t)groups * (blockIdx.x + 1) / gridDim.x) - g_begin;
-
-    if (threadIdx.x == 0) {
-        for (uint32_t st = 0; st < stages; ++st) {
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[st])) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&empty[st])),
-                         "r"(kStoreTmaConsumers / 32)
-                         : "memory");
-        }
-        failed = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    if (mine == 0) return;
-    volatile int *stop = &failed;
-
-    if (threadIdx.x < 32) {  // the producer
-        if (threadIdx.x != 0) return;
-        uint32_t issued = 0;
-        for (uint32_t k = 0; k < mine; ++k) {
-            const uint32_t st = k % stages;
-            if (k >= stages &&
-                !mbar_wait(smem_u32(&empty[st]), ((k / stages) - 1) & 1, globaltimer() + kWaitLimitNs)) {
-                atomicCAS(&g_device_error, 0, 3);
-                *stop = 1;
-            }
-            if (*stop) break;
-            const uint32_t t0 = (g_begin + k) * group;
-            const uint32_t cnt = n - t0 < group ? n - t0 : group;
-            const uint32_t bar = smem_u32(&full[st]);
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                         "r"(parts * cnt * row_bytes)
-                         : "memory");
-            for (uint32_t part = 0; part < parts; ++part) {
-                const uint64_t row0 = part ? p.value : p.key;
-                const int64_t stride = part ? p.value_stride : p.key_stride;
-                const uint32_t dst = smem_u32(ring + (size_t)st * stage_bytes + part * part_bytes);
-                if (stride == (int64_t)row_bytes) {
-                    asm volatile(
-                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                            dst),
-                        "l"(row0 + (uint64_t)t0 * row_bytes), "r"(cnt * row_bytes), "r"(bar)
-                        : "memory");
-                } else {
-                    for (uint32_t u = 0; u < cnt; ++u)
-                        asm volatile(
-                            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
-                            "[%3];" ::"r"(dst + u * row_bytes),
-                            "l"(row0 + (uint64_t)(t0 + u) * stride), "r"(row_bytes), "r"(bar)
-                            : "memory");
-                }
-            }
-            issued = k + 1;
-        }
-        // No bulk load may still be writing shared memory when the CTA exits: wait (bounded) for the last load
-        // issued into each stage; consumers wait for every one in the normal course, so this returns at once.
-        const uint64_t drain = globaltimer() + kWaitLimitNs;
-        for (uint32_t k = issued > stages ? issued - stages : 0; k < issued; ++k)
-            if (!mbar_wait(smem_u32(&full[k % stages]), (k / stages) & 1, drain)) {
-                atomicCAS(&g_device_error, 0, 3);
-                break;
-            }
-        return;
-    }
-
-    // Consumers: fixed positions within a token's rows, as kvx_store_kernel.
-    const uint32_t ct = threadIdx.x - 32;
-    const uint32_t lane_token = packed ? ct / per_token : 0;
-    const bool active = lane_token < tpp;
-    int32_t slots_now[kStoreTmaTokens], slots_next[kStoreTmaTokens];
-#pragma unroll
-    for (int i = 0; i < kStoreTmaTokens; ++i) slots_next[i] = -1;
-    auto load_slots = [&](uint32_t k, int32_t *out) {
-        const uint32_t t0 = (g_begin + k) * group;
-#pragma unroll
-        for (int i = 0; i < kStoreTmaTokens; ++i) {
-            const uint32_t t = t0 + lane_token + (uint32_t)i * tpp;
-            out[i] = t < n ? load_slot(p.dests[0], t) : -1;
-        }
-    };
-    if (active) load_slots(0, slots_now);
-    for (uint32_t k = 0; k < mine; ++k) {
-        const uint32_t st = k % stages;
-        if (active && k + 1 < mine) load_slots(k + 1, slots_next);  // in flight while this stage is written
-        if (!mbar_wait(smem_u32(&full[st]), (k / stages) & 1, globaltimer() + kWaitLimitNs)) {
-            atomicCAS(&g_device_error, 0, 3);
-            *stop = 1;
-            return;
-        }
-        if (*stop) return;
-        const uint32_t t0 = (g_begin + k) * group;
-        if (active) {
-            const unsigned char *stage = ring + (size_t)st * stage_bytes;
-            for (uint32_t w = packed ? ct % per_token : ct; w < per_token; w += packed ? per_token : kStoreTmaConsumers) {
-                const uint32_t vec = w % vecs;
-                const int32_t head = (int32_t)((w / vecs) % heads);
-                const uint32_t part = w / (vecs * heads);
-                const uint32_t byte_in_row = vec * 16;
-                const unsigned char *src = stage + part * part_bytes + (uint32_t)head * (uint32_t)p.head_bytes + byte_in_row;
-                uint4 data[kStoreTmaTokens];
-#pragma unroll
-                for (int i = 0; i < kStoreTmaTokens; ++i) {
-                    const uint32_t u = lane_token + (uint32_t)i * tpp;
-                    if (t0 + u < n) data[i] = *reinterpret_cast<const uint4 *>(src + u * row_bytes);
-                }
-                const StoreLane lane0 = lane_of(p.dests[0], part, head, byte_in_row);
-                if (lane0.base) {
-#pragma unroll
-                    for (int i = 0; i < kStoreTmaTokens; ++i)
-                        put<16, FAST>(lane0, t0 + lane_token + (uint32_t)i * tpp < n ? slots_now[i] : -1, data[i]);
-                }
-                for (int d = 1; d < p.n_dests; ++d) {
-                    const StoreDest &dst = p.dests[d];
-                    if (head < dst.src_first_head || head >= dst.src_first_head + dst.num_heads) continue;
-                    int32_t slot[kStoreTmaTokens];
-#pragma unroll
-                    for (int i = 0; i < kStoreTmaTokens; ++i) {
-                        const uint32_t t = t0 + lane_token + (uint32_t)i * tpp;
-                        slot[i] = t < n ? resolve_slot(p, d, t, slots_now[i]) : -1;
-                    }
-#pragma unroll
-                    for (int i = 0; i < kStoreTmaTokens; ++i)
-                        store_row<16>(p, dst, slot[i], part, head, byte_in_row, data[i]);
-                }
-            }
-        }
-        __syncwarp();
-        if ((threadIdx.x & 31) == 0)
-            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
-#pragma unroll
-        for (int i = 0; i < kStoreTmaTokens; ++i) slots_now[i] = slots_next[i];
-    }
-}
-
 // ------------------------------------------------------------------------------------------------ host side
 
 struct DeviceInfo {
     int sms = 0;
     size_t tma_smem_set = 0;
     int store_ctas_per_sm[5][2] = {};  // resident kvx_store_kernel<16, 8, 4, 2, 1; FAST> CTAs per SM
-    int store_tma_smem_set = 0;
 };
 
 std::mutex g_mutex;
@@ -1280,34 +1107,13 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     cfg.attrs = &attr;
     cfg.numAttrs = (flags & KVX_STORE_SERIAL) ? 0 : 1;
 
-    // Destination 0 with a power-of-two block size and strides below 2^32, and row strides below 2^32: the kernels'
+    // Destination 0 with a power-of-two block size and strides below 2^32, and row strides below 2^32: the kernel's
     // address arithmetic then stays in 32-bit multiplies.
     const kvx_store_dest &d0 = dests[0];
     auto small = [](int64_t v) { return v >= 0 && v < ((int64_t)1 << 32); };
     const bool fast = p.dests[0].block_shift >= 0 && small(d0.block_stride) && small(d0.token_stride) &&
                       small(key_stride) && small(value_stride);
-    // Rows on the TMA when every address is 16-byte aligned and two stages of a token group fit.
     const uint32_t parts = value ? 2u : 1u;
-    const uint64_t per_token16 = vec == 16 ? (uint64_t)parts * num_heads * (head_bytes / 16) : 0;  // >= 1 if 16
-    const uint64_t tpp16 = per_token16 && per_token16 <= kStoreTmaConsumers ? kStoreTmaConsumers / per_token16 : 1;
-    const uint64_t stage_bytes = (uint64_t)parts * tpp16 * kStoreTmaTokens * num_heads * head_bytes;
-    if (vec == 16 && !(flags & KVX_STORE_LSU) && 2 * stage_bytes <= kStoreTmaSmem) {
-        if (info->store_tma_smem_set == 0) {
-            KVX_CUDA(cudaFuncSetAttribute(kvx_store_tma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)kStoreTmaSmem));
-            KVX_CUDA(cudaFuncSetAttribute(kvx_store_tma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)kStoreTmaSmem));
-            info->store_tma_smem_set = 1;
-        }
-        const uint32_t stages = (uint32_t)std::min<uint64_t>(kStoreTmaMaxStages, kStoreTmaSmem / stage_bytes);
-        const uint64_t groups = ((uint64_t)num_tokens + tpp16 * kStoreTmaTokens - 1) / (tpp16 * kStoreTmaTokens);
-        cfg.gridDim = dim3((unsigned)std::min<uint64_t>(groups, (uint64_t)sms));
-        cfg.blockDim = dim3(kStoreTmaThreads);
-        cfg.dynamicSmemBytes = stages * stage_bytes;
-        KVX_CUDA(cudaLaunchKernelEx(&cfg, fast ? kvx_store_tma<true> : kvx_store_tma<false>, p, stages));
-        g_launches.fetch_add(1, std::memory_order_relaxed);
-        return KVX_OK;
-    }
 
     int vi = 0;
     while ((16 >> vi) != vec) ++vi;

@@ -14,20 +14,6 @@ from tests.helpers import bits, from_bits
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["tma", "lsu"])
-def store_path(request, monkeypatch):
-    """Every test runs both store kernels: rows staged by the TMA (the default for 16-byte-aligned rows) and rows
-    read by the threads (KVX_STORE_LSU, and the fallback for any other alignment)."""
-    if request.param == "lsu":
-        from lean_vllm_b200._native import STORE_LSU
-        from lean_vllm_b200.attention import kvx_cache
-
-        real = kvx_cache._launch
-        monkeypatch.setattr(kvx_cache, "_launch", lambda key, value, heads, head_bytes, dests, stream, flags:
-                            real(key, value, heads, head_bytes, dests, stream, flags | STORE_LSU))
-    return request.param
-
-
 @pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
 @pytest.mark.parametrize("layout", ["NHD", "HND"])
 def test_the_store_matches_the_reference(golden, layout, slot_dtype):
@@ -180,8 +166,8 @@ def test_chained_stores_see_what_the_kernels_before_them_wrote(serial):
 
 @pytest.mark.parametrize("head_dim", [128, 12], ids=["aligned", "unaligned"])
 def test_rows_strided_across_tokens_store_like_contiguous_ones(head_dim):
-    """Keys and values as views into a wider per-token tensor (a fused qkv output): the TMA path copies each token's
-    row on its own; a 24-byte head row (12 bf16) is not 16-byte aligned and takes the thread-read kernel."""
+    """Keys and values as views into a wider per-token tensor (a fused qkv output), with 16-byte vectors and, for a
+    24-byte head row (12 bf16), 8-byte ones."""
     g = torch.Generator(device="cuda").manual_seed(9)
     tokens, heads, blocks, block = 777, 4, 16, 64
     qkv = torch.randn(tokens, 3 * heads, head_dim, generator=g, device="cuda").to(torch.bfloat16)
