@@ -1355,6 +1355,93 @@ def run_step_exchange(args) -> None:
     dist.destroy_process_group()
 
 
+def run_copy_engine(args) -> None:
+    """A copy-engine baseline for the transfer kernel: the same loads as one cudaMemcpyAsync per (layer, K|V, block)
+    chunk -- what a DMA transport such as the reference's NIXL/UCX path issues per descriptor row
+    (nixl_connector.py:404-420) -- on the decode GPU's stream, against one kvx_copy launch for the same jobs. Qwen3-8B
+    shape, the workload's first --requests requests (4 by default), destination on --peer-device (NVLink) or the same
+    GPU. Both are timed with CUDA events; the copy-engine line also reports the host time spent issuing."""
+    import ctypes
+    import glob
+
+    import torch
+
+    from lean_vllm_b200.kv_transfer import transport
+    from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
+
+    spec = WORKLOADS["pair"]
+    src_dev = torch.device("cuda", 0)
+    dst_dev = torch.device("cuda", args.peer_device) if args.peer_device is not None else src_dev
+    if dst_dev != src_dev and not transport.enable_peer_access(dst_dev.index, src_dev.index):
+        raise SystemExit(f"cuda:{dst_dev.index} cannot reach cuda:{src_dev.index} directly")
+    lengths, reqs, num_blocks = workload(args.seed, args.requests or 4, spec)
+    src = alloc_cache(spec, 1, num_blocks, src_dev, fill=True, seed=3)
+    dst = alloc_cache(spec, 1, num_blocks, dst_dev, fill=False, seed=0)
+    payload = sum(request_bytes(len(s), spec) for s, _ in reqs)
+    candidates = glob.glob(os.path.join(os.path.dirname(os.path.dirname(torch.__file__)), "nvidia", "cuda_runtime",
+                                        "lib", "libcudart.so*"))
+    cudart = ctypes.CDLL(candidates[0])
+    cudart.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                       ctypes.c_void_p]
+    cudart.cudaMemcpyAsync.restype = ctypes.c_int
+    chunk = spec.kv_heads * spec.block * spec.head_dim * 2
+    rows = []  # (dst address, src address) per chunk, block_descs order
+    for s_ids, d_ids in reqs:
+        for layer in range(spec.layers):
+            for part in range(2):
+                for s_id, d_id in zip(s_ids, d_ids):
+                    rows.append((dst[layer][part, int(d_id)].data_ptr(), src[layer][part, int(s_id)].data_ptr()))
+    torch.cuda.set_device(dst_dev)
+    stream = torch.cuda.Stream(device=dst_dev)
+
+    def ce():
+        for d, s_ in rows:
+            rc = cudart.cudaMemcpyAsync(d, s_, chunk, 4, stream.cuda_stream)  # cudaMemcpyDefault
+            if rc:
+                raise RuntimeError(f"cudaMemcpyAsync failed with {rc}")
+
+    tables = [CacheTable.from_tensors(dst), CacheTable.from_tensors(src)]
+    jobs = [CopyJob(1, 0, s, d, 0, 0, spec.kv_heads) for s, d in reqs]
+
+    def kvx():
+        transport.copy(tables, jobs, stream.cuda_stream)
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                fn()
+            stream.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                fn()
+            host = (time.perf_counter() - t0) * 1e3 / args.steps
+            end.record(stream)
+            stream.synchronize()
+            return start.elapsed_time(end) / args.steps, host
+
+    with ClockSampler(dst_dev.index) as clocks:
+        ms_ce, host_ce = timed(ce)
+        ms_kvx, host_kvx = timed(kvx)
+    ok = digest(dst, reqs[-1][1], 0, spec.kv_heads, False, dst_dev) == digest(src, reqs[-1][0], 0, spec.kv_heads,
+                                                                           False, src_dev)
+    line = {
+        "metric": "KV transfer GB/s: one cudaMemcpyAsync per chunk (copy engines) vs one kvx_copy launch",
+        "unit": "GB/s payload", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
+        "config": {"workload": f"{spec.name}/{len(reqs)}-requests", "payload_bytes": payload, "chunks": len(rows),
+                   "chunk_bytes": chunk, "path": "NVLink pull" if dst_dev != src_dev else "same GPU"},
+        "copy_engine": {"ms": round(ms_ce, 4), "gb_per_s": round(payload / (ms_ce * 1e-3) / 1e9, 1),
+                        "host_issue_ms": round(host_ce, 4),
+                        "host_us_per_memcpy": round(host_ce * 1e3 / len(rows), 3)},
+        "kvx_copy": {"ms": round(ms_kvx, 4), "gb_per_s": round(payload / (ms_kvx * 1e-3) / 1e9, 1),
+                     "host_issue_ms": round(host_kvx, 4), "launches": 1},
+        "clocks": clocks.summary(),
+        "correct": bool(ok),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -1419,6 +1506,8 @@ def main(argv=None):
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")
     p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
+    p.add_argument("--copy-engine", action="store_true",
+                   help="baseline: one cudaMemcpyAsync per chunk (copy engines) against one kvx_copy launch")
     p.add_argument("--step-exchange", action="store_true",
                    help="host only: kv_connector_step's per-step output exchange, gloo gather vs step mailbox")
     p.add_argument("--rates", default="1,4,16,64", help="arrival rates for --poisson, requests per second")
@@ -1428,6 +1517,8 @@ def main(argv=None):
         run_reference(args)
     elif args.step_exchange:
         run_step_exchange(args)
+    elif args.copy_engine:
+        run_copy_engine(args)
     elif args.poisson:
         run_poisson(args)
     elif args.staged:

@@ -38,6 +38,8 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "kvx.h"
 
 namespace {
@@ -63,6 +65,13 @@ int fail(int code, const char *fmt, ...) {
     } while (0)
 
 std::atomic<uint64_t> g_launches{0};
+
+// An NVTX range around each entry point that launches work, so a timeline (nsys, ncu's range view) shows which call
+// queued which kernels. Without a tool attached, NVTX calls are no-ops.
+struct Range {
+    explicit Range(const char *name) { nvtxRangePushA(name); }
+    ~Range() { nvtxRangePop(); }
+};
 
 // ------------------------------------------------------------------------------------------------ launch params
 
@@ -1001,6 +1010,7 @@ int kvx_enable_peer_access(int device, int peer, int *out_can_access) {
 }
 
 int kvx_copy(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags, void *stream) {
+    Range range("kvx_copy");
     return copy_impl(caches, n_caches, jobs, n_jobs, flags, static_cast<cudaStream_t>(stream));
 }
 
@@ -1015,6 +1025,7 @@ int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, in
 
 int kvx_pack(const kvx_cache *src, const int32_t *src_block_ids, int n_blocks, int first_head, int num_heads,
              int latents, void *staging, uint64_t staging_bytes, int flags, void *stream) {
+    Range range("kvx_pack");
     std::vector<kvx_region> regions;
     std::vector<int32_t> identity;
     if (int rc = staging_cache(src, n_blocks, num_heads, latents, (uint64_t)(uintptr_t)staging, staging_bytes,
@@ -1027,6 +1038,7 @@ int kvx_pack(const kvx_cache *src, const int32_t *src_block_ids, int n_blocks, i
 
 int kvx_scatter(const void *staging, uint64_t staging_bytes, const kvx_cache *dst, const int32_t *dst_block_ids,
                 int n_blocks, int first_head, int num_heads, int latents, int flags, void *stream) {
+    Range range("kvx_scatter");
     std::vector<kvx_region> regions;
     std::vector<int32_t> identity;
     if (int rc = staging_cache(dst, n_blocks, num_heads, latents, (uint64_t)(uintptr_t)staging, staging_bytes,
@@ -1038,6 +1050,7 @@ int kvx_scatter(const void *staging, uint64_t staging_bytes, const kvx_cache *ds
 }
 
 int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream) {
+    Range range("kvx_push");
     if (bytes == 0) return KVX_OK;
     if (!dst || !src) return fail(KVX_ERR_INVALID, "null pointer");
     const kvx_region a = {(uint64_t)(uintptr_t)src, bytes, 0}, b = {(uint64_t)(uintptr_t)dst, bytes, 0};
@@ -1049,6 +1062,7 @@ int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream
 
 int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t value_stride, int num_tokens,
               int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int flags, void *stream) {
+    Range range("kvx_store");
     if (!key || !dests) return fail(KVX_ERR_INVALID, "null rows or destinations");
     if (num_tokens < 0 || num_heads < 1 || head_bytes < 1)
         return fail(KVX_ERR_INVALID, "bad row shape: %d tokens, %d heads of %d bytes", num_tokens, num_heads,
@@ -1148,6 +1162,7 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
 
 int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
                  void *wait_event, void *stream, kvx_xfer_t *out) {
+    Range range("kvx_transfer");
     if (!out) return fail(KVX_ERR_INVALID, "null pointer");
     *out = nullptr;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
