@@ -808,7 +808,8 @@ def run_layerwise(args) -> None:
                 if saves:
                     producer.start_load_kv(KVConnectorMetadata(reqs_to_save={
                         ids[i]: ReqToSave(reqs[i][0].tolist(), reqs[i][1].tolist(), f"lw-decode-{role.group}",
-                                          "127.0.0.1", base_port + 8, 1) for i in step}))
+                                          "127.0.0.1", base_port + 8, 1, num_tokens=int(lengths[i])) for i in step},
+                        save_progress={ids[i]: int(lengths[i]) for i in step}))  # whole prompts in this step
                     if tag == "warm-b" and step is steps[0]:
                         # First contact maps the decode cache on the transfer thread (once per decode instance);
                         # every later save finds it mapped and is ready at once.

@@ -118,6 +118,7 @@ class ReqToSave:
     remote_tp_size: int = 1
     push_id: str | None = None
     cached_blocks: int = 0  # leading local blocks that were prefix-cache hits: no store of this prefill writes them
+    num_tokens: int | None = None  # the prompt's tokens (None: every block full), so the last block's end is known
 
 
 @dataclass(slots=True)
@@ -129,9 +130,14 @@ class KVConnectorMetadata:
     reqs_to_recv: dict[str, ReqToRecv] = field(default_factory=dict)
     reqs_to_send: dict[str, list[int]] = field(default_factory=dict)  # held blocks a decode instance may now read
     reqs_to_save: dict[str, ReqToSave] = field(default_factory=dict)
+    # Of each request being saved: how many prompt tokens have KV once this step's layers have run. A per-layer save
+    # pushes the blocks those tokens fill (a chunked prefill's later chunks push again what they add); without it,
+    # everything is pushed at hand-over.
+    save_progress: dict[str, int] = field(default_factory=dict)
 
     def __bool__(self):
-        return bool(self.reqs_to_recv) or bool(self.reqs_to_send) or bool(self.reqs_to_save)
+        return bool(self.reqs_to_recv) or bool(self.reqs_to_send) or bool(self.reqs_to_save) or \
+            bool(self.save_progress)
 
 
 @dataclass(slots=True)

@@ -90,6 +90,7 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
         self._reqs_to_recv: dict[str, ReqToRecv] = {}
         self._reqs_to_send: dict[str, list[int]] = {}
         self._reqs_to_save: dict[str, ReqToSave] = {}
+        self._saving: dict[str, object] = {}  # request -> its sequence while its prompt is prefilled under a save
 
     def get_num_new_matched_tokens(self, seq, num_computed_tokens: int) -> tuple[int, bool]:
         params = seq.kv_transfer_params
@@ -97,7 +98,9 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
             # A prefill whose decode instance waits for a push: its blocks are allocated now, so save them.
             blocks = list(seq.block_table[: _cdiv(seq.num_prompt_tokens, self.block_size)])
             self._reqs_to_save[seq.request_id] = ReqToSave(blocks, push_id=str(params["kv_push_id"]),
-                                                           cached_blocks=num_computed_tokens // self.block_size)
+                                                           cached_blocks=num_computed_tokens // self.block_size,
+                                                           num_tokens=seq.num_prompt_tokens)
+            self._saving[seq.request_id] = seq
             return 0, False
         if not params or not params.get("do_remote_prefill"):
             return 0, False
@@ -131,11 +134,20 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
         )
 
     def build_connector_meta(self) -> KVConnectorMetadata:
-        metadata = KVConnectorMetadata(self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save)
+        # Called once per step, after scheduling (engine/scheduler.py:147, 260-263): each saved prompt's tokens with
+        # KV once this step runs, so per-layer saves push exactly what the step's chunk fills.
+        progress = {}
+        for request_id, seq in list(self._saving.items()):
+            done = min(seq.num_cached_tokens + seq.num_scheduled_tokens, seq.num_prompt_tokens)
+            progress[request_id] = done
+            if done >= seq.num_prompt_tokens:
+                del self._saving[request_id]
+        metadata = KVConnectorMetadata(self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save, progress)
         self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save = {}, {}, {}
         return metadata
 
     def request_finished(self, seq) -> tuple[bool, dict | None]:
+        self._saving.pop(seq.request_id, None)
         params = seq.kv_transfer_params
         if not params or not params.get("do_remote_decode") or seq.finish_reason not in ("length", "stop"):
             return False, None  # only a prefill that ran to its token hands over; an abort ends here
@@ -198,7 +210,8 @@ class _Save:
     tables: list = field(default_factory=list)  # their caches, mapped here, aligned with targets
     ready: bool = False  # every target mapped
     failed: bool = False
-    pushed: set = field(default_factory=set)  # layers launched
+    progress: int | None = None  # prompt tokens with KV as of the latest step (None: unknown, push at hand-over)
+    layer_blocks: dict = field(default_factory=dict)  # layer -> leading blocks already pushed in their final state
     inflight: int = 0  # launches not yet landed
     handed_over: bool = False  # the prefill is over (engine thread): no more per-layer pushes
     finishing: bool = False  # what was left is queued (transfer thread): done once nothing is in flight
@@ -320,6 +333,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     save.ready = True
                     continue
             self._put(("connect", request_id))
+        progress = getattr(metadata, "save_progress", None)
+        if progress:
+            with self._lock:
+                for request_id, tokens in progress.items():
+                    save = self._saves.get(request_id)
+                    if save is not None:
+                        save.progress = int(tokens)
         if metadata.reqs_to_send:
             deadline = monotonic() + envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
             finishing = []
@@ -343,31 +363,37 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._put(("load", request_id, req, ready))
 
     def save_kv_layer(self, layer_index: int):
-        """Pushes layer `layer_index` of every request being saved whose decode ranks are mapped, in one launch on
-        the side stream after the layer's store (an event on the engine's stream), held to a few SMs."""
+        """Pushes layer `layer_index` of every request being saved whose decode ranks are mapped -- the blocks this
+        step's chunk filled (its metadata's save_progress), from the first one not yet pushed in its final state --
+        in one launch on the side stream after the layer's store (an event on the engine's stream), held to a few
+        SMs. A block a chunk leaves partly filled is pushed again with the next chunk."""
         with self._lock:
-            active = [s for s in self._saves.values()
-                      if s.ready and not s.failed and not s.handed_over and layer_index not in s.pushed
-                      and layer_index not in s.stored]
+            active = []
+            for s in self._saves.values():
+                if not s.ready or s.failed or s.handed_over or layer_index in s.stored or s.progress is None:
+                    continue
+                start, end, final = self._layer_span(s, layer_index)
+                if end > start:
+                    active.append((s, start, end))
+                    s.layer_blocks[layer_index] = final
+                    s.inflight += 1
             if not active:
                 return
-            for save in active:
-                save.pushed.add(layer_index)
-                save.inflight += 1
+        saves = [entry[0] for entry in active]
         try:
             tables, jobs = self._push_jobs(active)
             ready = self.transport.ready_marker()
             xfer = self.transport.post(tables, jobs, ready, layer=self.layer_regions[layer_index],
-                                       flags=self._save_flags())
+                                       flags=self._save_flags(), save=True)
         except Exception as error:  # noqa: BLE001 - a failed save fails its loads, never the step
             logger.warning("pushing layer %d failed: %s", layer_index, error)
             with self._lock:
-                for save in active:
+                for save in saves:
                     save.inflight -= 1
                     save.failed = True
             return
         with self._lock:
-            self._pushes.append((xfer, active))
+            self._pushes.append((xfer, saves))
 
     def wait_for_save(self):
         """Saves are ordered after their layers on the GPU and awaited on the transfer thread: nothing to do."""
@@ -424,13 +450,22 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 targets.append(((req.remote_host, req.remote_port + decode_rank), decode_rank, mine))
         return targets
 
-    def _push_jobs(self, saves: list[_Save], first_blocks: int | None = None) -> tuple[list, list]:
-        """Copy jobs for the saves' blocks (only their first `first_blocks` if given) to every target decode rank."""
+    def _layer_span(self, save: _Save, layer: int) -> tuple[int, int, int]:
+        """Lock held. For a per-layer push of `layer`: the blocks [start, end) the save's progress has filled and not
+        yet pushed in their final state, and how many leading blocks are final once they land."""
+        total = len(save.req.local_block_ids)
+        tokens = save.req.num_tokens if save.req.num_tokens is not None else total * self.block_size
+        done = min(save.progress, tokens)
+        end = min(_cdiv(done, self.block_size), total)
+        final = end if done >= tokens else min(done // self.block_size, total)
+        return save.layer_blocks.get(layer, 0), end, final
+
+    def _push_jobs(self, spans: list) -> tuple[list, list]:
+        """Copy jobs to every target decode rank for each (save, first block, end block) span."""
         tables, jobs = [], []
-        for save in saves:
-            local, remote = list(save.req.local_block_ids), list(save.req.remote_block_ids)
-            if first_blocks is not None:
-                local, remote = local[:first_blocks], remote[:first_blocks]
+        for save, start, end in spans:
+            local = list(save.req.local_block_ids)[start:end]
+            remote = list(save.req.remote_block_ids)[start:end]
             for (key, _, mine), table in zip(save.targets, save.tables):
                 tables.append(table)
                 k = len(tables)
@@ -844,24 +879,35 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 return
             if not save.failed and not save.ready:
                 return
-            layers = range(len(self.layer_regions))
-            missing = [] if save.failed else [i for i in layers if i not in save.pushed and i not in save.stored]
+            total = len(save.req.local_block_ids)
+            # What no per-layer push covered: each layer's blocks from its first one not pushed in its final state.
+            starts: dict[int, list] = {}
+            if not save.failed:
+                for layer in range(len(self.layer_regions)):
+                    if layer not in save.stored and save.layer_blocks.get(layer, 0) < total:
+                        starts.setdefault(save.layer_blocks.get(layer, 0), []).append(layer)
+                        save.layer_blocks[layer] = total
             # Fused stores wrote only this prefill's new rows: prefix-cache hits need a copy of their own.
             cached = 0
             if not save.failed and save.stored:
-                cached = min(save.req.cached_blocks, len(save.req.local_block_ids))
-            save.pushed.update(missing)
+                cached = min(save.req.cached_blocks, total)
             ready = save.ready_marker
-        posts = [(None, None)] if len(missing) == len(self.layer_regions) else [(layer, None) for layer in missing]
+        posts = []  # (layer or None for all, first block, end block)
+        for start, layers in sorted(starts.items()):
+            if len(layers) == len(self.layer_regions):
+                posts.append((None, start, total))  # one launch for every layer
+            else:
+                posts += [(layer, start, total) for layer in layers]
         if cached:
-            posts.append((None, cached))
-        for layer, first_blocks in posts if (missing or cached) else []:
+            posts.append((None, 0, cached))
+        missing = bool(starts)
+        for layer, start, end in posts:
             with self._lock:
                 save.inflight += 1
             try:
-                tables, jobs = self._push_jobs([save], first_blocks)
+                tables, jobs = self._push_jobs([(save, start, end)])
                 region = None if layer is None else self.layer_regions[layer]
-                xfer = self.transport.post(tables, jobs, ready, layer=region)
+                xfer = self.transport.post(tables, jobs, ready, layer=region, save=True)
             except Exception as error:  # noqa: BLE001
                 logger.warning("pushing the KV of %s failed: %s", request_id, error)
                 with self._lock:

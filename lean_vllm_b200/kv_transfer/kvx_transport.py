@@ -88,12 +88,13 @@ class KvxTransport:
         return transport.job_bytes(self._caches(self.local, tables, layer), jobs)
 
     def post(self, tables: list[CacheTable], jobs: list[CopyJob], ready, layer=None,
-             flags: int | None = None) -> transport.Transfer:
+             flags: int | None = None, save: bool = False) -> transport.Transfer:
         """One launch for all jobs, after `ready`, on a side stream. `layer` = (first region, region count)
-        restricts every cache to one layer's regions; such a per-layer save runs on the high-priority stream
-        with `flags` (its SM budget)."""
+        restricts every cache to one layer's regions. A push of a save (`save`) runs on the high-priority save
+        stream, in order with the save's earlier pushes (a block pushed again must land after its older copy);
+        `flags` holds a per-layer push to its SM budget."""
         event = ready.cuda_event if ready is not None else 0
-        stream = self.save_stream if flags is not None else self.stream
+        stream = self.save_stream if save else self.stream
         xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags)
         self.doorbell.ring_after(stream.cuda_stream)
@@ -102,7 +103,7 @@ class KvxTransport:
     def fence(self, ready) -> transport.Transfer:
         """A transfer of nothing that completes once `ready` has: what a save whose layers were all stored fused
         (on the engine's stream) waits for before its decode instance hears that every byte landed."""
-        return self.post([], [], ready)
+        return self.post([], [], ready, save=True)
 
     # The fused store-and-push (kvx_store), on the engine's stream.
 

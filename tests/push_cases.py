@@ -45,8 +45,9 @@ def run_push(producers, consumers, layers_to_save, decode_first: bool = True):
     if decode_first:
         for consumer in consumers:
             consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
-    for producer in producers:
-        producer.start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
+    for producer in producers:  # the whole prompt is computed in this step
+        producer.start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)},
+                                                   save_progress={"p-1": len(REMOTE) * BLOCK}))
     for producer in producers:
         assert wait_ready(producer)
     for layer in layers_to_save:  # as the engine would, after each layer's store
@@ -73,6 +74,7 @@ class Seq:
     kv_transfer_params: dict
     num_cached_tokens: int = 0
     finish_reason: str | None = None
+    num_scheduled_tokens: int = 0
 
 
 @dataclass
@@ -106,8 +108,9 @@ class Flow:
     def prefill_runs(self, push_id="push-1", blocks=(7, 2, 9), layers=(0,)):
         seq = Seq("p-1", len(blocks) * BLOCK, list(blocks), {"do_remote_decode": True, "kv_push_id": push_id})
         assert self.prefill_half.get_num_new_matched_tokens(seq, 0) == (0, False)
+        seq.num_scheduled_tokens = seq.num_prompt_tokens  # the engine schedules the whole prompt in this step
         meta = self.prefill_half.build_connector_meta()
-        assert "p-1" in meta.reqs_to_save
+        assert "p-1" in meta.reqs_to_save and meta.save_progress == {"p-1": seq.num_prompt_tokens}
         for p in self.producers:
             p.start_load_kv(meta)
         sleep(0.05)

@@ -140,3 +140,95 @@ def test_hooks_without_saves_launch_nothing(sides):
 
 def test_a_consumer_that_accepts_pushes_serves_handshakes(sides):
     assert sides.make("kv_consumer", 1, full_cache(1, False), accept_push=True)[0]._server is not None
+
+
+def test_a_chunked_prefill_pushes_what_each_chunk_fills_and_the_partial_block_again(sides):
+    """A prompt prefilled in three chunks (ending mid-block): each chunk's per-layer push copies the blocks that
+    chunk filled from the first one not yet final -- the partly filled block goes again with the next chunk -- and
+    the decode blocks end up equal to the prefill's final blocks, with nothing left for hand-over."""
+    from lean_vllm_b200.kv_transfer.base import ReqToSave
+    from tests.connector_cases import BLOCK
+
+    layers = [full_cache(50 + i, False) for i in range(2)]
+    producers = sides.make("kv_producer", 1, [t.clone() for t in layers])
+    consumers = sides.make("kv_consumer", 1, [full_cache(60 + i, False) for i in range(2)], engine_id="decode",
+                           accept_push=True)
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    kv = consumers[0].kv_transfer
+    tokens = 3 * BLOCK - 1  # the last block holds one token less
+    save = ReqToSave(list(REMOTE), list(LOCAL), kv.engine_id, kv.kv_ip, kv.kv_port, 1, num_tokens=tokens)
+    producer = producers[0]
+    chunks = [(0, BLOCK + 1), (BLOCK + 1, 2 * BLOCK + 1), (2 * BLOCK + 1, tokens)]  # each ends inside a block
+    for step, (begin, end) in enumerate(chunks):
+        meta = KVConnectorMetadata(reqs_to_save={"p-1": save} if step == 0 else {}, save_progress={"p-1": end})
+        producer.start_load_kv(meta)
+        if step == 0:
+            from tests.push_cases import wait_ready
+
+            assert wait_ready(producer)
+        for layer, cache in enumerate(producer.kv_caches):
+            # The chunk's rows land in the prefill's blocks (new values), then the layer's hook runs.
+            for position in range(begin, end):
+                block, offset = REMOTE[position // BLOCK], position % BLOCK
+                cache[:, block, :, offset] = float(100 * layer + position)
+            producer.save_kv_layer(layer)
+    posts = [p for p in producer.transport.posts]
+    producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(producer).finished_sending == {"p-1"}
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    assert producer.transport.posts == posts  # every layer's blocks were final after the last chunk: no catch-up
+    assert len(posts) == 3 * 2  # one per chunk per layer
+    for layer in range(2):
+        got, have = consumers[0].kv_caches[layer], producer.kv_caches[layer]
+        for i, (d, s) in enumerate(zip(LOCAL, REMOTE)):
+            rows = BLOCK if i < 2 else BLOCK - 1
+            assert torch.equal(got[:, d, :, :rows], have[:, s, :, :rows]), (layer, i)
+
+
+def test_without_progress_a_layer_hook_pushes_nothing_and_hand_over_pushes_everything(sides):
+    """Metadata that never says how far the prefill got (an engine whose scheduler half does not report it): the
+    per-layer hooks cannot know which blocks are final, so the whole request goes at hand-over, in one launch."""
+    producers = sides.make("kv_producer", 1, [full_cache(70 + i, False) for i in range(2)])
+    consumers = sides.make("kv_consumer", 1, [full_cache(80 + i, False) for i in range(2)], engine_id="decode",
+                           accept_push=True)
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
+    from tests.push_cases import wait_ready
+
+    assert wait_ready(producers[0])
+    for layer in range(2):
+        producers[0].save_kv_layer(layer)
+    assert producers[0].transport.posts == []
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    assert [layer for layer, _ in producers[0].transport.posts] == [None]
+    for layer in range(2):
+        assert torch.equal(consumers[0].kv_caches[layer][:, LOCAL], producers[0].kv_caches[layer][:, REMOTE])
+
+
+def test_a_layer_whose_last_chunk_was_not_hooked_is_finished_at_hand_over(sides):
+    """Layer 1's hook did not run for the second chunk: hand-over pushes that layer's blocks from the first one
+    not yet final; layer 0, complete, is not copied again."""
+    from lean_vllm_b200.kv_transfer.base import ReqToSave
+    from tests.connector_cases import BLOCK
+    from tests.push_cases import wait_ready
+
+    producers = sides.make("kv_producer", 1, [full_cache(90 + i, False) for i in range(2)])
+    consumers = sides.make("kv_consumer", 1, [full_cache(95 + i, False) for i in range(2)], engine_id="decode",
+                           accept_push=True)
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    kv = consumers[0].kv_transfer
+    producer = producers[0]
+    save = ReqToSave(list(REMOTE), list(LOCAL), kv.engine_id, kv.kv_ip, kv.kv_port, 1)
+    producer.start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save}, save_progress={"p-1": BLOCK + 3}))
+    assert wait_ready(producer)
+    producer.save_kv_layer(0)
+    producer.save_kv_layer(1)
+    producer.start_load_kv(KVConnectorMetadata(save_progress={"p-1": 3 * BLOCK}))
+    producer.save_kv_layer(0)  # layer 1's hook never runs for this chunk
+    producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    layer_posts = [layer for layer, _ in producer.transport.posts]
+    assert layer_posts == [(0, 2), (2, 2), (0, 2), (2, 2)]  # 2 hooks, 1 hook, then layer 1 at hand-over
+    for layer in range(2):
+        assert torch.equal(consumers[0].kv_caches[layer][:, LOCAL], producer.kv_caches[layer][:, REMOTE])

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from lean_vllm_b200.kv_transfer import KVConnectorMetadata
-from tests.connector_cases import Sides, full_cache, wait_for
+from tests.connector_cases import BLOCK, Sides, full_cache, wait_for
 from tests.helpers import bits, full_of
 from tests.push_cases import LOCAL, REMOTE, pushed_recv, run_push, save_req, wait_ready
 
@@ -54,7 +54,8 @@ def test_a_layer_is_pushed_only_after_its_store_on_the_engine_stream(sides):
     producers = sides.make("kv_producer", 1, full_cache(0, False))
     consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
     consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
-    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(consumers)},
+                                                   save_progress={"p-1": 3 * BLOCK}))
     assert wait_ready(producers[0])
     cache = producers[0].kv_caches[0]
     torch.cuda._sleep(50_000_000)  # the layer's attention, still running ...
@@ -107,7 +108,7 @@ def test_a_fused_store_lands_the_new_rows_in_the_decode_blocks_on_the_gpu(sides,
     blocks in one kvx_store launch; hand-over then has nothing left to copy."""
     from lean_vllm_b200.kv_transfer import ReqToRecv
     from lean_vllm_b200.kv_transfer.base import ReqToSave
-    from tests.connector_cases import BLOCK, HEAD_DIM, LATENT_DIM, NUM_HEADS
+    from tests.connector_cases import HEAD_DIM, LATENT_DIM, NUM_HEADS
 
     prefill, decode = full_cache(0, mla), full_cache(1, mla)
     producers = sides.make("kv_producer", prefill_tp, prefill)

@@ -65,6 +65,7 @@ class EngineConfig:
     tensor_parallel_size: int = 1
     speculative: object = None
     kv_cache_layout: str = "HND"
+    kvx_accept_push: bool = False
 
 
 def kv_row(token: int, position: int, layer: int, part: int) -> torch.Tensor:
@@ -87,8 +88,9 @@ class StubRunner:
 
     step_kind = "eager"
 
-    def __init__(self, config, caches):
+    def __init__(self, config, caches, layer_hooks=False):
         self.caches = caches
+        self.layer_hooks = layer_hooks  # call save_kv_layer after each layer's store, as an engine with hooks does
         self.worker = CudaIpcConnectorWorker(config, 0)
         self.worker.register_kv_caches(caches)
         self.kv_step = KVConnectorStep(self.worker, 0, 1)
@@ -104,11 +106,13 @@ class StubRunner:
         for seq in seqs:
             begin = seq.num_cached_tokens
             end = begin + seq.num_scheduled_tokens
-            for position in range(begin, end):
-                block, offset = seq.block_table[position // BLOCK], position % BLOCK
-                for layer, cache in enumerate(self.caches):
+            for layer, cache in enumerate(self.caches):
+                for position in range(begin, end):
+                    block, offset = seq.block_table[position // BLOCK], position % BLOCK
                     for part in range(2):
                         cache[part, block, :, offset, :] = kv_row(seq.token_ids[position], position, layer, part)
+                if self.layer_hooks:
+                    self.worker.save_kv_layer(layer)
             if end >= seq.num_planned_tokens:  # the scheduler's sampling rows: a finished prefill or a decode step
                 sampled.append(100 + len(seq.token_ids))
         return Tokens(sampled)
@@ -157,12 +161,12 @@ def engines(monkeypatch):
         monkeypatch.setattr(Sequence, name, getattr(Sequence, name))  # restored after the test
     made = []
 
-    def make(role, engine_id):
+    def make(role, engine_id, accept_push=False, layer_hooks=False, max_batched=256):
         kv = KVTransferConfig(kv_connector="CudaIpcConnector", kv_role=role, kv_ip="127.0.0.1", kv_port=free_port(),
                               engine_id=engine_id)
-        config = EngineConfig(kv)
+        config = EngineConfig(kv, kvx_accept_push=accept_push, max_num_batched_tokens=max_batched)
         caches = [torch.zeros(2, BLOCKS, HEADS, BLOCK, DIM, dtype=torch.bfloat16) for _ in range(LAYERS)]
-        engine = Engine(config, StubRunner(config, caches))
+        engine = Engine(config, StubRunner(config, caches, layer_hooks))
         made.append(engine)
         return engine
 
@@ -234,3 +238,49 @@ def test_a_load_from_an_absent_prefill_instance_prefills_on_the_decode_side(engi
         got = decode.model_runner.caches[layer][:, blocks].transpose(2, 3).reshape(2, 3 * BLOCK, HEADS, DIM)
         for position in (0, len(prompt) - 1):
             assert torch.equal(got[0, position], kv_row(prompt[position], position, layer, 0))
+
+
+@pytest.mark.parametrize("layer_hooks, chunk", [(False, 256), (True, 256), (True, 6)],
+                         ids=["at-hand-over", "per-layer", "per-layer-chunked"])
+def test_the_reference_engine_runs_a_pushed_request_with_its_block_ids_exchanged(engines, layer_hooks, chunk):
+    """Push mode through the same unmodified engine code: the proxy sends the decode request first (kv_push, no
+    block ids) and the prefill request with the same push id; the decode engine admits and waits while its worker
+    announces the allocated blocks; the prefill engine's scheduler half turns its admission into a save, and the
+    prefill writes the decode blocks (per layer from save_kv_layer, or all at hand-over) before freeing its own.
+    With a 6-token step budget the prompt is prefilled in chunks that end inside blocks: each chunk's hooks push
+    what it filled (the scheduler half reports each step's progress), and the result is the same."""
+    prefill = engines("kv_producer", "prefill-engine", layer_hooks=layer_hooks, max_batched=chunk)
+    decode = engines("kv_consumer", "decode-engine", accept_push=True)
+    prompt = [60 + (i * 7) % 40 for i in range(19)]
+    push_id = "push-7"
+    decode_params = {"do_remote_prefill": True, "kv_push": True, "remote_request_id": push_id,
+                     "remote_engine_id": "", "remote_host": "127.0.0.1",
+                     "remote_port": prefill.config.kv_transfer.kv_port, "tp_size": 1, "remote_block_ids": []}
+    assert ref_kv.check_kv_transfer_params(decode_params, decode.config.kv_transfer) is None  # the server accepts it
+    decode_seq = decode.add(prompt, SamplingParams(max_tokens=2, ignore_eos=True, kv_transfer_params=decode_params),
+                            "d-7")
+    decode.step()
+    assert decode_seq.status == SequenceStatus.WAITING_FOR_REMOTE_KVS
+    dst_blocks = list(decode_seq.block_table[:3])
+    prefill_params = {"do_remote_decode": True, "kv_push_id": push_id}
+    assert ref_kv.check_kv_transfer_params(prefill_params, prefill.config.kv_transfer) is None
+    prefill_seq = prefill.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True,
+                                                     kv_transfer_params=prefill_params), "p-7")
+    prefill.step()
+    src_blocks = list(prefill_seq.block_table[:3])
+    if chunk < len(prompt):  # let the first chunk's save find the decode ranks mapped before the next chunk runs
+        worker = prefill.model_runner.worker
+        deadline = time.monotonic() + 10
+        while not worker._saves["p-7"].ready and time.monotonic() < deadline:
+            time.sleep(0.002)
+    step_until([prefill, decode], lambda out: decode.is_finished() and prefill.is_finished())
+    if chunk < len(prompt):
+        posts = prefill.model_runner.worker.transport.posts
+        assert sum(1 for layer, _ in posts if layer is not None) >= 2 * LAYERS  # per-layer pushes of later chunks
+    assert decode_seq.is_finished and len(decode_seq.token_ids) == len(prompt) + 2
+    assert prefill.scheduler.block_manager.free_block_queue.num_free_blocks == BLOCKS
+    for layer in range(LAYERS):
+        src = prefill.model_runner.caches[layer][:, src_blocks].transpose(2, 3).reshape(2, 3 * BLOCK, HEADS, DIM)
+        dst = decode.model_runner.caches[layer][:, dst_blocks].transpose(2, 3).reshape(2, 3 * BLOCK, HEADS, DIM)
+        assert torch.equal(src[:, : len(prompt)].view(torch.int16), dst[:, : len(prompt)].view(torch.int16)), layer
+    assert decode.metrics.registry.get_sample_value("lean_vllm:kv_transfers_total") == 1.0
