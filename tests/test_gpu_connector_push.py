@@ -147,3 +147,37 @@ def test_a_fused_store_lands_the_new_rows_in_the_decode_blocks_on_the_gpu(sides,
         assert torch.equal(have[0].reshape(-1, LATENT_DIM)[slots.cpu()], key.cpu())
     else:
         assert torch.equal(have[0].transpose(1, 2).reshape(-1, NUM_HEADS, HEAD_DIM)[slots.cpu()], key.cpu())
+
+
+def test_a_chunked_prefill_lands_its_final_blocks_on_the_gpu(sides):
+    """Three chunks ending inside blocks, each written on the engine's stream behind a long kernel before its layer
+    hooks run: every chunk re-pushes the partly filled block on the save stream, in order, so the decode blocks
+    end equal to the prefill's final ones."""
+    from lean_vllm_b200.kv_transfer.base import ReqToSave
+
+    producers = sides.make("kv_producer", 1, [full_cache(50 + i, False) for i in range(2)])
+    consumers = sides.make("kv_consumer", 1, [full_cache(60 + i, False) for i in range(2)], engine_id="decode",
+                           accept_push=True)
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": pushed_recv(producers)}))
+    kv = consumers[0].kv_transfer
+    tokens = 3 * BLOCK - 1
+    save = ReqToSave(list(REMOTE), list(LOCAL), kv.engine_id, kv.kv_ip, kv.kv_port, 1, num_tokens=tokens)
+    producer = producers[0]
+    for step, (begin, end) in enumerate([(0, BLOCK + 1), (BLOCK + 1, 2 * BLOCK + 1), (2 * BLOCK + 1, tokens)]):
+        producer.start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save} if step == 0 else {},
+                                                   save_progress={"p-1": end}))
+        if step == 0:
+            assert wait_ready(producer)
+        for layer, cache in enumerate(producer.kv_caches):
+            torch.cuda._sleep(5_000_000)  # the layer's compute, still running when the hook is called
+            for position in range(begin, end):
+                cache[:, REMOTE[position // BLOCK], :, position % BLOCK] = float(100 * layer + position)
+            producer.save_kv_layer(layer)
+    producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(producer).finished_sending == {"p-1"}
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    for layer in range(2):
+        got, have = consumers[0].kv_caches[layer].cpu(), producer.kv_caches[layer].cpu()
+        for i, (d, s) in enumerate(zip(LOCAL, REMOTE)):
+            rows = BLOCK if i < 2 else BLOCK - 1
+            assert torch.equal(got[:, d, :, :rows], have[:, s, :, :rows]), (layer, i)
