@@ -1198,13 +1198,19 @@ def run_poisson(args) -> None:
     else:
         every = [results]
     if rank == 0:
-        rows = next(r for r in every if r)
+        pairs = [r for r in every if r]  # one list of rate rows per decode rank (per pair)
         line = {"metric": "KV transfer latency under Poisson arrivals (connector API)", "unit": "ms",
                 "higher_is_better": False, "n_gpus": world,
                 "config": {"workload": f"{spec.name}/{'loopback-1gpu' if world == 1 else 'pair'} poisson",
+                           "pairs": len(pairs),
                            "prompt_lengths": "log-normal, median 2048, sigma 1.0, clipped [128, 32768]",
                            "decode_pool_blocks": pool},
-                "rates": rows}
+                "rates": pairs[0]}
+        if len(pairs) > 1:  # every pair runs the same seeded arrivals at once: the spread shows any interference
+            line["p50_ms_by_pair"] = {str(row["rate_req_per_s"]): [p[i]["p50_ms"] for p in pairs]
+                                      for i, row in enumerate(pairs[0])}
+            line["p99_ms_by_pair"] = {str(row["rate_req_per_s"]): [p[i]["p99_ms"] for p in pairs]
+                                      for i, row in enumerate(pairs[0])}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
