@@ -595,7 +595,8 @@ def run_gpu(args) -> None:
                            "bytes_reported_by_connector": e2e_bytes,
                            "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
                                     "get_finished() until every load finished_recving; one kvx launch per load, "
-                                    "block ids carried in the launch, completion by event query")}
+                                    "block ids carried in the launch, the transfer thread woken by a doorbell when "
+                                    "each copy lands")}
         if loopback and not peer_mode and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(reqs, spec, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
