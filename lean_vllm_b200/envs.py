@@ -12,6 +12,10 @@ environment_variables: dict[str, Callable[[], Any]] = {
     # A decode (kv_consumer) rank also answers handshakes on kv_port + rank, so prefill ranks can push into it.
     "LEAN_VLLM_KVX_ACCEPT_PUSH": lambda: os.getenv("LEAN_VLLM_KVX_ACCEPT_PUSH", "0").strip().lower()
     not in ("", "0", "false"),
+    # A decode instance of several ranks loading MLA latents (replicated on every rank) splits the copy: each rank
+    # pulls 1/tp of the blocks from the prefill rank, then the rest from its peer decode ranks, so the prefill GPU
+    # sends each byte once. Its ranks then answer handshakes on kv_port + rank, as with ACCEPT_PUSH.
+    "LEAN_VLLM_KVX_RELAY": lambda: os.getenv("LEAN_VLLM_KVX_RELAY", "0").strip().lower() not in ("", "0", "false"),
     # SMs a per-layer save's copy may use while the prefill computes (0: every SM).
     "LEAN_VLLM_KVX_SAVE_SMS": lambda: int(os.getenv("LEAN_VLLM_KVX_SAVE_SMS", "16")),
 }

@@ -50,6 +50,7 @@ IDLE_WAIT = 0.01  # the transfer thread's longest sleep: deadlines are checked a
 BELL_WAIT = 0.001  # its sleep with copies in flight whose completion rings its doorbell (a safety net only)
 BUSY_WAIT = 0.0002  # and with copies in flight on a transport without a doorbell, which it must poll
 BATCH_BYTES = 64 << 20  # loads planned in one pass share a launch until they add up to this much
+RELAY_WAIT = 60.0  # seconds a relayed load waits for its peer decode ranks' parts before it fails
 
 
 def _cdiv(a: int, b: int) -> int:
@@ -189,6 +190,16 @@ class _Batch:
 
 
 @dataclass(slots=True)
+class _Relay:
+    """A relayed latent load on one decode rank: its part of the blocks from the prefill rank, the rest from the
+    other decode ranks of its instance once each has its own part."""
+
+    parts: list  # (first, end) block positions of each decode rank's part
+    transfer: _Batch | None = None  # the copy of the peers' parts
+    waiting_since: float = field(default_factory=monotonic)
+
+
+@dataclass(slots=True)
 class _Load:
     """One request's pull: one kernel launch over every share."""
 
@@ -199,6 +210,7 @@ class _Load:
     started: float = field(default_factory=monotonic)
     num_bytes: int = 0
     failed: bool = False
+    relay: _Relay | None = None
 
 
 @dataclass(slots=True)
@@ -251,6 +263,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self.tp_size = config.tensor_parallel_size
         self.block_size = config.kvcache_block_size
         self.accept_push = bool(getattr(config, "kvx_accept_push", False)) or envs.LEAN_VLLM_KVX_ACCEPT_PUSH
+        self.relay = bool(getattr(config, "kvx_relay", False)) or envs.LEAN_VLLM_KVX_RELAY
         self.kv_caches: list = []
         self.num_heads = 0  # every rank's key heads together; 0 for a latent-only model
         self.layout: dict = {}
@@ -276,6 +289,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._loads: dict[str, _Load] = {}  # transfer thread only
         self._waits: dict[str, _Wait] = {}  # transfer thread only
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
+        self._relays: dict[str, _Load] = {}  # transfer thread only: loads past their own part, waiting for peers'
+        self._parts: dict[str, dict] = {}  # request -> {decode rank: its part landed}; under the lock
         self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
         self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
         self._thread: threading.Thread | None = None
@@ -298,7 +313,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self.layout = {"block_size": self.block_size, "layers": layers}
         self.transport = make_transport(self.kv_caches)
         kv = self.kv_transfer
-        if kv.is_producer or self.accept_push:
+        if kv.is_producer or self.accept_push or (self.relay and self.tp_size > 1):
             port = kv.kv_port + self.rank
             server = self._context.socket(zmq.ROUTER)
             try:
@@ -554,7 +569,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if self._server is not None:
                 poller.register(self._server, zmq.POLLIN)
             while True:
-                busy = self._loads or self._pushes
+                busy = self._loads or self._pushes or self._relays
                 if self._queue.empty():
                     # Sleep until a load is queued, a message comes, or (doorbell) a copy lands.
                     wait = (BELL_WAIT if bell is not None else BUSY_WAIT) if busy else IDLE_WAIT
@@ -585,6 +600,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 if self._server is not None:
                     self._serve()
                 self._poll()
+                self._poll_relays()
                 self._poll_pushes()
                 self._poll_waits()
         except zmq.ContextTerminated:
@@ -602,6 +618,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         for xfer, _ in self._pushes:
             self.transport.wait(xfer)
             self.transport.release(xfer)
+        for load in self._relays.values():
+            if load.relay.transfer is not None:
+                self.transport.wait(load.relay.transfer.xfer)
+                self.transport.release(load.relay.transfer.xfer)
         for remote in self._remotes.values():
             self.transport.close(remote.exported)
             remote.sock.close()
@@ -649,6 +669,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 request_id = self._push_ids.get(push_id)
             if request_id is not None:
                 self._connect(request_id)
+            return
+        if op == "part":
+            with self._lock:
+                self._parts.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
+                    message.get("ok"))
             return
         if op == "saved":
             with self._lock:
@@ -707,6 +732,15 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             heads = self._heads(req)
             shares: list[Share] = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
             load.unnotified = {share.remote_rank for share in shares}
+            if self.relay and self.tp_size > 1 and self.num_heads == 0:
+                # Latents are whole on every decode rank: this rank pulls its part from the prefill rank and the
+                # others' parts from them, so each byte crosses the prefill GPU's links once.
+                n = len(req.local_block_ids)
+                load.relay = _Relay([(n * r // self.tp_size, n * (r + 1) // self.tp_size)
+                                     for r in range(self.tp_size)])
+                for peer in range(self.tp_size):
+                    if peer != self.rank:
+                        self._handshake(self._peer_req(), peer)
             jobs, tables = [], []
             for i, share in enumerate(shares):
                 remote = self._handshake(req, share.remote_rank)
@@ -719,6 +753,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 job = CopyJob(1, 0, req.remote_block_ids, req.local_block_ids, share.remote_head, share.local_head,
                               share.num_heads, i == 0)
                 nbytes = self.transport.job_bytes([remote.table], [job])
+                if load.relay is not None and i == 0:  # the whole payload counts; only this rank's part is read
+                    load.num_bytes += nbytes
+                    first, end = load.relay.parts[self.rank]
+                    job = CopyJob(1, 0, req.remote_block_ids[first:end], req.local_block_ids[first:end],
+                                  share.remote_head, share.local_head, share.num_heads, True)
+                    nbytes = 0 if end == first else self.transport.job_bytes([remote.table], [job])
+                    load.num_bytes -= nbytes
                 if nbytes == 0:
                     self._notify(key, message)  # nothing to read from this rank, but it must count this reader
                     load.unnotified.discard(share.remote_rank)
@@ -729,6 +770,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 load.notify.append((key, message, share.remote_rank))
                 load.num_bytes += nbytes
             load.started = monotonic()
+            if not jobs and load.relay is not None:
+                del self._loads[request_id]
+                self._part_landed(request_id, load)  # an empty part: straight to the peers' parts
+                return
             if jobs:
                 batch.append((load, tables, jobs, ready))
                 # Launch as soon as the batch is big enough to keep the GPU busy while the next loads are planned;
@@ -786,13 +831,90 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                         self._notify(key, message)
                         load.unnotified.discard(remote_rank)
             del self._loads[request_id]
+            if load.relay is not None and not load.failed:
+                self._part_landed(request_id, load)
+                continue
+            self._finish_load(request_id, load)
+
+    def _finish_load(self, request_id: str, load: _Load):
+        if load.relay is not None:
+            if load.failed:
+                self._send_part(request_id, False)  # the peers' loads fail too, and prefill as this one does
             with self._lock:
-                if load.failed:
-                    self._finished.failed_recving.add(request_id)
+                self._parts.pop(request_id, None)
+        with self._lock:
+            if load.failed:
+                self._finished.failed_recving.add(request_id)
+            else:
+                self._finished.finished_recving.add(request_id)
+                self._finished.recv_stats[request_id] = KVTransferStats(monotonic() - load.started, load.num_bytes)
+
+    # Relay: a decode rank's own part landed; the other parts come from its peer decode ranks.
+
+    def _peer_req(self):
+        """A peer decode rank of this instance as _handshake addresses a producer."""
+        kv = self.kv_transfer
+        return ReqToRecv([], [], "", kv.engine_id, kv.kv_ip, kv.kv_port, self.tp_size)
+
+    def _send_part(self, request_id: str, ok: bool):
+        kv = self.kv_transfer
+        for peer in range(self.tp_size):
+            if peer != self.rank:
+                self._send((kv.kv_ip, kv.kv_port + peer), {"op": "part", "request": request_id, "rank": self.rank,
+                                                             "ok": ok})
+
+    def _part_landed(self, request_id: str, load: _Load):
+        self._send_part(request_id, True)
+        load.relay.waiting_since = monotonic()
+        self._relays[request_id] = load
+
+    def _poll_relays(self):
+        timeout = RELAY_WAIT
+        kv = self.kv_transfer
+        for request_id, load in list(self._relays.items()):
+            relay = load.relay
+            if relay.transfer is None:
+                with self._lock:
+                    got = dict(self._parts.get(request_id, {}))
+                peers = [r for r in range(self.tp_size) if r != self.rank]
+                if any(got.get(r) is False for r in peers):
+                    load.failed = True
+                    logger.warning("a peer decode rank could not load its part of %s, so it prefills here",
+                                   load.req.remote_request_id)
+                elif all(r in got for r in peers):
+                    tables, jobs = [], []
+                    local = list(load.req.local_block_ids)
+                    for r in peers:
+                        first, end = relay.parts[r]
+                        if end > first:
+                            tables.append(self._remotes[(kv.kv_ip, kv.kv_port + r)].table)
+                            jobs.append(CopyJob(len(tables), 0, local[first:end], local[first:end], 0, 0, 0, True))
+                    if jobs:
+                        try:
+                            relay.transfer = _Batch(self.transport.post(tables, jobs, None), 1)
+                            continue
+                        except Exception as error:  # noqa: BLE001
+                            logger.warning("copying the peers' parts of %s failed: %s", load.req.remote_request_id,
+                                           error)
+                            load.failed = True
+                elif relay.waiting_since + timeout < monotonic():
+                    load.failed = True
+                    logger.warning("the peer decode ranks never reported their parts of %s",
+                                   load.req.remote_request_id)
                 else:
-                    self._finished.finished_recving.add(request_id)
-                    self._finished.recv_stats[request_id] = KVTransferStats(monotonic() - load.started,
-                                                                           load.num_bytes)
+                    continue
+            else:
+                try:
+                    if not self.transport.done(relay.transfer.xfer):
+                        continue
+                except Exception as error:  # noqa: BLE001
+                    logger.warning("copying the peers' parts of %s failed in flight: %s", load.req.remote_request_id,
+                                   error)
+                    load.failed = True
+                self.transport.release(relay.transfer.xfer)
+                relay.transfer = None
+            del self._relays[request_id]
+            self._finish_load(request_id, load)
 
     def _send(self, key, message: dict):
         remote = self._remotes.get(key)
@@ -808,6 +930,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
 
     def _fail(self, load: _Load, error: Exception, in_flight: bool = False):
         req = load.req
+        if load.relay is not None and not load.failed:
+            request_id = next((rid for rid, entry in self._loads.items() if entry is load), None)
+            if request_id is not None:
+                self._send_part(request_id, False)
         if not load.failed:
             logger.warning("loading the KV of %s from %s:%d failed, so it prefills here: %s",
                            req.remote_request_id, req.remote_host, req.remote_port, error)
