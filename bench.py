@@ -296,6 +296,27 @@ def plan(spec: Workload, role: Role, reqs, mode: str):
     return peers, jobs
 
 
+def plan_relay(spec: Workload, role: Role, reqs):
+    """A decode rank's relayed latent load (LEAN_VLLM_KVX_RELAY): (peers, its own part of every request's blocks
+    from the prefill rank, the other decode ranks' parts from them). Parts are contiguous 1/decode_tp slices of each
+    request's blocks, as the connector cuts them."""
+    from lean_vllm_b200.kv_transfer.transport import CopyJob
+
+    peers = [("prefill", 0)] + [("decode", r) for r in range(spec.decode_tp) if r != role.tp_rank]
+    own, others = [], []
+    for s, d in reqs:
+        n = len(d)
+        cut = [n * r // spec.decode_tp for r in range(spec.decode_tp + 1)]
+        me = role.tp_rank
+        if cut[me + 1] > cut[me]:
+            own.append(CopyJob(1, 0, s[cut[me] : cut[me + 1]], d[cut[me] : cut[me + 1]], 0, 0, 0, True))
+        for r in range(spec.decode_tp):
+            if r != me and cut[r + 1] > cut[r]:
+                k = 1 + peers.index(("decode", r))
+                others.append(CopyJob(k, 0, d[cut[r] : cut[r + 1]], d[cut[r] : cut[r + 1]], 0, 0, 0, True))
+    return peers, own, others
+
+
 def alloc_cache(spec: Workload, tp: int, num_blocks: int, device, fill: bool, seed: int):
     import torch
 
@@ -421,8 +442,17 @@ def run_gpu(args) -> None:
         return CacheTable(out, nb)
 
     # Jobs: one per (request, share) on the launching rank; its peers' caches mapped over CUDA IPC.
-    peers, jobs = plan(spec, role, reqs, args.mode)
-    launching = bool(jobs)
+    relay = args.relay and spec.mla and spec.decode_tp > 1 and not loopback
+    if args.relay and not relay:
+        raise SystemExit("--relay applies to the MLA workload's decode ranks (--workload mla, N >= 3)")
+    relay_jobs = []
+    if relay and role.side == "decode":
+        peers, jobs, relay_jobs = plan_relay(spec, role, reqs)
+    elif relay:
+        peers, jobs = [], []
+    else:
+        peers, jobs = plan(spec, role, reqs, args.mode)
+    launching = bool(jobs) or bool(relay_jobs)
     if loopback:
         caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
     elif launching:
@@ -431,13 +461,19 @@ def run_gpu(args) -> None:
                                                    for side, tp_rank in peers]
     else:
         caches = []
-    my_bytes = transport.job_bytes(caches, jobs) if jobs else 0
+    my_bytes = (transport.job_bytes(caches, jobs) if jobs else 0) + \
+        (transport.job_bytes(caches, relay_jobs) if relay_jobs else 0)
     stream = torch.cuda.Stream(device=launch_device)
     sid = stream.cuda_stream
 
     def step():
         if jobs:
             transport.copy(caches, jobs, sid, copy_flags)
+        if relay:  # every decode rank's own part has landed before any rank copies it onward
+            stream.synchronize()
+            dist.barrier(group=gloo)
+            if relay_jobs:
+                transport.copy(caches, relay_jobs, sid, copy_flags)
 
     def barrier():
         torch.cuda.synchronize()
@@ -541,6 +577,8 @@ def run_gpu(args) -> None:
             egress = per_group / spec.prefill_tp  # TP splits heads evenly; latents: each decode rank pulls whole
             if spec.mla:
                 egress = per_group  # one producer feeds every decode rank a whole copy
+                if relay:  # ... or, relayed, each byte once; every decode rank still takes a whole copy in
+                    egress = per_group / spec.decode_tp
             ingress = per_group / spec.decode_tp
             link_bytes = max(egress, ingress)
             achieved = link_bytes / (ms_per_step * 1e-3) / 1e9
@@ -576,7 +614,7 @@ def run_gpu(args) -> None:
                 "blocks_per_step_per_group": step_blocks,
                 "payload_bytes_per_step": int(step_bytes_total),
                 "groups": groups,
-                "mode": "loopback" if loopback else args.mode,
+                "mode": "loopback" if loopback else args.mode + (" relayed" if relay else ""),
                 "engine": args.engine,
                 "parallelism": ("1 GPU" if loopback else
                                 f"{groups} independent prefill TP{spec.prefill_tp} -> decode TP{spec.decode_tp} groups"),
@@ -623,6 +661,7 @@ def e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo):
         tensor_parallel_size: int = 1
         kvcache_block_size: int = spec.block
         kv_cache_layout: str = "HND"
+        kvx_relay: bool = bool(args.relay)
 
     base_port = args.kv_port + 16 * role.group
     producer_worker = consumer_worker = None
@@ -1514,6 +1553,8 @@ def main(argv=None):
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")
     p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
+    p.add_argument("--relay", action="store_true",
+                   help="MLA workload: each decode rank pulls its part from the prefill rank, the rest from its peers")
     p.add_argument("--copy-engine", action="store_true",
                    help="baseline: one cudaMemcpyAsync per chunk (copy engines) against one kvx_copy launch")
     p.add_argument("--step-exchange", action="store_true",

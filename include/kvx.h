@@ -103,6 +103,8 @@ int kvx_ipc_export(const void *ptr, kvx_ipc_handle *out);
 
 /* Maps a peer's exported allocation into this process on the current device and returns the exported pointer's
  * address here. Reference-counted per allocation: a second open of the same allocation returns the same mapping.
+ * An allocation of this process is returned as is, with peer access from the current device enabled when it
+ * lives on another device (refused if the two cannot reach each other directly).
  * Replaces agent.add_remote_agent (nixl_connector.py:510). */
 int kvx_ipc_open(const kvx_ipc_handle *handle, void **out_ptr);
 

@@ -947,12 +947,18 @@ int kvx_ipc_export(const void *ptr, kvx_ipc_handle *out) {
 
 int kvx_ipc_open(const kvx_ipc_handle *h, void **out_ptr) {
     if (!h || !out_ptr) return fail(KVX_ERR_INVALID, "null pointer");
+    int dev;
+    KVX_CUDA(cudaGetDevice(&dev));
     if (h->pid == (int32_t)getpid()) {  // our own allocation: CUDA IPC cannot reopen it, and need not
+        if (h->device != dev) {  // ... but a kernel on this device reaches it only with peer access on
+            int can = 0;
+            if (int rc = kvx_enable_peer_access(dev, h->device, &can)) return rc;
+            if (!can)
+                return fail(KVX_ERR_INVALID, "device %d cannot reach device %d's memory directly", dev, h->device);
+        }
         *out_ptr = reinterpret_cast<void *>(h->ptr);
         return KVX_OK;
     }
-    int dev;
-    KVX_CUDA(cudaGetDevice(&dev));
     const auto key = std::make_pair(dev, std::string(reinterpret_cast<const char *>(h->handle), 64));
     std::lock_guard<std::mutex> lock(g_mutex);
     auto it = g_mappings.find(key);

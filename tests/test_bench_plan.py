@@ -113,3 +113,39 @@ def test_workload_draws_are_seeded_and_prefix_stable():
     ids = np.concatenate([s for s, _ in a[1]])
     assert len(set(ids.tolist())) == len(ids) and ids.max() < a[2]  # distinct source blocks inside the cache
     assert bench.request_bytes(32) == bench.BYTES_8K_REQUEST
+
+
+@pytest.mark.parametrize("world", [3, 8])
+def test_a_relayed_mla_load_lands_every_block_on_every_decode_rank(world):
+    """--relay: each decode rank's own part from the prefill rank, then (after every rank's part landed) the others'
+    parts from its peers; every decode rank ends with every requested latent block, the prefill rank sends each
+    block once."""
+    spec = tiny(bench.WORKLOADS["mla"])
+    _, reqs, num_blocks = bench.workload(3, None, spec)
+    roles = [bench.role_of(r, world, spec) for r in range(world)]
+    groups = world // spec.group_size
+
+    def rank_of(group, side, tp_rank):
+        return group * spec.group_size + (tp_rank if side == "prefill" else spec.prefill_tp + tp_rank)
+
+    mem = {rank: caches(spec, 1, num_blocks, seed=rank) for rank, role in enumerate(roles) if role.side != "idle"}
+    before = {rank: [a.copy() for a in layers] for rank, layers in mem.items()}
+    plans = {rank: bench.plan_relay(spec, role, reqs) for rank, role in enumerate(roles) if role.side == "decode"}
+    sent_from_prefill = 0
+    for phase in (1, 2):
+        for rank, (peers, own, others) in plans.items():
+            role = roles[rank]
+            for job in own if phase == 1 else others:
+                tables = [mem[rank]] + [mem[rank_of(role.group, side, tp)] for side, tp in peers]
+                apply(job, tables[job.src], tables[job.dst], True)
+                sent_from_prefill += len(job.src_block_ids) if phase == 1 else 0
+    assert sent_from_prefill == groups * sum(len(d) for _, d in reqs)  # each block leaves the prefill GPU once
+    for group in range(groups):
+        prefill = before[rank_of(group, "prefill", 0)]
+        for r in range(spec.decode_tp):
+            rank = rank_of(group, "decode", r)
+            for layer in range(spec.layers):
+                want = before[rank][layer].copy()
+                for s, d in reqs:
+                    want[:, d] = prefill[layer][:, s]
+                assert np.array_equal(mem[rank][layer], want), (group, r, layer)

@@ -159,3 +159,48 @@ def test_a_load_between_processes_on_different_gpus(golden, prefill_tp, decode_t
             proc.join(timeout=60)
             if proc.is_alive():
                 proc.kill()
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("decode_tp", [2, 4])
+def test_a_relayed_latent_load_between_processes(golden, monkeypatch, decode_tp):
+    """LEAN_VLLM_KVX_RELAY with the producer in a spawned process and the decode ranks on their own GPUs: each
+    decode rank pulls its part of the latent blocks from the producer over CUDA IPC, then the others' parts from its
+    peer decode ranks (in this process: peer access, no IPC), and lands what the reference's pull lands."""
+    if gpu_count() < 1 + decode_tp:
+        pytest.skip(f"needs {1 + decode_tp} GPUs")
+    monkeypatch.setenv("LEAN_VLLM_KVX_RELAY", "1")
+    _, arrays = golden
+    kv_port, decode_port = free_port(), free_port()
+    ctx = mp.get_context("spawn")
+    parent, child = ctx.Pipe()
+    proc = ctx.Process(target=_producer, args=(child, 0, kv_port, 1, 0, True))
+    proc.start()
+    consumers = []
+    try:
+        assert parent.poll(120) and parent.recv() == "ready"
+        for rank in range(decode_tp):
+            device = 1 + rank
+            torch.cuda.set_device(device)
+            kv = KVTransferConfig(kv_connector="CudaIpcConnector", kv_role="kv_consumer", kv_port=decode_port,
+                                  engine_id="decode")
+            worker = CudaIpcConnectorWorker(WorkerConfig(kv, tensor_parallel_size=decode_tp), rank)
+            worker.register_kv_caches([rank_cache(full_cache(1, True), rank, decode_tp).to(device)])
+            consumers.append(worker)
+        from lean_vllm_b200.kv_transfer import ReqToRecv
+
+        for worker in consumers:
+            torch.cuda.set_device(worker.kv_caches[0].device)
+            worker.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": ReqToRecv(
+                [0, 5, 3], [7, 2, 9], "p-1", "engine", "127.0.0.1", kv_port, 1)}))
+        outputs = [wait_for(w, timeout=60) for w in consumers]
+        assert KVOutputAggregator(decode_tp).aggregate(outputs).finished_recving == {"d-1"}
+        got = full_of([w.kv_caches[0].cpu() for w in consumers], True)
+        assert np.array_equal(bits(got), arrays[f"small_lat_tp1to{decode_tp}"])
+        assert parent.poll(60) and parent.recv() == "sent"
+    finally:
+        for worker in consumers:
+            worker.shutdown()
+        proc.join(timeout=60)
+        if proc.is_alive():
+            proc.kill()
