@@ -296,6 +296,14 @@ def plan(spec: Workload, role: Role, reqs, mode: str):
     return peers, jobs
 
 
+RELAY_CHUNKS = 8  # request chunks a relayed step is pipelined over
+
+
+def relay_chunk_count(n_requests: int) -> int:
+    """How many request chunks a relayed step has: every rank takes one barrier per chunk, so all must agree."""
+    return len(range(0, n_requests, max(1, -(-n_requests // RELAY_CHUNKS))))
+
+
 def plan_relay(spec: Workload, role: Role, reqs):
     """A decode rank's relayed latent load (LEAN_VLLM_KVX_RELAY): (peers, its own part of every request's blocks
     from the prefill rank, the other decode ranks' parts from them). Parts are contiguous 1/decode_tp slices of each
@@ -446,8 +454,14 @@ def run_gpu(args) -> None:
     if args.relay and not relay:
         raise SystemExit("--relay applies to the MLA workload's decode ranks (--workload mla, N >= 3)")
     relay_jobs = []
+    relay_chunks = []  # (own-part jobs, peer-part jobs) per chunk of the step's requests
     if relay and role.side == "decode":
-        peers, jobs, relay_jobs = plan_relay(spec, role, reqs)
+        chunk = max(1, -(-len(reqs) // RELAY_CHUNKS))
+        for first in range(0, len(reqs), chunk):
+            peers, own, others = plan_relay(spec, role, reqs[first : first + chunk])
+            relay_chunks.append((own, others))
+        jobs = [j for own, _ in relay_chunks for j in own]
+        relay_jobs = [j for _, others in relay_chunks for j in others]
     elif relay:
         peers, jobs = [], []
     else:
@@ -465,15 +479,25 @@ def run_gpu(args) -> None:
         (transport.job_bytes(caches, relay_jobs) if relay_jobs else 0)
     stream = torch.cuda.Stream(device=launch_device)
     sid = stream.cuda_stream
+    peer_stream = torch.cuda.Stream(device=launch_device)  # relayed: the copies from peer decode ranks
 
     def step():
-        if jobs:
-            transport.copy(caches, jobs, sid, copy_flags)
-        if relay:  # every decode rank's own part has landed before any rank copies it onward
-            stream.synchronize()
-            dist.barrier(group=gloo)
-            if relay_jobs:
-                transport.copy(caches, relay_jobs, sid, copy_flags)
+        if not relay:
+            if jobs:
+                transport.copy(caches, jobs, sid, copy_flags)
+            return
+        # Pipelined by chunks of requests: a chunk's parts go from the peers (second stream) once every decode
+        # rank's own part of it landed (host barrier), while the next chunk's own parts come from the prefill rank.
+        chunks = relay_chunks or [([], [])] * relay_chunk_count(len(reqs))
+        for c in range(len(chunks) + 1):
+            if c:
+                stream.synchronize()
+                dist.barrier(group=gloo)
+            if c < len(chunks) and chunks[c][0]:
+                transport.copy(caches, chunks[c][0], sid, copy_flags)
+            if c and chunks[c - 1][1]:
+                transport.copy(caches, chunks[c - 1][1], peer_stream.cuda_stream, copy_flags)
+        stream.wait_stream(peer_stream)  # the step ends when both streams have
 
     def barrier():
         torch.cuda.synchronize()

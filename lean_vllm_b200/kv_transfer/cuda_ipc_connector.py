@@ -891,7 +891,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                             jobs.append(CopyJob(len(tables), 0, local[first:end], local[first:end], 0, 0, 0, True))
                     if jobs:
                         try:
-                            relay.transfer = _Batch(self.transport.post(tables, jobs, None), 1)
+                            # Its own part landed after the load's ready event, so the blocks are free to write.
+                            relay.transfer = _Batch(self.transport.post(tables, jobs, None, relay=True), 1)
                             continue
                         except Exception as error:  # noqa: BLE001
                             logger.warning("copying the peers' parts of %s failed: %s", load.req.remote_request_id,

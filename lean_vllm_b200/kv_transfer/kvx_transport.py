@@ -37,6 +37,8 @@ class KvxTransport:
             self.stream = torch.cuda.Stream(device=self.device)
             # Per-layer saves go first when SMs free up between the prefill's kernels.
             self.save_stream = torch.cuda.Stream(device=self.device, priority=-10)
+            # A relayed load's copy from peer decode ranks runs beside the next loads' copies from the producer.
+            self.relay_stream = torch.cuda.Stream(device=self.device)
         # Rung after every post: the transfer thread sleeps on it instead of polling copies in flight.
         self.doorbell = transport.Doorbell()
         # One IPC handle per layer tensor; each region as (tensor, byte offset in it, block bytes, head bytes).
@@ -88,13 +90,14 @@ class KvxTransport:
         return transport.job_bytes(self._caches(self.local, tables, layer), jobs)
 
     def post(self, tables: list[CacheTable], jobs: list[CopyJob], ready, layer=None,
-             flags: int | None = None, save: bool = False) -> transport.Transfer:
+             flags: int | None = None, save: bool = False, relay: bool = False) -> transport.Transfer:
         """One launch for all jobs, after `ready`, on a side stream. `layer` = (first region, region count)
         restricts every cache to one layer's regions. A push of a save (`save`) runs on the high-priority save
         stream, in order with the save's earlier pushes (a block pushed again must land after its older copy);
-        `flags` holds a per-layer push to its SM budget."""
+        `flags` holds a per-layer push to its SM budget. A relayed load's copy from its peers (`relay`) runs on a
+        stream of its own, beside later loads' copies from the producer."""
         event = ready.cuda_event if ready is not None else 0
-        stream = self.save_stream if save else self.stream
+        stream = self.save_stream if save else self.relay_stream if relay else self.stream
         xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags)
         self.doorbell.ring_after(stream.cuda_stream)

@@ -89,7 +89,7 @@ class HostTransport:
     def job_bytes(self, tables, jobs, layer=None):
         return sum(n for (_, n), _ in self._pairs(tables, jobs, layer))
 
-    def post(self, tables, jobs, ready, layer=None, flags=None, save=False):
+    def post(self, tables, jobs, ready, layer=None, flags=None, save=False, relay=False):
         if HostTransport.fail == "posted":
             raise RuntimeError("the transport refused the copy")
         for (dst, n), (src, _) in list(self._pairs(tables, jobs, layer)):
