@@ -396,7 +396,9 @@ def run_gpu(args) -> None:
         gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
 
     engine = {"auto": ENGINE_AUTO, "lsu": ENGINE_LSU, "tma": ENGINE_TMA}[args.engine]
-    copy_flags = flags(engine, args.tile_bytes, args.ctas_per_sm)
+    # Relayed: the copies from the prefill rank and from the peers run at once on two streams, half the SMs each.
+    relay_sms = torch.cuda.get_device_properties(local_rank).multi_processor_count // 2 if args.relay else 0
+    copy_flags = flags(engine, args.tile_bytes, args.ctas_per_sm, relay_sms)
     lengths, reqs, num_blocks = workload(args.seed, args.requests, spec)
     step_blocks = sum(len(s) for s, _ in reqs)
     heads = split_heads(spec.kv_heads, spec.decode_tp, spec.prefill_tp)

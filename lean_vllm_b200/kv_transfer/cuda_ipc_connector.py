@@ -312,6 +312,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         # What a peer must match: every rank's heads together, so the two sides may split them differently.
         self.layout = {"block_size": self.block_size, "layers": layers}
         self.transport = make_transport(self.kv_caches)
+        if self.relay and self.tp_size > 1 and self.num_heads == 0 and hasattr(self.transport, "split_sms"):
+            self.transport.split_sms()  # relayed latent loads copy on two streams at once
         kv = self.kv_transfer
         if kv.is_producer or self.accept_push or (self.relay and self.tp_size > 1):
             port = kv.kv_port + self.rank

@@ -30,6 +30,7 @@ class KvxTransport:
         _native.lib()  # fail loudly here, at registration, if libkvx.so is missing
         self.local = CacheTable.from_tensors(kv_caches)
         engine = ENGINES.get(envs.LEAN_VLLM_KVX_ENGINE, _native.ENGINE_AUTO)
+        self.engine = engine
         self.flags = _native.flags(engine)
         # A per-layer save runs beside the prefill's kernels: hold it to a few SMs.
         self.save_flags = _native.flags(engine, sm_budget=min(max(envs.LEAN_VLLM_KVX_SAVE_SMS, 0), 255))
@@ -57,6 +58,13 @@ class KvxTransport:
             "device": self.device.index,
             "pid": os.getpid(),
         }
+
+    def split_sms(self):
+        """Relayed loads: copies from the producer and from peer decode ranks run at once on two streams, so each
+        is held to half the SMs (a TMA copy CTA fills most of an SM's shared memory; a few dozen SMs already keep
+        one NVLink direction full)."""
+        half = max(1, torch.cuda.get_device_properties(self.device).multi_processor_count // 2)
+        self.flags = _native.flags(self.engine, sm_budget=min(half, 255))
 
     def bind_thread(self):
         """CUDA's current device is per thread: the transfer thread works on the cache's device."""
