@@ -291,6 +291,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
         self._relays: dict[str, _Load] = {}  # transfer thread only: loads past their own part, waiting for peers'
         self._parts: dict[str, dict] = {}  # request -> {decode rank: its part landed}; under the lock
+        self._parts_seen: dict[str, float] = {}  # request -> when its first part message came (transfer thread)
         self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
         self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
         self._thread: threading.Thread | None = None
@@ -673,9 +674,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._connect(request_id)
             return
         if op == "part":
+            request = str(message.get("request"))
             with self._lock:
-                self._parts.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
-                    message.get("ok"))
+                self._parts.setdefault(request, {})[int(message.get("rank", -1))] = bool(message.get("ok"))
+            self._parts_seen.setdefault(request, monotonic())
             return
         if op == "saved":
             with self._lock:
@@ -844,6 +846,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._send_part(request_id, False)  # the peers' loads fail too, and prefill as this one does
             with self._lock:
                 self._parts.pop(request_id, None)
+            self._parts_seen.pop(request_id, None)
         with self._lock:
             if load.failed:
                 self._finished.failed_recving.add(request_id)
@@ -873,6 +876,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
     def _poll_relays(self):
         timeout = RELAY_WAIT
         kv = self.kv_transfer
+        now = monotonic()
+        for request_id, seen in list(self._parts_seen.items()):
+            # Parts for a load this rank finished (or never had) long ago: nobody will read them.
+            if request_id not in self._relays and request_id not in self._loads and seen + 2 * timeout < now:
+                del self._parts_seen[request_id]
+                with self._lock:
+                    self._parts.pop(request_id, None)
         for request_id, load in list(self._relays.items()):
             relay = load.relay
             if relay.transfer is None:

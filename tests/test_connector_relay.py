@@ -90,3 +90,21 @@ def test_a_peer_that_never_reports_its_part_fails_the_load_after_the_wait(sides,
     consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, list(LOCAL), list(REMOTE))}))
     out = wait_for(consumers[0])  # rank 1 never gets the load
     assert out.failed_recving == {"d-1"}
+
+
+def test_part_messages_nobody_reads_are_dropped_after_the_wait(sides, monkeypatch):
+    """A peer's part for a load this rank never had stays only twice RELAY_WAIT."""
+    monkeypatch.setattr(cuda_ipc_connector, "RELAY_WAIT", 0.1)
+    from time import monotonic, sleep
+
+    producers = sides.make("kv_producer", 1, full_cache(0, True))
+    consumers = sides.make("kv_consumer", 2, full_cache(1, True), engine_id="decode")
+    sent, recved = load(producers, consumers)
+    assert recved.finished_recving == {"d-1"}
+    worker = consumers[0]
+    worker._handle(b"peer", {"op": "part", "request": "never-here", "rank": 1, "ok": True})
+    assert "never-here" in worker._parts
+    deadline = monotonic() + 5
+    while "never-here" in worker._parts and monotonic() < deadline:
+        sleep(0.02)
+    assert "never-here" not in worker._parts and not worker._parts_seen
