@@ -231,8 +231,15 @@ int kvx_mailbox_release(void *box, uint64_t seq);
 int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, uint64_t *out_bytes);
 
 /* Reads and clears the device error word of the current device: 0, or the first error a kernel recorded -- 1 a copy's
- * bounded TMA wait ran out, 2 a store slot or block id past its cache (skipped). */
+ * bounded TMA wait ran out, 2 a store slot or block id past its cache (skipped), 4 kvx_wait_selftest gave up as
+ * designed. */
 int kvx_device_error(int *out_code);
+
+/* Runs, on `stream`, the bounded wait that guards every TMA copy against a transfer that never arrives: one
+ * thread waits on an mbarrier armed for bytes no copy will bring, gives up after limit_us (1 us .. 10 s) and
+ * records code 4 in the device word, as a stuck copy would (1). Nothing is copied, nothing faults or hangs; for
+ * tests of the failure path. */
+int kvx_wait_selftest(int limit_us, void *stream);
 
 /* Kernel launches issued by this process so far (all entry points), for launch accounting. */
 uint64_t kvx_launch_count(void);

@@ -144,6 +144,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kvx_job_bytes": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int,
                        ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "kvx_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "kvx_wait_selftest": ([ctypes.c_int, _P], ctypes.c_int),
     "kvx_launch_count": ([], ctypes.c_uint64),
 }
 

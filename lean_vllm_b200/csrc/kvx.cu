@@ -264,6 +264,19 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 
 constexpr int kTmaStages = 4;
 
+// The failure path of every TMA wait, on demand: an mbarrier armed for 16 bytes that no copy will bring, waited on
+// with the same bounded wait the copy kernels use. It gives up after `limit_ns`, records `code` in the device word
+// and returns -- the status a stuck copy would leave -- without copying, faulting or hanging anything.
+__global__ void __launch_bounds__(32) kvx_wait_selftest_kernel(uint64_t limit_ns, int code) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    const uint32_t b = smem_u32(&bar);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(16u) : "memory");
+    if (!mbar_wait(b, 0, globaltimer() + limit_ns)) atomicCAS(&g_device_error, 0, code);
+}
+
 __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(8) uint64_t full[kTmaStages];
@@ -1307,6 +1320,14 @@ int kvx_mailbox_collect(void *box, int world, uint64_t slot_bytes, uint64_t seq,
 int kvx_mailbox_release(void *box, uint64_t seq) {
     if (!box) return fail(KVX_ERR_INVALID, "null mailbox");
     __atomic_store_n(mailbox_word(box, 0), seq, __ATOMIC_RELEASE);
+    return KVX_OK;
+}
+
+int kvx_wait_selftest(int limit_us, void *stream) {
+    if (limit_us < 1 || limit_us > 10000000) return fail(KVX_ERR_INVALID, "limit %d us: 1 us to 10 s", limit_us);
+    kvx_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_us * 1000, 4);
+    KVX_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return KVX_OK;
 }
 

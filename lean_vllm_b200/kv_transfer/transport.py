@@ -235,6 +235,11 @@ def launch_count() -> int:
     return int(lib().kvx_launch_count())
 
 
+def wait_selftest(limit_us: int, stream: int = 0) -> None:
+    """Launches the bounded-wait self-test (kvx_wait_selftest): after limit_us the device word reads 4."""
+    check(lib().kvx_wait_selftest(limit_us, stream or None))
+
+
 def device_error() -> int:
     out = ctypes.c_int()
     check(lib().kvx_device_error(ctypes.byref(out)))

@@ -91,3 +91,11 @@ def test_a_doorbell_opens_and_closes_without_a_device():
     with pytest.raises(_native.KvxError, match="no open doorbell"):
         _native.check(_native.lib().kvx_doorbell_close(bell))
     b.close()
+
+
+def test_the_wait_selftest_checks_its_limit_before_launching():
+    if not os.path.exists(_native.LIB_PATH):
+        pytest.skip("libkvx.so is not built here")
+    for bad in (0, -5, 10_000_001):
+        with pytest.raises(_native.KvxError, match="limit"):
+            _native.check(_native.lib().kvx_wait_selftest(bad, None))

@@ -265,3 +265,22 @@ def test_ipc_export_and_open_in_the_same_process_is_the_pointer_itself():
 
 def test_the_device_error_word_starts_clear():
     assert transport.device_error() == 0
+
+
+def test_a_bounded_wait_that_runs_out_reports_and_leaves_the_context_usable():
+    """The failure path every TMA copy relies on, made to happen: an mbarrier waited on for bytes that never come
+    gives up after its limit and leaves code 4 in the device word; the device then copies as before."""
+    import time
+
+    assert transport.device_error() == 0
+    started = time.monotonic()
+    transport.wait_selftest(20_000)  # 20 ms
+    torch.cuda.synchronize()
+    assert time.monotonic() - started < 5
+    assert transport.device_error() == 4
+    assert transport.device_error() == 0  # read and cleared
+    src = _qwen_like(4, 1, seed=8)
+    dst = [torch.zeros_like(s) for s in src]
+    transport.copy([CacheTable.from_tensors(src), CacheTable.from_tensors(dst)], [CopyJob(0, 1, [1, 2], [0, 3], 0, 0, 8)])
+    torch.cuda.synchronize()
+    assert torch.equal(dst[0][:, [0, 3]], src[0][:, [1, 2]])
