@@ -124,3 +124,74 @@ def test_pull_and_announced_push_between_two_processes():
         errors.append(failures.get())
     assert not errors, errors
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+LATENT = 6
+
+
+def _latents(seed):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(1, BLOCKS, BLOCK, LATENT, generator=g).to(torch.bfloat16) for _ in range(2)]
+
+
+def _relay_rank(rank: int, world: int, master_port: int, kv_port: int, failures):
+    """Rank 0 a prefill instance (TP1), ranks 1-2 one decode instance (TP2) relaying MLA latents between them."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(master_port), LEAN_VLLM_KVX_RELAY="1")
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVTransferConfig, ReqToRecv, cuda_ipc_connector
+        from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorWorker
+        from tests.shm_transport import ShmTransport, shared_cache
+
+        cuda_ipc_connector.make_transport = ShmTransport
+        producer = rank == 0
+        layers = _latents(300 if producer else 400 + rank)
+        caches = [shared_cache(t.shape, t) for t in layers]
+        kv = KVTransferConfig(kv_role="kv_producer" if producer else "kv_consumer",
+                              kv_port=kv_port if producer else kv_port + 10, engine_id="p" if producer else "d")
+        worker = CudaIpcConnectorWorker(Cfg(kv, tensor_parallel_size=1 if producer else 2), 0 if producer else rank - 1)
+        worker.register_kv_caches(caches)
+        dist.barrier()
+        local, remote = [0, 5, 3, 8, 1], [7, 2, 9, 4, 6]
+        if producer:
+            worker.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-relay": remote}))
+            _wait(worker, "finished_sending", {"p-relay"})  # both decode ranks read their part
+        else:
+            worker.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-relay": ReqToRecv(
+                local, remote, "p-relay", "p", "127.0.0.1", kv_port, 1)}))
+            _wait(worker, "finished_recving", {"d-relay"})
+            prefill = _latents(300)
+            for layer in range(2):
+                assert torch.equal(caches[layer][:, local], prefill[layer][:, remote]), layer
+        dist.barrier()
+        worker.shutdown()
+        dist.destroy_process_group()
+    except BaseException as error:  # noqa: BLE001 - reported to the parent
+        failures.put(f"rank {rank}: {type(error).__name__}: {error}")
+        raise
+    finally:
+        from tests.shm_transport import remove_files
+
+        remove_files()
+
+
+def test_a_relayed_latent_load_between_three_processes():
+    """Each decode rank (its own process) pulls its part from the prefill process and the other part from its peer
+    process, through shared-file caches: both end with every latent block, the producer frees after both reads."""
+    if not os.path.isdir("/dev/shm"):
+        pytest.skip("needs /dev/shm")
+    ctx = mp.get_context("spawn")
+    failures = ctx.Queue()
+    master_port, kv_port = _free_port(), _free_port()
+    procs = [ctx.Process(target=_relay_rank, args=(r, 3, master_port, kv_port, failures)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not failures.empty():
+        errors.append(failures.get())
+    assert not errors, errors
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
