@@ -163,6 +163,8 @@ typedef struct kvx_store_dest {
 
 /* kvx_store flags: bits 16-23 CTAs per SM (0: as many as fit), bits 24-31 SM budget, as for copies; and */
 #define KVX_STORE_SERIAL 1     /* a plain launch: no overlap with the kernel before it on the stream */
+#define KVX_STORE_PEERS_ONLY 4 /* destination 0 is not written (its slots still place the peers' rows): the push
+                                  half of a store whose local half ran on another stream */
 
 /* Scatters num_tokens rows of keys and values [token][head][head_bytes] (or latents, with value = NULL and
  * num_heads = 1) into each destination's slots, one pass over the rows: destination 0 is the local cache

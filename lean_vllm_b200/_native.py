@@ -21,6 +21,7 @@ KVX_ERR_DEVICE = -4
 KVX_ERR_TIMEOUT = -5
 
 STORE_SERIAL = 1  # kvx_store flag: a plain launch, no overlap with the kernel before it
+STORE_PEERS_ONLY = 4  # kvx_store flag: only the peer destinations are written (destination 0 places their rows)
 
 ENGINE_AUTO = 0
 ENGINE_LSU = 1

@@ -353,6 +353,7 @@ struct StoreParams {
     uint64_t key, value;
     int64_t key_stride, value_stride;
     int32_t num_tokens, num_heads, head_bytes, n_dests;
+    int32_t peers_only, pad_;  // KVX_STORE_PEERS_ONLY: destination 0 places rows but is not written
     StoreDest dests[kMaxStoreDests];
 };
 
@@ -481,6 +482,7 @@ __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __gri
         const uint32_t byte_in_row = vec * VEC;
         const char *in_row = reinterpret_cast<const char *>(row0 + (uint64_t)head * p.head_bytes + byte_in_row);
         const StoreLane lane0 = lane_of(p.dests[0], part, head, byte_in_row);
+        const bool peers_only = p.peers_only != 0;
         const void *slots0 = p.dests[0].slots;
         const bool wide0 = p.dests[0].slot_bytes == 8;
         for (uint32_t t0 = blockIdx.x * tpp + lane_token; t0 < n; t0 += token_step * kStoreUnroll) {
@@ -496,7 +498,7 @@ __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __gri
                                      : static_cast<const int32_t *>(slots0)[t];
                 }
             }
-            if (lane0.base) {
+            if (lane0.base && !peers_only) {
 #pragma unroll
                 for (int u = 0; u < kStoreUnroll; ++u) put<VEC, FAST>(lane0, first[u], data[u]);
             }
@@ -1097,6 +1099,7 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     p.num_heads = num_heads;
     p.head_bytes = head_bytes;
     p.n_dests = n_dests;
+    p.peers_only = (flags & KVX_STORE_PEERS_ONLY) ? 1 : 0;
     uint64_t align_bits = p.key | p.value | (uint64_t)key_stride | (uint64_t)value_stride | (uint64_t)head_bytes;
     for (int d = 0; d < n_dests; ++d) {
         const kvx_store_dest &s = dests[d];

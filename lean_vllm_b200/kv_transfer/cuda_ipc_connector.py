@@ -510,13 +510,15 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         ranks' blocks of every request being saved whose decode instance was mapped at its first store. An engine
         calls this in place of the backend's store; it then needs no save_kv_layer for those layers."""
         targets = self._fused_targets(layer_index, latents=False)
-        self.transport.store(self.kv_caches[layer_index], key, value, slot_mapping, targets)
+        self.transport.store(self.kv_caches[layer_index], key, value, slot_mapping, targets,
+                             async_push=envs.LEAN_VLLM_KVX_FUSED_ASYNC)
 
     def store_latents(self, layer_index: int, latent, slot_mapping):
         """store_kv for an MLA layer's latents [tokens, 576] (attention/triton_cache.py:84-91); every decode rank
         takes a whole copy."""
         targets = self._fused_targets(layer_index, latents=True)
-        self.transport.store(self.kv_caches[layer_index], latent, None, slot_mapping, targets)
+        self.transport.store(self.kv_caches[layer_index], latent, None, slot_mapping, targets,
+                             async_push=envs.LEAN_VLLM_KVX_FUSED_ASYNC)
 
     def _fused_targets(self, layer_index: int, latents: bool) -> list:
         with self._lock:

@@ -142,15 +142,32 @@ class KvxTransport:
                                      num_heads=share.num_heads if k_region[2] else 1,
                                      dst_first_head=share.local_head if k_region[2] else 0, block_map=block_map)
 
-    def store(self, cache: torch.Tensor, key: torch.Tensor, value, slot_mapping: torch.Tensor, targets: list):
-        """The layer's store into `cache` (HND keys/values, or latents when value is None) and every target."""
+    def store(self, cache: torch.Tensor, key: torch.Tensor, value, slot_mapping: torch.Tensor, targets: list,
+              async_push: bool = False):
+        """The layer's store into `cache` (HND keys/values, or latents when value is None) and every target. With
+        `async_push`, one launch on the engine's stream writes the local cache (what attention waits for) and a
+        second on the save stream, after it and held to the save SM budget, writes the targets from the same rows
+        (KVX_STORE_PEERS_ONLY): the NVLink writes leave the prefill's critical path."""
         from lean_vllm_b200.attention.kvx_cache import store_kvcache, store_latents
 
-        if value is None:
-            store_latents(key, cache[0], slot_mapping, push_to=targets)
-        else:
-            view = cache.transpose(2, 3)  # (2, blocks, tokens, heads, dim), as the attention backend sees it
-            store_kvcache(key, value, view[0], view[1], slot_mapping, push_to=targets)
+        def launch(push_to, stream=None, flags=0):
+            if value is None:
+                store_latents(key, cache[0], slot_mapping, push_to=push_to, stream=stream, flags=flags)
+            else:
+                view = cache.transpose(2, 3)  # (2, blocks, tokens, heads, dim), as the attention backend sees it
+                store_kvcache(key, value, view[0], view[1], slot_mapping, push_to=push_to, stream=stream,
+                              flags=flags)
+
+        if not targets or not async_push:
+            launch(targets)
+            return
+        launch([])
+        self.save_stream.wait_event(torch.cuda.current_stream(self.device).record_event())
+        for tensor in (key, value, slot_mapping):
+            if tensor is not None:
+                tensor.record_stream(self.save_stream)  # the engine may free them once its own store is queued
+        budget = min(max(envs.LEAN_VLLM_KVX_SAVE_SMS, 0), 255)
+        launch(targets, self.save_stream.cuda_stream, _native.flags(sm_budget=budget) | _native.STORE_PEERS_ONLY)
 
     def done(self, xfer: transport.Transfer) -> bool:
         return xfer.done()

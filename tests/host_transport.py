@@ -122,7 +122,7 @@ class HostTransport:
         heads = (share.remote_head, share.num_heads, share.local_head) if k[2] else (0, 1, 0)
         return {"k": k, "v": v, "heads": heads, "block_map": block_map, "block_size": block_size, "table": table}
 
-    def store(self, cache, key, value, slot_mapping, targets):
+    def store(self, cache, key, value, slot_mapping, targets, async_push=False):
         self.stores.append((len(targets), key.shape[0]))
         latents = value is None
         block = cache.size(2) if latents else cache.size(3)

@@ -202,3 +202,28 @@ def test_block_sizes_that_are_not_powers_of_two_divide(block):
     store_kvcache(key, value, view[0], view[1], slots)
     torch.cuda.synchronize()
     assert np.array_equal(bits(cache), expected)
+
+
+def test_a_peers_only_store_writes_the_peers_and_not_the_local_cache():
+    """KVX_STORE_PEERS_ONLY: destination 0's slots (and block map) still place the peers' rows, but destination 0
+    itself is left as it was -- the push half of a store whose local half ran on the engine's stream."""
+    from lean_vllm_b200._native import STORE_PEERS_ONLY
+
+    key, value, cache, slots = _qwen_step(tokens=700)
+    peer = torch.zeros(2, 30, 8, 256, 128, device="cuda", dtype=torch.bfloat16)
+    block_map = torch.full((40,), -1, dtype=torch.int32, device="cuda")
+    used = torch.unique(slots[slots >= 0] // 256)
+    block_map[used] = torch.arange(used.numel(), dtype=torch.int32, device="cuda")
+    target = PushTarget.of(peer.transpose(2, 3)[0], peer.transpose(2, 3)[1], None, block_map=block_map)
+    before = cache.clone()
+    view = cache.transpose(2, 3)
+    store_kvcache(key, value, view[0], view[1], slots, push_to=[target], flags=STORE_PEERS_ONLY)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, before)
+    expected = torch.zeros_like(peer)
+    ev = expected.transpose(2, 3)
+    keep = slots >= 0
+    mapped = block_map[slots[keep] // 256].long() * 256 + slots[keep] % 256
+    ev[0].reshape(-1, 8, 128)[mapped] = key[keep]
+    ev[1].reshape(-1, 8, 128)[mapped] = value[keep]
+    assert torch.equal(peer, expected)
