@@ -210,7 +210,7 @@ def test_a_peers_only_store_writes_the_peers_and_not_the_local_cache():
     from lean_vllm_b200._native import STORE_PEERS_ONLY
 
     key, value, cache, slots = _qwen_step(tokens=700)
-    peer = torch.zeros(2, 30, 8, 256, 128, device="cuda", dtype=torch.bfloat16)
+    peer = torch.zeros(2, 40, 8, 256, 128, device="cuda", dtype=torch.bfloat16)  # room for every used block
     block_map = torch.full((40,), -1, dtype=torch.int32, device="cuda")
     used = torch.unique(slots[slots >= 0] // 256)
     block_map[used] = torch.arange(used.numel(), dtype=torch.int32, device="cuda")
