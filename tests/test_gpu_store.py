@@ -220,10 +220,11 @@ def test_a_peers_only_store_writes_the_peers_and_not_the_local_cache():
     store_kvcache(key, value, view[0], view[1], slots, push_to=[target], flags=STORE_PEERS_ONLY)
     torch.cuda.synchronize()
     assert torch.equal(cache, before)
+    # The same rows stored straight into a copy of the peer at the mapped slots (a plain store: verified above
+    # against the reference's torch store).
     expected = torch.zeros_like(peer)
     ev = expected.transpose(2, 3)
-    keep = slots >= 0
-    mapped = block_map[slots[keep] // 256].long() * 256 + slots[keep] % 256
-    ev[0].reshape(-1, 8, 128)[mapped] = key[keep]
-    ev[1].reshape(-1, 8, 128)[mapped] = value[keep]
+    mapped = torch.where(slots >= 0, block_map[slots.clamp(min=0) // 256].long() * 256 + slots % 256, -1)
+    store_kvcache(key, value, ev[0], ev[1], mapped)
+    torch.cuda.synchronize()
     assert torch.equal(peer, expected)
