@@ -1,6 +1,7 @@
 """Generates the golden fixtures in this folder by running lean-vLLM's own NixlConnectorWorker.
 
-Run it where the reference checkout is importable (REFERENCE_ROOT, default /root/reference):
+Run it where the reference checkout is importable (REFERENCE_ROOT, default: a "reference" folder beside this
+repository):
 
     python tests/golden/make_golden.py
 
@@ -28,8 +29,8 @@ from time import monotonic, sleep
 import numpy as np
 import torch
 
-REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
+REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", os.path.join(HERE, "..", "..", "..", "reference"))
 sys.dont_write_bytecode = True  # the reference tree is read-only
 sys.path.insert(0, REFERENCE_ROOT)
 

@@ -19,7 +19,8 @@ from dataclasses import dataclass
 import pytest
 import torch
 
-REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
+# A lean-vLLM checkout: REFERENCE_ROOT, else a "reference" folder beside this repository.
+REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", os.path.join(os.path.dirname(__file__), "..", "..", "reference"))
 if not os.path.isdir(os.path.join(REFERENCE_ROOT, "lean_vllm")):
     pytest.skip("no lean-vLLM reference checkout", allow_module_level=True)
 sys.path.insert(0, REFERENCE_ROOT)
