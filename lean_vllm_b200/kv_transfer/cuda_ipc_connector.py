@@ -177,6 +177,7 @@ class _Remote:
     exported: dict
     table: object  # the transport's view of the peer rank's cache, mapped into this process
     sock: object  # DEALER kept open for notifications
+    per_block: dict = field(default_factory=dict)  # (share, latents) -> bytes one block of a load moves
 
 
 @dataclass(slots=True)
@@ -750,21 +751,19 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             jobs, tables = [], []
             for i, share in enumerate(shares):
                 remote = self._handshake(req, share.remote_rank)
-                if max(req.remote_block_ids, default=-1) >= remote.num_blocks:
-                    raise RuntimeError(f"a block id past the producer's {remote.num_blocks} blocks")
                 readers = readers_of(share.remote_rank, req.remote_tp_size, self.tp_size, heads)
                 key = (req.remote_host, req.remote_port + share.remote_rank)
                 message = f"{req.remote_request_id}:{readers}"
                 # Latents come whole from the first producer rank only (nixl_connector.py:403).
                 job = CopyJob(1, 0, req.remote_block_ids, req.local_block_ids, share.remote_head, share.local_head,
                               share.num_heads, i == 0)
-                nbytes = self.transport.job_bytes([remote.table], [job])
+                nbytes = self._job_bytes(remote, job)
                 if load.relay is not None and i == 0:  # the whole payload counts; only this rank's part is read
                     load.num_bytes += nbytes
                     first, end = load.relay.parts[self.rank]
                     job = CopyJob(1, 0, req.remote_block_ids[first:end], req.local_block_ids[first:end],
                                   share.remote_head, share.local_head, share.num_heads, True)
-                    nbytes = 0 if end == first else self.transport.job_bytes([remote.table], [job])
+                    nbytes = self._job_bytes(remote, job)
                     load.num_bytes -= nbytes
                 if nbytes == 0:
                     self._notify(key, message)  # nothing to read from this rank, but it must count this reader
@@ -789,6 +788,29 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     batch.clear()
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
             self._fail(load, error)
+
+    def _job_bytes(self, remote: _Remote, job: CopyJob) -> int:
+        """What the job moves: the reference's descriptor-length sum (nixl_connector.py:421). The bytes of one block
+        come from the transport's planner once per producer rank and share (it checks the heads and regions); every
+        load's block ids are range-checked here, as the planner would, so a bad id fails its own load before any
+        launch."""
+        src, dst = job.src_block_ids, job.dst_block_ids
+        if len(src) != len(dst):
+            raise ValueError(f"{len(src)} source blocks for {len(dst)} destination blocks")
+        if not src:
+            return 0
+        if min(src) < 0 or max(src) >= remote.num_blocks:
+            raise RuntimeError(f"a block id past the producer's {remote.num_blocks} blocks")
+        local_blocks = int(self.kv_caches[0].size(1))
+        if min(dst) < 0 or max(dst) >= local_blocks:
+            raise RuntimeError(f"a block id past this rank's {local_blocks} blocks")
+        key = (job.src_first_head, job.dst_first_head, job.num_heads, job.latents)
+        per_block = remote.per_block.get(key)
+        if per_block is None:
+            one = CopyJob(job.src, job.dst, [0], [0], job.src_first_head, job.dst_first_head, job.num_heads,
+                          job.latents)
+            per_block = remote.per_block[key] = self.transport.job_bytes([remote.table], [one])
+        return per_block * len(src)
 
     def _post_loads(self, batch: list):
         """One launch for every load planned in this pass that waits on the same ready event: their jobs share one
