@@ -16,6 +16,7 @@ import ctypes
 import mmap
 import os
 import pickle
+import tempfile
 import uuid
 
 from lean_vllm_b200._native import check, lib
@@ -106,7 +107,9 @@ class KVConnectorStep:
         if world_size > 1 and exchange == "mailbox":
             import torch.distributed as dist
 
-            path = [f"/dev/shm/kvx-step-{os.getpid()}-{uuid.uuid4().hex[:12]}" if rank == 0 else None]
+            # Host shared memory where the node has it (/dev/shm), else the temporary directory.
+            folder = "/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir()
+            path = [os.path.join(folder, f"kvx-step-{os.getpid()}-{uuid.uuid4().hex[:12]}") if rank == 0 else None]
             if rank == 0:
                 self.mailbox = StepMailbox(path[0], world_size, rank, slot_bytes, create=True)
             dist.broadcast_object_list(path, src=0, group=group)
