@@ -101,11 +101,15 @@ def test_an_announced_push_through_both_halves_on_the_gpu(sides, golden, prefill
     assert np.array_equal(bits(got), arrays[f"small_{key}_tp{prefill_tp}to{decode_tp}"])
 
 
+@pytest.mark.parametrize("split", [False, True], ids=["one-launch", "push-on-save-stream"])
 @pytest.mark.parametrize("prefill_tp, decode_tp, mla", [(1, 1, False), (2, 4, False), (4, 2, False),
                                                         (1, 2, True)])
-def test_a_fused_store_lands_the_new_rows_in_the_decode_blocks_on_the_gpu(sides, prefill_tp, decode_tp, mla):
+def test_a_fused_store_lands_the_new_rows_in_the_decode_blocks_on_the_gpu(sides, monkeypatch, prefill_tp, decode_tp,
+                                                                          mla, split):
     """store_kv writes each rank's new rows into its own cache and, through the block map, into every decode rank's
-    blocks in one kvx_store launch; hand-over then has nothing left to copy."""
+    blocks -- in one kvx_store launch, or (LEAN_VLLM_KVX_FUSED_ASYNC) the local half on the engine's stream and the
+    push half on the save stream; hand-over then has nothing left to copy."""
+    monkeypatch.setenv("LEAN_VLLM_KVX_FUSED_ASYNC", "1" if split else "0")
     from lean_vllm_b200.kv_transfer import ReqToRecv
     from lean_vllm_b200.kv_transfer.base import ReqToSave
     from tests.connector_cases import HEAD_DIM, LATENT_DIM, NUM_HEADS
