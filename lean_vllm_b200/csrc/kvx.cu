@@ -656,6 +656,7 @@ int choose(int flags, uint64_t align_bits, Config &cfg) {
         return fail(KVX_ERR_INVALID, "the TMA engine needs 16-byte aligned addresses and lengths");
     cfg.engine = (engine == KVX_ENGINE_LSU || !tma_ok) ? KVX_ENGINE_LSU : KVX_ENGINE_TMA;
     const int log_tile = (flags >> 8) & 0xff;
+    if (log_tile > 24) return fail(KVX_ERR_INVALID, "tile of 2^%d bytes", log_tile);  // before any shift by it
     const int ctas = (flags >> 16) & 0xff;
     cfg.sm_budget = (flags >> 24) & 0xff;
     if (cfg.engine == KVX_ENGINE_TMA) {
@@ -668,7 +669,6 @@ int choose(int flags, uint64_t align_bits, Config &cfg) {
         cfg.ctas_per_sm = ctas ? ctas : 2;
         if (cfg.tile_bytes < (uint32_t)cfg.vec) return fail(KVX_ERR_INVALID, "tile smaller than a vector");
     }
-    if (log_tile > 24) return fail(KVX_ERR_INVALID, "tile of 2^%d bytes", log_tile);
     return KVX_OK;
 }
 
