@@ -1,5 +1,5 @@
 """The connector's transport on CUDA devices: a rank's cache exported over CUDA IPC, peers' caches mapped, one kvx
-launch per load on a side stream, completion by event.
+launch per load on a side stream, completion by event, announced by a doorbell the transfer thread sleeps on.
 
 It replaces the NIXL agent under NixlConnectorWorker call for call: register_memory/get_agent_metadata
 (nixl_connector.py:240-244) -> `exported`; add_remote_agent (:510) -> open; initialize_xfer + transfer (:411-420)
