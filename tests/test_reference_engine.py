@@ -285,3 +285,42 @@ def test_the_reference_engine_runs_a_pushed_request_with_its_block_ids_exchanged
         dst = decode.model_runner.caches[layer][:, dst_blocks].transpose(2, 3).reshape(2, 3 * BLOCK, HEADS, DIM)
         assert torch.equal(src[:, : len(prompt)].view(torch.int16), dst[:, : len(prompt)].view(torch.int16)), layer
     assert decode.metrics.registry.get_sample_value("lean_vllm:kv_transfers_total") == 1.0
+
+
+def test_blocks_the_decode_engine_already_caches_are_not_pulled_again(engines):
+    """The decode engine served the same prompt before, so its prefix cache holds the leading full blocks: the
+    reference scheduler admits the remote request with those blocks cached, the connector's load covers only the
+    rest (the reference's own rule, nixl_connector.py:134-146), and the decode cache still ends equal, position for
+    position, to the prefill's KV."""
+    prefill, decode = engines("kv_producer", "prefill-engine"), engines("kv_consumer", "decode-engine")
+    prompt = [40 + (i * 11) % 50 for i in range(21)]  # 21 tokens: two full blocks and a partial one
+    decode.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True), "warm")  # computed here, published
+    step_until([decode], lambda out: decode.is_finished())
+    prefill.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True, kv_transfer_params={"do_remote_decode": True}),
+                "p-2")
+    outputs = step_until([prefill], lambda out: any(o.finished for o in out))
+    params = next(o.kv_transfer_params for o in outputs if o.finished)
+    worker = decode.model_runner.worker
+    seen = []
+    real_start = worker.start_load_kv
+
+    def recording(metadata):
+        seen.extend(metadata.reqs_to_recv.values())
+        return real_start(metadata)
+
+    worker.start_load_kv = recording
+    seq = decode.add(prompt, SamplingParams(max_tokens=2, ignore_eos=True, kv_transfer_params=params), "d-2")
+    decode.step()
+    dst_blocks = list(seq.block_table[:3])
+    assert seq.num_cached_tokens == 2 * BLOCK  # the trailing partial block always recomputes
+    (req,) = seen
+    assert req.local_block_ids == dst_blocks[2:] and req.remote_block_ids == params["remote_block_ids"][2:]
+    step_until([prefill, decode], lambda out: decode.is_finished() and prefill.is_finished())
+    src_blocks = params["remote_block_ids"]
+    for layer in range(LAYERS):
+        src = prefill.model_runner.caches[layer][:, src_blocks].transpose(2, 3).reshape(2, 3 * BLOCK, HEADS, DIM)
+        dst = decode.model_runner.caches[layer][:, dst_blocks].transpose(2, 3).reshape(2, 3 * BLOCK, HEADS, DIM)
+        assert torch.equal(src[:, : len(prompt)].view(torch.int16), dst[:, : len(prompt)].view(torch.int16)), layer
+    # The connector counted the one block it read: 2 parts x layers x heads x block x dim x 2 bytes.
+    assert decode.metrics.registry.get_sample_value("lean_vllm:kv_transfer_bytes_sum") == \
+        2 * LAYERS * HEADS * BLOCK * DIM * 2
