@@ -92,6 +92,7 @@ class StubRunner:
     def __init__(self, config, caches, layer_hooks=False):
         self.caches = caches
         self.layer_hooks = layer_hooks  # call save_kv_layer after each layer's store, as an engine with hooks does
+        self.batches: list = []  # (request, tokens scheduled) of every batch run
         self.worker = CudaIpcConnectorWorker(config, 0)
         self.worker.register_kv_caches(caches)
         self.kv_step = KVConnectorStep(self.worker, 0, 1)
@@ -104,6 +105,7 @@ class StubRunner:
 
     def run(self, seqs):
         sampled = []
+        self.batches.append([(seq.request_id, seq.num_scheduled_tokens) for seq in seqs])
         for seq in seqs:
             begin = seq.num_cached_tokens
             end = begin + seq.num_scheduled_tokens
@@ -324,3 +326,38 @@ def test_blocks_the_decode_engine_already_caches_are_not_pulled_again(engines):
     # The connector counted the one block it read: 2 parts x layers x heads x block x dim x 2 bytes.
     assert decode.metrics.registry.get_sample_value("lean_vllm:kv_transfer_bytes_sum") == \
         2 * LAYERS * HEADS * BLOCK * DIM * 2
+
+
+def test_an_abort_mid_load_frees_the_decode_blocks_once_the_load_ended(engines):
+    """The decode request is aborted right after its load started: the reference scheduler keeps its blocks (the
+    loader may still be writing them) until the connector reports the load over, then frees them; the prefill
+    side still has its blocks read and released."""
+    prefill, decode = engines("kv_producer", "prefill-engine"), engines("kv_consumer", "decode-engine")
+    prompt = [45 + (i * 7) % 40 for i in range(20)]
+    prefill.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True, kv_transfer_params={"do_remote_decode": True}),
+                "p-3")
+    outputs = step_until([prefill], lambda out: any(o.finished for o in out))
+    params = next(o.kv_transfer_params for o in outputs if o.finished)
+    decode.add(prompt, SamplingParams(max_tokens=2, ignore_eos=True, kv_transfer_params=params), "d-3")
+    decode.step()
+    assert decode.scheduler.abort("d-3")
+    assert decode.scheduler.block_manager.free_block_queue.num_free_blocks < BLOCKS  # held for the loader
+    step_until([prefill, decode], lambda out: decode.is_finished() and prefill.is_finished())
+    assert decode.scheduler.block_manager.free_block_queue.num_free_blocks == BLOCKS
+    assert prefill.scheduler.block_manager.free_block_queue.num_free_blocks == BLOCKS
+
+
+def test_the_prefill_s_released_blocks_stay_in_its_prefix_cache(engines):
+    """Once the decode side has read them, the prefill engine frees the held blocks into its prefix cache: the same
+    prompt served again there finds its full blocks cached."""
+    prefill, decode = engines("kv_producer", "prefill-engine"), engines("kv_consumer", "decode-engine")
+    prompt = [50 + (i * 5) % 30 for i in range(21)]
+    prefill.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True, kv_transfer_params={"do_remote_decode": True}),
+                "p-4")
+    outputs = step_until([prefill], lambda out: any(o.finished for o in out))
+    params = next(o.kv_transfer_params for o in outputs if o.finished)
+    decode.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True, kv_transfer_params=params), "d-4")
+    step_until([prefill, decode], lambda out: decode.is_finished() and prefill.is_finished())
+    prefill.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True), "again")
+    prefill.step()
+    assert prefill.model_runner.batches[-1] == [("again", len(prompt) - 2 * BLOCK)]  # two full blocks were hits
