@@ -310,18 +310,20 @@ def plan_relay(spec: Workload, role: Role, reqs):
     request's blocks, as the connector cuts them."""
     from lean_vllm_b200.kv_transfer.transport import CopyJob
 
+    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import relay_parts
+
     peers = [("prefill", 0)] + [("decode", r) for r in range(spec.decode_tp) if r != role.tp_rank]
     own, others = [], []
     for s, d in reqs:
-        n = len(d)
-        cut = [n * r // spec.decode_tp for r in range(spec.decode_tp + 1)]
+        parts = relay_parts(len(d), spec.decode_tp)
         me = role.tp_rank
-        if cut[me + 1] > cut[me]:
-            own.append(CopyJob(1, 0, s[cut[me] : cut[me + 1]], d[cut[me] : cut[me + 1]], 0, 0, 0, True))
-        for r in range(spec.decode_tp):
-            if r != me and cut[r + 1] > cut[r]:
+        first, end = parts[me]
+        if end > first:
+            own.append(CopyJob(1, 0, s[first:end], d[first:end], 0, 0, 0, True))
+        for r, (first, end) in enumerate(parts):
+            if r != me and end > first:
                 k = 1 + peers.index(("decode", r))
-                others.append(CopyJob(k, 0, d[cut[r] : cut[r + 1]], d[cut[r] : cut[r + 1]], 0, 0, 0, True))
+                others.append(CopyJob(k, 0, d[first:end], d[first:end], 0, 0, 0, True))
     return peers, own, others
 
 

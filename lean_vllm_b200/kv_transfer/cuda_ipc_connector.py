@@ -57,6 +57,12 @@ def _cdiv(a: int, b: int) -> int:
     return -(-a // b)
 
 
+def relay_parts(n_blocks: int, tp_size: int) -> list[tuple[int, int]]:
+    """A relayed load's parts: decode rank r pulls block positions [first, end) of part r from the producer, the
+    other parts from its peers. Contiguous, balanced to a block, and empty where there are fewer blocks than ranks."""
+    return [(n_blocks * r // tp_size, n_blocks * (r + 1) // tp_size) for r in range(tp_size)]
+
+
 def node_id() -> str:
     """Identifies this machine's boot: CUDA IPC mappings work only between processes of one node."""
     try:
@@ -742,9 +748,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if self.relay and self.tp_size > 1 and self.num_heads == 0:
                 # Latents are whole on every decode rank: this rank pulls its part from the prefill rank and the
                 # others' parts from them, so each byte crosses the prefill GPU's links once.
-                n = len(req.local_block_ids)
-                load.relay = _Relay([(n * r // self.tp_size, n * (r + 1) // self.tp_size)
-                                     for r in range(self.tp_size)])
+                load.relay = _Relay(relay_parts(len(req.local_block_ids), self.tp_size))
                 for peer in range(self.tp_size):
                     if peer != self.rank:
                         self._handshake(self._peer_req(), peer)
