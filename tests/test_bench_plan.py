@@ -149,3 +149,16 @@ def test_a_relayed_mla_load_lands_every_block_on_every_decode_rank(world):
                 for s, d in reqs:
                     want[:, d] = prefill[layer][:, s]
                 assert np.array_equal(mem[rank][layer], want), (group, r, layer)
+
+
+def test_the_command_line_parses_every_mode():
+    """Every mode's flags parse (argparse only; the modes themselves need GPUs)."""
+    import contextlib
+    import io
+
+    with contextlib.redirect_stdout(io.StringIO()) as out, pytest.raises(SystemExit) as done:
+        bench.main(["--help"])
+    assert done.value.code == 0
+    for flag in ("--relay", "--staged", "--store", "--poisson", "--layerwise", "--copy-engine", "--step-exchange",
+                 "--impl", "--peer-device", "--serial"):
+        assert flag in out.getvalue(), flag
