@@ -187,6 +187,19 @@ class _Remote:
 
 
 @dataclass(slots=True)
+class _Retired:
+    """A peer rank's mapping replaced after the peer restarted under a new engine id. Copies and stores queued
+    before the swap may still read or write it, so it closes only once every stream that can carry them has run
+    past the swap: the engine's stream (its marker, recorded when the engine thread next polls) and each of the
+    transport's streams (an empty transfer posted after that)."""
+
+    remote: _Remote
+    passed: bool = False  # the engine thread polled since: nothing it queues from then on names the mapping
+    marker: object = None  # the engine stream's event at that poll
+    fences: list | None = None  # empty transfers after the marker, one per transport stream
+
+
+@dataclass(slots=True)
 class _Batch:
     """One launch shared by the loads planned in one pass of the transfer thread."""
 
@@ -282,6 +295,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._notified: dict[str, list] = {}  # request -> [notifications, readers, first seen]
         self._saves: dict[str, _Save] = {}  # producer: requests pushed layer by layer
         self._saved: dict[str, dict] = {}  # decode: request -> {producer rank: landed ok}, may precede the wait
+        self._saved_seen: dict[str, float] = {}  # request -> when its first landing word came; under the lock
         self._push_ids: dict[str, str] = {}  # producer: push id -> request id, for saves awaiting their decode ranks
         self._expects: dict[str, dict] = {}  # producer: push id -> a decode rank's announcement, may come first
         self._finished = KVConnectorOutput()
@@ -293,6 +307,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._deferred: list = []  # messages that came while a handshake wait answered handshakes only
         self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
         self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table) of _remotes; under the lock
+        self._retired: list[_Retired] = []  # replaced mappings not yet closed; both threads, under the lock
         self._loads: dict[str, _Load] = {}  # transfer thread only
         self._waits: dict[str, _Wait] = {}  # transfer thread only
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
@@ -424,6 +439,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         """Saves are ordered after their layers on the GPU and awaited on the transfer thread: nothing to do."""
 
     def get_finished(self) -> KVConnectorOutput:
+        with self._lock:
+            swapped = [r for r in self._retired if not r.passed]
+        if swapped:
+            # Every store and push this thread queued naming a replaced mapping was queued before this point.
+            marker = self.transport.ready_marker()
+            with self._lock:
+                for retired in swapped:
+                    retired.marker, retired.passed = marker, True
         now = monotonic()
         timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
         with self._lock:
@@ -615,6 +638,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._poll_relays()
                 self._poll_pushes()
                 self._poll_waits()
+                self._poll_retired()  # last: after every post this pass made
         except zmq.ContextTerminated:
             pass
         finally:
@@ -634,6 +658,18 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if load.relay.transfer is not None:
                 self.transport.wait(load.relay.transfer.xfer)
                 self.transport.release(load.relay.transfer.xfer)
+        drain = getattr(self.transport, "drain", None)
+        if drain is not None:
+            try:
+                drain()  # the engine's own stores into peers' blocks, on streams this thread does not track
+            except Exception as error:  # noqa: BLE001 - a device that failed runs nothing more: close regardless
+                logger.warning("waiting for the device before closing KV mappings failed: %s", error)
+        with self._lock:
+            retired, self._retired = self._retired, []
+        for entry in retired:
+            for fence in entry.fences or []:
+                self.transport.release(fence)
+            self.transport.close(entry.remote.exported)
         for remote in self._remotes.values():
             self.transport.close(remote.exported)
             remote.sock.close()
@@ -689,9 +725,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             self._parts_seen.setdefault(request, monotonic())
             return
         if op == "saved":
+            request = str(message.get("request"))
             with self._lock:
-                self._saved.setdefault(str(message.get("request")), {})[int(message.get("rank", -1))] = bool(
-                    message.get("ok"))
+                self._saved.setdefault(request, {})[int(message.get("rank", -1))] = bool(message.get("ok"))
+                self._saved_seen.setdefault(request, monotonic())
             return
         if op == "handshake":
             reply = {
@@ -1186,6 +1223,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 ok = complete and all(saved[rank] for rank in wait.expected)
                 if complete:
                     self._saved.pop(wait.req.remote_request_id, None)
+                    self._saved_seen.pop(wait.req.remote_request_id, None)
             if not complete and wait.started + timeout >= now:
                 continue
             del self._waits[request_id]
@@ -1196,6 +1234,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 else:
                     logger.warning("the pushed KV of %s did not land, so it prefills here", wait.req.remote_request_id)
                     self._finished.failed_recving.add(request_id)
+        awaited = {wait.req.remote_request_id for wait in self._waits.values()}
+        with self._lock:
+            for request, seen in list(self._saved_seen.items()):
+                if request not in awaited and seen + timeout < now:
+                    # Landing words no wait here took (an aborted decode request, or one for the instance that ran
+                    # on this port before): dropped as unread prefill blocks are.
+                    del self._saved_seen[request]
+                    self._saved.pop(request, None)
 
     def _handshake(self, req, remote_rank: int, fresh: bool = False) -> _Remote:
         """The peer rank's cache, asked for once per peer and mapped here, checked to match this engine. An empty
@@ -1209,11 +1255,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         elif remote is not None and (remote.engine_id == req.remote_engine_id or not req.remote_engine_id):
             return remote
         if remote is not None:
-            del self._remotes[key]  # restarted since: ask afresh
-            with self._lock:
-                self._mapped.pop(key, None)
-            self.transport.close(remote.exported)
-            remote.sock.close()
+            self._retire(key, remote)  # restarted since: ask afresh
         sock = self._context.socket(zmq.DEALER)
         keep = False
         try:
@@ -1244,6 +1286,43 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         finally:
             if not keep:
                 sock.close()
+
+    def _retire(self, key, remote: _Remote):
+        """Drops a peer rank that restarted under a new engine id. Its old mapping stays open until nothing queued
+        can reach it (_poll_retired); saves pushing into it fail now, so no later store or push names it."""
+        del self._remotes[key]
+        remote.sock.close()
+        with self._lock:
+            self._mapped.pop(key, None)
+            for save in self._saves.values():
+                if any(table is remote.table for table in save.tables):
+                    save.failed = True  # its decode instance is gone: the one now at that port hears "not ok"
+            self._retired.append(_Retired(remote))
+
+    def _poll_retired(self):
+        """Closes replaced mappings once the engine thread has polled since the swap and every transport stream has
+        run past that poll's marker."""
+        with self._lock:
+            retired = [r for r in self._retired if r.passed]
+        for entry in retired:
+            close = False
+            try:
+                if entry.fences is None:
+                    entry.fences = []
+                    for stream in ({}, {"save": True}, {"relay": True}):
+                        entry.fences.append(self.transport.post([], [], entry.marker, **stream))
+                    continue
+                if not all(self.transport.done(fence) for fence in entry.fences):
+                    continue
+                close = True
+            except Exception as error:  # noqa: BLE001 - a mapping kept open is harmless; one closed early is not
+                logger.warning("keeping a replaced KV mapping open: %s", error)
+            for fence in entry.fences:
+                self.transport.release(fence)
+            if close:
+                self.transport.close(entry.remote.exported)
+            with self._lock:
+                self._retired.remove(entry)
 
     def _ask(self, key) -> dict:
         """One handshake round trip on a socket of its own, for its reply only."""

@@ -179,6 +179,10 @@ class KvxTransport:
     def release(self, xfer: transport.Transfer):
         xfer.release()
 
+    def drain(self):
+        """Waits for everything queued on the cache's device, by any thread: before peers' mappings close."""
+        torch.cuda.synchronize(self.device)
+
     def shutdown(self):
         """After every transfer was waited for: rings still queued then find the doorbell closed."""
         self.doorbell.close()

@@ -30,6 +30,7 @@ class HostTransport:
         self.ids = count()
         self.pending: dict[int, list] = {}
         self.opened = 0
+        self.closed: list[tuple] = []  # (exported, posts made by then) of every mapping closed
         self.posts: list[tuple] = []  # (layer, number of jobs) of every post, for tests to inspect
         self.stores: list[tuple] = []  # (number of peer targets, rows) of every store
         HostTransport.instances.append(self)
@@ -46,6 +47,10 @@ class HostTransport:
 
     def close(self, exported):
         self.opened -= 1
+        self.closed.append((exported, len(self.posts)))
+
+    def drain(self):
+        pass
 
     def _tables(self, tables, layer):
         out = [self.exported, *tables]

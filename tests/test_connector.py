@@ -3,7 +3,7 @@ case by case (tests/test_nixl_connector.py), with the results checked against th
 reference connector itself."""
 
 import socket
-from time import sleep
+from time import monotonic, sleep
 
 import numpy as np
 import pytest
@@ -213,8 +213,21 @@ def test_a_restarted_producer_is_asked_afresh_and_the_old_mapping_closed(sides):
     second = sides.make("kv_producer", 1, full_cache(2, False), port=first[0].kv_transfer.kv_port,
                         engine_id="prefill-b")
     consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-2": recv(second, [1], [4])}))
+    deadline = monotonic() + 5
+    while not consumers[0]._retired and monotonic() < deadline:
+        sleep(0.002)
+    # A copy queued before the swap may still read the old mapping: it stays open until the engine thread polls.
+    sleep(0.05)
+    transport = consumers[0].transport
+    assert transport.opened == 2 and not transport.closed
     assert wait_for(consumers[0]).finished_recving == {"d-2"}
-    assert consumers[0].transport.opened == 1
+    while transport.opened != 1 and monotonic() < deadline:
+        consumers[0].get_finished()
+        sleep(0.002)
+    assert transport.opened == 1 and not consumers[0]._retired
+    (exported, posts_by_then), = transport.closed
+    assert exported["spans"] == [list(span) for span in first[0].transport.spans]  # the first producer's
+    assert transport.posts[posts_by_then - 3 : posts_by_then] == [(None, 0)] * 3  # a fence on every stream first
     assert torch.equal(consumers[0].kv_caches[0][:, 1], rank_cache(full_cache(2, False), 0, 1)[:, 4])
 
 

@@ -8,10 +8,10 @@ import pytest
 import torch
 
 from lean_vllm_b200.kv_transfer import KVConnectorMetadata, KVConnectorOutput, cuda_ipc_connector
-from tests.connector_cases import TP_PAIRS, Sides, full_cache, wait_for
+from tests.connector_cases import BLOCK, TP_PAIRS, Sides, full_cache, wait_for
 from tests.helpers import bits, full_of
 from tests.host_transport import HostTransport
-from tests.push_cases import LOCAL, REMOTE, pushed_recv, run_push, save_req
+from tests.push_cases import LOCAL, REMOTE, pushed_recv, run_push, save_req, wait_ready
 
 
 @pytest.fixture(autouse=True)
@@ -97,6 +97,59 @@ def test_a_decode_instance_that_does_not_answer_fails_the_push_and_its_wait(side
     assert wait_for(producers[0]) == KVConnectorOutput(finished_sending={"p-1"})  # the blocks are freed
     assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})  # and the decode side prefills
     assert torch.equal(consumers[0].kv_caches[0], before)
+
+
+def test_a_save_into_a_decode_instance_that_restarted_fails_and_its_old_mapping_outlives_what_was_queued(sides):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    first = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode-a", accept_push=True)
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save_req(first)},
+                                                   save_progress={"p-1": len(REMOTE) * BLOCK}))
+    assert wait_ready(producers[0])
+    producers[0].save_kv_layer(0)  # queued into decode-a's blocks
+    first[0].shutdown()
+    sleep(0.05)
+    second = sides.make("kv_consumer", 1, full_cache(2, False), port=first[0].kv_transfer.kv_port,
+                        engine_id="decode-b", accept_push=True)
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={"p-2": save_req(second)}))
+    assert wait_ready(producers[0], "p-2")
+    assert producers[0]._saves["p-1"].failed  # its decode instance is gone: nothing more is pushed into it
+    transport = producers[0].transport
+    sleep(0.05)
+    assert transport.opened == 2 and not transport.closed  # the engine thread has not polled since the swap
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    assert wait_for(producers[0]).finished_sending == {"p-1"}  # its blocks are freed
+    deadline = monotonic() + 5
+    while transport.opened != 1 and monotonic() < deadline:
+        producers[0].get_finished()
+        sleep(0.002)
+    assert transport.opened == 1 and len(transport.closed) == 1
+    while "p-1" not in second[0]._saved and monotonic() < deadline:
+        sleep(0.002)
+    assert second[0]._saved["p-1"] == {0: False}  # the instance now at that port hears "not ok", and ignores it
+
+
+def test_a_landing_word_no_wait_takes_is_dropped_at_the_timeout(sides, monkeypatch):
+    import json
+
+    import zmq
+
+    monkeypatch.setenv("LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT", "0.3")
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    context = zmq.Context()
+    sock = context.socket(zmq.DEALER)
+    try:
+        sock.connect(f"tcp://127.0.0.1:{consumers[0].kv_transfer.kv_port}")
+        sock.send(json.dumps({"op": "saved", "request": "aborted", "rank": 0, "ok": True}).encode())
+        deadline = monotonic() + 5
+        while "aborted" not in consumers[0]._saved and monotonic() < deadline:
+            sleep(0.002)
+        assert consumers[0]._saved["aborted"] == {0: True}  # kept: its wait may come later
+        while "aborted" in consumers[0]._saved and monotonic() < deadline:
+            sleep(0.01)
+        assert "aborted" not in consumers[0]._saved and not consumers[0]._saved_seen
+    finally:
+        sock.close(linger=0)
+        context.term()
 
 
 def test_a_push_refused_when_posted_tells_the_decode_side_it_failed(sides):
