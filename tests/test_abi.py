@@ -99,3 +99,60 @@ def test_the_wait_selftest_checks_its_limit_before_launching():
     for bad in (0, -5, 10_000_001):
         with pytest.raises(_native.KvxError, match="limit"):
             _native.check(_native.lib().kvx_wait_selftest(bad, None))
+
+
+C_CLIENT = r"""
+#include <stdio.h>
+#include <string.h>
+#include "kvx.h"
+
+/* What a C host binding does: describe caches and jobs in host memory and ask the library. */
+int main(void) {
+    kvx_region src_regions[2] = {{1ull << 40, 4096, 512}, {2ull << 40, 4096, 512}};
+    kvx_region dst_regions[2] = {{3ull << 40, 2048, 512}, {4ull << 40, 2048, 512}};
+    kvx_cache caches[2] = {{src_regions, 2, 10}, {dst_regions, 2, 6}};
+    int32_t src_ids[2] = {9, 0}, dst_ids[2] = {5, 1}, bad_ids[1] = {6};
+    kvx_job job = {0, 1, src_ids, dst_ids, 2, 2, 0, 4, 0};
+    uint64_t bytes = 0;
+    unsigned char box[4096];
+    uint64_t lens[2];
+    if (kvx_abi_version() != KVX_ABI_VERSION) return 1;
+    if (kvx_job_bytes(caches, 2, &job, 1, &bytes) != KVX_OK || bytes != 2 * 2 * 4 * 512) return 2;
+    job.dst_block_ids = bad_ids;
+    job.src_block_ids = src_ids;
+    job.n_blocks = 1;
+    if (kvx_job_bytes(caches, 2, &job, 1, &bytes) != KVX_ERR_RANGE) return 3;
+    if (strstr(kvx_last_error(), "destination block id 6") == NULL) return 4;
+    /* One process as both ranks of a two-rank mailbox. */
+    if (kvx_mailbox_bytes(2, 64) > sizeof box) return 5;
+    memset(box, 0, sizeof box);
+    if (kvx_mailbox_post(box, 2, 1, 64, 1, "done", 4, 1.0) != KVX_OK) return 6;
+    if (kvx_mailbox_collect(box, 2, 64, 1, lens, 1.0) != KVX_OK || lens[1] != 4) return 7;
+    if (memcmp(box + 64 + kvx_mailbox_stride(64) + 16, "done", 4) != 0) return 8;
+    if (kvx_mailbox_release(box, 1) != KVX_OK) return 9;
+    if (kvx_mailbox_post(box, 2, 1, 64, 3, "", 0, 0.05) != KVX_ERR_TIMEOUT) return 10; /* step 2 was never read */
+    puts("ok");
+    return 0;
+}
+"""
+
+
+def test_a_plain_c99_client_compiles_against_the_header_and_runs_without_a_device(tmp_path):
+    """The boundary is C: the header compiles as strict C99, and a C program linked to libkvx.so gets the same
+    answers the ctypes binding gets (host validation and the step mailbox need no GPU)."""
+    import shutil
+    import subprocess
+
+    if not os.path.exists(_native.LIB_PATH):
+        pytest.skip("libkvx.so is not built here")
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    source = tmp_path / "client.c"
+    source.write_text(C_CLIENT)
+    binary = tmp_path / "client"
+    lib_dir = os.path.dirname(_native.LIB_PATH)
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    str(source), "-o", str(binary), "-L", lib_dir, "-lkvx", f"-Wl,-rpath,{lib_dir}"],
+                   check=True, capture_output=True, text=True)
+    run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.strip() == "ok", (run.returncode, run.stdout, run.stderr)
