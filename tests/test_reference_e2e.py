@@ -5,7 +5,8 @@ reference's connector table (as INTEGRATION.md does) carrying the KV between the
 It follows the reference's own check (tests/test_disagg_e2e.py:1-7, 94-124). The decode engine recomputes only the
 last prompt token, attending to the pulled KV. Its greedy tokens must therefore equal the prefill engine's when that
 engine runs the same prompt split the same way: all but one token, then that one. The prefill engine frees every
-held block once the decode engine has read them.
+held block once the decode engine has them. Both directions run: the reference's pull, and this package's push with
+the block ids announced by the decode instance.
 
 What runs on CPU here: the reference engine (scheduler, block manager, model runner, torch attention backend) and
 this package's connector halves, handshake, reader counting and release. The byte copy is the host transport's
@@ -113,19 +114,23 @@ def _engine(model: str, cache_folder: str, **kwargs):
     return LLMEngine(model, **ENGINE_ARGS, **kwargs)
 
 
-def _prefill(conn, model: str, cache_folder: str, kv_port: int):
+def _prefill(conn, model: str, cache_folder: str, kv_port: int, push_id: str | None):
     engine = _engine(model, cache_folder, enable_prefix_caching=False, long_prefill_token_threshold=len(PROMPT) - 1,
                      kv_transfer_config=json.dumps(dict(kv_connector="CudaIpcConnector", kv_role="kv_producer",
                                                         kv_port=kv_port)))
     from lean_vllm.sampling_params import SamplingParams
 
-    hand_off = SamplingParams(temperature=0, max_tokens=1, kv_transfer_params={"do_remote_decode": True})
-    engine.add_request(list(PROMPT), hand_off, "p-1")
-    params = None
-    while params is None:
-        params = next((output.kv_transfer_params for output in engine.step()[0] if output.finished), None)
-    conn.send(params)
-    while not engine.is_finished():  # until the decode engine has read the blocks and let them go
+    params = {"do_remote_decode": True}
+    if push_id is not None:  # the decode request came first and waits: push into the blocks it announces
+        conn.send("serving")
+        conn.recv()
+        params["kv_push_id"] = push_id
+    engine.add_request(list(PROMPT), SamplingParams(temperature=0, max_tokens=1, kv_transfer_params=params), "p-1")
+    result = None
+    while result is None:
+        result = next((output.kv_transfer_params for output in engine.step()[0] if output.finished), None)
+    conn.send(result)
+    while not engine.is_finished():  # until the decode engine has the blocks and they are let go
         engine.step()
         sleep(0.001)
     conn.send(engine.scheduler.block_manager.usage)
@@ -133,9 +138,10 @@ def _prefill(conn, model: str, cache_folder: str, kv_port: int):
     conn.send(reference[0]["token_ids"])
 
 
-def _decode(conn, model: str, cache_folder: str):
-    engine = _engine(model, cache_folder,
-                     kv_transfer_config=json.dumps(dict(kv_connector="CudaIpcConnector", kv_role="kv_consumer")))
+def _decode(conn, model: str, cache_folder: str, kv_port: int):
+    os.environ["LEAN_VLLM_KVX_ACCEPT_PUSH"] = "1"  # serves on kv_port, so a prefill engine may push into it
+    engine = _engine(model, cache_folder, kv_transfer_config=json.dumps(
+        dict(kv_connector="CudaIpcConnector", kv_role="kv_consumer", kv_port=kv_port)))
     from lean_vllm.sampling_params import SamplingParams
 
     params = conn.recv()
@@ -157,36 +163,55 @@ def _receive(conn, process, what: str, timeout: float = 300.0):
     raise AssertionError(what)
 
 
-def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carried(tmp_path):
-    model = str(tmp_path / "model")
-    make_checkpoint(model)
-    caches = tmp_path / "caches"
-    caches.mkdir()
+def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
-        kv_port = s.getsockname()[1]
+        return s.getsockname()[1]
+
+
+@pytest.fixture(scope="module")
+def checkpoint(tmp_path_factory):
+    folder = str(tmp_path_factory.mktemp("qwen3-random"))
+    make_checkpoint(folder)
+    return folder
+
+
+@pytest.mark.parametrize("mode", ["pull", "push"])
+def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carried(checkpoint, tmp_path, mode):
+    """Pull: the prefill finishes, hands its kv_transfer_params over, and the decode engine reads the blocks. Push:
+    the decode request is admitted first (kv_push, no block ids) and announces its blocks; the prefill engine,
+    given the same push id, writes them (all at hand-over: the reference model calls no per-layer hook)."""
+    caches = tmp_path / "caches"
+    caches.mkdir()
+    prefill_port, decode_port = _free_port(), _free_port()
+    push_id = "push-1" if mode == "push" else None
     ctx = mp.get_context("spawn")
     prefill_conn, prefill_child = ctx.Pipe()
     decode_conn, decode_child = ctx.Pipe()
-    processes = [
-        ctx.Process(target=_prefill, args=(prefill_child, model, str(caches), kv_port)),
-        ctx.Process(target=_decode, args=(decode_child, model, str(caches))),
-    ]
-    for process in processes:
+    prefill = ctx.Process(target=_prefill, args=(prefill_child, checkpoint, str(caches), prefill_port, push_id))
+    decode = ctx.Process(target=_decode, args=(decode_child, checkpoint, str(caches), decode_port))
+    for process in (prefill, decode):
         process.start()
-    prefill, decode = processes
     try:
-        params = _receive(prefill_conn, prefill, "the prefill engine never handed off")
-        assert params["do_remote_prefill"] and params["remote_port"] == kv_port
-        decode_conn.send(params)
+        if push_id is None:
+            params = _receive(prefill_conn, prefill, "the prefill engine never handed off")
+            assert params["do_remote_prefill"] and params["remote_port"] == prefill_port
+            decode_conn.send(params)
+        else:
+            assert _receive(prefill_conn, prefill, "the prefill engine never came up") == "serving"
+            decode_conn.send({"do_remote_prefill": True, "kv_push": True, "remote_request_id": push_id,
+                              "remote_engine_id": "", "remote_host": "127.0.0.1", "remote_port": prefill_port,
+                              "tp_size": 1, "remote_block_ids": []})
+            prefill_conn.send("go")
+            _receive(prefill_conn, prefill, "the prefill engine never finished its request")
         token_ids, num_prefill_tokens = _receive(decode_conn, decode, "the decode engine never finished")
-        assert _receive(prefill_conn, prefill, "the prefill engine kept its blocks") == 0.0  # all freed once read
+        assert _receive(prefill_conn, prefill, "the prefill engine kept its blocks") == 0.0  # all freed
         reference = _receive(prefill_conn, prefill, "the prefill engine's own run never finished")
     finally:
-        for process in processes:
+        for process in (prefill, decode):
             process.join(timeout=60)
             if process.is_alive():
                 process.kill()
-    assert num_prefill_tokens == 1  # only the last prompt token ran here; the rest was pulled
+    assert num_prefill_tokens == 1  # only the last prompt token ran here; the rest came from the prefill engine
     assert len(token_ids) == MAX_TOKENS or token_ids[-1] == VOCAB
     assert token_ids == reference
