@@ -231,6 +231,31 @@ def test_a_restarted_producer_is_asked_afresh_and_the_old_mapping_closed(sides):
     assert torch.equal(consumers[0].kv_caches[0][:, 1], rank_cache(full_cache(2, False), 0, 1)[:, 4])
 
 
+@pytest.mark.parametrize("failure", ["posted", "in flight"])
+def test_a_replaced_mapping_whose_fences_fail_stays_open(sides, failure):
+    """If the transport cannot show that the streams ran past the swap, the old mapping is never closed: one kept
+    open costs address space, one closed under a copy faults it."""
+    first = sides.make("kv_producer", 1, full_cache(0, False), engine_id="prefill-a")
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(first, [0], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    first[0].shutdown()
+    sleep(0.05)
+    second = sides.make("kv_producer", 1, full_cache(2, False), port=first[0].kv_transfer.kv_port,
+                        engine_id="prefill-b")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-2": recv(second, [1], [4])}))
+    deadline = monotonic() + 5
+    while not consumers[0]._retired and monotonic() < deadline:
+        sleep(0.002)
+    sleep(0.05)  # the load's own post is made in the pass that swapped the mapping
+    HostTransport.fail = failure
+    while consumers[0]._retired and monotonic() < deadline:
+        consumers[0].get_finished()
+        sleep(0.002)
+    assert not consumers[0]._retired
+    assert consumers[0].transport.opened == 2 and not consumers[0].transport.closed
+
+
 def test_a_taken_port_is_named(sides):
     with socket.socket() as taken:
         taken.bind(("127.0.0.1", 0))
