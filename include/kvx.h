@@ -181,7 +181,9 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
 int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
                  void *wait_event, void *stream, kvx_xfer_t *out);
 
-/* KVX_OK once the transfer's copies have landed, KVX_PENDING while in flight, <0 on failure.
+/* KVX_OK once the transfer's copies have landed, KVX_PENDING while in flight, <0 on failure: KVX_ERR_CUDA if the
+ * launch failed, KVX_ERR_DEVICE if a copy on its device gave up a bounded wait (bit 1 of the device error word,
+ * read without waiting on other streams once the transfer's event has completed).
  * Replaces check_xfer_state (nixl_connector.py:431). */
 int kvx_check_xfer(kvx_xfer_t xfer);
 
@@ -232,16 +234,17 @@ int kvx_mailbox_release(void *box, uint64_t seq);
  * (nixl_connector.py:421). Validates like kvx_copy; launches nothing. */
 int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, uint64_t *out_bytes);
 
-/* Reads and clears the device error word of the current device: 0, or the first error a kernel recorded -- 1 a copy's
- * bounded TMA wait ran out, 2 a store slot or block id past its cache (skipped), 4 kvx_wait_selftest gave up as
- * designed. */
+/* Reads and clears the device error word of the current device: 0, or the OR of the errors kernels recorded since
+ * the last read -- 1 a copy's bounded TMA wait ran out (its bytes did not all land), 2 a store slot or block id past
+ * its cache (skipped), 4 kvx_wait_selftest gave up as designed. While bit 1 is set, kvx_check_xfer fails every
+ * transfer on that device that completes (KVX_ERR_DEVICE): which copy gave up is not recorded. */
 int kvx_device_error(int *out_code);
 
 /* Runs, on `stream`, the bounded wait that guards every TMA copy against a transfer that never arrives: one
  * thread waits on an mbarrier armed for bytes no copy will bring, gives up after limit_us (1 us .. 10 s) and
- * records code 4 in the device word, as a stuck copy would (1). Nothing is copied, nothing faults or hangs; for
- * tests of the failure path. */
-int kvx_wait_selftest(int limit_us, void *stream);
+ * records `code` in the device word: 4 (the self-test's own bit), or 1 to stand in for a stuck copy. Nothing is
+ * copied, nothing faults or hangs; for tests of the failure path. */
+int kvx_wait_selftest(int limit_us, int code, void *stream);
 
 /* Kernel launches issued by this process so far (all entry points), for launch accounting. */
 uint64_t kvx_launch_count(void);

@@ -40,6 +40,10 @@ class KvxRangeError(KvxError):
     """A block id or head range outside its cache (nixl_connector.py:398-399)."""
 
 
+class KvxDeviceError(KvxError):
+    """A kernel gave up a bounded wait: a copy whose bytes did not all land (kvx_device_error reads the word)."""
+
+
 class KvxTimeout(KvxError):
     """A host wait ran out: a rank that never posted its step to the mailbox."""
 
@@ -145,7 +149,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kvx_job_bytes": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int,
                        ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "kvx_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
-    "kvx_wait_selftest": ([ctypes.c_int, _P], ctypes.c_int),
+    "kvx_wait_selftest": ([ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
     "kvx_launch_count": ([], ctypes.c_uint64),
 }
 
@@ -180,7 +184,8 @@ def check(rc: int) -> int:
     if rc >= 0:
         return rc
     message = lib().kvx_last_error().decode(errors="replace")
-    raise {KVX_ERR_RANGE: KvxRangeError, KVX_ERR_TIMEOUT: KvxTimeout}.get(rc, KvxError)(rc, message)
+    raise {KVX_ERR_RANGE: KvxRangeError, KVX_ERR_TIMEOUT: KvxTimeout, KVX_ERR_DEVICE: KvxDeviceError}.get(
+        rc, KvxError)(rc, message)
 
 
 def flags(engine: int = ENGINE_AUTO, tile_bytes: int = 0, ctas_per_sm: int = 0, sm_budget: int = 0) -> int:

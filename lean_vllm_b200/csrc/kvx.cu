@@ -106,7 +106,12 @@ struct Params {
 };
 static_assert(sizeof(Params) <= 32764, "kernel parameter space is 32764 bytes");
 
-__device__ int g_device_error;  // first bounded-wait failure on this device, read by kvx_device_error
+// Errors kernels record on this device, as bits (read and cleared by kvx_device_error): a copy's bounded TMA wait ran
+// out (its bytes did not all land), a store slot or block id past its cache (skipped), the wait self-test gave up.
+constexpr int kErrCopyWait = 1;
+constexpr int kErrPastCache = 2;
+constexpr int kErrSelftest = 4;
+__device__ int g_device_error;
 
 struct Tile {
     const char *src;
@@ -274,7 +279,7 @@ __global__ void __launch_bounds__(32) kvx_wait_selftest_kernel(uint64_t limit_ns
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(16u) : "memory");
-    if (!mbar_wait(b, 0, globaltimer() + limit_ns)) atomicCAS(&g_device_error, 0, code);
+    if (!mbar_wait(b, 0, globaltimer() + limit_ns)) atomicOr(&g_device_error, code);
 }
 
 __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Params p) {
@@ -322,7 +327,7 @@ __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Param
         }
     }
     if (!ok) {
-        atomicCAS(&g_device_error, 0, p.error_code);
+        atomicOr(&g_device_error, p.error_code);
         // Loads issued but not waited for may still be writing shared memory: give each a bounded wait.
         const uint64_t issued = mine < landed + kTmaStages ? mine : landed + kTmaStages;
         const uint64_t drain = globaltimer() + kWaitLimitNs;
@@ -373,7 +378,7 @@ __device__ __forceinline__ int32_t resolve_slot(const StoreParams &p, int d, uin
     const int32_t shift0 = p.dests[0].block_shift;
     const uint32_t b = shift0 >= 0 ? (uint32_t)first_slot >> shift0 : (uint32_t)first_slot / block_size0;
     if (b >= (uint32_t)dst.block_map_len) {
-        atomicCAS(&g_device_error, 0, 2);
+        atomicOr(&g_device_error, kErrPastCache);
         return -1;
     }
     const int32_t mapped = dst.block_map[b];  // a block no save covers maps to -1
@@ -411,7 +416,7 @@ template <int VEC, bool FAST>
 __device__ __forceinline__ void put(const StoreLane &l, int32_t slot, typename Vec<VEC>::T data) {
     if (slot < 0) return;  // padding: no cache slot
     if (slot >= l.limit) {
-        atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
+        atomicOr(&g_device_error, kErrPastCache);  // a slot past the cache: skipped, never written
         return;
     }
     uint64_t at;
@@ -432,7 +437,7 @@ __device__ __forceinline__ void store_row(const StoreParams &p, const StoreDest 
                                           int32_t head, uint32_t byte_in_row, typename Vec<VEC>::T data) {
     if (slot < 0) return;  // padding: no cache slot
     if (slot >= dst.num_blocks * dst.block_size) {
-        atomicCAS(&g_device_error, 0, 2);  // a slot past the cache: skipped, never written
+        atomicOr(&g_device_error, kErrPastCache);  // a slot past the cache: skipped, never written
         return;
     }
     const uint32_t block = dst.block_shift >= 0 ? (uint32_t)slot >> dst.block_shift
@@ -679,7 +684,7 @@ int launch(Params &p, const Config &cfg, cudaStream_t stream) {
     const int sms = cfg.sm_budget > 0 && cfg.sm_budget < info->sms ? cfg.sm_budget : info->sms;
     const uint64_t cap = (uint64_t)sms * cfg.ctas_per_sm;
     const unsigned grid = (unsigned)std::min<uint64_t>(p.total_tiles, cap);
-    p.error_code = 1;
+    p.error_code = kErrCopyWait;
     if (cfg.engine == KVX_ENGINE_TMA) {
         const size_t smem = (size_t)cfg.tile_bytes * kTmaStages;
         if (info->tma_smem_set < smem) {
@@ -925,6 +930,37 @@ std::shared_ptr<Bell> find_bell(int id) {
     std::lock_guard<std::mutex> lock(g_bells_mu);
     auto it = g_bells.find(id);
     return it == g_bells.end() ? nullptr : it->second;
+}
+
+// ------------------------------------------------------------------------------------------------ error word probe
+
+// Reads a device's error word without waiting on anyone else's streams: a 4-byte copy on a non-blocking stream of the
+// library's own into pinned host memory (one pair per device, under a lock), then a wait on that stream alone.
+struct ErrorProbe {
+    cudaStream_t stream = nullptr;
+    int *word = nullptr;
+};
+std::mutex g_probe_mu;
+std::map<int, ErrorProbe> g_probes;
+
+int read_device_errors(int device, int *out_bits) {
+    std::lock_guard<std::mutex> lock(g_probe_mu);
+    int prev;
+    KVX_CUDA(cudaGetDevice(&prev));
+    if (prev != device) KVX_CUDA(cudaSetDevice(device));
+    ErrorProbe &probe = g_probes[device];
+    cudaError_t e = cudaSuccess;
+    if (!probe.stream) e = cudaStreamCreateWithFlags(&probe.stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess && !probe.word) e = cudaHostAlloc(reinterpret_cast<void **>(&probe.word), sizeof(int),
+                                                           cudaHostAllocPortable);
+    if (e == cudaSuccess)
+        e = cudaMemcpyFromSymbolAsync(probe.word, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                      probe.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(probe.stream);
+    if (e == cudaSuccess) *out_bits = *probe.word;
+    if (prev != device) (void)cudaSetDevice(prev);
+    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+    return KVX_OK;
 }
 
 }  // namespace
@@ -1206,12 +1242,18 @@ int kvx_check_xfer(kvx_xfer_t xfer) {
     if (!xfer) return fail(KVX_ERR_INVALID, "null transfer");
     Xfer *x = reinterpret_cast<Xfer *>(xfer);
     const cudaError_t e = cudaEventQuery(x->done);
-    if (e == cudaSuccess) return KVX_OK;
     if (e == cudaErrorNotReady) {
         (void)cudaGetLastError();
         return KVX_PENDING;
     }
-    return fail(KVX_ERR_CUDA, "transfer failed: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "transfer failed: %s", cudaGetErrorString(e));
+    // The event says the launch ended. A TMA copy that gave up a bounded wait ends too, with its bytes not all
+    // landed, and says so only in the device word: look there before reporting success.
+    int bits = 0;
+    if (int rc = read_device_errors(x->device, &bits)) return rc;
+    if (bits & kErrCopyWait)
+        return fail(KVX_ERR_DEVICE, "a copy on device %d gave up a bounded wait, so not every byte landed", x->device);
+    return KVX_OK;
 }
 
 int kvx_release_xfer(kvx_xfer_t xfer) {
@@ -1326,9 +1368,12 @@ int kvx_mailbox_release(void *box, uint64_t seq) {
     return KVX_OK;
 }
 
-int kvx_wait_selftest(int limit_us, void *stream) {
+int kvx_wait_selftest(int limit_us, int code, void *stream) {
     if (limit_us < 1 || limit_us > 10000000) return fail(KVX_ERR_INVALID, "limit %d us: 1 us to 10 s", limit_us);
-    kvx_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_us * 1000, 4);
+    if (code != kErrSelftest && code != kErrCopyWait)
+        return fail(KVX_ERR_INVALID, "code %d: %d (the self-test's) or %d (a stuck copy's)", code, kErrSelftest,
+                    kErrCopyWait);
+    kvx_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_us * 1000, code);
     KVX_CUDA(cudaGetLastError());
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return KVX_OK;

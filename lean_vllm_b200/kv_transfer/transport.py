@@ -235,9 +235,10 @@ def launch_count() -> int:
     return int(lib().kvx_launch_count())
 
 
-def wait_selftest(limit_us: int, stream: int = 0) -> None:
-    """Launches the bounded-wait self-test (kvx_wait_selftest): after limit_us the device word reads 4."""
-    check(lib().kvx_wait_selftest(limit_us, stream or None))
+def wait_selftest(limit_us: int, code: int = 4, stream: int = 0) -> None:
+    """Launches the bounded-wait self-test (kvx_wait_selftest): after limit_us the device word has bit `code` set
+    (4, the self-test's own; 1 stands in for a stuck copy, which fails the device's transfers until it is read)."""
+    check(lib().kvx_wait_selftest(limit_us, code, stream or None))
 
 
 def device_error() -> int:

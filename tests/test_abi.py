@@ -98,7 +98,10 @@ def test_the_wait_selftest_checks_its_limit_before_launching():
         pytest.skip("libkvx.so is not built here")
     for bad in (0, -5, 10_000_001):
         with pytest.raises(_native.KvxError, match="limit"):
-            _native.check(_native.lib().kvx_wait_selftest(bad, None))
+            _native.check(_native.lib().kvx_wait_selftest(bad, 4, None))
+    for bad in (0, 2, 3, 8):
+        with pytest.raises(_native.KvxError, match="the self-test's"):
+            _native.check(_native.lib().kvx_wait_selftest(1000, bad, None))
 
 
 C_CLIENT = r"""

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from lean_vllm_b200._native import ENGINE_LSU, ENGINE_TMA, KvxError, KvxRangeError, flags
+from lean_vllm_b200._native import ENGINE_LSU, ENGINE_TMA, KvxDeviceError, KvxError, KvxRangeError, flags
 from lean_vllm_b200.kv_transfer import transport
 from lean_vllm_b200.kv_transfer.shares import head_shares, split_heads
 from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
@@ -283,4 +283,28 @@ def test_a_bounded_wait_that_runs_out_reports_and_leaves_the_context_usable():
     dst = [torch.zeros_like(s) for s in src]
     transport.copy([CacheTable.from_tensors(src), CacheTable.from_tensors(dst)], [CopyJob(0, 1, [1, 2], [0, 3], 0, 0, 8)])
     torch.cuda.synchronize()
+    assert torch.equal(dst[0][:, [0, 3]], src[0][:, [1, 2]])
+
+
+def test_a_copy_that_gave_up_fails_the_transfers_that_end_after_it_until_the_word_is_read():
+    """A TMA copy whose bounded wait ran out ends with its bytes not all landed, and only the device word says so.
+    The self-test sets that bit (1) without copying anything: the next transfer's check must fail rather than
+    report the load landed, and once the word is read and cleared a transfer succeeds again."""
+    src = _qwen_like(4, 1, seed=9)
+    dst = [torch.zeros_like(s) for s in src]
+    caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
+    jobs = [CopyJob(0, 1, [1, 2], [0, 3], 0, 0, 8)]
+    stream = torch.cuda.current_stream().cuda_stream
+    assert transport.device_error() == 0
+    transport.wait_selftest(20_000, code=1, stream=stream)  # 20 ms
+    xfer = transport.transfer(caches, jobs, stream)
+    torch.cuda.synchronize()
+    with pytest.raises(KvxDeviceError, match="gave up a bounded wait"):
+        xfer.done()
+    xfer.release()
+    assert transport.device_error() == 1
+    xfer = transport.transfer(caches, jobs, stream)
+    torch.cuda.synchronize()
+    assert xfer.done()
+    xfer.release()
     assert torch.equal(dst[0][:, [0, 3]], src[0][:, [1, 2]])
