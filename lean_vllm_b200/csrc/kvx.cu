@@ -606,8 +606,8 @@ int plan(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs,
                                 (unsigned long long)a.head_bytes, (unsigned long long)b.head_bytes);
                 if (job.num_heads < 0 || job.src_first_head < 0 || job.dst_first_head < 0)
                     return fail(KVX_ERR_INVALID, "job %d: negative head range", j);
-                if ((uint64_t)(job.src_first_head + job.num_heads) * a.head_bytes > a.block_bytes ||
-                    (uint64_t)(job.dst_first_head + job.num_heads) * b.head_bytes > b.block_bytes)
+                if (((uint64_t)job.src_first_head + (uint64_t)job.num_heads) * a.head_bytes > a.block_bytes ||
+                    ((uint64_t)job.dst_first_head + (uint64_t)job.num_heads) * b.head_bytes > b.block_bytes)
                     return fail(KVX_ERR_RANGE, "job %d: heads [%d, +%d) / [%d, +%d) pass the end of a block", j,
                                 job.src_first_head, job.num_heads, job.dst_first_head, job.num_heads);
                 chunk = (uint64_t)job.num_heads * a.head_bytes;
@@ -1149,7 +1149,7 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
         if (num_tokens > 0 && !s.slot_mapping && !s.block_map)
             return fail(KVX_ERR_INVALID, "destination %d: null slots", d);
         if (s.src_first_head < 0 || s.num_heads < 0 || s.dst_first_head < 0 ||
-            s.src_first_head + s.num_heads > num_heads)
+            (int64_t)s.src_first_head + s.num_heads > num_heads)
             return fail(KVX_ERR_RANGE, "destination %d: heads [%d, +%d) of %d", d, s.src_first_head, s.num_heads,
                         num_heads);
         if (s.block_stride < 0 || s.token_stride < 0 || s.head_stride < 0)

@@ -52,6 +52,8 @@ def test_host_validation_runs_without_a_device():
         job_bytes([src, dst], [CopyJob(0, 1, [9], [6], 2, 0, 4)])
     with pytest.raises(_native.KvxRangeError, match="pass the end of a block"):
         job_bytes([src, dst], [CopyJob(0, 1, [0], [0], 0, 1, 4)])
+    with pytest.raises(_native.KvxRangeError, match="pass the end of a block"):  # no int32 wrap-around
+        job_bytes([src, dst], [CopyJob(0, 1, [0], [0], 2**31 - 1, 0, 2**31 - 1)])
     with pytest.raises(_native.KvxError, match="outside the 2 given"):
         job_bytes([src, dst], [CopyJob(0, 2, [0], [0], 0, 0, 1)])
 
