@@ -1544,9 +1544,16 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: bf16-sized host caches, seeded shuffled block tables",
-        "config": {"workload": f"{spec.name} (reference CPU transfer path, TP1 -> TP1)",
-                   "requests": "bounded sample per step",
-                   "prompt_lengths": f"{spec.lengths[0]} [{spec.lengths[1]}, {spec.lengths[2]}], seed {args.seed}"},
+        # The same workload our arm names at this N (so the two lines compare), timed on a bounded sample of it.
+        "config": {"workload": (f"{spec.name}/loopback-1gpu" if args.gpus == 1 else
+                                f"{spec.name}/{args.gpus // spec.group_size}x-tp{spec.prefill_tp}to{spec.decode_tp}"),
+                   "shape": spec.describe(),
+                   "requests_per_step": len(reqs),
+                   "prompt_lengths": f"{spec.lengths[0]} [{spec.lengths[1]}, {spec.lengths[2]}], seed {args.seed}",
+                   "mode": args.mode,
+                   "timed_sample": base["sample"],
+                   "path": "the reference's CPU transfer path: block_descs rows and one memmove per row (the NIXL "
+                           "READ its tests fake), restated in C, rows split over every host thread"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": base["cores"], "kind": "port",
                          "sample": base["sample"]},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
