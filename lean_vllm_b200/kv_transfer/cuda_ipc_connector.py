@@ -687,7 +687,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         if not answer_only and self._deferred:
             deferred, self._deferred = self._deferred, []
             for identity, message in deferred:
-                self._handle(identity, message)
+                self._handle_one(identity, message)
         while True:
             try:
                 identity, raw = self._server.recv_multipart(zmq.NOBLOCK)
@@ -703,7 +703,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if answer_only and message.get("op") != "handshake":
                 self._deferred.append((identity, message))
                 continue
+            self._handle_one(identity, message)
+
+    def _handle_one(self, identity, message: dict):
+        """A peer's message whose fields do not parse is dropped with a warning: it must not end this thread."""
+        try:
             self._handle(identity, message)
+        except (ValueError, TypeError, AttributeError) as error:
+            logger.warning("ignoring a malformed KV message %.200r: %s", message, error)
 
     def _handle(self, identity, message: dict):
         op = message.get("op")
@@ -712,8 +719,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             return
         if op == "expect":
             push_id = str(message.get("push_id"))
+            # Parsed here, so one that does not parse is dropped before _connect (which also runs from the queue).
+            expect = {"skip": int(message.get("skip", 0)), "block_ids": [int(b) for b in message.get("block_ids", [])],
+                      "engine_id": str(message.get("engine_id", "")), "host": str(message.get("host", "")),
+                      "port": int(message.get("port", 0)), "tp_size": int(message.get("tp_size", 1))}
+            if expect["tp_size"] < 1 or expect["skip"] < 0:
+                raise ValueError("an announcement with tp_size below 1 or a negative skip")
             with self._lock:
-                self._expects.setdefault(push_id, message)
+                self._expects.setdefault(push_id, expect)
                 request_id = self._push_ids.get(push_id)
             if request_id is not None:
                 self._connect(request_id)
@@ -1041,13 +1054,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 if expect is None:
                     return  # its decode ranks have not announced themselves yet
                 self._push_ids.pop(str(save.req.push_id), None)
-                skip = int(expect.get("skip", 0))
-                remote_ids = [int(b) for b in expect.get("block_ids", [])]
+                skip, remote_ids = expect["skip"], expect["block_ids"]
                 local_ids = list(save.req.local_block_ids)[skip:]
-                save.req = ReqToSave(local_ids, remote_ids, str(expect.get("engine_id", "")),
-                                     str(expect.get("host", "")), int(expect.get("port", 0)),
-                                     int(expect.get("tp_size", 1)), save.req.push_id,
-                                     max(save.req.cached_blocks - skip, 0))
+                save.req = ReqToSave(local_ids, remote_ids, expect["engine_id"], expect["host"], expect["port"],
+                                     expect["tp_size"], save.req.push_id, max(save.req.cached_blocks - skip, 0))
                 save.targets = self._targets(save.req)
                 if len(local_ids) != len(remote_ids):
                     save.failed = True  # still mapped below, so the decode ranks hear that nothing comes

@@ -256,6 +256,36 @@ def test_a_replaced_mapping_whose_fences_fail_stays_open(sides, failure):
     assert consumers[0].transport.opened == 2 and not consumers[0].transport.closed
 
 
+def test_malformed_messages_are_dropped_and_the_rank_keeps_serving(sides, caplog):
+    """Garbage, and messages whose fields do not parse, reach a producer rank's socket; each is dropped with a
+    warning, and the rank still answers handshakes and counts readers."""
+    import json
+
+    import zmq
+
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    context = zmq.Context()
+    sock = context.socket(zmq.DEALER)
+    try:
+        sock.connect(f"tcp://127.0.0.1:{producers[0].kv_transfer.kv_port}")
+        for message in (b"not json", b"[1, 2]", {"op": "part", "request": "x", "rank": "one", "ok": True},
+                        {"op": "saved", "request": "x", "rank": [0]}, {"op": "expect", "push_id": "p", "tp_size": 0},
+                        {"op": "expect", "push_id": "p", "block_ids": ["a"]}, {"op": "notify", "message": "no-colon"}):
+            sock.send(message if isinstance(message, bytes) else json.dumps(message).encode())
+        sleep(0.1)
+    finally:
+        sock.close(linger=0)
+        context.term()
+    assert producers[0]._thread.is_alive()
+    assert not producers[0]._expects
+    assert "ignoring a malformed KV message" in caplog.text
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    assert wait_for(producers[0]).finished_sending == {"p-1"}
+
+
 def test_a_taken_port_is_named(sides):
     with socket.socket() as taken:
         taken.bind(("127.0.0.1", 0))
