@@ -347,6 +347,29 @@ def test_an_abort_mid_load_frees_the_decode_blocks_once_the_load_ended(engines):
     assert prefill.scheduler.block_manager.free_block_queue.num_free_blocks == BLOCKS
 
 
+def test_an_abort_while_pushed_holds_the_decode_blocks_until_the_pushes_landed(engines):
+    """Push mode: the decode request is aborted while it waits for the prefill to write its blocks. The reference
+    scheduler keeps them (the prefill may still be pushing into them) until the connector reports the wait over,
+    which it does once the prefill has said every push landed; then both sides have freed everything."""
+    prefill = engines("kv_producer", "prefill-engine")
+    decode = engines("kv_consumer", "decode-engine", accept_push=True)
+    prompt = [50 + (i * 3) % 40 for i in range(21)]
+    push_id = "push-9"
+    decode_params = {"do_remote_prefill": True, "kv_push": True, "remote_request_id": push_id,
+                     "remote_engine_id": "", "remote_host": "127.0.0.1",
+                     "remote_port": prefill.config.kv_transfer.kv_port, "tp_size": 1, "remote_block_ids": []}
+    decode.add(prompt, SamplingParams(max_tokens=2, ignore_eos=True, kv_transfer_params=decode_params), "d-9")
+    decode.step()
+    assert decode.scheduler.abort("d-9")
+    assert decode.scheduler.block_manager.free_block_queue.num_free_blocks < BLOCKS  # held for the pushes
+    prefill.add(prompt, SamplingParams(max_tokens=1, ignore_eos=True,
+                                       kv_transfer_params={"do_remote_decode": True, "kv_push_id": push_id}), "p-9")
+    step_until([prefill, decode], lambda out: decode.is_finished() and prefill.is_finished())
+    assert decode.scheduler.block_manager.free_block_queue.num_free_blocks == BLOCKS
+    assert prefill.scheduler.block_manager.free_block_queue.num_free_blocks == BLOCKS
+    assert prefill.model_runner.worker.transport.posts  # the prefill did push into the held blocks
+
+
 def test_the_prefill_s_released_blocks_stay_in_its_prefix_cache(engines):
     """Once the decode side has read them, the prefill engine frees the held blocks into its prefix cache: the same
     prompt served again there finds its full blocks cached."""
