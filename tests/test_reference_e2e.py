@@ -6,7 +6,9 @@ It follows the reference's own check (tests/test_disagg_e2e.py:1-7, 94-124). The
 last prompt token, attending to the pulled KV. Its greedy tokens must therefore equal the prefill engine's when that
 engine runs the same prompt split the same way: all but one token, then that one. The prefill engine frees every
 held block once the decode engine has them. Both directions run: the reference's pull, and this package's push with
-the block ids announced by the decode instance.
+the block ids announced by the decode instance. A TP2 prefill engine feeding a TP1 decode engine runs too: there the
+two engines' tokens are not comparable (different summation orders), so the decode rank instead compares every
+pulled token row, head by head, with the producer rank that computed it.
 
 What runs on CPU here: the reference engine (scheduler, block manager, model runner, torch attention backend) and
 this package's connector halves, handshake, reader counting and release. The byte copy is the host transport's
@@ -18,7 +20,6 @@ import json
 import multiprocessing as mp
 import os
 import socket
-import sys
 from time import sleep
 
 import pytest
@@ -28,7 +29,7 @@ REFERENCE_ROOT = os.path.abspath(
 if not os.path.isdir(os.path.join(REFERENCE_ROOT, "lean_vllm")):
     pytest.skip("no lean-vLLM reference checkout", allow_module_level=True)
 
-VOCAB = 256  # word-level tokens "t0".."t255", then "<eos>"
+VOCAB = 256  # word-level tokens "t0".."t255", then "<eos>" and "<pad>"
 PROMPT = [(7 * i + 3) % VOCAB for i in range(90)]  # five 16-token blocks and a bit
 MAX_TOKENS = 16
 ENGINE_ARGS = dict(enforce_eager=True, kvcache_memory_gb=0.01, max_model_len=256, max_num_batched_tokens=256)
@@ -42,14 +43,16 @@ def make_checkpoint(folder: str):
     from tokenizers import Tokenizer, models, pre_tokenizers
 
     os.makedirs(folder, exist_ok=True)
-    words = Tokenizer(models.WordLevel({f"t{i}": i for i in range(VOCAB)} | {"<eos>": VOCAB}, unk_token="t0"))
+    # "<pad>" is never produced by the prompt; it makes the table even, as a TP2 engine splits it in halves.
+    words = Tokenizer(models.WordLevel({f"t{i}": i for i in range(VOCAB)} | {"<eos>": VOCAB, "<pad>": VOCAB + 1},
+                                       unk_token="t0"))
     words.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
     words.save(os.path.join(folder, "tokenizer.json"))
     with open(os.path.join(folder, "tokenizer_config.json"), "w") as f:
         json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "eos_token": "<eos>", "unk_token": "t0"}, f)
     hidden, inner, heads, kv_heads, dim, layers = 64, 128, 4, 2, 32, 2
     with open(os.path.join(folder, "config.json"), "w") as f:
-        json.dump({"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "vocab_size": VOCAB + 1,
+        json.dump({"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "vocab_size": VOCAB + 2,
                    "hidden_size": hidden, "intermediate_size": inner, "num_hidden_layers": layers,
                    "num_attention_heads": heads, "num_key_value_heads": kv_heads, "head_dim": dim,
                    "max_position_embeddings": 512, "rms_norm_eps": 1e-6, "rope_theta": 1000000.0,
@@ -60,7 +63,7 @@ def make_checkpoint(folder: str):
     def weight(*shape):
         return (torch.randn(*shape, generator=generator) * 0.1).to(torch.bfloat16)
 
-    tensors = {"model.embed_tokens.weight": weight(VOCAB + 1, hidden), "lm_head.weight": weight(VOCAB + 1, hidden),
+    tensors = {"model.embed_tokens.weight": weight(VOCAB + 2, hidden), "lm_head.weight": weight(VOCAB + 2, hidden),
                "model.norm.weight": torch.ones(hidden, dtype=torch.bfloat16)}
     for i in range(layers):
         at = f"model.layers.{i}."
@@ -81,41 +84,22 @@ def make_checkpoint(folder: str):
 
 
 def _engine(model: str, cache_folder: str, **kwargs):
-    """A reference LLMEngine on CPU with CudaIpcConnector in its connector table, its KV caches in shared files."""
+    """A reference LLMEngine on CPU with CudaIpcConnector in its connector table and its KV caches in shared files,
+    on every tensor-parallel rank (tests/kvx_reference_runner.py)."""
     os.environ["LEAN_VLLM_DEVICE"] = "cpu"
-    import torch
-
-    torch._dynamo.config.disable = True  # the reference compiles a few layers; this image has no OpenMP for inductor
-    sys.path.insert(0, REFERENCE_ROOT)
-    import lean_vllm.kv_transfer as ref_kv
-    from lean_vllm.engine import model_runner
+    os.environ["KVX_REFERENCE_ROOT"] = REFERENCE_ROOT
+    os.environ["KVX_TEST_CACHE_DIR"] = cache_folder
+    import tests.kvx_reference_runner  # noqa: F401 - the setup, in this process and every rank it spawns
     from lean_vllm.engine.llm_engine import LLMEngine
 
-    from lean_vllm_b200.kv_transfer import cuda_ipc_connector
-    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorScheduler, CudaIpcConnectorWorker
-    from tests.shm_transport import ShmTransport, shared_cache
-
-    ref_kv.CONNECTORS["CudaIpcConnector"] = (CudaIpcConnectorScheduler, CudaIpcConnectorWorker)
-    cuda_ipc_connector.make_transport = ShmTransport
-    allocate = model_runner.ModelRunner.allocate_kv_cache
-
-    def shared_empty(shape, **_):
-        assert torch.get_default_dtype() == torch.bfloat16
-        return shared_cache(tuple(shape), directory=cache_folder)
-
-    def allocate_shared(self):  # the engine's own allocation, with each layer's tensor in a shared file
-        empty, torch.empty = torch.empty, shared_empty
-        try:
-            allocate(self)
-        finally:
-            torch.empty = empty
-
-    model_runner.ModelRunner.allocate_kv_cache = allocate_shared
     return LLMEngine(model, **ENGINE_ARGS, **kwargs)
 
 
-def _prefill(conn, model: str, cache_folder: str, kv_port: int, push_id: str | None):
-    engine = _engine(model, cache_folder, enable_prefix_caching=False, long_prefill_token_threshold=len(PROMPT) - 1,
+def _prefill(conn, model: str, cache_folder: str, kv_port: int, push_id: str | None, tp: int):
+    # The prompt runs split n-1 + 1 where the split is comparable (TP1). The reference engine at TP > 1 cannot run a
+    # chunk that samples nothing (its logits gather reshapes zero rows), so there the prompt runs whole.
+    split = dict(long_prefill_token_threshold=len(PROMPT) - 1) if tp == 1 else {}
+    engine = _engine(model, cache_folder, enable_prefix_caching=False, tensor_parallel_size=tp, **split,
                      kv_transfer_config=json.dumps(dict(kv_connector="CudaIpcConnector", kv_role="kv_producer",
                                                         kv_port=kv_port)))
     from lean_vllm.sampling_params import SamplingParams
@@ -134,23 +118,65 @@ def _prefill(conn, model: str, cache_folder: str, kv_port: int, push_id: str | N
         engine.step()
         sleep(0.001)
     conn.send(engine.scheduler.block_manager.usage)
-    reference = engine.generate([list(PROMPT)], SamplingParams(temperature=0, max_tokens=MAX_TOKENS), use_tqdm=False)
-    conn.send(reference[0]["token_ids"])
+    conn.recv()  # the decode side has compared its copy with the freed blocks: they may be reused now
+    reference = None
+    if tp == 1:  # across sizes the tokens are not comparable (see the test)
+        reference = engine.generate([list(PROMPT)], SamplingParams(temperature=0, max_tokens=MAX_TOKENS),
+                                    use_tqdm=False)[0]["token_ids"]
+    conn.send(reference)
+    engine.exit()  # the other ranks leave their loop before this process ends
 
 
-def _decode(conn, model: str, cache_folder: str, kv_port: int):
+def _pulled_bytes_match(worker, req, positions: int) -> bool:
+    """This decode rank's copy of the first `positions` prompt tokens against every producer rank's blocks, mapped
+    here by the handshake: each head share of head_shares, token rows compared byte for byte, every layer, K and V."""
+    import ctypes
+
+    from lean_vllm_b200.kv_transfer.shares import head_shares, split_heads
+
+    heads = split_heads(worker.num_heads, worker.tp_size, req.remote_tp_size)
+    block = worker.block_size
+    compared = 0
+    for share in head_shares(worker.rank, worker.tp_size, req.remote_tp_size, heads):
+        remote = worker._remotes[(req.remote_host, req.remote_port + share.remote_rank)].table["regions"]
+        for (mine, my_block, my_head), (theirs, their_block, their_head) in zip(worker.transport.regions, remote):
+            row = my_head // block  # one token of one head
+            for i, (local, src) in enumerate(zip(req.local_block_ids, req.remote_block_ids)):
+                tokens = min(block, positions - i * block)
+                for k in range(share.num_heads if tokens > 0 else 0):
+                    a = mine + local * my_block + (share.local_head + k) * my_head
+                    b = theirs + src * their_block + (share.remote_head + k) * their_head
+                    if ctypes.string_at(a, tokens * row) != ctypes.string_at(b, tokens * row):
+                        return False
+                    compared += tokens * row
+    return compared > 0
+
+
+def _decode(conn, model: str, cache_folder: str, kv_port: int, tp: int):
     os.environ["LEAN_VLLM_KVX_ACCEPT_PUSH"] = "1"  # serves on kv_port, so a prefill engine may push into it
-    engine = _engine(model, cache_folder, kv_transfer_config=json.dumps(
+    engine = _engine(model, cache_folder, tensor_parallel_size=tp, kv_transfer_config=json.dumps(
         dict(kv_connector="CudaIpcConnector", kv_role="kv_consumer", kv_port=kv_port)))
     from lean_vllm.sampling_params import SamplingParams
 
+    worker, loads = engine.model_runner.kv_connector, {}
+    start_load_kv = worker.start_load_kv
+
+    def recording(metadata):  # what the scheduler half asked this rank to load
+        loads.update(metadata.reqs_to_recv)
+        start_load_kv(metadata)
+
+    worker.start_load_kv = recording
     params = conn.recv()
     sampling_params = SamplingParams(temperature=0, max_tokens=MAX_TOKENS, kv_transfer_params=params)
     outputs = engine.generate([list(PROMPT)], sampling_params, use_tqdm=False)
     # A prometheus counter: its total over labels.
     prefill_tokens = sum(sample.value for family in engine.metrics.prefill_tokens.collect()
                          for sample in family.samples if sample.name.endswith("_total"))
-    conn.send((outputs[0]["token_ids"], prefill_tokens))
+    # The last prompt token's slot was recomputed here, so the copy is compared up to it.
+    (req,) = loads.values()
+    match = None if req.pushed else _pulled_bytes_match(worker, req, len(PROMPT) - 1)
+    conn.send((outputs[0]["token_ids"], prefill_tokens, match))
+    engine.exit()
 
 
 def _receive(conn, process, what: str, timeout: float = 300.0):
@@ -176,11 +202,16 @@ def checkpoint(tmp_path_factory):
     return folder
 
 
-@pytest.mark.parametrize("mode", ["pull", "push"])
-def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carried(checkpoint, tmp_path, mode):
+@pytest.mark.parametrize("mode, prefill_tp, decode_tp", [("pull", 1, 1), ("push", 1, 1), ("pull", 2, 1)],
+                         ids=["pull", "push", "pull-tp2-to-tp1"])
+def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carried(checkpoint, tmp_path, mode,
+                                                                                  prefill_tp, decode_tp):
     """Pull: the prefill finishes, hands its kv_transfer_params over, and the decode engine reads the blocks. Push:
     the decode request is admitted first (kv_push, no block ids) and announces its blocks; the prefill engine,
-    given the same push id, writes them (all at hand-over: the reference model calls no per-layer hook)."""
+    given the same push id, writes them (all at hand-over: the reference model calls no per-layer hook). With a TP2
+    prefill engine, each of its ranks holds one of the two KV heads, and the TP1 decode rank takes a share from each
+    (head_shares), through the reference's own multi-rank step (gather_object over gloo). Every pull is also checked
+    byte for byte against the producer ranks' blocks."""
     caches = tmp_path / "caches"
     caches.mkdir()
     prefill_port, decode_port = _free_port(), _free_port()
@@ -188,24 +219,27 @@ def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carrie
     ctx = mp.get_context("spawn")
     prefill_conn, prefill_child = ctx.Pipe()
     decode_conn, decode_child = ctx.Pipe()
-    prefill = ctx.Process(target=_prefill, args=(prefill_child, checkpoint, str(caches), prefill_port, push_id))
-    decode = ctx.Process(target=_decode, args=(decode_child, checkpoint, str(caches), decode_port))
+    prefill = ctx.Process(target=_prefill, args=(prefill_child, checkpoint, str(caches), prefill_port, push_id,
+                                                 prefill_tp))
+    decode = ctx.Process(target=_decode, args=(decode_child, checkpoint, str(caches), decode_port, decode_tp))
     for process in (prefill, decode):
         process.start()
     try:
         if push_id is None:
             params = _receive(prefill_conn, prefill, "the prefill engine never handed off")
             assert params["do_remote_prefill"] and params["remote_port"] == prefill_port
+            assert params["tp_size"] == prefill_tp
             decode_conn.send(params)
         else:
             assert _receive(prefill_conn, prefill, "the prefill engine never came up") == "serving"
             decode_conn.send({"do_remote_prefill": True, "kv_push": True, "remote_request_id": push_id,
                               "remote_engine_id": "", "remote_host": "127.0.0.1", "remote_port": prefill_port,
-                              "tp_size": 1, "remote_block_ids": []})
+                              "tp_size": prefill_tp, "remote_block_ids": []})
             prefill_conn.send("go")
             _receive(prefill_conn, prefill, "the prefill engine never finished its request")
-        token_ids, num_prefill_tokens = _receive(decode_conn, decode, "the decode engine never finished")
+        token_ids, num_prefill_tokens, bytes_match = _receive(decode_conn, decode, "the decode engine never finished")
         assert _receive(prefill_conn, prefill, "the prefill engine kept its blocks") == 0.0  # all freed
+        prefill_conn.send("compared")
         reference = _receive(prefill_conn, prefill, "the prefill engine's own run never finished")
     finally:
         for process in (prefill, decode):
@@ -214,4 +248,9 @@ def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carrie
                 process.kill()
     assert num_prefill_tokens == 1  # only the last prompt token ran here; the rest came from the prefill engine
     assert len(token_ids) == MAX_TOKENS or token_ids[-1] == VOCAB
-    assert token_ids == reference
+    if mode == "pull":
+        assert bytes_match  # every head of every pulled token, bit for bit, from the rank that computed it
+    if prefill_tp == decode_tp:
+        assert token_ids == reference
+    # Across tensor-parallel sizes the two engines sum in different orders, so their greedy tokens may differ in
+    # bf16; the bytes above are the exact check there.
