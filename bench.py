@@ -4,7 +4,7 @@
                     [--engine auto|lsu|tma]
     python bench.py --impl reference ...      # the reference's CPU transfer path (restated in oracle/), host cores
 
-Workloads (seeded N(0,1) bf16 caches, block ids from seeded shuffled free lists):
+Workloads (the benchmark's configurations; seeded N(0,1) bf16 caches, block ids from seeded shuffled free lists):
   pair    Qwen3-8B-shaped KV (36 layers x {K,V}, 8 KV heads x 128, 256-token blocks, HND), prefill TP1 -> decode TP1,
           64 requests, prompt lengths uniform in [1024, 8192]. N=1: same-device loopback on cuda:0 (HBM-bound);
           N even: N/2 independent pairs (ranks 2p -> 2p+1) over NVLink.
@@ -1133,9 +1133,9 @@ def run_store(args) -> None:
 
 
 def run_poisson(args) -> None:
-    """BASELINE config 5's arrival sweep through the connector's public API: Qwen3-8B-shaped KV, prefill TP1 ->
+    """The arrival-rate sweep through the connector's public API: Qwen3-8B-shaped KV, prefill TP1 ->
     decode TP1 (a pair over NVLink at N=2, the same GPU at N=1), requests arriving as a Poisson process at each rate
-    in --rates, prompt lengths log-normal with median 2048 and sigma 1.0 (a choice: BASELINE does not give sigma),
+    in --rates, prompt lengths log-normal with median 2048 and sigma 1.0 (a choice: the configuration gives no sigma),
     clipped to [128, 32768]. The decode side allocates each request's blocks from a free list and returns them when
     its load finishes; the prefill side holds random source blocks. Per rate: p50/p99 of each load's latency (from
     its start_load_kv to the get_finished that reports it, host clock) and the bytes moved over the wall time."""
@@ -1586,7 +1586,7 @@ def main(argv=None):
     p.add_argument("--serial", action="store_true", help="with --store: plain launches (KVX_STORE_SERIAL)")
     p.add_argument("--fused", action="store_true",
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
-    p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals (BASELINE config 5)")
+    p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals at 1-64 requests/s")
     p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
     p.add_argument("--relay", action="store_true",
                    help="MLA workload: each decode rank pulls its part from the prefill rank, the rest from its peers")

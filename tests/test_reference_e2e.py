@@ -1,6 +1,6 @@
 """Disaggregated prefill end to end with the reference's real engine and model: a prefill and a decode LLMEngine of
 lean-vLLM, each in its own process, on a small random-weight Qwen3 on CPU, with CudaIpcConnector registered in the
-reference's connector table (as INTEGRATION.md does) carrying the KV between them.
+reference's connector table (as a maintainer registers it) carrying the KV between them.
 
 It follows the reference's own check (tests/test_disagg_e2e.py:1-7, 94-124). The decode engine recomputes only the
 last prompt token, attending to the pulled KV. Its greedy tokens must therefore equal the prefill engine's when that

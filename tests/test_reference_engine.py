@@ -1,6 +1,6 @@
 """The drop-in, proven against the reference's own engine code: lean-vLLM's Scheduler, BlockManager and
 LLMEngine step loop (imported from a reference checkout, unmodified) drive CudaIpcConnector through the reference's
-connector factory, exactly as INTEGRATION.md registers it. Runs on CPU: the runner is a stub whose model "computes"
+connector factory, exactly as a maintainer registers it. Runs on CPU: the runner is a stub whose model "computes"
 a deterministic KV row per (token, position) into the worker's caches, and the transport is the host one.
 
 A prefill engine finishes a request with do_remote_decode, holds its blocks and returns kv_transfer_params; a decode
