@@ -231,6 +231,26 @@ def test_a_restarted_producer_is_asked_afresh_and_the_old_mapping_closed(sides):
     assert torch.equal(consumers[0].kv_caches[0][:, 1], rank_cache(full_cache(2, False), 0, 1)[:, 4])
 
 
+def test_a_replaced_mapping_the_engine_never_polled_past_closes_at_shutdown(sides):
+    first = sides.make("kv_producer", 1, full_cache(0, False), engine_id="prefill-a")
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(first, [0], [4])}))
+    assert wait_for(consumers[0]).finished_recving == {"d-1"}
+    first[0].shutdown()
+    sleep(0.05)
+    second = sides.make("kv_producer", 1, full_cache(2, False), port=first[0].kv_transfer.kv_port,
+                        engine_id="prefill-b")
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-2": recv(second, [1], [4])}))
+    deadline = monotonic() + 5
+    while not consumers[0]._retired and monotonic() < deadline:
+        sleep(0.002)
+    sleep(0.05)
+    transport = consumers[0].transport
+    assert transport.opened == 2  # no poll since the swap: still open
+    consumers[0].shutdown()  # waits for the device (the host transport's drain), then closes every mapping
+    assert transport.opened == 0 and len(transport.closed) == 2
+
+
 @pytest.mark.parametrize("failure", ["posted", "in flight"])
 def test_a_replaced_mapping_whose_fences_fail_stays_open(sides, failure):
     """If the transport cannot show that the streams ran past the swap, the old mapping is never closed: one kept
