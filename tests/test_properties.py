@@ -1,9 +1,10 @@
 """Properties the connector's arithmetic must keep for every size, checked over generated cases (hypothesis):
 head shares tile each consumer rank's heads exactly once from the right producer heads, readers count the same
-overlaps from the other side, relay parts partition a load's blocks, and per-layer save spans leave every block
-pushed in its final state once the prompt is done -- whatever the chunking."""
+overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
+pushed in its final state once the prompt is done -- whatever the chunking -- and the native planner's byte count
+and range checks agree with the oracle's block_descs."""
 
-from hypothesis import given, settings
+from hypothesis import event, given, settings
 from hypothesis import strategies as st
 
 from lean_vllm_b200.kv_transfer.cuda_ipc_connector import _cdiv, relay_parts
@@ -92,3 +93,69 @@ def test_per_layer_spans_end_with_every_block_final_whatever_the_chunking(block,
         save.layer_blocks[0] = final
     assert save.layer_blocks[0] == blocks  # hand-over finds nothing left
     assert all(last_pushed_at[b] >= last_written_at[b] for b in range(blocks))
+
+
+@st.composite
+def planner_cases(draw):
+    """Region tables for both sides of a job (keys/values or latent layers), and one job whose ids and head range
+    may fall outside them. Addresses are never touched: only the host planner runs."""
+    layers = draw(st.lists(st.sampled_from(["kv", "latent"]), min_size=1, max_size=4))
+    head_bytes = draw(st.integers(1, 512))
+    src_heads, dst_heads = draw(st.integers(1, 8)), draw(st.integers(1, 8))
+    page = draw(st.integers(1, 4096))
+    src_blocks, dst_blocks = draw(st.integers(1, 12)), draw(st.integers(1, 12))
+
+    def table(heads, base):
+        regions = []
+        for i, kind in enumerate(layers):
+            for part in ((0, 1) if kind == "kv" else (0,)):
+                addr = base + (2 * i + part) * (1 << 32)
+                regions.append((addr, heads * head_bytes, head_bytes) if kind == "kv" else (addr, page, 0))
+        return regions
+
+    n = draw(st.integers(0, 6) if draw(st.integers(0, 9)) == 0 else st.integers(1, 6))  # empty loads now and then
+    bad_id, bad_heads = draw(st.integers(0, 4)) == 0, draw(st.integers(0, 4)) == 0  # mostly valid jobs
+    src_ids = draw(st.lists(st.integers(-1 if bad_id else 0, src_blocks if bad_id else src_blocks - 1),
+                            min_size=n, max_size=n))
+    dst_ids = draw(st.lists(st.integers(-1 if bad_id else 0, dst_blocks if bad_id else dst_blocks - 1),
+                            min_size=n, max_size=n))
+    if bad_heads:
+        src_head, dst_head, heads = draw(st.integers(0, 9)), draw(st.integers(0, 9)), draw(st.integers(0, 9))
+    else:
+        heads = draw(st.integers(0, min(src_heads, dst_heads)))
+        src_head, dst_head = draw(st.integers(0, src_heads - heads)), draw(st.integers(0, dst_heads - heads))
+    job = (src_head, dst_head, heads, draw(st.booleans()))
+    return (table(src_heads, 1 << 44), src_blocks), (table(dst_heads, 1 << 45), dst_blocks), src_ids, dst_ids, job
+
+
+@settings(max_examples=400, deadline=None)
+@given(planner_cases())
+def test_the_native_planner_counts_and_refuses_what_the_oracle_says(case):
+    """kvx_job_bytes (the planner every launch runs) against block_descs: the same byte count for any tables and
+    job, and a range error exactly where a block id or head range falls outside a cache."""
+    import os
+
+    import pytest
+
+    from lean_vllm_b200 import _native
+    from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob, job_bytes
+    from oracle.kv_oracle import Region, block_descs
+
+    if not os.path.exists(_native.LIB_PATH):
+        pytest.skip("libkvx.so is not built here")
+    (src_regions, src_blocks), (dst_regions, dst_blocks), src_ids, dst_ids, (src_head, dst_head, heads, latents) = case
+    job = CopyJob(0, 1, src_ids, dst_ids, src_head, dst_head, heads, latents)
+    tables = [CacheTable(src_regions, src_blocks), CacheTable(dst_regions, dst_blocks)]
+    ids_out = any(not 0 <= b < src_blocks for b in src_ids) or any(not 0 <= b < dst_blocks for b in dst_ids)
+    heads_out = any(h and (first + heads) * h > block
+                    for regions, first in ((src_regions, src_head), (dst_regions, dst_head))
+                    for _, block, h in regions)
+    if src_ids and (ids_out or heads_out):
+        event("refused: " + ("block id" if ids_out else "head range"))
+        with pytest.raises(_native.KvxRangeError):
+            job_bytes(tables, [job])
+        return
+    rows = block_descs([Region(*r) for r in src_regions], src_ids, src_head, heads, latents)
+    expected = int(rows[:, 1].sum()) if len(rows) else 0
+    event("counted: " + ("nothing" if expected == 0 else "bytes"))
+    assert job_bytes(tables, [job]) == expected
