@@ -103,6 +103,18 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
     """Scatter keys/values [num_tokens, heads, dim] into [num_blocks, block_size, heads, dim] caches by their
     strides (an HND cache's transposed view too); slot -1 skips. Also into every PushTarget in `push_to`."""
     num_tokens, num_heads, head_dim = key.shape
+    # Rows are copied as bytes, head by head: anything that would make a row land past its slot is refused here.
+    if value.shape != key.shape or k_cache.dim() != 4 or k_cache.shape != v_cache.shape:
+        raise ValueError(f"keys {tuple(key.shape)} and values {tuple(value.shape)} into caches "
+                         f"{tuple(k_cache.shape)} / {tuple(v_cache.shape)}: shapes must match")
+    if k_cache.size(2) != num_heads or k_cache.size(3) != head_dim:
+        raise ValueError(f"{num_heads} heads of {head_dim} into a cache of {k_cache.size(2)} heads of "
+                         f"{k_cache.size(3)}")
+    if len({key.dtype, value.dtype, k_cache.dtype, v_cache.dtype}) != 1:
+        raise TypeError(f"keys, values and caches must share a dtype (a byte copy converts nothing): {key.dtype}, "
+                        f"{value.dtype}, {k_cache.dtype}, {v_cache.dtype}")
+    if len({key.device, value.device, k_cache.device, v_cache.device}) != 1:
+        raise ValueError("keys, values and the local caches must be on one device")
     if key.stride(-1) != 1 or value.stride(-1) != 1 or key.stride(1) != head_dim or value.stride(1) != head_dim:
         raise ValueError("each token's heads must be contiguous rows of head_dim")
     if k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1:
@@ -128,6 +140,13 @@ def store_latents(latent: torch.Tensor, latent_cache: torch.Tensor, slot_mapping
     """Scatter latents [num_tokens, dim] into a [num_blocks, block_size, dim] cache; slot -1 skips. Also into every
     PushTarget in `push_to` (MLA latents are whole on every rank, so each decode rank takes a full copy)."""
     num_tokens, dim = latent.shape
+    if latent_cache.dim() != 3 or latent_cache.size(2) != dim:
+        raise ValueError(f"latents of {dim} into a cache {tuple(latent_cache.shape)}")
+    if latent.dtype != latent_cache.dtype:
+        raise TypeError(f"latents and cache must share a dtype (a byte copy converts nothing): {latent.dtype}, "
+                        f"{latent_cache.dtype}")
+    if latent.device != latent_cache.device:
+        raise ValueError("latents and the local cache must be on one device")
     if latent.stride(-1) != 1 or latent_cache.stride(-2) != dim or latent_cache.stride(-1) != 1:
         raise ValueError("latent rows and cache tokens must be contiguous")
     if len(push_to) > 8:

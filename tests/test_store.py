@@ -28,3 +28,27 @@ def test_padding_slots_leave_the_cache_alone(golden):
     cache = arrays["store_NHD_before"].copy()
     store_kvcache(arrays["store_key"], arrays["store_value"], cache[0], cache[1], np.full(10, -1))
     assert np.array_equal(cache, arrays["store_NHD_before"])
+
+
+def test_the_kvx_store_refuses_rows_that_would_not_fit_their_slots():
+    """kvx_store copies rows as bytes: a dtype, head count or head size that differs from the cache's would write
+    past each slot, so the wrappers refuse it before anything reaches the device (these run on CPU tensors)."""
+    import pytest
+    import torch
+
+    from lean_vllm_b200.attention.kvx_cache import store_kvcache, store_latents
+
+    key = torch.zeros(4, 2, 8, dtype=torch.bfloat16)
+    cache = torch.zeros(3, 16, 2, 8, dtype=torch.bfloat16)
+    slots = torch.arange(4)
+    with pytest.raises(TypeError, match="share a dtype"):
+        store_kvcache(key.float(), key.float(), cache, cache, slots)
+    with pytest.raises(ValueError, match="2 heads of 8 into a cache of 4 heads of 8"):
+        wide = torch.zeros(3, 16, 4, 8, dtype=torch.bfloat16)
+        store_kvcache(key, key, wide, wide, slots)
+    with pytest.raises(ValueError, match="shapes must match"):
+        store_kvcache(key, key[:, :1], cache, cache, slots)
+    with pytest.raises(ValueError, match="latents of 8 into a cache"):
+        store_latents(key[:, 0], torch.zeros(3, 16, 16, dtype=torch.bfloat16), slots)
+    with pytest.raises(TypeError, match="share a dtype"):
+        store_latents(key[:, 0].float(), torch.zeros(3, 16, 8, dtype=torch.bfloat16), slots)
