@@ -161,3 +161,19 @@ def test_a_plain_c99_client_compiles_against_the_header_and_runs_without_a_devic
                    check=True, capture_output=True, text=True)
     run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.strip() == "ok", (run.returncode, run.stdout, run.stderr)
+
+
+def test_the_binding_passes_as_many_arguments_as_each_prototype_takes():
+    """The ctypes table and the header agree entry by entry -- parameter count and return type -- so a prototype
+    that gains or loses a parameter cannot be called with the old argument list, nor a 64-bit result truncated."""
+    with open(os.path.join(ROOT, "include", "kvx.h")) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    found = re.findall(r"^(int|uint64_t|const char \*)\s*(kvx_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M)
+    assert {name for _, name, _ in found} == set(_native.SIGNATURES)
+    returns = {"int": ctypes.c_int, "uint64_t": ctypes.c_uint64, "const char *": ctypes.c_char_p}
+    for ret, name, params in found:
+        params = params.strip()
+        count = 0 if params in ("", "void") else params.count(",") + 1
+        argtypes, restype = _native.SIGNATURES[name]
+        assert len(argtypes) == count, name
+        assert restype is returns[ret], name
