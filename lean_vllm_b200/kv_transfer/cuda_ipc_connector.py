@@ -398,9 +398,9 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     self._put(("finish", request_id, ready))
         if metadata.reqs_to_recv:
             # Freshly allocated blocks may still be written by a step in flight; the copy waits for it on the GPU.
+            # One queue item for the step's loads: the transfer thread plans them in one pass, so they share launches.
             ready = self.transport.ready_marker()
-            for request_id, req in metadata.reqs_to_recv.items():
-                self._put(("load", request_id, req, ready))
+            self._put(("loads", ready, list(metadata.reqs_to_recv.items())))
 
     def save_kv_layer(self, layer_index: int):
         """Pushes layer `layer_index` of every request being saved whose decode ranks are mapped -- the blocks this
@@ -625,8 +625,9 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     return
                 batch: list = []
                 for item in items:
-                    if item[0] == "load":
-                        self._start(*item[1:], batch)
+                    if item[0] == "loads":
+                        for request_id, req in item[2]:
+                            self._start(request_id, req, item[1], batch)
                     elif item[0] == "connect":
                         self._connect(item[1])
                     elif item[0] == "finish":
@@ -714,8 +715,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
 
     def _handle(self, identity, message: dict):
         op = message.get("op")
-        if op == "notify":
-            self._count(message.get("message", ""))
+        if op == "notify":  # one "req:readers" notification, or several a reader batched into one message
+            batch = message.get("messages")
+            for note in batch if isinstance(batch, list) else [message.get("message", "")]:
+                self._count(str(note))
             return
         if op == "expect":
             push_id = str(message.get("push_id"))
@@ -892,16 +895,27 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 load.transfer = shared
 
     def _poll(self):
+        notes: dict[tuple, list] = {}  # producer rank -> the notifications of every load this pass finished
+        try:
+            self._poll_loads(notes)
+        finally:
+            for key, messages in notes.items():
+                self._notify(key, *messages)
+
+    def _poll_loads(self, notes: dict):
+        queried: set[int] = set()  # launches asked once this pass: the loads sharing one finish together
         for request_id, load in list(self._loads.items()):
             if load.transfer is not None:
                 shared = load.transfer
-                try:
-                    if not shared.done and not self.transport.done(shared.xfer):
-                        continue
-                    shared.done = True
-                except Exception as error:  # noqa: BLE001
-                    shared.done = True
-                    shared.error = shared.error or error
+                if not shared.done and id(shared) not in queried:
+                    queried.add(id(shared))
+                    try:
+                        shared.done = self.transport.done(shared.xfer)
+                    except Exception as error:  # noqa: BLE001
+                        shared.done = True
+                        shared.error = shared.error or error
+                if not shared.done:
+                    continue
                 if shared.error is not None:
                     self._fail(load, RuntimeError(f"a kvx copy failed in flight: {shared.error}"), in_flight=True)
                 shared.refs -= 1
@@ -910,7 +924,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 load.transfer = None
                 if not load.failed:
                     for key, message, remote_rank in load.notify:
-                        self._notify(key, message)
+                        notes.setdefault(key, []).append(message)
                         load.unnotified.discard(remote_rank)
             del self._loads[request_id]
             if load.relay is not None and not load.failed:
@@ -1016,8 +1030,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         except zmq.ZMQError as error:  # the peer times out instead
             logger.debug("notifying %s:%d failed: %s", key[0], key[1], error)
 
-    def _notify(self, key, message: str):
-        self._send(key, {"op": "notify", "message": message})
+    def _notify(self, key, *messages: str):
+        """Reader notifications for one producer rank (the NIXL notification's role): the loads that finished in one
+        pass of this thread share one message, which costs a socket send rather than one per load."""
+        if len(messages) == 1:
+            self._send(key, {"op": "notify", "message": messages[0]})
+        elif messages:
+            self._send(key, {"op": "notify", "messages": list(messages)})
 
     def _fail(self, load: _Load, error: Exception, in_flight: bool = False):
         req = load.req

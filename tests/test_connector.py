@@ -306,6 +306,32 @@ def test_malformed_messages_are_dropped_and_the_rank_keeps_serving(sides, caplog
     assert wait_for(producers[0]).finished_sending == {"p-1"}
 
 
+def test_loads_that_finish_together_notify_their_producer_in_one_message(sides, monkeypatch):
+    """Two loads started in one step share a launch and land together: the producer rank gets one message carrying
+    both reader notifications (one socket send, not one per load) and frees both requests."""
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    sent = []
+    send = consumers[0]._send
+    monkeypatch.setattr(consumers[0], "_send", lambda key, message: (sent.append(message), send(key, message))[1])
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4], "p-2": [5]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={
+        "d-1": recv(producers, [0], [4], remote_request_id="p-1"),
+        "d-2": recv(producers, [1], [5], remote_request_id="p-2")}))
+    done, deadline = set(), monotonic() + 10
+    while done != {"d-1", "d-2"} and monotonic() < deadline:
+        done |= consumers[0].get_finished().finished_recving
+        sleep(0.002)
+    assert done == {"d-1", "d-2"}
+    freed, deadline = set(), monotonic() + 10
+    while freed != {"p-1", "p-2"} and monotonic() < deadline:
+        freed |= producers[0].get_finished().finished_sending
+        sleep(0.002)
+    assert freed == {"p-1", "p-2"}
+    notes = [m for m in sent if m.get("op") == "notify"]
+    assert len(notes) == 1 and sorted(notes[0]["messages"]) == ["p-1:1", "p-2:1"]
+
+
 def test_a_taken_port_is_named(sides):
     with socket.socket() as taken:
         taken.bind(("127.0.0.1", 0))
