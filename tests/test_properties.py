@@ -1,8 +1,8 @@
 """Properties the connector's arithmetic must keep for every size, checked over generated cases (hypothesis):
 head shares tile each consumer rank's heads exactly once from the right producer heads, readers count the same
 overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
-pushed in its final state once the prompt is done -- whatever the chunking -- and the native planner's byte count
-and range checks agree with the oracle's block_descs."""
+pushed in its final state once the prompt is done -- whatever the chunking -- the native planner's byte count
+and range checks agree with the oracle's block_descs, and the output aggregator agrees with the reference's own."""
 
 from hypothesis import event, given, settings
 from hypothesis import strategies as st
@@ -159,3 +159,68 @@ def test_the_native_planner_counts_and_refuses_what_the_oracle_says(case):
     expected = int(rows[:, 1].sum()) if len(rows) else 0
     event("counted: " + ("nothing" if expected == 0 else "bytes"))
     assert job_bytes(tables, [job]) == expected
+
+
+def _reference_kv():
+    """The reference checkout's kv_transfer package (REFERENCE_ROOT, else a "reference" folder beside this
+    repository), or None."""
+    import importlib
+    import os
+    import sys
+
+    root = os.environ.get("REFERENCE_ROOT", os.path.join(os.path.dirname(__file__), "..", "..", "reference"))
+    if not os.path.isdir(os.path.join(root, "lean_vllm")):
+        return None
+    sys.path.insert(0, root)
+    try:
+        return importlib.import_module("lean_vllm.kv_transfer.base")
+    except ImportError:
+        return None
+    finally:
+        sys.path.remove(root)
+
+
+@st.composite
+def rank_outputs(draw):
+    """A few steps of every rank's output: request ids from a small pool, each rank reporting any of them."""
+    world = draw(st.integers(1, 4))
+    pool = ["r0", "r1", "r2", "r3", "r4"]
+    ids = st.sets(st.sampled_from(pool), max_size=3)
+    steps = []
+    for _ in range(draw(st.integers(1, 4))):
+        step = []
+        for _ in range(world):
+            recving, failed = draw(ids), draw(ids)
+            stats = {rid: (draw(st.floats(0, 5, allow_nan=False)), draw(st.integers(0, 1 << 40))) for rid in recving}
+            step.append((draw(ids), recving, failed, draw(ids), stats))
+        steps.append(step)
+    return world, steps
+
+
+@settings(max_examples=300, deadline=None)
+@given(rank_outputs())
+def test_the_aggregator_matches_the_reference_s_on_any_rank_outputs(case):
+    """KVOutputAggregator against the reference's own (kv_transfer/base.py:125-165), step after step: the same
+    finished, failed and expired sets and the same merged stats (slowest rank's time, every rank's bytes)."""
+    import pytest
+
+    from lean_vllm_b200.kv_transfer.base import KVConnectorOutput, KVOutputAggregator, KVTransferStats
+
+    ref = _reference_kv()
+    if ref is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    world, steps = case
+    ours, theirs = KVOutputAggregator(world), ref.KVOutputAggregator(world)
+    for step in steps:
+        mine = ours.aggregate([KVConnectorOutput(set(s), set(r), set(f), set(e),
+                                                 {k: KVTransferStats(*v) for k, v in st_.items()})
+                               for s, r, f, e, st_ in step])
+        ref_out = theirs.aggregate([ref.KVConnectorOutput(set(s), set(r), set(f), set(e),
+                                                          {k: ref.KVTransferStats(*v) for k, v in st_.items()})
+                                    for s, r, f, e, st_ in step])
+        assert mine.finished_sending == ref_out.finished_sending
+        assert mine.finished_recving == ref_out.finished_recving
+        assert mine.failed_recving == ref_out.failed_recving
+        assert mine.expired_sending == ref_out.expired_sending
+        assert {k: (v.seconds, v.num_bytes) for k, v in mine.recv_stats.items()} == \
+            {k: (v.seconds, v.num_bytes) for k, v in ref_out.recv_stats.items()}
