@@ -2,7 +2,8 @@
 head shares tile each consumer rank's heads exactly once from the right producer heads, readers count the same
 overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
 pushed in its final state once the prompt is done -- whatever the chunking -- the native planner's byte count
-and range checks agree with the oracle's block_descs, and the output aggregator agrees with the reference's own."""
+and range checks agree with the oracle's block_descs, and the output aggregator and the pull-mode scheduler half
+agree with the reference's own."""
 
 from hypothesis import event, given, settings
 from hypothesis import strategies as st
@@ -224,3 +225,60 @@ def test_the_aggregator_matches_the_reference_s_on_any_rank_outputs(case):
         assert mine.expired_sending == ref_out.expired_sending
         assert {k: (v.seconds, v.num_bytes) for k, v in mine.recv_stats.items()} == \
             {k: (v.seconds, v.num_bytes) for k, v in ref_out.recv_stats.items()}
+
+
+@st.composite
+def scheduler_events(draw):
+    """A request as both scheduler halves see it (pull mode): its prompt and block table, prefix hits here, the
+    kv_transfer_params it arrives with (the block count sometimes wrong), and how it finishes."""
+    block = 16
+    prompt = draw(st.integers(1, 200))
+    blocks = -(-prompt // block)
+    table = draw(st.lists(st.integers(0, 999), min_size=blocks, max_size=blocks + 1, unique=True))
+    cached = draw(st.integers(0, blocks - 1 if prompt % block == 0 else blocks)) * block
+    cached = min(cached, (prompt - 1) // block * block)  # the last prompt token is always computed here
+    remote = draw(st.lists(st.integers(0, 999), min_size=blocks, max_size=blocks)) if draw(st.integers(0, 4)) else \
+        draw(st.lists(st.integers(0, 999), max_size=blocks + 2))
+    params = {"do_remote_prefill": draw(st.booleans()), "do_remote_decode": draw(st.booleans()),
+              "remote_request_id": "p-1", "remote_engine_id": draw(st.sampled_from(["e1", "e2"])),
+              "remote_block_ids": remote, "remote_host": "10.0.0.1", "remote_port": draw(st.integers(1, 65535)),
+              "tp_size": draw(st.integers(1, 8))}
+    return block, prompt, table, cached, params, draw(st.sampled_from(["length", "stop", "abort", None]))
+
+
+@settings(max_examples=300, deadline=None)
+@given(scheduler_events())
+def test_the_scheduler_half_matches_the_reference_s_in_pull_mode(event):
+    """CudaIpcConnectorScheduler against the reference's NixlConnectorScheduler (nixl_connector.py:111-168) on the
+    same request: the same admission answer, the same load (ids, remote request, engine, address, tp_size), the
+    same step metadata and the same hand-over params."""
+    import copy
+    import importlib
+    import types
+
+    import pytest
+
+    from lean_vllm_b200.kv_transfer.cuda_ipc_connector import CudaIpcConnectorScheduler
+
+    if _reference_kv() is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    nixl = importlib.import_module("lean_vllm.kv_transfer.nixl_connector")
+    block, prompt, table, cached, params, finish = event
+    kv = types.SimpleNamespace(engine_id="this-engine", kv_ip="10.0.0.2", kv_port=15000)
+    config = types.SimpleNamespace(kv_transfer=kv, kvcache_block_size=block, tensor_parallel_size=2)
+    results = []
+    for half in (CudaIpcConnectorScheduler(config), nixl.NixlConnectorScheduler(config)):
+        seq = types.SimpleNamespace(request_id="r", num_prompt_tokens=prompt, block_table=list(table),
+                                    num_cached_tokens=cached, kv_transfer_params=copy.deepcopy(params),
+                                    finish_reason=finish, num_scheduled_tokens=0)
+        matched = half.get_num_new_matched_tokens(seq, cached)
+        if matched[1]:
+            half.update_state_after_alloc(seq, matched[0])
+        meta = half.build_connector_meta()
+        loads = {rid: (list(r.local_block_ids), list(r.remote_block_ids), r.remote_request_id, r.remote_engine_id,
+                       r.remote_host, r.remote_port, r.remote_tp_size) for rid, r in meta.reqs_to_recv.items()}
+        handed = half.request_finished(seq)
+        sends = half.build_connector_meta().reqs_to_send
+        results.append((matched, loads, dict(meta.reqs_to_send), handed, {k: list(v) for k, v in sends.items()},
+                        seq.kv_transfer_params))
+    assert results[0] == results[1]
