@@ -2,8 +2,8 @@
 head shares tile each consumer rank's heads exactly once from the right producer heads, readers count the same
 overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
 pushed in its final state once the prompt is done -- whatever the chunking -- the native planner's byte count
-and range checks agree with the oracle's block_descs, and the output aggregator and the pull-mode scheduler half
-agree with the reference's own."""
+and range checks agree with the oracle's block_descs, and the output aggregator, the pull-mode scheduler half and
+the request-params check agree with the reference's own."""
 
 from hypothesis import event, given, settings
 from hypothesis import strategies as st
@@ -282,3 +282,25 @@ def test_the_scheduler_half_matches_the_reference_s_in_pull_mode(event):
         results.append((matched, loads, dict(meta.reqs_to_send), handed, {k: list(v) for k, v in sends.items()},
                         seq.kv_transfer_params))
     assert results[0] == results[1]
+
+
+@settings(max_examples=400, deadline=None)
+@given(st.dictionaries(
+    st.sampled_from(["do_remote_prefill", "do_remote_decode", "remote_block_ids", "remote_request_id",
+                     "remote_engine_id", "remote_host", "remote_port", "tp_size", "kv_push", "kv_push_id"]),
+    st.one_of(st.booleans(), st.integers(-2, 70000), st.text(max_size=4), st.none(),
+              st.lists(st.integers(0, 9), max_size=3), st.lists(st.text(max_size=2), max_size=2))),
+    st.sampled_from(["kv_producer", "kv_consumer", "kv_both", None]))
+def test_request_params_are_judged_as_the_reference_judges_them(params, role):
+    """check_kv_transfer_params (what the API server asks before admitting a request) gives the reference's answer,
+    word for word, on any params object and engine role."""
+    import pytest
+
+    from lean_vllm_b200.kv_transfer.base import KVTransferConfig, check_kv_transfer_params
+
+    ref = _reference_kv()
+    if ref is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    ours = KVTransferConfig(kv_role=role) if role else None
+    theirs = ref.KVTransferConfig(kv_role=role) if role else None
+    assert check_kv_transfer_params(dict(params), ours) == ref.check_kv_transfer_params(dict(params), theirs)
