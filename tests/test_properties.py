@@ -3,7 +3,7 @@ head shares tile each consumer rank's heads exactly once from the right producer
 overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
 pushed in its final state once the prompt is done -- whatever the chunking -- the native planner's byte count
 and range checks agree with the oracle's block_descs, and the output aggregator, the pull-mode scheduler half and
-the request-params check agree with the reference's own."""
+the request-params and --kv-transfer-config checks agree with the reference's own."""
 
 from hypothesis import event, given, settings
 from hypothesis import strategies as st
@@ -304,3 +304,34 @@ def test_request_params_are_judged_as_the_reference_judges_them(params, role):
     ours = KVTransferConfig(kv_role=role) if role else None
     theirs = ref.KVTransferConfig(kv_role=role) if role else None
     assert check_kv_transfer_params(dict(params), ours) == ref.check_kv_transfer_params(dict(params), theirs)
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.dictionaries(
+    st.sampled_from(["kv_connector", "kv_role", "kv_ip", "kv_port", "engine_id", "kv_buffer_device"]),
+    st.one_of(st.sampled_from(["kv_producer", "kv_consumer", "kv_both", "NixlConnector"]), st.integers(-1, 70000),
+              st.text(max_size=3), st.none(), st.floats(allow_nan=False, allow_infinity=False), st.booleans())))
+def test_kv_transfer_config_parses_as_the_reference_parses_it(value):
+    """--kv-transfer-config JSON: accepted or refused exactly when the reference's is, with the same fields (the
+    connector name's default and the random engine id aside)."""
+    import json
+
+    import pytest
+    from pydantic import ValidationError
+
+    from lean_vllm_b200.kv_transfer.base import KVTransferConfig
+
+    ref = _reference_kv()
+    if ref is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    text = json.dumps(value)
+    got = []
+    for cls in (KVTransferConfig, ref.KVTransferConfig):
+        try:
+            config = cls.parse(text)
+        except ValidationError:
+            got.append("refused")
+            continue
+        got.append((config.kv_role, config.kv_ip, config.kv_port, config.engine_id if "engine_id" in value else None,
+                    config.kv_connector if "kv_connector" in value else None))
+    assert got[0] == got[1]
