@@ -2,8 +2,9 @@
 head shares tile each consumer rank's heads exactly once from the right producer heads, readers count the same
 overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
 pushed in its final state once the prompt is done -- whatever the chunking -- the native planner's byte count
-and range checks agree with the oracle's block_descs, and the output aggregator, the pull-mode scheduler half and
-the request-params and --kv-transfer-config checks agree with the reference's own."""
+and range checks agree with the oracle's block_descs, the store oracle writes what the reference's torch store
+writes, and the output aggregator, the pull-mode scheduler half and the request-params and --kv-transfer-config
+checks agree with the reference's own."""
 
 from hypothesis import event, given, settings
 from hypothesis import strategies as st
@@ -335,3 +336,60 @@ def test_kv_transfer_config_parses_as_the_reference_parses_it(value):
         got.append((config.kv_role, config.kv_ip, config.kv_port, config.engine_id if "engine_id" in value else None,
                     config.kv_connector if "kv_connector" in value else None))
     assert got[0] == got[1]
+
+
+@st.composite
+def store_steps(draw):
+    """A step's rows for a paged cache: shape, layout (NHD, or HND seen through its transposed view), and distinct
+    slots with -1 padding among them, as an engine's slot mapping has."""
+    blocks, block, heads, dim = draw(st.integers(1, 5)), draw(st.integers(1, 8)), draw(st.integers(1, 4)), \
+        draw(st.integers(1, 8))
+    slots = draw(st.lists(st.one_of(st.integers(0, blocks * block - 1), st.just(-1)), max_size=blocks * block))
+    seen, distinct = set(), []
+    for slot in slots:  # an engine never maps two rows of a step to one slot: repeats become padding
+        distinct.append(slot if slot < 0 or slot not in seen else -1)
+        seen.add(slot)
+    slots = distinct
+    return blocks, block, heads, dim, slots, draw(st.sampled_from(["NHD", "HND"])), draw(st.integers(0, 1 << 16))
+
+
+@settings(max_examples=200, deadline=None)
+@given(store_steps())
+def test_the_store_oracle_writes_what_the_reference_s_torch_store_writes(step):
+    """oracle.kv_oracle.store_kvcache / store_latents -- what the kvx_store GPU tests are checked against -- against
+    the reference's TorchAttention store (attention/torch_backend.py:34-60) on any shape, layout and slot mapping."""
+    import importlib
+
+    import numpy as np
+    import pytest
+    import torch
+
+    from oracle.kv_oracle import store_kvcache, store_latents
+
+    if _reference_kv() is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    torch_store = importlib.import_module("lean_vllm.attention.torch_backend").TorchAttention
+    blocks, block, heads, dim, slots, layout, seed = step
+    g = torch.Generator().manual_seed(seed)
+    n = len(slots)
+    key, value = (torch.randn(n, heads, dim, generator=g).to(torch.bfloat16) for _ in range(2))
+    shape = (2, blocks, block, heads, dim) if layout == "NHD" else (2, blocks, heads, block, dim)
+    cache = torch.randn(*shape, generator=g).to(torch.bfloat16)
+
+    def views(c):
+        return (c[0], c[1]) if layout == "NHD" else (c[0].transpose(1, 2), c[1].transpose(1, 2))
+
+    theirs = cache.clone()
+    torch_store.store_kvcache(None, key, value, *views(theirs), torch.tensor(slots, dtype=torch.long))
+    mine = cache.clone().view(torch.int16).numpy()
+    k_view, v_view = (mine[0], mine[1]) if layout == "NHD" else (mine[0].swapaxes(1, 2), mine[1].swapaxes(1, 2))
+    store_kvcache(key.view(torch.int16).numpy(), value.view(torch.int16).numpy(), k_view, v_view, slots)
+    assert np.array_equal(mine, theirs.view(torch.int16).numpy())
+
+    latent = torch.randn(n, dim, generator=g).to(torch.bfloat16)
+    lat_cache = torch.randn(blocks, block, dim, generator=g).to(torch.bfloat16)
+    theirs_lat = lat_cache.clone()
+    torch_store.store_latents(None, latent, theirs_lat, torch.tensor(slots, dtype=torch.long))
+    mine_lat = lat_cache.clone().view(torch.int16).numpy()
+    store_latents(latent.view(torch.int16).numpy(), mine_lat, slots)
+    assert np.array_equal(mine_lat, theirs_lat.view(torch.int16).numpy())
