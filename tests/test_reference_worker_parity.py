@@ -1,7 +1,9 @@
 """The worker half against the reference's own, on generated loads: lean-vLLM's NixlConnectorWorker (over the
 memmove NIXL agent of tests/golden/make_golden.py) and CudaIpcConnectorWorker (over the host transport) load the same
 blocks between the same caches, for any pair of tensor-parallel sizes, keys/values or latents, any block ids and
-any prefix hit. The decode ranks' caches must end bit for bit equal, and each rank must count the same bytes.
+any prefix hit. The decode ranks' caches must end bit for bit equal, and each rank must count the same bytes. The
+same loads also run as pushes (this package's ReqToSave, written by the prefill ranks at hand-over): the decode
+caches must end as the reference's pull leaves them.
 
 The golden fixtures pin a few such loads; this runs as many as hypothesis draws. Skipped where no reference
 checkout is present (REFERENCE_ROOT)."""
@@ -19,7 +21,8 @@ REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", os.path.join(HERE, "..", "..",
 if not os.path.isdir(os.path.join(REFERENCE_ROOT, "lean_vllm")):
     pytest.skip("no lean-vLLM reference checkout", allow_module_level=True)
 
-from lean_vllm_b200.kv_transfer import KVConnectorMetadata, cuda_ipc_connector  # noqa: E402
+from lean_vllm_b200.kv_transfer import KVConnectorMetadata, ReqToRecv, cuda_ipc_connector  # noqa: E402
+from lean_vllm_b200.kv_transfer.base import ReqToSave  # noqa: E402
 from tests.connector_cases import Sides, recv, wait_for  # noqa: E402
 from tests.host_transport import HostTransport  # noqa: E402
 
@@ -50,13 +53,14 @@ def loads(draw):
     remote = draw(st.lists(st.integers(0, BLOCKS - 1), min_size=n, max_size=n, unique=True))
     local = draw(st.lists(st.integers(0, BLOCKS - 1), min_size=n, max_size=n, unique=True))
     hits = draw(st.integers(0, n))  # leading blocks the decode instance already holds: not read
-    return prefill_tp, decode_tp, mla, layers, local[hits:], remote[hits:], draw(st.integers(0, 1 << 16))
+    mode = draw(st.sampled_from(["pull", "push"]))
+    return prefill_tp, decode_tp, mla, layers, local[hits:], remote[hits:], draw(st.integers(0, 1 << 16)), mode
 
 
 @settings(max_examples=30, deadline=None, suppress_health_check=[HealthCheck.too_slow])
 @given(loads())
 def test_a_load_lands_what_the_reference_worker_lands(load):
-    prefill_tp, decode_tp, mla, n_layers, local, remote, seed = load
+    prefill_tp, decode_tp, mla, n_layers, local, remote, seed, mode = load
     ref = _reference()
     shape = (1, BLOCKS, BLOCK, LATENT) if mla else (2, BLOCKS, HEADS, BLOCK, DIM)
     prefill = [ref.seeded(shape, seed + i) for i in range(n_layers)]
@@ -68,12 +72,24 @@ def test_a_load_lands_what_the_reference_worker_lands(load):
     sides = Sides("cpu")
     try:
         producers = sides.make("kv_producer", prefill_tp, [p.clone() for p in prefill])
-        consumers = sides.make("kv_consumer", decode_tp, [d.clone() for d in decode], engine_id="decode")
-        for producer in producers:
-            producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(remote)}))
-        for consumer in consumers:
-            consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, list(local),
-                                                                                list(remote))}))
+        consumers = sides.make("kv_consumer", decode_tp, [d.clone() for d in decode], engine_id="decode",
+                               accept_push=mode == "push")
+        if mode == "pull":
+            for producer in producers:
+                producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(remote)}))
+            for consumer in consumers:
+                consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, list(local),
+                                                                                    list(remote))}))
+        else:  # the decode side waits; the prefill ranks push everything at hand-over (no per-layer hooks)
+            kv_p, kv_d = producers[0].kv_transfer, consumers[0].kv_transfer
+            for consumer in consumers:
+                consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": ReqToRecv(
+                    list(local), list(remote), "p-1", kv_p.engine_id, kv_p.kv_ip, kv_p.kv_port, prefill_tp,
+                    pushed=True)}))
+            save = ReqToSave(list(remote), list(local), kv_d.engine_id, kv_d.kv_ip, kv_d.kv_port, decode_tp)
+            for producer in producers:
+                producer.start_load_kv(KVConnectorMetadata(reqs_to_save={"p-1": save}))
+                producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(remote)}))
         outputs = [wait_for(consumer) for consumer in consumers]
         assert all(out.finished_recving == {"d-1"} for out in outputs)
         assert [out.recv_stats["d-1"].num_bytes for out in outputs] == want_bytes
