@@ -3,7 +3,8 @@ memmove NIXL agent of tests/golden/make_golden.py) and CudaIpcConnectorWorker (o
 blocks between the same caches, for any pair of tensor-parallel sizes, keys/values or latents, any block ids and
 any prefix hit. The decode ranks' caches must end bit for bit equal, and each rank must count the same bytes. The
 same loads also run as pushes (this package's ReqToSave, written by the prefill ranks at hand-over): the decode
-caches must end as the reference's pull leaves them.
+caches must end as the reference's pull leaves them. And as relayed loads (LEAN_VLLM_KVX_RELAY: latents split
+between decode ranks, each pulling its part and copying the rest from its peers), which must land the same bytes.
 
 The golden fixtures pin a few such loads; this runs as many as hypothesis draws. Skipped where no reference
 checkout is present (REFERENCE_ROOT)."""
@@ -23,7 +24,7 @@ if not os.path.isdir(os.path.join(REFERENCE_ROOT, "lean_vllm")):
 
 from lean_vllm_b200.kv_transfer import KVConnectorMetadata, ReqToRecv, cuda_ipc_connector  # noqa: E402
 from lean_vllm_b200.kv_transfer.base import ReqToSave  # noqa: E402
-from tests.connector_cases import Sides, recv, wait_for  # noqa: E402
+from tests.connector_cases import Sides, free_port, recv, wait_for  # noqa: E402
 from tests.host_transport import HostTransport  # noqa: E402
 
 BLOCKS, BLOCK, HEADS, DIM, LATENT = 12, 4, 12, 8, 6
@@ -41,6 +42,9 @@ def _reference():
         module = importlib.util.module_from_spec(spec)
         sys.modules[spec.name] = module  # its dataclasses look their module up while it runs
         spec.loader.exec_module(module)
+        # Its ranks bind port + rank: take ports whose whole span is free and never handed out before, as this
+        # package's side does, so many loads in a row do not collide.
+        module.free_port = free_port
     return sys.modules["kvx_make_golden"]
 
 
@@ -53,11 +57,11 @@ def loads(draw):
     remote = draw(st.lists(st.integers(0, BLOCKS - 1), min_size=n, max_size=n, unique=True))
     local = draw(st.lists(st.integers(0, BLOCKS - 1), min_size=n, max_size=n, unique=True))
     hits = draw(st.integers(0, n))  # leading blocks the decode instance already holds: not read
-    mode = draw(st.sampled_from(["pull", "push"]))
+    mode = draw(st.sampled_from(["pull", "push", "relay"]))
     return prefill_tp, decode_tp, mla, layers, local[hits:], remote[hits:], draw(st.integers(0, 1 << 16)), mode
 
 
-@settings(max_examples=30, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
 @given(loads())
 def test_a_load_lands_what_the_reference_worker_lands(load):
     prefill_tp, decode_tp, mla, n_layers, local, remote, seed, mode = load
@@ -69,12 +73,14 @@ def test_a_load_lands_what_the_reference_worker_lands(load):
 
     make_transport, fail = cuda_ipc_connector.make_transport, HostTransport.fail
     cuda_ipc_connector.make_transport, HostTransport.fail = HostTransport, None
+    relay = os.environ.get("LEAN_VLLM_KVX_RELAY")
+    os.environ["LEAN_VLLM_KVX_RELAY"] = "1" if mode == "relay" else "0"
     sides = Sides("cpu")
     try:
         producers = sides.make("kv_producer", prefill_tp, [p.clone() for p in prefill])
         consumers = sides.make("kv_consumer", decode_tp, [d.clone() for d in decode], engine_id="decode",
                                accept_push=mode == "push")
-        if mode == "pull":
+        if mode in ("pull", "relay"):
             for producer in producers:
                 producer.start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(remote)}))
             for consumer in consumers:
@@ -99,3 +105,7 @@ def test_a_load_lands_what_the_reference_worker_lands(load):
     finally:
         sides.close()
         cuda_ipc_connector.make_transport, HostTransport.fail = make_transport, fail
+        if relay is None:
+            os.environ.pop("LEAN_VLLM_KVX_RELAY", None)
+        else:
+            os.environ["LEAN_VLLM_KVX_RELAY"] = relay
