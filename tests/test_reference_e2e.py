@@ -19,7 +19,6 @@ there is no network to fetch one. Skipped where no reference checkout is present
 import json
 import multiprocessing as mp
 import os
-import socket
 from time import sleep
 
 import pytest
@@ -190,9 +189,10 @@ def _receive(conn, process, what: str, timeout: float = 300.0):
 
 
 def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A port whose span (kv_port + rank for every rank) is free and was not handed out before here."""
+    from tests.connector_cases import free_port
+
+    return free_port()
 
 
 @pytest.fixture(scope="module")
