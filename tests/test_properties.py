@@ -393,3 +393,26 @@ def test_the_store_oracle_writes_what_the_reference_s_torch_store_writes(step):
     mine_lat = lat_cache.clone().view(torch.int16).numpy()
     store_latents(latent.view(torch.int16).numpy(), mine_lat, slots)
     assert np.array_equal(mine_lat, theirs_lat.view(torch.int16).numpy())
+
+
+@settings(max_examples=500, deadline=None)
+@given(st.integers(1, 8), st.integers(1, 8), st.integers(1, 32), st.data())
+def test_head_shares_and_reader_counts_are_the_reference_s(tp, remote_tp, multiple, data):
+    """head_shares and the reader count a producer rank waits for, against the reference's own functions
+    (nixl_connector.py:60-77, 400-401) on any split: every consumer rank of any pair of tensor-parallel sizes, up
+    to 256 heads (the golden table holds 372 splits of these)."""
+    import importlib
+
+    import pytest
+
+    if _reference_kv() is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    nixl = importlib.import_module("lean_vllm.kv_transfer.nixl_connector")
+    heads = split_heads(0, tp, remote_tp) * multiple
+    rank = data.draw(st.integers(0, tp - 1))
+    ours = head_shares(rank, tp, remote_tp, heads)
+    theirs = nixl.head_shares(rank, tp, remote_tp, heads)
+    assert [tuple(s) for s in ours] == [tuple(s) for s in theirs]
+    for share in theirs:
+        assert readers_of(share.remote_rank, remote_tp, tp, heads) == \
+            len(nixl.head_shares(share.remote_rank, remote_tp, tp, heads))
