@@ -3,8 +3,8 @@ head shares tile each consumer rank's heads exactly once from the right producer
 overlaps from the other side, relay parts partition a load's blocks, per-layer save spans leave every block
 pushed in its final state once the prompt is done -- whatever the chunking -- the native planner's byte count
 and range checks agree with the oracle's block_descs, the store oracle writes what the reference's torch store
-writes, and the output aggregator, the pull-mode scheduler half and the request-params and --kv-transfer-config
-checks agree with the reference's own."""
+writes, and head shares, reader counts, descriptor rows, the output aggregator, the pull-mode scheduler half and the
+request-params and --kv-transfer-config checks agree with the reference's own functions."""
 
 from hypothesis import event, given, settings
 from hypothesis import strategies as st
@@ -416,3 +416,25 @@ def test_head_shares_and_reader_counts_are_the_reference_s(tp, remote_tp, multip
     for share in theirs:
         assert readers_of(share.remote_rank, remote_tp, tp, heads) == \
             len(nixl.head_shares(share.remote_rank, remote_tp, tp, heads))
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.lists(st.tuples(st.integers(1, 1 << 40), st.integers(1, 1 << 20), st.sampled_from([0, 16, 512, 65536])),
+                min_size=0, max_size=6),
+       st.lists(st.integers(0, 4096), max_size=8), st.integers(0, 8), st.integers(0, 8), st.booleans())
+def test_the_oracle_s_descriptor_rows_are_the_reference_s(regions, block_ids, first_head, num_heads, latents):
+    """oracle.kv_oracle.block_descs -- the byte map every parity check here rests on -- against the reference's own
+    block_descs (nixl_connector.py:89-108): the same (address, length, device) rows in the same order."""
+    import importlib
+
+    import numpy as np
+    import pytest
+
+    from oracle.kv_oracle import Region, block_descs
+
+    if _reference_kv() is None:
+        pytest.skip("no lean-vLLM reference checkout")
+    nixl = importlib.import_module("lean_vllm.kv_transfer.nixl_connector")
+    ours = block_descs([Region(*r) for r in regions], block_ids, first_head, num_heads, latents, device_id=3)
+    theirs = nixl.block_descs([nixl.Region(*r) for r in regions], block_ids, first_head, num_heads, latents, 3)
+    assert ours.shape == theirs.shape and np.array_equal(ours.astype(np.uint64), theirs)
