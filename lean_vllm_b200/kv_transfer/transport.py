@@ -68,10 +68,6 @@ class CacheTable:
                 raise ValueError("every layer must hold the same number of blocks")
         return cls(regions, num_blocks or 0)
 
-    def rebased(self, mapping: dict[int, int]) -> "CacheTable":
-        """The same regions at other addresses: `mapping` takes each exporter address to its local mapping."""
-        return CacheTable([(mapping[a], b, h) for a, b, h in self.regions], self.num_blocks)
-
     def struct(self) -> Cache:
         if self._struct is None:
             array = (Region * max(len(self.regions), 1))(*[Region(a, b, h) for a, b, h in self.regions])
