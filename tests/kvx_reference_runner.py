@@ -35,7 +35,19 @@ cuda_ipc_connector.make_transport = ShmTransport
 
 
 class SharedCacheModelRunner(model_runner.ModelRunner):
-    """The reference's ModelRunner, with its KV caches allocated in shared files."""
+    """The reference's ModelRunner, with its KV caches allocated in shared files. With KVX_TEST_STEP=mailbox its
+    kv_connector_step is this package's KVConnectorStep, wired in as a maintainer would: the ranks' outputs reach
+    rank 0 through the shared-memory step mailbox instead of gather_object."""
+
+    def kv_connector_step(self, metadata):
+        if os.environ.get("KVX_TEST_STEP") != "mailbox":
+            return super().kv_connector_step(metadata)
+        if getattr(self, "_kv_step", None) is None:  # every rank gets here on the same step, through call()
+            from lean_vllm_b200.kv_transfer import KVConnectorStep
+
+            self._kv_step = KVConnectorStep(self.kv_connector, self.rank, self.world_size,
+                                            group=getattr(self, "call_group", None))
+        return self._kv_step(metadata)
 
     def allocate_kv_cache(self):
         def shared_empty(shape, **_):

@@ -98,6 +98,8 @@ def _prefill(conn, model: str, cache_folder: str, kv_port: int, push_id: str | N
     # The prompt runs split n-1 + 1 where the split is comparable (TP1). The reference engine at TP > 1 cannot run a
     # chunk that samples nothing (its logits gather reshapes zero rows), so there the prompt runs whole.
     split = dict(long_prefill_token_threshold=len(PROMPT) - 1) if tp == 1 else {}
+    if tp > 1:  # the ranks' connector outputs reach rank 0 through KVConnectorStep's mailbox, not gather_object
+        os.environ["KVX_TEST_STEP"] = "mailbox"
     engine = _engine(model, cache_folder, enable_prefix_caching=False, tensor_parallel_size=tp, **split,
                      kv_transfer_config=json.dumps(dict(kv_connector="CudaIpcConnector", kv_role="kv_producer",
                                                         kv_port=kv_port)))
@@ -116,7 +118,8 @@ def _prefill(conn, model: str, cache_folder: str, kv_port: int, push_id: str | N
     while not engine.is_finished():  # until the decode engine has the blocks and they are let go
         engine.step()
         sleep(0.001)
-    conn.send(engine.scheduler.block_manager.usage)
+    step = getattr(engine.model_runner, "_kv_step", None)  # KVConnectorStep, where it replaced the gather
+    conn.send((engine.scheduler.block_manager.usage, step.exchange if step is not None else None))
     conn.recv()  # the decode side has compared its copy with the freed blocks: they may be reused now
     reference = None
     if tp == 1:  # across sizes the tokens are not comparable (see the test)
@@ -210,8 +213,9 @@ def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carrie
     the decode request is admitted first (kv_push, no block ids) and announces its blocks; the prefill engine,
     given the same push id, writes them (all at hand-over: the reference model calls no per-layer hook). With a TP2
     prefill engine, each of its ranks holds one of the two KV heads, and the TP1 decode rank takes a share from each
-    (head_shares), through the reference's own multi-rank step (gather_object over gloo). Every pull is also checked
-    byte for byte against the producer ranks' blocks."""
+    (head_shares); that engine's ranks hand rank 0 their connector outputs through KVConnectorStep's shared-memory
+    mailbox, wired into the reference's ModelRunner as a maintainer would. Every pull is also checked byte for byte
+    against the producer ranks' blocks."""
     caches = tmp_path / "caches"
     caches.mkdir()
     prefill_port, decode_port = _free_port(), _free_port()
@@ -238,7 +242,9 @@ def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carrie
             prefill_conn.send("go")
             _receive(prefill_conn, prefill, "the prefill engine never finished its request")
         token_ids, num_prefill_tokens, bytes_match = _receive(decode_conn, decode, "the decode engine never finished")
-        assert _receive(prefill_conn, prefill, "the prefill engine kept its blocks") == 0.0  # all freed
+        usage, exchange = _receive(prefill_conn, prefill, "the prefill engine kept its blocks")
+        assert usage == 0.0  # every held block freed
+        assert exchange == ("mailbox" if prefill_tp > 1 else None)
         prefill_conn.send("compared")
         reference = _receive(prefill_conn, prefill, "the prefill engine's own run never finished")
     finally:
