@@ -156,6 +156,8 @@ def _pulled_bytes_match(worker, req, positions: int) -> bool:
 
 def _decode(conn, model: str, cache_folder: str, kv_port: int, tp: int):
     os.environ["LEAN_VLLM_KVX_ACCEPT_PUSH"] = "1"  # serves on kv_port, so a prefill engine may push into it
+    if tp > 1:  # the load ends once both ranks report it, through KVConnectorStep's mailbox
+        os.environ["KVX_TEST_STEP"] = "mailbox"
     engine = _engine(model, cache_folder, tensor_parallel_size=tp, kv_transfer_config=json.dumps(
         dict(kv_connector="CudaIpcConnector", kv_role="kv_consumer", kv_port=kv_port)))
     from lean_vllm.sampling_params import SamplingParams
@@ -176,8 +178,9 @@ def _decode(conn, model: str, cache_folder: str, kv_port: int, tp: int):
                          for sample in family.samples if sample.name.endswith("_total"))
     # The last prompt token's slot was recomputed here, so the copy is compared up to it.
     (req,) = loads.values()
-    match = None if req.pushed else _pulled_bytes_match(worker, req, len(PROMPT) - 1)
-    conn.send((outputs[0]["token_ids"], prefill_tokens, match))
+    match = None if req.pushed else _pulled_bytes_match(worker, req, len(PROMPT) - 1)  # this rank's heads
+    step = getattr(engine.model_runner, "_kv_step", None)
+    conn.send((outputs[0]["token_ids"], prefill_tokens, match, step.exchange if step is not None else None))
     engine.exit()
 
 
@@ -205,8 +208,9 @@ def checkpoint(tmp_path_factory):
     return folder
 
 
-@pytest.mark.parametrize("mode, prefill_tp, decode_tp", [("pull", 1, 1), ("push", 1, 1), ("pull", 2, 1)],
-                         ids=["pull", "push", "pull-tp2-to-tp1"])
+@pytest.mark.parametrize("mode, prefill_tp, decode_tp", [("pull", 1, 1), ("push", 1, 1), ("pull", 2, 1),
+                                                         ("pull", 1, 2)],
+                         ids=["pull", "push", "pull-tp2-to-tp1", "pull-tp1-to-tp2"])
 def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carried(checkpoint, tmp_path, mode,
                                                                                   prefill_tp, decode_tp):
     """Pull: the prefill finishes, hands its kv_transfer_params over, and the decode engine reads the blocks. Push:
@@ -214,8 +218,9 @@ def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carrie
     given the same push id, writes them (all at hand-over: the reference model calls no per-layer hook). With a TP2
     prefill engine, each of its ranks holds one of the two KV heads, and the TP1 decode rank takes a share from each
     (head_shares); that engine's ranks hand rank 0 their connector outputs through KVConnectorStep's shared-memory
-    mailbox, wired into the reference's ModelRunner as a maintainer would. Every pull is also checked byte for byte
-    against the producer ranks' blocks."""
+    mailbox, wired into the reference's ModelRunner as a maintainer would. A TP1 prefill engine feeding a TP2 decode
+    engine has each decode rank pull its own head and the load end once both ranks report it, through the same
+    mailbox. Every pull is also checked byte for byte against the producer ranks' blocks (on decode rank 0)."""
     caches = tmp_path / "caches"
     caches.mkdir()
     prefill_port, decode_port = _free_port(), _free_port()
@@ -241,7 +246,9 @@ def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carrie
                               "tp_size": prefill_tp, "remote_block_ids": []})
             prefill_conn.send("go")
             _receive(prefill_conn, prefill, "the prefill engine never finished its request")
-        token_ids, num_prefill_tokens, bytes_match = _receive(decode_conn, decode, "the decode engine never finished")
+        token_ids, num_prefill_tokens, bytes_match, decode_exchange = _receive(decode_conn, decode,
+                                                                               "the decode engine never finished")
+        assert decode_exchange == ("mailbox" if decode_tp > 1 else None)
         usage, exchange = _receive(prefill_conn, prefill, "the prefill engine kept its blocks")
         assert usage == 0.0  # every held block freed
         assert exchange == ("mailbox" if prefill_tp > 1 else None)
