@@ -209,8 +209,8 @@ def checkpoint(tmp_path_factory):
 
 
 @pytest.mark.parametrize("mode, prefill_tp, decode_tp", [("pull", 1, 1), ("push", 1, 1), ("pull", 2, 1),
-                                                         ("pull", 1, 2)],
-                         ids=["pull", "push", "pull-tp2-to-tp1", "pull-tp1-to-tp2"])
+                                                         ("pull", 1, 2), ("push", 1, 2)],
+                         ids=["pull", "push", "pull-tp2-to-tp1", "pull-tp1-to-tp2", "push-tp1-to-tp2"])
 def test_the_reference_decode_engine_continues_from_the_kv_this_connector_carried(checkpoint, tmp_path, mode,
                                                                                   prefill_tp, decode_tp):
     """Pull: the prefill finishes, hands its kv_transfer_params over, and the decode engine reads the blocks. Push:
