@@ -317,6 +317,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
         self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
         self._thread: threading.Thread | None = None
+        self._errors_seen: set = set()  # (step, error type, message) the transfer thread has logged
 
     # -------------------------------------------------------------------------------------------- engine thread
 
@@ -627,23 +628,35 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 for item in items:
                     if item[0] == "loads":
                         for request_id, req in item[2]:
-                            self._start(request_id, req, item[1], batch)
+                            self._guarded(self._start, request_id, req, item[1], batch)
                     elif item[0] == "connect":
-                        self._connect(item[1])
+                        self._guarded(self._connect, item[1])
                     elif item[0] == "finish":
-                        self._finish(*item[1:])
-                self._post_loads(batch)
+                        self._guarded(self._finish, *item[1:])
+                self._guarded(self._post_loads, batch)
                 if self._server is not None:
-                    self._serve()
-                self._poll()
-                self._poll_relays()
-                self._poll_pushes()
-                self._poll_waits()
-                self._poll_retired()  # last: after every post this pass made
+                    self._guarded(self._serve)
+                for poll in (self._poll, self._poll_relays, self._poll_pushes, self._poll_waits,
+                             self._poll_retired):  # retired mappings last: after every post this pass made
+                    self._guarded(poll)
         except zmq.ContextTerminated:
             pass
         finally:
             self._close()
+
+    def _guarded(self, step, *args):
+        """One step of the transfer thread. An error nothing below expected is logged (once per kind) and the thread
+        goes on serving: if it ended, every load on this rank would wait for ever, since a decode engine has no
+        deadline on a pull. Closing the context still ends the thread."""
+        try:
+            step(*args)
+        except zmq.ContextTerminated:
+            raise
+        except Exception as error:  # noqa: BLE001
+            kind = (getattr(step, "__name__", str(step)), type(error).__name__, str(error)[:200])
+            if kind not in self._errors_seen:
+                self._errors_seen.add(kind)
+                logger.exception("the KV transfer thread hit an unexpected error in %s and carries on", kind[0])
 
     def _close(self):
         released = set()
@@ -710,7 +723,9 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         """A peer's message whose fields do not parse is dropped with a warning: it must not end this thread."""
         try:
             self._handle(identity, message)
-        except (ValueError, TypeError, AttributeError) as error:
+        except zmq.ContextTerminated:
+            raise
+        except Exception as error:  # noqa: BLE001 - whatever a peer sends must not end this thread
             logger.warning("ignoring a malformed KV message %.200r: %s", message, error)
 
     def _handle(self, identity, message: dict):

@@ -332,6 +332,23 @@ def test_loads_that_finish_together_notify_their_producer_in_one_message(sides, 
     assert len(notes) == 1 and sorted(notes[0]["messages"]) == ["p-1:1", "p-2:1"]
 
 
+def test_an_unexpected_error_in_a_step_is_logged_once_and_the_thread_carries_on(sides, caplog):
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    worker = consumers[0]
+
+    def broken():
+        raise ZeroDivisionError("planted in a test")
+
+    worker._poll_waits = broken  # runs every pass of the transfer thread
+    sleep(0.1)
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [4]}))
+    worker.start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0], [4])}))
+    assert wait_for(worker).finished_recving == {"d-1"}
+    assert worker._thread.is_alive()
+    assert caplog.text.count("hit an unexpected error in broken") == 1
+
+
 def test_a_taken_port_is_named(sides):
     with socket.socket() as taken:
         taken.bind(("127.0.0.1", 0))
