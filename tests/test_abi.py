@@ -142,21 +142,24 @@ int main(void) {
 """
 
 
-def test_a_plain_c99_client_compiles_against_the_header_and_runs_without_a_device(tmp_path):
-    """The boundary is C: the header compiles as strict C99, and a C program linked to libkvx.so gets the same
-    answers the ctypes binding gets (host validation and the step mailbox need no GPU)."""
+@pytest.mark.parametrize("compiler, standard, suffix", [("gcc", "-std=c99", ".c"), ("g++", "-std=c++17", ".cpp")],
+                         ids=["c99", "c++17"])
+def test_a_plain_client_compiles_against_the_header_and_runs_without_a_device(tmp_path, compiler, standard, suffix):
+    """The boundary is C: the header compiles as strict C99 (and, through its extern "C" block, as C++17), and a
+    program linked to libkvx.so gets the same answers the ctypes binding gets (host validation and the step mailbox
+    need no GPU)."""
     import shutil
     import subprocess
 
     if not os.path.exists(_native.LIB_PATH):
         pytest.skip("libkvx.so is not built here")
-    if shutil.which("gcc") is None:
-        pytest.skip("no C compiler")
-    source = tmp_path / "client.c"
+    if shutil.which(compiler) is None:
+        pytest.skip(f"no {compiler}")
+    source = tmp_path / f"client{suffix}"
     source.write_text(C_CLIENT)
     binary = tmp_path / "client"
     lib_dir = os.path.dirname(_native.LIB_PATH)
-    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(ROOT, "include"),
+    subprocess.run([compiler, standard, "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(ROOT, "include"),
                     str(source), "-o", str(binary), "-L", lib_dir, "-lkvx", f"-Wl,-rpath,{lib_dir}"],
                    check=True, capture_output=True, text=True)
     run = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
