@@ -5,13 +5,13 @@ half, the kv_transfer_params it returns, the handshake on kv_port + rank, the he
 tensor-parallel sizes, reader counting and the release/expiry rules are the reference's. What changes is below the
 worker: instead of registering memory with a NIXL agent and posting one-sided READs, each rank exports its cache
 through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts one kvx kernel launch per load
-(small loads started together share one), which gathers the shares' blocks from every producer rank's HBM over
-NVLink and scatters them into its own blocks.
+(the loads of one step, planned together, share launches up to 64 MB), which gathers the shares' blocks from every
+producer rank's HBM over NVLink and scatters them into its own blocks.
 The launch waits on the stream for the load's ready event (no host synchronisation); a native watcher rings an
 eventfd once the copy's event completes, and the transfer thread sleeps on that, its ZMQ socket and its work queue
 together, so it wakes when a copy lands or a message or a load arrives rather than polling on a timer; and a
 consumer rank tells each producer rank it read from once its bytes have landed (the NIXL notification's role) over
-the same ZMQ channel as the handshake.
+the same ZMQ channel as the handshake, in one message for all the loads that landed in one pass.
 
 It adds a layer-by-layer push the reference does not have (its docs list vLLM's save_kv_layer as unsupported,
 docs/disaggregated-prefill.md:29-30): given ReqToSave entries naming a decode instance's allocated blocks, a
@@ -801,7 +801,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             entry[0] += 1
             self._release_if_read(request_id)
 
-    # Pull: one launch per load, then poll it.
+    # Pull: plan the step's loads, launch them (small ones together), then poll each launch once per pass.
 
     def _start(self, request_id: str, req: ReqToRecv, ready, batch: list):
         """Plans one load (handshakes, shares, byte count); `_post_loads` launches the batch."""
