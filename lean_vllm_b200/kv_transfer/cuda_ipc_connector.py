@@ -317,7 +317,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
         self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
         self._thread: threading.Thread | None = None
-        self._errors_seen: set = set()  # (step, error type, message) the transfer thread has logged
+        self._errors_seen: set = set()  # (step, error type) the transfer thread has logged
 
     # -------------------------------------------------------------------------------------------- engine thread
 
@@ -653,7 +653,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         except zmq.ContextTerminated:
             raise
         except Exception as error:  # noqa: BLE001
-            kind = (getattr(step, "__name__", str(step)), type(error).__name__, str(error)[:200])
+            kind = (getattr(step, "__name__", str(step)), type(error).__name__)  # bounded: no request ids
             if kind not in self._errors_seen:
                 self._errors_seen.add(kind)
                 logger.exception("the KV transfer thread hit an unexpected error in %s and carries on", kind[0])
