@@ -349,6 +349,31 @@ def test_an_unexpected_error_in_a_step_is_logged_once_and_the_thread_carries_on(
     assert caplog.text.count("hit an unexpected error in broken") == 1
 
 
+def test_two_kv_both_instances_load_from_each_other_at_once(sides):
+    """kv_both (the reference's default role): each instance holds a prefill the other loads, and both loads start
+    together, so their handshakes cross -- each rank answers the other's while it waits for its own reply. Both
+    loads land bit for bit and both held requests are freed."""
+    a = sides.make("kv_both", 1, full_cache(0, False), engine_id="engine-a")
+    b = sides.make("kv_both", 1, full_cache(1, False), engine_id="engine-b")
+    before_a, before_b = a[0].kv_caches[0].clone(), b[0].kv_caches[0].clone()
+    a[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"pa": [4]}))
+    b[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"pb": [6]}))
+    a[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"from-b": recv(b, [2], [6], remote_request_id="pb")}))
+    b[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"from-a": recv(a, [3], [4], remote_request_id="pa")}))
+    got_a, got_b, deadline = KVConnectorOutput(), KVConnectorOutput(), monotonic() + 10
+    while monotonic() < deadline and not (got_a.finished_recving and got_a.finished_sending and
+                                          got_b.finished_recving and got_b.finished_sending):
+        for worker, got in ((a[0], got_a), (b[0], got_b)):
+            out = worker.get_finished()
+            got.finished_recving |= out.finished_recving
+            got.finished_sending |= out.finished_sending
+        sleep(0.002)
+    assert got_a.finished_recving == {"from-b"} and got_a.finished_sending == {"pa"}
+    assert got_b.finished_recving == {"from-a"} and got_b.finished_sending == {"pb"}
+    assert torch.equal(a[0].kv_caches[0][:, 2], before_b[:, 6])
+    assert torch.equal(b[0].kv_caches[0][:, 3], before_a[:, 4])
+
+
 def test_a_taken_port_is_named(sides):
     with socket.socket() as taken:
         taken.bind(("127.0.0.1", 0))
