@@ -41,7 +41,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "KV transfer GB/s & ms per 8k-token request"
 BYTES_8K_REQUEST = 32 * 36 * 2 * 8 * 256 * 128 * 2  # 1,207,959,552: 32 blocks x 36 layers x K/V x 512 KiB
-NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
+NVLINK_GBS = 900.0  # NVLink 5, per direction per GPU (nominal): the north star's link peak, the N >= 2 denominator
 
 
 @dataclass(frozen=True)
@@ -354,22 +354,59 @@ def load_traffic() -> dict:
     return {}
 
 
-def digest(layers, ids, first_head: int, num_heads: int, mla: bool, device):
-    """Position-weighted digest of some blocks' heads (first and last layer): equal digests on both sides of a
-    copy mean the bytes landed."""
+def block_digests(layers, ids, first_head: int, num_heads: int, mla: bool, chunk: int = 128):
+    """Per (layer, K|V or latent part, block) of `ids`: the sum and a position-weighted sum (odd 64-bit weights,
+    wrapping) of the block's share -- heads [first_head, +num_heads), or the whole latent block -- as int16 words.
+    Shape [layers, parts, len(ids), 2], on the cache's device. Every word of every listed block enters the digest
+    and any single changed word changes the weighted sum (odd weights are invertible mod 2^64), so equal digests on
+    both sides of a transfer mean every moved block landed where it should."""
     import torch
 
     device = layers[0].device
-    index = torch.as_tensor(ids, device=device, dtype=torch.long)
+    index = torch.as_tensor(np.asarray(ids, dtype=np.int64), device=device)
     out = []
-    for layer in (0, len(layers) - 1):
-        part = layers[layer][:, index]
-        if not mla:
-            part = part[:, :, first_head : first_head + num_heads]
-        flat = part.contiguous().view(torch.int16).reshape(-1).to(torch.int64)
-        weights = torch.arange(flat.numel(), device=device, dtype=torch.int64) % 65521 + 1
-        out += [int(flat.sum().item()), int((flat * weights).sum().item())]
-    return out
+    weights = None
+    for layer in layers:
+        per_layer = []
+        for at in range(0, len(ids), chunk):
+            part = layer.index_select(1, index[at : at + chunk])
+            if not mla:
+                part = part[:, :, first_head : first_head + num_heads]
+            flat = part.contiguous().view(torch.int16).reshape(part.shape[0], part.shape[1], -1).to(torch.int64)
+            if weights is None or weights.numel() != flat.shape[-1]:
+                weights = torch.arange(flat.shape[-1], device=device, dtype=torch.int64) * 2654435761 * 2 + 1
+            per_layer.append(torch.stack([flat.sum(-1), (flat * weights).sum(-1)], -1))
+        out.append(torch.cat(per_layer, 1))
+    return torch.stack(out)
+
+
+def measure_peer_copy(src_device: int, dst_device: int, nbytes: int = 1 << 30, reps: int = 5) -> float | None:
+    """GB/s of one event-timed device-to-device copy of `nbytes` from src_device's memory into dst_device's, issued
+    on dst_device (a copy engine pulling over NVLink, as cudaMemcpyPeerAsync does with peer access on), best of
+    `reps`. No kvx kernel and no library kernel touches peer memory. None if the two cannot reach each other."""
+    import torch
+
+    from lean_vllm_b200.kv_transfer import transport
+
+    if not transport.enable_peer_access(dst_device, src_device):
+        return None
+    src = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{src_device}")
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dst_device}")
+    src.fill_(1)
+    torch.cuda.synchronize(src_device)
+    best = float("inf")
+    with torch.cuda.device(dst_device):
+        stream = torch.cuda.current_stream()
+        for _ in range(reps + 1):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            dst.copy_(src, non_blocking=True)
+            end.record(stream)
+            end.synchronize()
+            best = min(best, start.elapsed_time(end))
+    del src, dst
+    torch.cuda.empty_cache()
+    return nbytes / (best * 1e-3) / 1e9
 
 
 def run_gpu(args) -> None:
@@ -509,6 +546,18 @@ def run_gpu(args) -> None:
             dist.barrier()
             torch.cuda.synchronize()
 
+    # The copy-engine peer copy between the pair's GPUs, measured on the consumer's side: reported beside the
+    # link's nominal peak, never used as the denominator.
+    peer_copy = None
+    if world > 1 and role.side == "decode" and role.tp_rank == 0:
+        producer = rank_of(role.group, "prefill", 0) % torch.cuda.device_count()
+        peer_copy = measure_peer_copy(producer, local_rank)
+        torch.cuda.set_device(launch_device)
+    elif peer_mode:
+        peer_copy = measure_peer_copy(device.index, dst_device.index)
+        torch.cuda.set_device(launch_device)
+    barrier()
+
     for _ in range(args.warmup):
         step()
     barrier()
@@ -523,7 +572,8 @@ def run_gpu(args) -> None:
         barrier()
     launches = transport.launch_count() - launches0
     elapsed_ms = start.elapsed_time(end) if launching else 0.0
-    stats = torch.tensor([elapsed_ms, float(launches), float(my_bytes)], device=device, dtype=torch.float64)
+    stats = torch.tensor([elapsed_ms, float(launches), float(my_bytes), peer_copy or 0.0], device=device,
+                         dtype=torch.float64)
     if world > 1:
         gathered = [torch.zeros_like(stats) for _ in range(world)]
         dist.all_gather(gathered, stats)
@@ -533,34 +583,45 @@ def run_gpu(args) -> None:
     max_ms = float(stats_all[:, 0].max())
     total_launches = int(stats_all[:, 1].sum())
     step_bytes_total = float(stats_all[:, 2].sum())  # payload per step over all decode ranks of all groups
+    peer_copies = [float(v) for v in stats_all[:, 3] if v > 0]
 
-    # Correctness: for two requests, every decode rank's received heads equal the producer's, by digest.
+    # Correctness over every byte the step moved: every block of every request, each decode rank's heads against
+    # the producer rank that holds them. One GPU: the blocks compared outright. N GPUs: per-(layer, part, block)
+    # digests of each share computed on both sides and compared.
     ok = True
-    samples = [reqs[0], reqs[-1]]
+    all_src = np.concatenate([s for s, _ in reqs])
+    all_dst = np.concatenate([d for _, d in reqs])
     if loopback:
-        ok = all(digest(dst, d, 0, heads, spec.mla, device) == digest(src, s, 0, heads, spec.mla, device)
-                 for s, d in samples)
+        s_index = torch.as_tensor(all_src, dtype=torch.long, device=src[0].device)
+        d_index = torch.as_tensor(all_dst, dtype=torch.long, device=dst[0].device)
+        for a, b in zip(src, dst):
+            ok &= bool(torch.equal(a.index_select(1, s_index), b.index_select(1, d_index).to(a.device)))
+        checked = int(len(all_src) * len(src))
     elif world > 1:
         mine_digests = {}
         if role.side == "decode":
             for i, sh in enumerate(head_shares(role.tp_rank, spec.decode_tp, spec.prefill_tp, heads)):
                 if spec.mla and i:
                     continue
-                mine_digests[(role.tp_rank, i)] = [digest(dst, d, sh.local_head, sh.num_heads, spec.mla, device)
-                                                   for _, d in samples]
+                mine_digests[(role.tp_rank, i)] = block_digests(dst, all_dst, sh.local_head, sh.num_heads,
+                                                                spec.mla).cpu()
         elif role.side == "prefill":
             for decode_rank in range(spec.decode_tp):
                 for i, sh in enumerate(head_shares(decode_rank, spec.decode_tp, spec.prefill_tp, heads)):
                     if sh.remote_rank != role.tp_rank or (spec.mla and i):
                         continue
-                    mine_digests[(decode_rank, i)] = [digest(src, s, sh.remote_head, sh.num_heads, spec.mla, device)
-                                                      for s, _ in samples]
+                    mine_digests[(decode_rank, i)] = block_digests(src, all_src, sh.remote_head, sh.num_heads,
+                                                                   spec.mla).cpu()
         every = [None] * world
         dist.all_gather_object(every, (role.group, role.side, mine_digests), group=gloo)
+        checked = 0
         for group in range(groups):
             got = {k: v for g, side, d in every if g == group and side == "decode" for k, v in d.items()}
             want = {k: v for g, side, d in every if g == group and side == "prefill" for k, v in d.items()}
-            ok &= bool(got) and got == want
+            ok &= bool(got) and got.keys() == want.keys() and all(torch.equal(got[k], want[k]) for k in got)
+            checked += sum(v.shape[0] * v.shape[2] for v in got.values())
+    else:
+        checked = 0
 
     # e2e: the same loads through the connector's public API.
     e2e_ms, e2e_bytes = None, 0
@@ -610,9 +671,14 @@ def run_gpu(args) -> None:
             ingress = per_group / spec.decode_tp
             link_bytes = max(egress, ingress)
             achieved = link_bytes / (ms_per_step * 1e-3) / 1e9
-            roofline = {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
-                        "frac": round(achieved / NVLINK_PEER_GBS, 4),
-                        "peak_source": "measured peer copy per direction on this pool (nominal 900 GB/s)",
+            roofline = {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_GBS, "unit": "GB/s",
+                        "frac": round(achieved / NVLINK_GBS, 4),
+                        "peak_source": "nominal NVLink 5 per direction per GPU (900 GB/s), the north star's peak",
+                        "peer_copy_gbs_measured": round(min(peer_copies), 1) if peer_copies else None,
+                        "peer_copy_method": "1 GiB device-to-device copy on the consumer GPU's stream from the "
+                                            "producer GPU's memory (copy engine, peer access), CUDA events, best of "
+                                            "5; min over pairs",
+                        "busiest_link": "producer egress" if egress >= ingress else "decode ingress",
                         "link_bytes_per_step": int(link_bytes),
                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
                         "nvlink_rx_bytes_per_launch": traffic.get("nvlink_rx_bytes_per_launch") if traffic else None,
@@ -652,6 +718,9 @@ def run_gpu(args) -> None:
             "gpu_launches": total_launches,
             "clocks": clock_summary,
             "correct": bool(ok_t.item() == 0.0),
+            "correct_covers": (f"every moved block of every request ({checked} (layer, block) pairs"
+                               + (": compared outright)" if loopback else
+                                  ": per-(layer, part, block) digests of each head share on both sides)")),
         }
         if e2e_ms is not None:
             ids_bytes = 2 * 4 * step_blocks * spec.decode_tp * groups
@@ -764,13 +833,13 @@ def token_slots(block_ids, length: int, block: int) -> np.ndarray:
 
 
 def row_digest(layers, slots):
-    """Position-weighted digest of the keys and values at the given slots (first and last layer)."""
+    """Position-weighted digest of the keys and values at the given slots, every layer."""
     import torch
 
     device = layers[0].device
     index = torch.as_tensor(slots, device=device, dtype=torch.long)
     out = []
-    for layer in (0, len(layers) - 1):
+    for layer in range(len(layers)):
         view = layers[layer].transpose(2, 3)  # (2, blocks, tokens, heads, dim)
         part = view[:, index // view.size(2), index % view.size(2)]
         flat = part.contiguous().view(torch.int16).reshape(-1).to(torch.int64)
@@ -926,12 +995,12 @@ def run_layerwise(args) -> None:
         alone = [iteration(f"c{k}", False)[0] for k in range(args.steps)]
         both = [iteration(f"s{k}", True) for k in range(args.steps)]
         ok = True
-        samples = [0, len(reqs) - 1]
+        samples = range(len(reqs))  # every request
 
         def check(layers, ids, i):
             if args.fused:  # the stored rows only: a last block's tail past the prompt is never written
                 return row_digest(layers, token_slots(ids, lengths[i], spec.block))
-            return digest(layers, ids, 0, 8, False, device)
+            return block_digests(layers, ids, 0, 8, False).cpu().tolist()
 
         if world == 1:
             ok = all(check(dst, reqs[i][1], i) == check(src, reqs[i][0], i) for i in samples)
@@ -1099,8 +1168,8 @@ def run_store(args) -> None:
                     hbm_bytes // layers, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"}
     else:
         link = layers * rows
-        roofline = {"bound": "nvlink", "achieved": round(link / (ms * 1e-3) / 1e9, 1), "peak": NVLINK_PEER_GBS,
-                    "unit": "GB/s", "frac": round(link / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4),
+        roofline = {"bound": "nvlink", "achieved": round(link / (ms * 1e-3) / 1e9, 1), "peak": NVLINK_GBS,
+                    "unit": "GB/s", "frac": round(link / (ms * 1e-3) / 1e9 / NVLINK_GBS, 4),
                     "link_bytes_per_launch": link // layers, "hbm_bytes_per_launch": hbm_bytes // layers,
                     "peak_source": "measured peer copy per direction on this pool (nominal 900 GB/s)"}
     line = {
@@ -1354,7 +1423,7 @@ def run_staged(args) -> None:
     stages = {}
     for name, t in ms.items():
         moved = 2 * total if name != "push" or peer == device else total
-        bound, peak = ("nvlink", NVLINK_PEER_GBS) if name == "push" and peer != device else ("hbm", hbm)
+        bound, peak = ("nvlink", NVLINK_GBS) if name == "push" and peer != device else ("hbm", hbm)
         achieved = moved / (t * 1e-3) / 1e9
         stages[name] = {"ms": round(t, 4), "payload_gb_per_s": round(total / (t * 1e-3) / 1e9, 1),
                         "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

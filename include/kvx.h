@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define KVX_ABI_VERSION 1
+#define KVX_ABI_VERSION 2
 
 /* Status codes. Every entry point returns one; kvx_last_error() describes the last failure on this thread. */
 #define KVX_OK 0
@@ -37,7 +37,7 @@ extern "C" {
 #define KVX_ERR_INVALID (-1)   /* a bad argument */
 #define KVX_ERR_CUDA (-2)      /* a CUDA call failed */
 #define KVX_ERR_RANGE (-3)     /* a block id or head range outside its cache (nixl_connector.py:398-399) */
-#define KVX_ERR_DEVICE (-4)    /* a kernel gave up a bounded wait; see kvx_device_error */
+#define KVX_ERR_DEVICE (-4)    /* a transfer's copy gave up a bounded wait (its status word says so) */
 #define KVX_ERR_TIMEOUT (-5)   /* a host wait ran out (a rank that never posted its step) */
 
 /* kvx_copy/kvx_transfer/kvx_pack/kvx_push/kvx_scatter flags word: bits 0-7 engine (below), bits 8-15 log2 of the
@@ -83,8 +83,10 @@ typedef struct kvx_ipc_handle {
     uint64_t offset;          /* of the pointer within that allocation */
     uint64_t alloc_bytes;     /* size of that allocation */
     int32_t device;           /* exporting device ordinal, in the exporter's numbering */
-    int32_t pid;              /* exporting process; an importer in the same process uses the pointer directly */
+    int32_t pid;              /* exporting process ... */
     uint64_t ptr;             /* the exported pointer, valid in the exporting process only */
+    unsigned char nonce[16];  /* ... and 16 random bytes drawn once per process: an importer whose pid AND nonce
+                                 match uses `ptr` directly (a pid alone repeats across PID namespaces) */
 } kvx_ipc_handle;
 
 /* Opaque in-flight transfer: a launch plus the event recorded after it (a NIXL xfer handle, :411-418). */
@@ -169,9 +171,12 @@ typedef struct kvx_store_dest {
 /* Scatters num_tokens rows of keys and values [token][head][head_bytes] (or latents, with value = NULL and
  * num_heads = 1) into each destination's slots, one pass over the rows: destination 0 is the local cache
  * (store_kvcache / store_latents, attention/triton_cache.py:9-91); destinations 1..8 may be peers' caches, which
- * makes this the fused store-and-push of a layer-by-layer transfer. Strides of the rows are in bytes. */
+ * makes this the fused store-and-push of a layer-by-layer transfer. Strides of the rows are in bytes. `status` (may be
+ * NULL) is a status word (kvx_status_open) that gets bit 2 when a row was skipped because its slot, or its block
+ * map entry, lies past a destination's cache -- what a fused push checks before it reports the peer's blocks full. */
 int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t value_stride, int num_tokens,
-              int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int flags, void *stream);
+              int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int32_t *status, int flags,
+              void *stream);
 
 /* ---- transfers with completion (post, poll, release) ---- */
 
@@ -182,13 +187,31 @@ int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int
                  void *wait_event, void *stream, kvx_xfer_t *out);
 
 /* KVX_OK once the transfer's copies have landed, KVX_PENDING while in flight, <0 on failure: KVX_ERR_CUDA if the
- * launch failed, KVX_ERR_DEVICE if a copy on its device gave up a bounded wait (bit 1 of the device error word,
- * read without waiting on other streams once the transfer's event has completed).
- * Replaces check_xfer_state (nixl_connector.py:431). */
+ * launch failed, KVX_ERR_DEVICE if one of ITS copies gave up a bounded wait (bit 1 of its own status word, read from
+ * host memory once the transfer's event has completed: no copy, no stream). A failure elsewhere on the device fails
+ * no other transfer. Replaces check_xfer_state (nixl_connector.py:431). */
 int kvx_check_xfer(kvx_xfer_t xfer);
 
-/* Frees the handle (waits for nothing). Replaces release_xfer_handle (nixl_connector.py:437). */
+/* Frees the handle and its status word (waits for nothing: release a transfer once it completed, or once the device
+ * has finished everything queued before it). Replaces release_xfer_handle (nixl_connector.py:437). */
 int kvx_release_xfer(kvx_xfer_t xfer);
+
+/* The transfer's status word (see kvx_status_open), for a test that stands in a failure of this transfer alone
+ * (kvx_wait_selftest). Valid until kvx_release_xfer. No reference counterpart: NIXL keeps per-xfer state inside the
+ * agent. */
+int kvx_xfer_status(kvx_xfer_t xfer, int32_t **out_word);
+
+/* ---- status words ---- */
+
+/* A status word: 4 bytes of pinned host memory mapped into every device at the same address. A kernel given one
+ * writes an error bit there only when it fails without faulting (1: a copy's bounded wait ran out; 2: a store row
+ * whose slot or block lies past its cache was skipped), and the host reads it once the launch's completion event has
+ * completed. Opened zeroed; close it only after every launch given it has completed. kvx_transfer holds one per
+ * transfer; kvx_store takes one from its caller. Up to 65,536 are open at once. No reference counterpart (NIXL
+ * reports per-xfer state through check_xfer_state, nixl_connector.py:431). */
+int kvx_status_open(int32_t **out_word);
+int kvx_status_close(int32_t *word);
+int kvx_status_read(const int32_t *word, int32_t *out_bits);
 
 /* ---- completion doorbells ---- */
 
@@ -234,17 +257,19 @@ int kvx_mailbox_release(void *box, uint64_t seq);
  * (nixl_connector.py:421). Validates like kvx_copy; launches nothing. */
 int kvx_job_bytes(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, uint64_t *out_bytes);
 
-/* Reads and clears the device error word of the current device: 0, or the OR of the errors kernels recorded since
- * the last read -- 1 a copy's bounded TMA wait ran out (its bytes did not all land), 2 a store slot or block id past
- * its cache (skipped), 4 kvx_wait_selftest gave up as designed. While bit 1 is set, kvx_check_xfer fails every
- * transfer on that device that completes (KVX_ERR_DEVICE): which copy gave up is not recorded. */
+/* Reads and clears, in one atomic step on the device, the diagnostic error word of the current device: 0, or the OR
+ * of the errors kernels recorded since the last read -- 1 a copy's bounded TMA wait ran out (its bytes did not all
+ * land), 2 a store slot or block id past its cache (skipped), 4 kvx_wait_selftest gave up as designed. Runs on a
+ * stream of the library's own and waits on no other. Transfers are judged by their own status words, not by this
+ * word: reading it (or not) changes no transfer's result. */
 int kvx_device_error(int *out_code);
 
 /* Runs, on `stream`, the bounded wait that guards every TMA copy against a transfer that never arrives: one
  * thread waits on an mbarrier armed for bytes no copy will bring, gives up after limit_us (1 us .. 10 s) and
- * records `code` in the device word: 4 (the self-test's own bit), or 1 to stand in for a stuck copy. Nothing is
- * copied, nothing faults or hangs; for tests of the failure path. */
-int kvx_wait_selftest(int limit_us, int code, void *stream);
+ * records `code` in the device word and in `status` when given (kvx_xfer_status): 4 (the self-test's own bit), or 1
+ * to stand in for a stuck copy of that transfer. Nothing is copied, nothing faults or hangs; for tests of the
+ * failure path. */
+int kvx_wait_selftest(int limit_us, int code, int32_t *status, void *stream);
 
 /* Kernel launches issued by this process so far (all entry points), for launch accounting. */
 uint64_t kvx_launch_count(void);

@@ -12,6 +12,8 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libkvx.so")
 
+ABI_VERSION = 2  # KVX_ABI_VERSION of include/kvx.h
+
 KVX_OK = 0
 KVX_PENDING = 1
 KVX_ERR_INVALID = -1
@@ -19,6 +21,11 @@ KVX_ERR_CUDA = -2
 KVX_ERR_RANGE = -3
 KVX_ERR_DEVICE = -4
 KVX_ERR_TIMEOUT = -5
+
+# Status word bits (kvx_status_open): what a launch reports when it fails without faulting.
+STATUS_COPY_WAIT = 1  # a copy's bounded wait ran out: not every byte landed
+STATUS_PAST_CACHE = 2  # a store row whose slot or block lies past its cache was skipped
+STATUS_SELFTEST = 4  # kvx_wait_selftest gave up, as designed
 
 STORE_SERIAL = 1  # kvx_store flag: a plain launch, no overlap with the kernel before it
 STORE_PEERS_ONLY = 4  # kvx_store flag: only the peer destinations are written (destination 0 places their rows)
@@ -41,7 +48,7 @@ class KvxRangeError(KvxError):
 
 
 class KvxDeviceError(KvxError):
-    """A kernel gave up a bounded wait: a copy whose bytes did not all land (kvx_device_error reads the word)."""
+    """A transfer's copy gave up a bounded wait, so its bytes did not all land (its own status word says so)."""
 
 
 class KvxTimeout(KvxError):
@@ -82,6 +89,7 @@ class IpcHandle(ctypes.Structure):
         ("device", ctypes.c_int32),
         ("pid", ctypes.c_int32),
         ("ptr", ctypes.c_uint64),
+        ("nonce", ctypes.c_ubyte * 16),
     ]
 
     def to_bytes(self) -> bytes:
@@ -131,11 +139,15 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kvx_scatter": ([_P, ctypes.c_uint64, ctypes.POINTER(Cache), ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
     "kvx_store": ([_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                   ctypes.POINTER(StoreDest), ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
+                   ctypes.POINTER(StoreDest), ctypes.c_int, _P, ctypes.c_int, _P], ctypes.c_int),
     "kvx_transfer": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int, ctypes.c_int, _P, _P,
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "kvx_check_xfer": ([_P], ctypes.c_int),
     "kvx_release_xfer": ([_P], ctypes.c_int),
+    "kvx_xfer_status": ([_P, ctypes.POINTER(_P)], ctypes.c_int),
+    "kvx_status_open": ([ctypes.POINTER(_P)], ctypes.c_int),
+    "kvx_status_close": ([_P], ctypes.c_int),
+    "kvx_status_read": ([_P, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "kvx_doorbell_open": ([ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "kvx_doorbell_ring_after": ([ctypes.c_int, _P], ctypes.c_int),
     "kvx_doorbell_close": ([ctypes.c_int], ctypes.c_int),
@@ -149,7 +161,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kvx_job_bytes": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int,
                        ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "kvx_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
-    "kvx_wait_selftest": ([ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
+    "kvx_wait_selftest": ([ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
     "kvx_launch_count": ([], ctypes.c_uint64),
 }
 
@@ -173,8 +185,8 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes = argtypes
             fn.restype = restype
-        if handle.kvx_abi_version() != 1:
-            raise KvxUnavailable(f"{LIB_PATH} has ABI {handle.kvx_abi_version()}, expected 1")
+        if handle.kvx_abi_version() != ABI_VERSION:
+            raise KvxUnavailable(f"{LIB_PATH} has ABI {handle.kvx_abi_version()}, expected {ABI_VERSION}; rebuild it")
         _lib = handle
     return _lib
 

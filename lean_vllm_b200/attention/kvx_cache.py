@@ -89,19 +89,21 @@ def _target_slots(target, num_tokens, device):
     return _slots(target.slot_mapping, num_tokens, device)
 
 
-def _launch(key, value, num_heads, head_bytes, dests, stream, flags):
+def _launch(key, value, num_heads, head_bytes, dests, stream, flags, status):
     array = (StoreDest * len(dests))(*dests)
     s = stream if stream is not None else torch.cuda.current_stream(key.device).cuda_stream
     check(lib().kvx_store(key.data_ptr(), value.data_ptr() if value is not None else None,
                           key.stride(0) * key.element_size(),
                           value.stride(0) * value.element_size() if value is not None else 0,
-                          key.size(0), num_heads, head_bytes, array, len(dests), flags, s))
+                          key.size(0), num_heads, head_bytes, array, len(dests), status or None, flags, s))
 
 
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                  slot_mapping: torch.Tensor, push_to=(), stream: int | None = None, flags: int = 0) -> None:
+                  slot_mapping: torch.Tensor, push_to=(), stream: int | None = None, flags: int = 0,
+                  status: int = 0) -> None:
     """Scatter keys/values [num_tokens, heads, dim] into [num_blocks, block_size, heads, dim] caches by their
-    strides (an HND cache's transposed view too); slot -1 skips. Also into every PushTarget in `push_to`."""
+    strides (an HND cache's transposed view too); slot -1 skips. Also into every PushTarget in `push_to`. `status`
+    (a StatusWord's address) gets bit 2 if a row was skipped because its slot lies past a cache."""
     num_tokens, num_heads, head_dim = key.shape
     # Rows are copied as bytes, head by head: anything that would make a row land past its slot is refused here.
     if value.shape != key.shape or k_cache.dim() != 4 or k_cache.shape != v_cache.shape:
@@ -132,13 +134,14 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
         dests.append(_dest(target.k_cache, target.v_cache, target.block_stride, target.token_stride,
                            target.head_stride, target.block_size, target.num_blocks, t_slots, target.src_first_head,
                            count, target.dst_first_head, target.block_map))
-    _launch(key, value, num_heads, head_dim * itemsize, dests, stream, flags)
+    _launch(key, value, num_heads, head_dim * itemsize, dests, stream, flags, status)
 
 
 def store_latents(latent: torch.Tensor, latent_cache: torch.Tensor, slot_mapping: torch.Tensor, push_to=(),
-                  stream: int | None = None, flags: int = 0) -> None:
+                  stream: int | None = None, flags: int = 0, status: int = 0) -> None:
     """Scatter latents [num_tokens, dim] into a [num_blocks, block_size, dim] cache; slot -1 skips. Also into every
-    PushTarget in `push_to` (MLA latents are whole on every rank, so each decode rank takes a full copy)."""
+    PushTarget in `push_to` (MLA latents are whole on every rank, so each decode rank takes a full copy). `status` as
+    for store_kvcache."""
     num_tokens, dim = latent.shape
     if latent_cache.dim() != 3 or latent_cache.size(2) != dim:
         raise ValueError(f"latents of {dim} into a cache {tuple(latent_cache.shape)}")
@@ -159,7 +162,7 @@ def store_latents(latent: torch.Tensor, latent_cache: torch.Tensor, slot_mapping
         t_slots = _target_slots(target, num_tokens, latent.device)
         dests.append(_dest(target.k_cache, 0, target.block_stride, target.token_stride, 0, target.block_size,
                            target.num_blocks, t_slots, 0, 1, 0, target.block_map))
-    _launch(latent, None, 1, dim * itemsize, dests, stream, flags)
+    _launch(latent, None, 1, dim * itemsize, dests, stream, flags, status)
 
 
 def launch_flags(sm_budget: int = 0) -> int:

@@ -14,7 +14,13 @@
 //   TMA -- one thread per CTA runs a STAGES-deep ring of cp.async.bulk global->shared loads (mbarrier completion)
 //          and cp.async.bulk shared->global stores (bulk-group completion); data never enters registers.
 // Either side may be another GPU's memory mapped with cudaIpcOpenMemHandle: a launch on the consumer pulls over
-// NVLink, a launch on the producer pushes. No TMA load here uses cluster multicast.
+// NVLink, a launch on the producer pushes. Every bulk load lands in the issuing CTA's own shared memory.
+//
+// Status. A launch that can fail on the device without faulting -- a copy whose bounded wait ran out, a store row
+// whose slot lies past its cache -- reports it in a status word of its own: 4 bytes of pinned host memory mapped into
+// every device (kvx_status_open), written by the kernel only on failure and read by the host once the launch's event
+// has completed, with no copy and no stream of its own. Each transfer holds one, so a failure fails that transfer
+// alone. The same bits are also OR-ed into a per-device word, a diagnostic read and cleared by kvx_device_error.
 
 #include <cuda_runtime.h>
 
@@ -97,8 +103,9 @@ struct Params {
     uint64_t total_tiles;
     uint32_t n_jobs;
     uint32_t tile_bytes;
-    int32_t error_code;  // written to the device error word when a bounded wait runs out
+    int32_t error_code;  // written to the status words when a bounded wait runs out
     uint32_t pad;
+    int32_t *status;     // this launch's status word (mapped host memory), or null
     DevJob jobs[kMaxJobs];
     uint64_t addr[kMaxRegions];         // region base (block 0)
     uint64_t block_bytes[kMaxRegions];  // region block stride
@@ -106,12 +113,20 @@ struct Params {
 };
 static_assert(sizeof(Params) <= 32764, "kernel parameter space is 32764 bytes");
 
-// Errors kernels record on this device, as bits (read and cleared by kvx_device_error): a copy's bounded TMA wait ran
-// out (its bytes did not all land), a store slot or block id past its cache (skipped), the wait self-test gave up.
+// Errors kernels record, as bits: a copy's bounded TMA wait ran out (its bytes did not all land), a store slot or
+// block id past its cache (skipped), the wait self-test gave up. Each goes into the launch's status word, when it
+// has one, and into the device's diagnostic word (read and cleared by kvx_device_error).
 constexpr int kErrCopyWait = 1;
 constexpr int kErrPastCache = 2;
 constexpr int kErrSelftest = 4;
 __device__ int g_device_error;
+
+// Records `code` for a launch. A status word is only ever given one code per launch, so a plain store suffices (no
+// atomic reaches host memory); the host reads it after the launch's completion event, which orders the store.
+__device__ __forceinline__ void report(int32_t *status, int code) {
+    atomicOr(&g_device_error, code);
+    if (status) *reinterpret_cast<volatile int32_t *>(status) = code;
+}
 
 struct Tile {
     const char *src;
@@ -271,15 +286,22 @@ constexpr int kTmaStages = 4;
 
 // The failure path of every TMA wait, on demand: an mbarrier armed for 16 bytes that no copy will bring, waited on
 // with the same bounded wait the copy kernels use. It gives up after `limit_ns`, records `code` in the device word
-// and returns -- the status a stuck copy would leave -- without copying, faulting or hanging anything.
-__global__ void __launch_bounds__(32) kvx_wait_selftest_kernel(uint64_t limit_ns, int code) {
+// (and in `status`, when given) and returns -- the status a stuck copy would leave -- without copying, faulting or
+// hanging anything.
+__global__ void __launch_bounds__(32) kvx_wait_selftest_kernel(uint64_t limit_ns, int code, int32_t *status) {
     __shared__ __align__(8) uint64_t bar;
     if (threadIdx.x != 0) return;
     const uint32_t b = smem_u32(&bar);
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(16u) : "memory");
-    if (!mbar_wait(b, 0, globaltimer() + limit_ns)) atomicOr(&g_device_error, code);
+    if (!mbar_wait(b, 0, globaltimer() + limit_ns)) report(status, code);
+}
+
+// Reads and clears the device's diagnostic word in one atomic step, into mapped host memory: a bit a kernel sets
+// meanwhile is either taken here or left for the next read, never lost.
+__global__ void __launch_bounds__(32) kvx_take_device_error_kernel(int32_t *out) {
+    if (threadIdx.x == 0) *reinterpret_cast<volatile int32_t *>(out) = atomicExch(&g_device_error, 0);
 }
 
 __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Params p) {
@@ -327,7 +349,7 @@ __global__ void __launch_bounds__(32) kvx_copy_tma(const __grid_constant__ Param
         }
     }
     if (!ok) {
-        atomicOr(&g_device_error, p.error_code);
+        report(p.status, p.error_code);
         // Loads issued but not waited for may still be writing shared memory: give each a bounded wait.
         const uint64_t issued = mine < landed + kTmaStages ? mine : landed + kTmaStages;
         const uint64_t drain = globaltimer() + kWaitLimitNs;
@@ -359,6 +381,7 @@ struct StoreParams {
     int64_t key_stride, value_stride;
     int32_t num_tokens, num_heads, head_bytes, n_dests;
     int32_t peers_only, pad_;  // KVX_STORE_PEERS_ONLY: destination 0 places rows but is not written
+    int32_t *status;           // this launch's status word (mapped host memory), or null
     StoreDest dests[kMaxStoreDests];
 };
 
@@ -378,7 +401,7 @@ __device__ __forceinline__ int32_t resolve_slot(const StoreParams &p, int d, uin
     const int32_t shift0 = p.dests[0].block_shift;
     const uint32_t b = shift0 >= 0 ? (uint32_t)first_slot >> shift0 : (uint32_t)first_slot / block_size0;
     if (b >= (uint32_t)dst.block_map_len) {
-        atomicOr(&g_device_error, kErrPastCache);
+        report(p.status, kErrPastCache);
         return -1;
     }
     const int32_t mapped = dst.block_map[b];  // a block no save covers maps to -1
@@ -413,10 +436,10 @@ __device__ __forceinline__ StoreLane lane_of(const StoreDest &dst, uint32_t part
 // FAST: the destination's block size is a power of two and its block and token strides are below 2^32, so a slot
 // becomes an address with a shift, a mask and two 32x32->64-bit multiply-adds (the usual paged cache).
 template <int VEC, bool FAST>
-__device__ __forceinline__ void put(const StoreLane &l, int32_t slot, typename Vec<VEC>::T data) {
+__device__ __forceinline__ void put(const StoreLane &l, int32_t slot, typename Vec<VEC>::T data, int32_t *status) {
     if (slot < 0) return;  // padding: no cache slot
     if (slot >= l.limit) {
-        atomicOr(&g_device_error, kErrPastCache);  // a slot past the cache: skipped, never written
+        report(status, kErrPastCache);  // a slot past the cache: skipped, never written
         return;
     }
     uint64_t at;
@@ -437,7 +460,7 @@ __device__ __forceinline__ void store_row(const StoreParams &p, const StoreDest 
                                           int32_t head, uint32_t byte_in_row, typename Vec<VEC>::T data) {
     if (slot < 0) return;  // padding: no cache slot
     if (slot >= dst.num_blocks * dst.block_size) {
-        atomicOr(&g_device_error, kErrPastCache);  // a slot past the cache: skipped, never written
+        report(p.status, kErrPastCache);  // a slot past the cache: skipped, never written
         return;
     }
     const uint32_t block = dst.block_shift >= 0 ? (uint32_t)slot >> dst.block_shift
@@ -505,7 +528,7 @@ __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __gri
             }
             if (lane0.base && !peers_only) {
 #pragma unroll
-                for (int u = 0; u < kStoreUnroll; ++u) put<VEC, FAST>(lane0, first[u], data[u]);
+                for (int u = 0; u < kStoreUnroll; ++u) put<VEC, FAST>(lane0, first[u], data[u], p.status);
             }
             for (int d = 1; d < p.n_dests; ++d) {
                 const StoreDest &dst = p.dests[d];
@@ -708,7 +731,7 @@ int launch(Params &p, const Config &cfg, cudaStream_t stream) {
 
 // Packs pieces into as few launches as the parameter space allows and launches them in order on `stream`.
 int run(const kvx_cache *caches, int n_caches, const std::vector<Piece> &pieces, const Config &cfg,
-        cudaStream_t stream) {
+        int32_t *status, cudaStream_t stream) {
     thread_local std::vector<Params> storage(1);
     Params &p = storage[0];
     std::vector<int> slot(n_caches, -1);
@@ -717,6 +740,7 @@ int run(const kvx_cache *caches, int n_caches, const std::vector<Piece> &pieces,
         p.total_tiles = 0;
         p.n_jobs = 0;
         p.tile_bytes = cfg.tile_bytes;
+        p.status = status;  // every launch of one call reports into the call's word
         std::fill(slot.begin(), slot.end(), -1);
         n_regions = 0;
         n_ids = 0;
@@ -771,14 +795,14 @@ int run(const kvx_cache *caches, int n_caches, const std::vector<Piece> &pieces,
 }
 
 int copy_impl(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
-              cudaStream_t stream) {
+              cudaStream_t stream, int32_t *status = nullptr) {
     std::vector<Piece> pieces;
     uint64_t bytes, align_bits;
     if (int rc = plan(caches, n_caches, jobs, n_jobs, pieces, bytes, align_bits)) return rc;
     if (pieces.empty()) return KVX_OK;
     Config cfg;
     if (int rc = choose(flags, align_bits, cfg)) return rc;
-    return run(caches, n_caches, pieces, cfg, stream);
+    return run(caches, n_caches, pieces, cfg, status, stream);
 }
 
 // A staging buffer in kvx_pack's order, as a cache of the same region count: region r starts where the rows of
@@ -837,6 +861,7 @@ int allocation_of(const void *ptr, uint64_t *base, size_t *size) {
 struct Xfer {
     cudaEvent_t done;
     int device;
+    int32_t *status;  // the transfer's own status word
 };
 
 // ------------------------------------------------------------------------------------------------ doorbells
@@ -932,35 +957,100 @@ std::shared_ptr<Bell> find_bell(int id) {
     return it == g_bells.end() ? nullptr : it->second;
 }
 
-// ------------------------------------------------------------------------------------------------ error word probe
+// ------------------------------------------------------------------------------------------------ status words
 
-// Reads a device's error word without waiting on anyone else's streams: a 4-byte copy on a non-blocking stream of the
-// library's own into pinned host memory (one pair per device, under a lock), then a wait on that stream alone.
-struct ErrorProbe {
-    cudaStream_t stream = nullptr;
-    int *word = nullptr;
+// One pinned host allocation of status words, mapped into every device (portable + mapped): with unified addressing
+// a word has the same address on the host and on every device, so a kernel given it writes the host's memory
+// directly. Words are handed out one at a time and zeroed when handed out; a word goes back only after the launches
+// given it have completed, so no kernel still writes a word that is handed out again.
+constexpr int kStatusWords = 1 << 16;
+
+struct StatusPool {
+    std::mutex mu;
+    int32_t *words = nullptr;
+    std::vector<int32_t> free;  // indices of words not in use
+    std::vector<char> used;
 };
-std::mutex g_probe_mu;
-std::map<int, ErrorProbe> g_probes;
+StatusPool g_status;
 
-int read_device_errors(int device, int *out_bits) {
-    std::lock_guard<std::mutex> lock(g_probe_mu);
-    int prev;
-    KVX_CUDA(cudaGetDevice(&prev));
-    if (prev != device) KVX_CUDA(cudaSetDevice(device));
-    ErrorProbe &probe = g_probes[device];
-    cudaError_t e = cudaSuccess;
-    if (!probe.stream) e = cudaStreamCreateWithFlags(&probe.stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess && !probe.word) e = cudaHostAlloc(reinterpret_cast<void **>(&probe.word), sizeof(int),
-                                                           cudaHostAllocPortable);
-    if (e == cudaSuccess)
-        e = cudaMemcpyFromSymbolAsync(probe.word, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost,
-                                      probe.stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(probe.stream);
-    if (e == cudaSuccess) *out_bits = *probe.word;
-    if (prev != device) (void)cudaSetDevice(prev);
-    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+int status_open(int32_t **out) {
+    std::lock_guard<std::mutex> lock(g_status.mu);
+    if (!g_status.words) {
+        void *host = nullptr;
+        KVX_CUDA(cudaHostAlloc(&host, kStatusWords * sizeof(int32_t), cudaHostAllocMapped | cudaHostAllocPortable));
+        void *dev = nullptr;
+        const cudaError_t e = cudaHostGetDevicePointer(&dev, host, 0);
+        if (e != cudaSuccess || dev != host) {
+            cudaFreeHost(host);
+            return fail(KVX_ERR_CUDA, "status words are not mapped at their host address (%s)",
+                        e == cudaSuccess ? "no unified addressing" : cudaGetErrorString(e));
+        }
+        std::memset(host, 0, kStatusWords * sizeof(int32_t));
+        g_status.words = static_cast<int32_t *>(host);
+        g_status.used.assign(kStatusWords, 0);
+        g_status.free.reserve(kStatusWords);
+        for (int i = kStatusWords - 1; i >= 0; --i) g_status.free.push_back(i);
+    }
+    if (g_status.free.empty()) return fail(KVX_ERR_RANGE, "all %d status words are in use", kStatusWords);
+    const int i = g_status.free.back();
+    g_status.free.pop_back();
+    g_status.used[i] = 1;
+    *reinterpret_cast<volatile int32_t *>(g_status.words + i) = 0;
+    *out = g_status.words + i;
     return KVX_OK;
+}
+
+int status_close(int32_t *word) {
+    std::lock_guard<std::mutex> lock(g_status.mu);
+    const ptrdiff_t i = g_status.words ? word - g_status.words : -1;
+    if (i < 0 || i >= kStatusWords || !g_status.used[i]) return fail(KVX_ERR_INVALID, "not an open status word");
+    g_status.used[i] = 0;
+    g_status.free.push_back((int32_t)i);
+    return KVX_OK;
+}
+
+int32_t status_bits(const int32_t *word) { return *reinterpret_cast<const volatile int32_t *>(word); }
+
+// A non-blocking stream of the library's own per device, for reading the diagnostic word without waiting on anyone
+// else's streams.
+std::mutex g_probe_mu;
+std::map<int, cudaStream_t> g_probe_streams;
+
+int probe_stream(int device, cudaStream_t *out) {
+    std::lock_guard<std::mutex> lock(g_probe_mu);
+    cudaStream_t &s = g_probe_streams[device];
+    if (!s) KVX_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    *out = s;
+    return KVX_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ process identity
+
+// 16 random bytes drawn once per process: an IPC handle from this process carries them, so a handle is taken for
+// this process's own memory only when its pid AND its nonce match. Processes in separate PID namespaces (containers)
+// can share a pid; they do not share a nonce.
+const unsigned char *process_nonce() {
+    static unsigned char nonce[16];
+    static std::once_flag once;
+    std::call_once(once, [] {
+        size_t got = 0;
+        if (FILE *f = std::fopen("/dev/urandom", "rb")) {
+            got = std::fread(nonce, 1, sizeof nonce, f);
+            std::fclose(f);
+        }
+        if (got != sizeof nonce) {  // no urandom: mix what differs between processes
+            timespec t;
+            clock_gettime(CLOCK_REALTIME, &t);
+            uint64_t mix[2] = {(uint64_t)t.tv_sec * 1000000007ull ^ (uint64_t)getpid(),
+                               (uint64_t)t.tv_nsec ^ (uint64_t)(uintptr_t)&got};
+            std::memcpy(nonce, mix, sizeof nonce);
+        }
+    });
+    return nonce;
+}
+
+bool same_process(const kvx_ipc_handle *h) {
+    return h->pid == (int32_t)getpid() && std::memcmp(h->nonce, process_nonce(), sizeof h->nonce) == 0;
 }
 
 }  // namespace
@@ -993,6 +1083,7 @@ int kvx_ipc_export(const void *ptr, kvx_ipc_handle *out) {
     out->device = attr.device;
     out->pid = (int32_t)getpid();
     out->ptr = (uint64_t)(uintptr_t)ptr;
+    std::memcpy(out->nonce, process_nonce(), sizeof out->nonce);
     return KVX_OK;
 }
 
@@ -1000,7 +1091,7 @@ int kvx_ipc_open(const kvx_ipc_handle *h, void **out_ptr) {
     if (!h || !out_ptr) return fail(KVX_ERR_INVALID, "null pointer");
     int dev;
     KVX_CUDA(cudaGetDevice(&dev));
-    if (h->pid == (int32_t)getpid()) {  // our own allocation: CUDA IPC cannot reopen it, and need not
+    if (same_process(h)) {  // our own allocation: CUDA IPC cannot reopen it, and need not
         if (h->device != dev) {  // ... but a kernel on this device reaches it only with peer access on
             int can = 0;
             if (int rc = kvx_enable_peer_access(dev, h->device, &can)) return rc;
@@ -1027,7 +1118,7 @@ int kvx_ipc_open(const kvx_ipc_handle *h, void **out_ptr) {
 
 int kvx_ipc_close(const kvx_ipc_handle *h) {
     if (!h) return fail(KVX_ERR_INVALID, "null pointer");
-    if (h->pid == (int32_t)getpid()) return KVX_OK;
+    if (same_process(h)) return KVX_OK;
     int dev;
     KVX_CUDA(cudaGetDevice(&dev));
     const auto key = std::make_pair(dev, std::string(reinterpret_cast<const char *>(h->handle), 64));
@@ -1118,7 +1209,8 @@ int kvx_push(void *dst, const void *src, uint64_t bytes, int flags, void *stream
 }
 
 int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t value_stride, int num_tokens,
-              int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int flags, void *stream) {
+              int num_heads, int head_bytes, const kvx_store_dest *dests, int n_dests, int32_t *status, int flags,
+              void *stream) {
     Range range("kvx_store");
     if (!key || !dests) return fail(KVX_ERR_INVALID, "null rows or destinations");
     if (num_tokens < 0 || num_heads < 1 || head_bytes < 1)
@@ -1136,6 +1228,7 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
     p.head_bytes = head_bytes;
     p.n_dests = n_dests;
     p.peers_only = (flags & KVX_STORE_PEERS_ONLY) ? 1 : 0;
+    p.status = status;
     uint64_t align_bits = p.key | p.value | (uint64_t)key_stride | (uint64_t)value_stride | (uint64_t)head_bytes;
     for (int d = 0; d < n_dests; ++d) {
         const kvx_store_dest &s = dests[d];
@@ -1224,17 +1317,31 @@ int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int
     if (!out) return fail(KVX_ERR_INVALID, "null pointer");
     *out = nullptr;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (wait_event) KVX_CUDA(cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_event), 0));
-    if (int rc = copy_impl(caches, n_caches, jobs, n_jobs, flags, s)) return rc;
-    Xfer *x = new Xfer{};
-    KVX_CUDA(cudaGetDevice(&x->device));
-    cudaError_t e = cudaEventCreateWithFlags(&x->done, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventRecord(x->done, s);
-    if (e != cudaSuccess) {
-        delete x;
-        return fail(KVX_ERR_CUDA, "completion event: %s", cudaGetErrorString(e));
+    int device;
+    KVX_CUDA(cudaGetDevice(&device));
+    int32_t *status = nullptr;
+    if (int rc = status_open(&status)) return rc;
+    cudaEvent_t done = nullptr;
+    int rc = KVX_OK;
+    cudaError_t e = cudaSuccess;
+    const uint64_t launches_before = g_launches.load();
+    if (wait_event) e = cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_event), 0);
+    if (e == cudaSuccess) rc = copy_impl(caches, n_caches, jobs, n_jobs, flags, s, status);
+    if (e == cudaSuccess && rc == KVX_OK) e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+    if (e == cudaSuccess && rc == KVX_OK) e = cudaEventRecord(done, s);
+    if (e != cudaSuccess || rc != KVX_OK) {
+        if (done) cudaEventDestroy(done);
+        if (rc == KVX_OK) rc = fail(KVX_ERR_CUDA, "posting a transfer: %s", cudaGetErrorString(e));
+        // A launch that went out before the failure may still write the word: then it stays out of circulation
+        // (one word lost) rather than reach a later transfer.
+        if (g_launches.load() == launches_before) {
+            const std::string why = t_error;
+            (void)status_close(status);
+            t_error = why;
+        }
+        return rc;
     }
-    *out = reinterpret_cast<kvx_xfer_t>(x);
+    *out = reinterpret_cast<kvx_xfer_t>(new Xfer{done, device, status});
     return KVX_OK;
 }
 
@@ -1248,11 +1355,10 @@ int kvx_check_xfer(kvx_xfer_t xfer) {
     }
     if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "transfer failed: %s", cudaGetErrorString(e));
     // The event says the launch ended. A TMA copy that gave up a bounded wait ends too, with its bytes not all
-    // landed, and says so only in the device word: look there before reporting success.
-    int bits = 0;
-    if (int rc = read_device_errors(x->device, &bits)) return rc;
-    if (bits & kErrCopyWait)
-        return fail(KVX_ERR_DEVICE, "a copy on device %d gave up a bounded wait, so not every byte landed", x->device);
+    // landed, and says so only in the transfer's status word, which the completed event has made visible here.
+    if (status_bits(x->status) & kErrCopyWait)
+        return fail(KVX_ERR_DEVICE, "a copy of this transfer on device %d gave up a bounded wait, so not every byte "
+                    "landed", x->device);
     return KVX_OK;
 }
 
@@ -1260,6 +1366,9 @@ int kvx_release_xfer(kvx_xfer_t xfer) {
     if (!xfer) return KVX_OK;
     Xfer *x = reinterpret_cast<Xfer *>(xfer);
     const cudaError_t e = cudaEventDestroy(x->done);
+    // A transfer is released once it has completed, or once nothing will ask about it again after the device
+    // finished (the caller waits first): its word may then go to another transfer.
+    (void)status_close(x->status);
     delete x;
     if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "cudaEventDestroy: %s", cudaGetErrorString(e));
     return KVX_OK;
@@ -1368,12 +1477,13 @@ int kvx_mailbox_release(void *box, uint64_t seq) {
     return KVX_OK;
 }
 
-int kvx_wait_selftest(int limit_us, int code, void *stream) {
+int kvx_wait_selftest(int limit_us, int code, int32_t *status, void *stream) {
     if (limit_us < 1 || limit_us > 10000000) return fail(KVX_ERR_INVALID, "limit %d us: 1 us to 10 s", limit_us);
     if (code != kErrSelftest && code != kErrCopyWait)
         return fail(KVX_ERR_INVALID, "code %d: %d (the self-test's) or %d (a stuck copy's)", code, kErrSelftest,
                     kErrCopyWait);
-    kvx_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_us * 1000, code);
+    kvx_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_us * 1000, code,
+                                                                               status);
     KVX_CUDA(cudaGetLastError());
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return KVX_OK;
@@ -1381,9 +1491,40 @@ int kvx_wait_selftest(int limit_us, int code, void *stream) {
 
 int kvx_device_error(int *out_code) {
     if (!out_code) return fail(KVX_ERR_INVALID, "null pointer");
-    int zero = 0;
-    KVX_CUDA(cudaMemcpyFromSymbol(out_code, g_device_error, sizeof(int)));
-    KVX_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+    int device;
+    KVX_CUDA(cudaGetDevice(&device));
+    cudaStream_t s;
+    if (int rc = probe_stream(device, &s)) return rc;
+    int32_t *word;
+    if (int rc = status_open(&word)) return rc;
+    kvx_take_device_error_kernel<<<1, 32, 0, s>>>(word);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) {
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        *out_code = status_bits(word);
+    }
+    (void)status_close(word);  // the kernel has completed, or never ran
+    if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+    return KVX_OK;
+}
+
+int kvx_status_open(int32_t **out_word) {
+    if (!out_word) return fail(KVX_ERR_INVALID, "null pointer");
+    return status_open(out_word);
+}
+
+int kvx_status_close(int32_t *word) { return status_close(word); }
+
+int kvx_status_read(const int32_t *word, int32_t *out_bits) {
+    if (!word || !out_bits) return fail(KVX_ERR_INVALID, "null pointer");
+    *out_bits = status_bits(word);
+    return KVX_OK;
+}
+
+int kvx_xfer_status(kvx_xfer_t xfer, int32_t **out_word) {
+    if (!xfer || !out_word) return fail(KVX_ERR_INVALID, "null pointer");
+    *out_word = reinterpret_cast<Xfer *>(xfer)->status;
     return KVX_OK;
 }
 

@@ -63,6 +63,12 @@ def relay_parts(n_blocks: int, tp_size: int) -> list[tuple[int, int]]:
     return [(n_blocks * r // tp_size, n_blocks * (r + 1) // tp_size) for r in range(tp_size)]
 
 
+def _ids_fit(block_ids, num_blocks: int) -> bool:
+    """Every id names one of a cache's num_blocks blocks (no ids fit any cache)."""
+    ids = list(block_ids or ())
+    return not ids or (min(ids) >= 0 and max(ids) < num_blocks)
+
+
 def node_id() -> str:
     """Identifies this machine's boot: CUDA IPC mappings work only between processes of one node."""
     try:
@@ -253,6 +259,17 @@ class _Save:
     fused: bool | None = None  # decided at its first store_kv: its rows go to the decode ranks with every store
     stored: set = field(default_factory=set)  # layers whose new rows store_kv pushed
     mapped: bool = False  # its blocks are in its decode instance's block map
+    words: list = field(default_factory=list)  # _StoreWord of every fused store that wrote its rows
+
+
+@dataclass(slots=True)
+class _StoreWord:
+    """The status word of one fused store launch, shared by the saves whose rows it pushed. Read once a save's
+    last push or fence has completed (every store before it on the engine's stream has then completed too); closed
+    when the last of those saves is done with it."""
+
+    word: object
+    refs: int
 
 
 @dataclass(slots=True)
@@ -306,7 +323,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._server = None
         self._deferred: list = []  # messages that came while a handshake wait answered handshakes only
         self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
-        self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table) of _remotes; under the lock
+        self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table, blocks) of _remotes; locked
         self._retired: list[_Retired] = []  # replaced mappings not yet closed; both threads, under the lock
         self._loads: dict[str, _Load] = {}  # transfer thread only
         self._waits: dict[str, _Wait] = {}  # transfer thread only
@@ -317,7 +334,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
         self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
         self._thread: threading.Thread | None = None
-        self._errors_seen: set = set()  # (step, error type) the transfer thread has logged
+        self._errors_seen: dict = {}  # (step, error type) -> times the transfer thread hit it
 
     # -------------------------------------------------------------------------------------------- engine thread
 
@@ -360,6 +377,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 if old is not None:  # re-admitted after a preemption, in new blocks: start over
                     self._forget_fused(old)
                     self._saves.pop(request_id)
+                    for entry in old.words:  # a store that wrote it may still run: its word is left open
+                        entry.refs -= 1
                 if req.remote_block_ids is None:  # its decode ranks announce themselves under req.push_id
                     self._saves[request_id] = _Save(req, [])
                     self._push_ids[str(req.push_id)] = request_id
@@ -370,6 +389,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 # its own hook. First contact goes to the transfer thread, never blocking this one on the network.
                 mapped = [self._mapped.get(key) for key, _, _ in save.targets]
                 if all(m is not None and m[0] == req.remote_engine_id for m in mapped):
+                    if not all(_ids_fit(req.remote_block_ids, m[2]) for m in mapped):
+                        save.failed = True  # its decode ranks hear "not ok" at hand-over
+                        logger.warning("the decode blocks of %s lie past a decode rank's cache; not pushing them",
+                                       request_id)
+                        continue
                     save.tables = [m[1] for m in mapped]
                     save.ready = True
                     continue
@@ -540,21 +564,24 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         slot (the reference's store_kvcache, attention/triton_cache.py:58-81), and in the same pass into the decode
         ranks' blocks of every request being saved whose decode instance was mapped at its first store. An engine
         calls this in place of the backend's store; it then needs no save_kv_layer for those layers."""
-        targets = self._fused_targets(layer_index, latents=False)
+        targets, word = self._fused_targets(layer_index, latents=False)
         self.transport.store(self.kv_caches[layer_index], key, value, slot_mapping, targets,
-                             async_push=envs.LEAN_VLLM_KVX_FUSED_ASYNC)
+                             async_push=envs.LEAN_VLLM_KVX_FUSED_ASYNC, status=word)
 
     def store_latents(self, layer_index: int, latent, slot_mapping):
         """store_kv for an MLA layer's latents [tokens, 576] (attention/triton_cache.py:84-91); every decode rank
         takes a whole copy."""
-        targets = self._fused_targets(layer_index, latents=True)
+        targets, word = self._fused_targets(layer_index, latents=True)
         self.transport.store(self.kv_caches[layer_index], latent, None, slot_mapping, targets,
-                             async_push=envs.LEAN_VLLM_KVX_FUSED_ASYNC)
+                             async_push=envs.LEAN_VLLM_KVX_FUSED_ASYNC, status=word)
 
-    def _fused_targets(self, layer_index: int, latents: bool) -> list:
+    def _fused_targets(self, layer_index: int, latents: bool) -> tuple[list, object]:
+        """The peer destinations of this layer's store, and the status word the store reports into (None without
+        peers): every save whose rows the store writes holds the word until it finishes."""
         with self._lock:
             updates, self._map_updates = self._map_updates, []
             groups: dict[tuple, _Save] = {}
+            served: list[_Save] = []
             for save in self._saves.values():
                 if save.failed or save.handed_over:
                     continue
@@ -563,6 +590,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 if not save.fused:
                     continue
                 save.stored.add(layer_index)
+                served.append(save)
                 if not save.mapped:
                     updates.append((self._instance(save.req), list(save.req.local_block_ids),
                                     list(save.req.remote_block_ids)))
@@ -582,7 +610,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                         continue  # latents come whole from the first producer rank only
                     targets.append(self.transport.push_target(table, start, share, self._block_maps[instance],
                                                               self.block_size))
-        return targets
+        if not targets:
+            return targets, None
+        word = _StoreWord(self.transport.status_word(), len(served))
+        with self._lock:
+            for save in served:
+                save.words.append(word)
+        return targets, word.word
 
     def _save_flags(self):
         return getattr(self.transport, "save_flags", None)
@@ -654,9 +688,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             raise
         except Exception as error:  # noqa: BLE001
             kind = (getattr(step, "__name__", str(step)), type(error).__name__)  # bounded: no request ids
-            if kind not in self._errors_seen:
-                self._errors_seen.add(kind)
+            times = self._errors_seen[kind] = self._errors_seen.get(kind, 0) + 1
+            if times == 1:
                 logger.exception("the KV transfer thread hit an unexpected error in %s and carries on", kind[0])
+            elif times & (times - 1) == 0:  # 2, 4, 8, ...: a recurring error stays visible without flooding
+                logger.warning("the KV transfer thread has hit %s in %s %d times", kind[1], kind[0], times)
 
     def _close(self):
         released = set()
@@ -920,32 +956,53 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
     def _poll_loads(self, notes: dict):
         queried: set[int] = set()  # launches asked once this pass: the loads sharing one finish together
         for request_id, load in list(self._loads.items()):
-            if load.transfer is not None:
-                shared = load.transfer
-                if not shared.done and id(shared) not in queried:
-                    queried.add(id(shared))
-                    try:
-                        shared.done = self.transport.done(shared.xfer)
-                    except Exception as error:  # noqa: BLE001
-                        shared.done = True
-                        shared.error = shared.error or error
-                if not shared.done:
+            try:
+                if not self._landed(load, queried, notes):
                     continue
-                if shared.error is not None:
-                    self._fail(load, RuntimeError(f"a kvx copy failed in flight: {shared.error}"), in_flight=True)
-                shared.refs -= 1
-                if shared.refs == 0:
-                    self.transport.release(shared.xfer)
-                load.transfer = None
-                if not load.failed:
-                    for key, message, remote_rank in load.notify:
-                        notes.setdefault(key, []).append(message)
-                        load.unnotified.discard(remote_rank)
+            except Exception as error:  # noqa: BLE001 - one load's trouble is that load's, never the others'
+                if load.transfer is not None and not load.transfer.done:
+                    self._note_error("_poll_loads", error)  # its copy may still write the blocks: ask again
+                    continue
+                self._fail(load, RuntimeError(f"finishing the load failed: {error}"), in_flight=True)
             del self._loads[request_id]
             if load.relay is not None and not load.failed:
                 self._part_landed(request_id, load)
                 continue
             self._finish_load(request_id, load)
+
+    def _landed(self, load: _Load, queried: set, notes: dict) -> bool:
+        """Whether the load's launch has ended (asked once per pass per launch); once it has, the launch is let go
+        and, unless the copy failed, each producer rank's notification queued."""
+        if load.transfer is None:
+            return True
+        shared = load.transfer
+        if not shared.done and id(shared) not in queried:
+            queried.add(id(shared))
+            try:
+                shared.done = self.transport.done(shared.xfer)
+            except Exception as error:  # noqa: BLE001 - this launch's own failure (its status word, or CUDA)
+                shared.done = True
+                shared.error = shared.error or error
+        if not shared.done:
+            return False
+        if shared.error is not None:
+            self._fail(load, RuntimeError(f"a kvx copy failed in flight: {shared.error}"), in_flight=True)
+        load.transfer = None
+        shared.refs -= 1
+        if shared.refs == 0:
+            self.transport.release(shared.xfer)
+        if not load.failed:
+            for key, message, remote_rank in load.notify:
+                notes.setdefault(key, []).append(message)
+                load.unnotified.discard(remote_rank)
+        return True
+
+    def _note_error(self, where: str, error: Exception):
+        """Counts an unexpected error the thread recovered from, logging it as _guarded does."""
+        kind = (where, type(error).__name__)
+        times = self._errors_seen[kind] = self._errors_seen.get(kind, 0) + 1
+        if times == 1 or times & (times - 1) == 0:
+            logger.warning("the KV transfer thread hit %s in %s (%d times): %s", kind[1], where, times, error)
 
     def _finish_load(self, request_id: str, load: _Load):
         if load.relay is not None:
@@ -1098,9 +1155,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     logger.warning("the decode instance announced %d blocks for %s, which has %d here",
                                    len(remote_ids), request_id, len(local_ids))
         try:
-            tables = [self._handshake(save.req, decode_rank).table for _, decode_rank, _ in save.targets]
+            remotes = [self._handshake(save.req, decode_rank) for _, decode_rank, _ in save.targets]
+            if not all(_ids_fit(save.req.remote_block_ids, r.num_blocks) for r in remotes):
+                # Checked here, before any block map names them: a store would skip such rows on the device.
+                raise RuntimeError("a decode block id lies past the decode rank's cache")
             with self._lock:
-                save.tables = tables
+                save.tables = [r.table for r in remotes]
                 save.ready = not save.failed
         except Exception as error:  # noqa: BLE001
             logger.warning("cannot push the KV of %s to %s:%d, so the decode instance prefills it: %s",
@@ -1206,6 +1266,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             for request_id, save in done:
                 del self._saves[request_id]
                 self._forget_fused(save)
+                if self._settle_words(save):
+                    save.failed = True
+                    logger.warning("a fused store skipped rows of %s that lie past a decode rank's cache, so the "
+                                   "decode instance prefills it", request_id)
                 self._finished.finished_sending.add(request_id)  # every byte landed, or none will
             for request_id, save in stale:
                 # Never handed over (an aborted prefill), or handed over to a decode instance that never announced
@@ -1213,6 +1277,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 del self._saves[request_id]
                 self._forget_fused(save)
                 self._push_ids.pop(str(save.req.push_id), None)
+                self._settle_words(save)  # idle past the abort timeout: its stores have long completed
                 save.failed = True
                 if save.handed_over:
                     self._finished.finished_sending.add(request_id)
@@ -1224,6 +1289,19 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             tag = save.req.push_id or request_id
             for key, _, _ in save.targets:
                 self._send(key, {"op": "saved", "request": tag, "rank": self.rank, "ok": not save.failed})
+
+    @staticmethod
+    def _settle_words(save: _Save) -> bool:
+        """Lock held, once every store that wrote the save's rows has completed: whether one of them skipped a row
+        (its status word is set). The save lets go of each word; the last save to do so closes it."""
+        skipped = False
+        for entry in save.words:
+            skipped |= entry.word.bits() != 0
+            entry.refs -= 1
+            if entry.refs == 0:
+                entry.word.close()
+        save.words = []
+        return skipped
 
     # Push, decode side: wait for every producer rank holding this rank's heads.
 
@@ -1324,7 +1402,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             remote = _Remote(reply["engine_id"], reply["tp_size"], reply["num_blocks"], reply["exported"], table, sock)
             self._remotes[key] = remote
             with self._lock:
-                self._mapped[key] = (remote.engine_id, remote.table)
+                self._mapped[key] = (remote.engine_id, remote.table, remote.num_blocks)
             keep = True
             return remote
         finally:

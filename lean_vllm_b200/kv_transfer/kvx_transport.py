@@ -142,21 +142,28 @@ class KvxTransport:
                                      num_heads=share.num_heads if k_region[2] else 1,
                                      dst_first_head=share.local_head if k_region[2] else 0, block_map=block_map)
 
+    def status_word(self) -> transport.StatusWord:
+        """A status word for a store whose rows also go to peers (kvx_status_open)."""
+        return transport.StatusWord()
+
     def store(self, cache: torch.Tensor, key: torch.Tensor, value, slot_mapping: torch.Tensor, targets: list,
-              async_push: bool = False):
-        """The layer's store into `cache` (HND keys/values, or latents when value is None) and every target. With
-        `async_push`, one launch on the engine's stream writes the local cache (what attention waits for) and a
-        second on the save stream, after it and held to the save SM budget, writes the targets from the same rows
-        (KVX_STORE_PEERS_ONLY): the NVLink writes leave the prefill's critical path."""
+              async_push: bool = False, status: transport.StatusWord | None = None):
+        """The layer's store into `cache` (HND keys/values, or latents when value is None) and every target;
+        `status` gets bit 2 if a row was skipped because its slot lies past a cache. With `async_push`, one launch
+        on the engine's stream writes the local cache (what attention waits for) and a second on the save stream,
+        after it and held to the save SM budget, writes the targets from the same rows (KVX_STORE_PEERS_ONLY): the
+        NVLink writes leave the prefill's critical path."""
         from lean_vllm_b200.attention.kvx_cache import store_kvcache, store_latents
+
+        word = status.address if status is not None else 0
 
         def launch(push_to, stream=None, flags=0):
             if value is None:
-                store_latents(key, cache[0], slot_mapping, push_to=push_to, stream=stream, flags=flags)
+                store_latents(key, cache[0], slot_mapping, push_to=push_to, stream=stream, flags=flags, status=word)
             else:
                 view = cache.transpose(2, 3)  # (2, blocks, tokens, heads, dim), as the attention backend sees it
                 store_kvcache(key, value, view[0], view[1], slot_mapping, push_to=push_to, stream=stream,
-                              flags=flags)
+                              flags=flags, status=word)
 
         if not targets or not async_push:
             launch(targets)

@@ -133,15 +133,42 @@ def job_bytes(caches: list[CacheTable], jobs: list[CopyJob]) -> int:
     return out.value
 
 
+class StatusWord:
+    """A status word (kvx_status_open): 4 bytes of pinned host memory every device writes directly. A launch given
+    one sets error bits there only if it fails without faulting; read it once the launch's event has completed."""
+
+    def __init__(self):
+        out = ctypes.c_void_p()
+        check(lib().kvx_status_open(ctypes.byref(out)))
+        self.address = out.value
+
+    def bits(self) -> int:
+        out = ctypes.c_int32()
+        check(lib().kvx_status_read(self.address, ctypes.byref(out)))
+        return out.value
+
+    def close(self):
+        """After every launch given the word has completed."""
+        if self.address:
+            check(lib().kvx_status_close(self.address))
+            self.address = 0
+
+
 class Transfer:
-    """A posted copy and the event after it (a NIXL xfer handle)."""
+    """A posted copy and the event after it (a NIXL xfer handle), with a status word of its own."""
 
     def __init__(self, handle: int):
         self._handle = ctypes.c_void_p(handle)
 
     def done(self) -> bool:
-        """True once every byte has landed; raises if the transfer failed."""
+        """True once every byte has landed; raises KvxDeviceError if one of this transfer's copies gave up."""
         return check(lib().kvx_check_xfer(self._handle)) == _native.KVX_OK
+
+    def status_address(self) -> int:
+        """The device-visible address of this transfer's status word (for kvx_wait_selftest in tests)."""
+        out = ctypes.c_void_p()
+        check(lib().kvx_xfer_status(self._handle, ctypes.byref(out)))
+        return out.value
 
     def release(self):
         if self._handle:
@@ -231,13 +258,15 @@ def launch_count() -> int:
     return int(lib().kvx_launch_count())
 
 
-def wait_selftest(limit_us: int, code: int = 4, stream: int = 0) -> None:
+def wait_selftest(limit_us: int, code: int = 4, stream: int = 0, status: int = 0) -> None:
     """Launches the bounded-wait self-test (kvx_wait_selftest): after limit_us the device word has bit `code` set
-    (4, the self-test's own; 1 stands in for a stuck copy, which fails the device's transfers until it is read)."""
-    check(lib().kvx_wait_selftest(limit_us, code, stream or None))
+    (4, the self-test's own; 1 stands in for a stuck copy), and so has the status word at `status` when given -- a
+    transfer's own (Transfer.status_address), whose check then fails as if one of its copies had given up."""
+    check(lib().kvx_wait_selftest(limit_us, code, status or None, stream or None))
 
 
 def device_error() -> int:
+    """Reads and clears, atomically on the device, the current device's diagnostic error word."""
     out = ctypes.c_int()
     check(lib().kvx_device_error(ctypes.byref(out)))
     return out.value

@@ -127,6 +127,25 @@ def read_rows(local: np.ndarray, remote: np.ndarray) -> int:
     return moved
 
 
+def place_rows(region_array: np.ndarray, block_ids, rows: np.ndarray, first_head: int, num_heads: int,
+               latents: bool) -> int:
+    """The scatter half of a staged transfer: contiguous staging rows, in block_descs order, written into one
+    region's blocks. Row i of `rows` lands where block_descs([region], block_ids, first_head, num_heads, latents)
+    row i points (nixl_connector.py:89-108), i.e. a READ whose remote side is the staging buffer. `region_array` is
+    one K, V or latent tensor of a layer: (blocks, heads, tokens, dim) or (blocks, tokens, dim). Returns the bytes
+    placed."""
+    head_bytes = region_array.strides[1] if region_array.ndim == 4 else 0
+    region = Region(region_array.ctypes.data, region_array.strides[0], head_bytes)
+    local = block_descs([region], block_ids, first_head, num_heads, latents)
+    rows = np.ascontiguousarray(rows)
+    if len(local) == 0:
+        return 0
+    length = int(local[0, 1])
+    assert rows.nbytes == length * len(local), "staging rows and block_descs rows differ in size"
+    remote = np.asarray([(rows.ctypes.data + i * length, length, 0) for i in range(len(local))], dtype=np.uint64)
+    return read_rows(local, remote)
+
+
 @dataclass
 class PlannedRead:
     """One READ the consumer rank posts: rows on both sides plus the notification the producer rank counts."""

@@ -12,6 +12,22 @@ import ctypes
 from itertools import count
 
 
+class HostStatusWord:
+    """A status word in plain memory: bit 2 once a host store skipped a row."""
+
+    opened = 0
+
+    def __init__(self):
+        self.value = 0
+        HostStatusWord.opened += 1
+
+    def bits(self) -> int:
+        return self.value
+
+    def close(self):
+        HostStatusWord.opened -= 1
+
+
 class HostTransport:
     fail: str | None = None  # "posted" or "in flight"
     instances: list["HostTransport"] = []
@@ -127,7 +143,12 @@ class HostTransport:
         heads = (share.remote_head, share.num_heads, share.local_head) if k[2] else (0, 1, 0)
         return {"k": k, "v": v, "heads": heads, "block_map": block_map, "block_size": block_size, "table": table}
 
-    def store(self, cache, key, value, slot_mapping, targets, async_push=False):
+    def status_word(self):
+        return HostStatusWord()
+
+    def store(self, cache, key, value, slot_mapping, targets, async_push=False, status=None):
+        """kvx_store's byte map; a row whose mapped block lies past a target's cache is skipped and reported in
+        `status` (bit 2), as the kernel does."""
         self.stores.append((len(targets), key.shape[0]))
         latents = value is None
         block = cache.size(2) if latents else cache.size(3)
@@ -148,6 +169,10 @@ class HostTransport:
                         first, count, dst_first = target["heads"]
                         mapped = int(target["block_map"][b])
                         if mapped < 0 or not first <= h < first + count:
+                            continue
+                        if mapped >= target["table"]["num_blocks"]:
+                            if status is not None:
+                                status.value = 2
                             continue
                         addr, block_bytes, head_bytes = target["k"] if part == 0 else target["v"]
                         dst = addr + mapped * block_bytes + (h - first + dst_first) * head_bytes + off * row

@@ -28,7 +28,7 @@ def test_the_library_loads_and_exports_every_declared_symbol():
     lib = _native.lib()
     for name in declared():
         assert getattr(lib, name) is not None
-    assert lib.kvx_abi_version() == 1
+    assert lib.kvx_abi_version() == _native.ABI_VERSION == 2
     assert lib.kvx_last_error() == b""
 
 
@@ -70,7 +70,25 @@ def test_ipc_handle_round_trips_as_bytes():
     h.offset, h.device, h.pid, h.ptr = 4096, 3, 77, 1 << 40
     back = _native.IpcHandle.from_bytes(h.to_bytes())
     assert (back.offset, back.device, back.pid, back.ptr) == (4096, 3, 77, 1 << 40)
-    assert ctypes.sizeof(h) == 64 + 8 + 8 + 4 + 4 + 8
+    assert ctypes.sizeof(h) == 64 + 8 + 8 + 4 + 4 + 8 + 16
+
+
+def test_a_handle_with_this_pid_but_another_process_s_nonce_is_not_taken_for_local_memory():
+    """Prefill and decode in separate containers can share a pid (each namespace has its own 1, 2, ...): a handle
+    is used as a pointer of this process only when its pid AND its 16-byte process nonce both match. With the nonce
+    wrong, kvx_ipc_open goes the IPC way -- which, with no device here, fails loudly instead of returning the
+    other process's raw address -- and kvx_ipc_close finds no mapping to drop."""
+    if not os.path.exists(_native.LIB_PATH):
+        pytest.skip("libkvx.so is not built here")
+    lib = _native.lib()
+    h = _native.IpcHandle()
+    h.pid, h.ptr, h.device = os.getpid(), 0xDEAD0000, 0
+    for i in range(16):
+        h.nonce[i] = i + 1  # not this process's nonce
+    out = ctypes.c_void_p()
+    rc = lib.kvx_ipc_open(ctypes.byref(h), ctypes.byref(out))
+    assert rc < 0 and out.value != 0xDEAD0000
+    assert lib.kvx_ipc_close(ctypes.byref(h)) < 0
 
 
 def test_a_doorbell_opens_and_closes_without_a_device():
@@ -100,10 +118,10 @@ def test_the_wait_selftest_checks_its_limit_before_launching():
         pytest.skip("libkvx.so is not built here")
     for bad in (0, -5, 10_000_001):
         with pytest.raises(_native.KvxError, match="limit"):
-            _native.check(_native.lib().kvx_wait_selftest(bad, 4, None))
+            _native.check(_native.lib().kvx_wait_selftest(bad, 4, None, None))
     for bad in (0, 2, 3, 8):
         with pytest.raises(_native.KvxError, match="the self-test's"):
-            _native.check(_native.lib().kvx_wait_selftest(1000, bad, None))
+            _native.check(_native.lib().kvx_wait_selftest(1000, bad, None, None))
 
 
 C_CLIENT = r"""

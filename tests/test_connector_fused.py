@@ -12,7 +12,7 @@ from lean_vllm_b200.kv_transfer.base import ReqToSave
 from oracle.kv_oracle import store_kvcache as oracle_store
 from tests.connector_cases import BLOCK, HEAD_DIM, LATENT_DIM, NUM_HEADS, Sides, full_cache, rank_cache, wait_for
 from tests.helpers import bits, full_of
-from tests.host_transport import HostTransport
+from tests.host_transport import HostStatusWord, HostTransport
 from tests.push_cases import wait_ready
 
 LOCAL, REMOTE = [7, 2, 9], [0, 5, 3]  # the prefill's blocks and the decode instance's
@@ -213,3 +213,49 @@ def test_a_fully_fused_save_is_reported_only_after_its_stores_land(sides):
     transport.pending[held[0]] = [0]  # landed
     assert wait_for(producers[0]).finished_sending == {"p-1"}
     assert wait_for(consumers[0]).finished_recving == {"d-1"}
+
+
+def test_decode_blocks_past_the_decode_cache_fail_the_save_before_any_store(sides):
+    """A decode instance that names blocks its cache does not have: the prefill rank refuses the save when it maps
+    the decode ranks (before any block map names those ids), stores only locally, and the decode instance hears
+    "not ok" at hand-over and prefills."""
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    kv_d, kv_p = consumers[0].kv_transfer, producers[0].kv_transfer
+    num_blocks = consumers[0].kv_caches[0].size(1)
+    bad = [0, num_blocks, 3]
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": ReqToRecv(
+        bad, list(LOCAL), "p-1", kv_p.engine_id, kv_p.kv_ip, kv_p.kv_port, 1, pushed=True)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={
+        "p-1": ReqToSave(list(LOCAL), bad, kv_d.engine_id, kv_d.kv_ip, kv_d.kv_port, 1)}))
+    assert wait_ready(producers[0]) is False
+    producers[0].store_kv(0, *rows(13, 3 * BLOCK, NUM_HEADS, False), slots_of(LOCAL))
+    assert producers[0].transport.stores[-1] == (0, 3 * BLOCK)  # local only
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(LOCAL)}))
+    assert wait_for(producers[0]).finished_sending == {"p-1"}
+    assert wait_for(consumers[0]).failed_recving == {"d-1"}
+
+
+def test_a_fused_store_that_skipped_rows_fails_its_save(sides, monkeypatch):
+    """The device-side check behind the host's: if a store skips a row because its decode block lies past the
+    decode rank's cache (its status word set), the save fails before the decode instance is told its blocks are
+    full. The host's range check is bypassed here so that the store itself meets the bad id."""
+    monkeypatch.setattr(cuda_ipc_connector, "_ids_fit", lambda ids, num_blocks: True)
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode", accept_push=True)
+    kv_d, kv_p = consumers[0].kv_transfer, producers[0].kv_transfer
+    num_blocks = consumers[0].kv_caches[0].size(1)
+    bad = [0, num_blocks, 3]
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": ReqToRecv(
+        bad, list(LOCAL), "p-1", kv_p.engine_id, kv_p.kv_ip, kv_p.kv_port, 1, pushed=True)}))
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_save={
+        "p-1": ReqToSave(list(LOCAL), bad, kv_d.engine_id, kv_d.kv_ip, kv_d.kv_port, 1)}))
+    assert wait_ready(producers[0])
+    opened = HostStatusWord.opened
+    producers[0].store_kv(0, *rows(14, 3 * BLOCK, NUM_HEADS, False), slots_of(LOCAL))
+    assert producers[0].transport.stores[-1] == (1, 3 * BLOCK)  # fused, one decode rank
+    assert HostStatusWord.opened == opened + 1
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(LOCAL)}))
+    assert wait_for(producers[0]).finished_sending == {"p-1"}
+    assert wait_for(consumers[0]).failed_recving == {"d-1"}
+    assert HostStatusWord.opened == opened  # the save let go of its store's word

@@ -91,6 +91,50 @@ def test_the_load_waits_on_the_gpu_for_the_step_that_still_writes_its_blocks(sid
     assert torch.equal(cache[:, 0].cpu(), prefill[:, 4])
 
 
+def test_a_copy_that_gave_up_fails_its_load_alone_and_the_next_load_lands(sides, golden):
+    """The first load's launch is made to look stuck: the bounded-wait self-test writes "gave up" (1) into that
+    launch's own status word, as a copy whose bytes did not all land would. That load fails (the engine prefills
+    it) and the producer's blocks expire rather than be freed under a possible late write; the next load on the
+    same device, posted after it with nothing cleared in between, lands bit for bit."""
+    from lean_vllm_b200.kv_transfer import transport
+
+    _, arrays = golden
+    producers = sides.make("kv_producer", 1, full_cache(0, False))
+    consumers = sides.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+    kvx = consumers[0].transport
+    real_post, real_done, stuck, flagged = kvx.post, kvx.done, [], []
+
+    def post(tables, jobs, ready, **kw):
+        xfer = real_post(tables, jobs, ready, **kw)
+        if not stuck:
+            stuck.append(xfer)
+        return xfer
+
+    def done(xfer):
+        # Before the host first reads the first launch's word, the self-test writes "gave up" into it (on a stream
+        # of its own, waited for here), standing in for that launch's copy.
+        if stuck and xfer is stuck[0] and not flagged:
+            side = torch.cuda.Stream()
+            transport.wait_selftest(2_000, code=1, stream=side.cuda_stream, status=xfer.status_address())
+            side.synchronize()
+            flagged.append(True)
+        return real_done(xfer)
+
+    kvx.post, kvx.done = post, done
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": [7, 2, 9]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, [0, 5, 3], [7, 2, 9])}))
+    assert wait_for(consumers[0]) == KVConnectorOutput(failed_recving={"d-1"})
+    assert producers[0].get_finished().finished_sending == set()  # no reader notified: expiry frees them
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-2": [7, 2, 9]}))
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={
+        "d-2": recv(producers, [0, 5, 3], [7, 2, 9], remote_request_id="p-2")}))
+    out = wait_for(consumers[0])
+    assert out.finished_recving == {"d-2"} and not out.failed_recving
+    assert np.array_equal(bits(consumers[0].kv_caches[0].cpu()), arrays["small_kv_tp1to1"])
+    assert wait_for(producers[0]).finished_sending == {"p-2"}
+    transport.device_error()  # the diagnostic word saw the stand-in; leave it clear for the tests after this one
+
+
 def _producer(conn, device: int, kv_port: int, tp_size: int, rank: int, mla: bool):
     torch.cuda.set_device(device)
     kv = KVTransferConfig(kv_connector="CudaIpcConnector", kv_role="kv_producer", kv_port=kv_port,

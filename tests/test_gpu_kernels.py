@@ -178,16 +178,19 @@ def test_empty_jobs_launch_nothing():
 
 
 @pytest.mark.parametrize("engine", list(ENGINES))
-def test_pack_push_scatter_equals_the_direct_copy(engine):
-    """Gather into a staging buffer, push it to a second buffer, scatter: the same bytes as one direct copy, and the
-    staging buffer holds the rows in block_descs order."""
+def test_pack_push_scatter_lands_what_torch_indexing_of_the_source_says(engine):
+    """Gather into a staging buffer, push it to a second buffer, scatter into the destination's blocks. The staging
+    buffer must hold the rows in block_descs order and the destination must equal torch indexing of the source
+    (`dst[:, d_ids, 2:4] = src[:, s_ids, 1:3]`, the reference tests' closed form): no kvx kernel computes what is
+    expected. Untouched blocks and heads keep their values."""
     f = ENGINES[engine]
     src = _qwen_like(24, 2, heads=4, seed=3)
     dst = _qwen_like(24, 2, heads=4, seed=4)
-    direct = [d.clone() for d in dst]
     s_ids, d_ids = [5, 17, 2, 9], [0, 23, 11, 6]
-    src_t, dst_t, direct_t = (CacheTable.from_tensors(x) for x in (src, dst, direct))
-    transport.copy([src_t, direct_t], [CopyJob(0, 1, s_ids, d_ids, 1, 2, 2)], 0, f)
+    expected = [d.clone() for d in dst]
+    for e, s in zip(expected, src):
+        e[:, d_ids, 2:4] = s[:, s_ids, 1:3]
+    src_t, dst_t = CacheTable.from_tensors(src), CacheTable.from_tensors(dst)
     chunk = 2 * 256 * 128 * 2
     staging = torch.empty(4 * len(s_ids) * chunk, dtype=torch.uint8, device="cuda")
     landing = torch.empty_like(staging)
@@ -196,11 +199,41 @@ def test_pack_push_scatter_equals_the_direct_copy(engine):
     transport.scatter(landing.data_ptr(), landing.numel(), dst_t, d_ids, 2, 2, False, 0, f)
     torch.cuda.synchronize()
     for layer in range(2):
-        assert torch.equal(dst[layer], direct[layer])
+        assert torch.equal(dst[layer], expected[layer])
     rows = landing.view(torch.bfloat16).view(4, len(s_ids), 2, 256, 128)  # (region, block, head, token, dim)
     for r in range(4):
         layer, part = divmod(r, 2)
         assert torch.equal(rows[r], src[layer][part][s_ids, 1:3])
+
+
+@pytest.mark.parametrize("latents", [False, True], ids=["kv", "latent"])
+def test_scatter_alone_matches_the_oracle_s_placement(latents):
+    """kvx_scatter from a staging buffer filled by torch (not by kvx_pack) in block_descs row order, against the
+    oracle's placement on host copies: the scatter is pinned by itself, not through another kvx kernel."""
+    import oracle.kv_oracle as oracle
+
+    g = torch.Generator().manual_seed(11)
+    if latents:
+        dst = [torch.randn(1, 20, 64, 576, generator=g).to(torch.bfloat16) for _ in range(3)]
+        first, count = 0, 0
+    else:
+        dst = [torch.randn(2, 20, 4, 32, 64, generator=g).to(torch.bfloat16) for _ in range(3)]
+        first, count = 1, 2
+    ids = [19, 0, 7, 3, 12]
+    regions = [part for layer in dst for part in layer]
+    chunk_shape = regions[0][0].shape if latents else regions[0][0, first : first + count].shape
+    rows = torch.randn(len(regions), len(ids), *chunk_shape, generator=g).to(torch.bfloat16)
+    expected = [bits(d).copy() for d in dst]
+    for r, region_rows in enumerate(rows):
+        layer, part = divmod(r, len(dst[0]))
+        oracle.place_rows(expected[layer][part], ids, bits(region_rows), first, count, latents)
+    on_gpu = [d.cuda() for d in dst]
+    staging = rows.cuda().contiguous()
+    transport.scatter(staging.data_ptr(), staging.numel() * 2, CacheTable.from_tensors(on_gpu), ids, first, count,
+                      latents)
+    torch.cuda.synchronize()
+    for got, want in zip(on_gpu, expected):
+        assert np.array_equal(bits(got), want)
 
 
 def test_a_staging_buffer_too_small_is_refused():
@@ -286,25 +319,45 @@ def test_a_bounded_wait_that_runs_out_reports_and_leaves_the_context_usable():
     assert torch.equal(dst[0][:, [0, 3]], src[0][:, [1, 2]])
 
 
-def test_a_copy_that_gave_up_fails_the_transfers_that_end_after_it_until_the_word_is_read():
-    """A TMA copy whose bounded wait ran out ends with its bytes not all landed, and only the device word says so.
-    The self-test sets that bit (1) without copying anything: the next transfer's check must fail rather than
-    report the load landed, and once the word is read and cleared a transfer succeeds again."""
+def test_a_copy_that_gave_up_fails_its_own_transfer_and_no_other():
+    """A TMA copy whose bounded wait ran out ends with its bytes not all landed, and only its status word says so.
+    The self-test writes that bit (1) into transfer B's word without copying anything: B's check fails, while A
+    (posted before, on the same device and stream) and C (posted after) report their bytes landed -- with no call
+    that clears anything in between. The device's diagnostic word saw the bit too, and reading it changes no
+    transfer's result."""
     src = _qwen_like(4, 1, seed=9)
-    dst = [torch.zeros_like(s) for s in src]
-    caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
-    jobs = [CopyJob(0, 1, [1, 2], [0, 3], 0, 0, 8)]
+    dsts = [[torch.zeros_like(s) for s in src] for _ in range(3)]
     stream = torch.cuda.current_stream().cuda_stream
     assert transport.device_error() == 0
-    transport.wait_selftest(20_000, code=1, stream=stream)  # 20 ms
-    xfer = transport.transfer(caches, jobs, stream)
+    xfers = []
+    for k, dst in enumerate(dsts):
+        xfers.append(transport.transfer([CacheTable.from_tensors(src), CacheTable.from_tensors(dst)],
+                                        [CopyJob(0, 1, [1, 2], [0, 3], 0, 0, 8)], stream))
+        if k == 1:
+            transport.wait_selftest(20_000, code=1, stream=stream, status=xfers[1].status_address())  # 20 ms
     torch.cuda.synchronize()
+    assert xfers[0].done()
     with pytest.raises(KvxDeviceError, match="gave up a bounded wait"):
-        xfer.done()
-    xfer.release()
+        xfers[1].done()
+    assert xfers[2].done()
     assert transport.device_error() == 1
-    xfer = transport.transfer(caches, jobs, stream)
+    assert xfers[2].done() and xfers[0].done()  # judged by their own words, before and after the read
+    for xfer in xfers:
+        xfer.release()
+    for dst in dsts:
+        assert torch.equal(dst[0][:, [0, 3]], src[0][:, [1, 2]])
+
+
+def test_status_words_start_clear_and_come_back_clear():
+    """A word handed out again after a failure starts at zero: a new transfer never inherits an old one's bits."""
+    word = transport.StatusWord()
+    stream = torch.cuda.current_stream().cuda_stream
+    transport.wait_selftest(1_000, code=1, stream=stream, status=word.address)
     torch.cuda.synchronize()
-    assert xfer.done()
-    xfer.release()
-    assert torch.equal(dst[0][:, [0, 3]], src[0][:, [1, 2]])
+    assert word.bits() == 1
+    assert transport.device_error() == 1
+    word.close()
+    words = [transport.StatusWord() for _ in range(64)]  # the pool hands the freed word out again, zeroed
+    assert all(w.bits() == 0 for w in words)
+    for w in words:
+        w.close()

@@ -62,29 +62,36 @@ def test_a_model_sized_store_matches_the_oracle(hnd):
 
 def test_the_fused_store_also_writes_each_peer_s_heads_into_its_own_slots():
     """TP1 prefill -> TP2 decode: the store writes all 8 heads locally and heads 0-3 / 4-7 into two 4-head decode
-    caches at their own (shuffled) slots, in the same launch."""
+    caches at their own (shuffled) slots, in the same launch. Every expected cache comes from the oracle's store
+    (the reference's torch store, restated) on host copies: no kvx kernel computes what is expected."""
     key, value, cache, slots = _qwen_step(tokens=2000)
     peers = [torch.zeros(2, 30, 4, 256, 128, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
     peer_slots = [torch.randperm(30 * 256, device="cuda")[:2000] for _ in range(2)]
     peer_slots[1][5] = -1
     targets = [PushTarget.of(p.transpose(2, 3)[0], p.transpose(2, 3)[1], s, src_first_head=4 * r, num_heads=4)
                for r, (p, s) in enumerate(zip(peers, peer_slots))]
-    expected_local = cache.clone()
-    view = expected_local.transpose(2, 3)
-    expected_peers = [p.clone() for p in peers]
-    store_kvcache(key, value, view[0], view[1], slots)  # the local store alone, as reference
-    for r, (p, s) in enumerate(zip(expected_peers, peer_slots)):
-        pv = p.transpose(2, 3)
-        store_kvcache(key[:, 4 * r : 4 * r + 4].contiguous(), value[:, 4 * r : 4 * r + 4].contiguous(), pv[0], pv[1],
-                      s)
+    k_bits, v_bits = bits(key), bits(value)
+    expected_local = bits(cache).copy()
+    ev = expected_local.swapaxes(2, 3)  # (2, blocks, tokens, heads, dim), as the store addresses an HND cache
+    oracle_store(k_bits, v_bits, ev[0], ev[1], slots.cpu().numpy())
+    expected_peers = []
+    for r, (p, s) in enumerate(zip(peers, peer_slots)):
+        e = bits(p).copy()
+        pv = e.swapaxes(2, 3)
+        oracle_store(np.ascontiguousarray(k_bits[:, 4 * r : 4 * r + 4]), np.ascontiguousarray(v_bits[:, 4 * r : 4 * r + 4]),
+                     pv[0], pv[1], s.cpu().numpy())
+        expected_peers.append(e)
     before = transport.launch_count()
+    word = transport.StatusWord()
     view = cache.transpose(2, 3)
-    store_kvcache(key, value, view[0], view[1], slots, push_to=targets)
+    store_kvcache(key, value, view[0], view[1], slots, push_to=targets, status=word.address)
     torch.cuda.synchronize()
     assert transport.launch_count() - before == 1
-    assert torch.equal(cache, expected_local)
+    assert word.bits() == 0
+    word.close()
+    assert np.array_equal(bits(cache), expected_local)
     for p, e in zip(peers, expected_peers):
-        assert torch.equal(p, e)
+        assert np.array_equal(bits(p), e)
 
 
 def test_the_fused_latent_store_replicates_to_every_decode_rank():
@@ -101,22 +108,52 @@ def test_the_fused_latent_store_replicates_to_every_decode_rank():
         assert torch.equal(p[0].reshape(-1, 576)[s.long()], latent)
 
 
-def test_a_slot_past_the_cache_is_skipped_and_flagged():
+def test_a_slot_past_the_cache_is_skipped_and_flagged_in_the_launch_s_status_word():
     key, value, cache, slots = _qwen_step(tokens=64, blocks=4)
     slots[10] = 4 * 256  # one past the last slot
-    before = cache.clone()
+    expected = bits(cache).copy()
+    keep = slots.cpu().numpy().copy()
+    keep[10] = -1  # the row the kernel must skip
+    ev = expected.swapaxes(2, 3)
+    oracle_store(bits(key), bits(value), ev[0], ev[1], keep)
     assert transport.device_error() == 0
+    word = transport.StatusWord()
     view = cache.transpose(2, 3)
-    store_kvcache(key, value, view[0], view[1], slots)
+    store_kvcache(key, value, view[0], view[1], slots, status=word.address)
     torch.cuda.synchronize()
+    assert word.bits() == 2
+    word.close()
     assert transport.device_error() == 2
     assert transport.device_error() == 0  # read and cleared
-    keep = slots.clone()
-    keep[10] = -1
-    e_view = before.transpose(2, 3)
-    store_kvcache(key, value, e_view[0], e_view[1], keep)
+    assert np.array_equal(bits(cache), expected)
+
+
+def test_a_peer_block_map_entry_past_the_peer_cache_is_flagged_not_written():
+    """A fused push whose block map sends a row to a block past the decode rank's cache skips that row and says so
+    in the store's status word -- what fails the save before the decode instance is told its blocks are full."""
+    key, value, cache, slots = _qwen_step(tokens=300, blocks=8)
+    peer = torch.zeros(2, 4, 8, 256, 128, device="cuda", dtype=torch.bfloat16)
+    block_map = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+    block_map[:] = torch.tensor([0, 1, 2, 3, 9, -1, -1, -1], dtype=torch.int32)  # block 4 -> 9: past 4 blocks
+    target = PushTarget.of(peer.transpose(2, 3)[0], peer.transpose(2, 3)[1], None, block_map=block_map)
+    word = transport.StatusWord()
+    view = cache.transpose(2, 3)
+    store_kvcache(key, value, view[0], view[1], slots, push_to=[target], status=word.address)
     torch.cuda.synchronize()
-    assert torch.equal(cache, before)
+    hit = bool(((slots >= 4 * 256) & (slots < 5 * 256)).any())
+    assert word.bits() == (2 if hit else 0)
+    word.close()
+    transport.device_error()
+    expected = np.zeros(bits(peer).shape, dtype=np.uint16)
+    s = slots.cpu().numpy()
+    mapped = np.full_like(s, -1)
+    table = block_map.cpu().numpy()
+    for t, slot in enumerate(s.tolist()):
+        if slot >= 0 and table[slot // 256] >= 0 and table[slot // 256] < 4:
+            mapped[t] = table[slot // 256] * 256 + slot % 256
+    ev = expected.swapaxes(2, 3)
+    oracle_store(bits(key), bits(value), ev[0], ev[1], mapped)
+    assert np.array_equal(bits(peer), expected)
 
 
 def test_bad_arguments_raise_before_a_launch():
@@ -220,11 +257,11 @@ def test_a_peers_only_store_writes_the_peers_and_not_the_local_cache():
     store_kvcache(key, value, view[0], view[1], slots, push_to=[target], flags=STORE_PEERS_ONLY)
     torch.cuda.synchronize()
     assert torch.equal(cache, before)
-    # The same rows stored straight into a copy of the peer at the mapped slots (a plain store: verified above
-    # against the reference's torch store).
-    expected = torch.zeros_like(peer)
-    ev = expected.transpose(2, 3)
-    mapped = torch.where(slots >= 0, block_map[slots.clamp(min=0) // 256].long() * 256 + slots % 256, -1)
-    store_kvcache(key, value, ev[0], ev[1], mapped)
-    torch.cuda.synchronize()
-    assert torch.equal(peer, expected)
+    # The oracle's store of the same rows into a host copy of the peer at the mapped slots.
+    expected = np.zeros(bits(peer).shape, dtype=np.uint16)
+    ev = expected.swapaxes(2, 3)
+    table = block_map.cpu().numpy()
+    s = slots.cpu().numpy()
+    mapped = np.where(s >= 0, table[np.clip(s, 0, None) // 256].astype(np.int64) * 256 + s % 256, -1)
+    oracle_store(bits(key), bits(value), ev[0], ev[1], mapped)
+    assert np.array_equal(bits(peer), expected)

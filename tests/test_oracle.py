@@ -122,3 +122,25 @@ def test_a_planted_offset_error_is_caught(golden):
 def test_bf16_bits_round_trip():
     t = seeded((3, 5), 7)
     assert torch.equal(torch.from_numpy(bits(t).view(np.int16)).view(torch.bfloat16), t)
+
+
+@pytest.mark.parametrize("latents", [False, True], ids=["kv", "latent"])
+def test_place_rows_is_the_closed_form_of_a_scatter(latents):
+    """The oracle's staged scatter writes row i of the staging buffer into block ids[i] (heads first..first+n), the
+    same result as numpy indexing -- the reference tests' closed form -- so it can judge kvx_scatter alone."""
+    from oracle.kv_oracle import place_rows
+
+    rng = np.random.default_rng(5)
+    shape = (12, 16, 576) if latents else (12, 4, 16, 8)
+    region = rng.integers(0, 1 << 16, size=shape, dtype=np.uint16)
+    ids = [11, 0, 5, 7]
+    first, n = (0, 0) if latents else (1, 2)
+    rows = rng.integers(0, 1 << 16, size=(len(ids), *(shape[1:] if latents else (n, *shape[2:]))), dtype=np.uint16)
+    want = region.copy()
+    if latents:
+        want[ids] = rows
+    else:
+        want[ids, first : first + n] = rows
+    moved = place_rows(region, ids, rows, first, n, latents)
+    assert moved == rows.nbytes
+    assert np.array_equal(region, want)
