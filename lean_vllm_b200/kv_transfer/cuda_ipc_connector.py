@@ -40,6 +40,7 @@ from lean_vllm_b200.kv_transfer.base import (
     ReqToRecv,
     ReqToSave,
 )
+from lean_vllm_b200.kv_transfer.holds import Holds
 from lean_vllm_b200.kv_transfer.shares import Share, head_shares, readers_of, split_heads
 from lean_vllm_b200.kv_transfer.transport import CopyJob
 
@@ -69,6 +70,23 @@ def _ids_fit(block_ids, num_blocks: int) -> bool:
     return not ids or (min(ids) >= 0 and max(ids) < num_blocks)
 
 
+def _peer_mismatch(reply: dict, key, req, layout: dict, node: str) -> str | None:
+    """Why a peer's handshake reply cannot serve this load, or None. The fields both sides of a deployment compare
+    (nixl_connector.py:490-501, plus the node: CUDA IPC reaches only GPUs of one machine)."""
+    where = f"{key[0]}:{key[1]}"
+    checks = (
+        (bool(req.remote_engine_id) and reply["engine_id"] != req.remote_engine_id,
+         lambda: f"{where} is engine {reply['engine_id']}, not {req.remote_engine_id}"),
+        (reply["tp_size"] != req.remote_tp_size,
+         lambda: f"{where} runs tp_size {reply['tp_size']}, not {req.remote_tp_size}"),
+        (reply["layout"] != json.loads(json.dumps(layout)),  # as the JSON round trip left the peer's
+         lambda: f"{where} lays its KV cache out as {reply['layout']}, this engine as {layout}; "
+                 "serve the same model, dtype and block size"),
+        (reply.get("node") != node, lambda: f"{where} runs on another node; CUDA IPC needs both on one node"),
+    )
+    return next((message() for failed, message in checks if failed), None)
+
+
 def node_id() -> str:
     """Identifies this machine's boot: CUDA IPC mappings work only between processes of one node."""
     try:
@@ -85,8 +103,22 @@ def make_transport(kv_caches):
     return KvxTransport(kv_caches)
 
 
+def _request_kind(params) -> str | None:
+    """What a request's kv_transfer_params ask of this instance: "save" (a prefill whose decode instance waits for
+    pushed blocks), "pull" (a decode that reads a finished prefill's blocks), "pushed" (a decode whose blocks will be
+    pushed to it), or None (nothing to transfer)."""
+    if not params:
+        return None
+    if params.get("do_remote_decode") and params.get("kv_push_id"):
+        return "save"
+    if params.get("do_remote_prefill"):
+        return "pushed" if params.get("kv_push") else "pull"
+    return None
+
+
 class CudaIpcConnectorScheduler(KVConnectorScheduler):
-    """The engine's half, as NixlConnectorScheduler (nixl_connector.py:111-168).
+    """The engine's half (the reference's NixlConnectorScheduler, nixl_connector.py:111-168): it admits loads,
+    hands each step's work to the worker ranks as metadata, and describes a finished prefill's blocks to the proxy.
 
     Push mode adds two optional kv_transfer_params keys the reference does not have. A decode request sent before
     its prefill carries "kv_push": true (with remote_block_ids empty): it is admitted, allocated and left waiting,
@@ -105,78 +137,85 @@ class CudaIpcConnectorScheduler(KVConnectorScheduler):
         self._reqs_to_save: dict[str, ReqToSave] = {}
         self._saving: dict[str, object] = {}  # request -> its sequence while its prompt is prefilled under a save
 
+    def _prompt_blocks(self, seq) -> int:
+        return _cdiv(seq.num_prompt_tokens, self.block_size)
+
     def get_num_new_matched_tokens(self, seq, num_computed_tokens: int) -> tuple[int, bool]:
+        """(tokens the decode instance will receive instead of computing, whether they arrive asynchronously)."""
+        kind = _request_kind(seq.kv_transfer_params)
+        if kind == "save":
+            self._begin_save(seq, num_computed_tokens)
+            return 0, False
+        if kind is None or (kind == "pull" and not self._load_fits(seq)):
+            return 0, False
+        # Any split of heads between the two instances works: shares cover every tp_size pair.
+        return seq.num_prompt_tokens - num_computed_tokens, True
+
+    def _begin_save(self, seq, num_computed_tokens: int):
+        """A prefill whose decode instance waits for a push: its blocks are allocated now, so they are saved."""
+        self._reqs_to_save[seq.request_id] = ReqToSave(
+            list(seq.block_table[: self._prompt_blocks(seq)]), push_id=str(seq.kv_transfer_params["kv_push_id"]),
+            cached_blocks=num_computed_tokens // self.block_size, num_tokens=seq.num_prompt_tokens)
+        self._saving[seq.request_id] = seq
+
+    def _load_fits(self, seq) -> bool:
+        """A pull must name one remote block per prompt block; otherwise the prompt is prefilled here."""
         params = seq.kv_transfer_params
-        if params and params.get("do_remote_decode") and params.get("kv_push_id"):
-            # A prefill whose decode instance waits for a push: its blocks are allocated now, so save them.
-            blocks = list(seq.block_table[: _cdiv(seq.num_prompt_tokens, self.block_size)])
-            self._reqs_to_save[seq.request_id] = ReqToSave(blocks, push_id=str(params["kv_push_id"]),
-                                                           cached_blocks=num_computed_tokens // self.block_size,
-                                                           num_tokens=seq.num_prompt_tokens)
-            self._saving[seq.request_id] = seq
-            return 0, False
-        if not params or not params.get("do_remote_prefill"):
-            return 0, False
-        if params.get("kv_push"):  # the blocks will be pushed here: nothing to check against yet
-            return seq.num_prompt_tokens - num_computed_tokens, True
-        expected = _cdiv(seq.num_prompt_tokens, self.block_size)
-        given = len(params["remote_block_ids"])
-        if given != expected:
-            logger.warning("prefilling %s here instead: %d remote blocks for a %d-block prompt", seq.request_id,
-                           given, expected)
-            params["do_remote_prefill"] = False
-            return 0, False
-        return seq.num_prompt_tokens - num_computed_tokens, True  # any tp_size: shares cover every split
+        wanted, named = self._prompt_blocks(seq), len(params["remote_block_ids"])
+        if named == wanted:
+            return True
+        logger.warning("prefilling %s here instead: %d remote blocks for a %d-block prompt", seq.request_id,
+                       named, wanted)
+        params["do_remote_prefill"] = False
+        return False
 
     def update_state_after_alloc(self, seq, num_external_tokens: int):
         params = seq.kv_transfer_params
-        params["do_remote_prefill"] = False  # one load per request; a preempted one recomputes
-        cached = seq.num_cached_tokens // self.block_size  # blocks this instance already holds are not read
-        pushed = bool(params.get("kv_push"))
-        prompt_blocks = _cdiv(seq.num_prompt_tokens, self.block_size)
+        params["do_remote_prefill"] = False  # one load per request: a preempted one recomputes
+        skip = seq.num_cached_tokens // self.block_size  # blocks this instance already holds are not loaded again
+        table = list(seq.block_table)
+        if params.get("kv_push"):  # the producer learns the blocks from the workers' announcement
+            local, remote = table[skip : self._prompt_blocks(seq)], []
+        else:
+            local, remote = table[skip:], list(params["remote_block_ids"][skip:])
         self._reqs_to_recv[seq.request_id] = ReqToRecv(
-            local_block_ids=list(seq.block_table[cached:prompt_blocks] if pushed else seq.block_table[cached:]),
-            remote_block_ids=[] if pushed else list(params["remote_block_ids"][cached:]),
-            remote_request_id=params["remote_request_id"],
-            remote_engine_id=params["remote_engine_id"],
-            remote_host=params["remote_host"],
-            remote_port=params["remote_port"],
-            remote_tp_size=params.get("tp_size", 1),
-            pushed=pushed,
-            skip_blocks=cached if pushed else 0,
-        )
+            local_block_ids=local, remote_block_ids=remote, remote_request_id=params["remote_request_id"],
+            remote_engine_id=params["remote_engine_id"], remote_host=params["remote_host"],
+            remote_port=params["remote_port"], remote_tp_size=params.get("tp_size", 1),
+            pushed=bool(params.get("kv_push")), skip_blocks=skip if params.get("kv_push") else 0)
 
     def build_connector_meta(self) -> KVConnectorMetadata:
-        # Called once per step, after scheduling (engine/scheduler.py:147, 260-263): each saved prompt's tokens with
-        # KV once this step runs, so per-layer saves push exactly what the step's chunk fills.
+        """The step's work for the worker ranks. Built once per step after scheduling (engine/scheduler.py:147,
+        260-263), so each saved prompt's progress -- its tokens with KV once this step runs -- lets per-layer
+        saves push exactly what the step's chunk fills."""
         progress = {}
         for request_id, seq in list(self._saving.items()):
-            done = min(seq.num_cached_tokens + seq.num_scheduled_tokens, seq.num_prompt_tokens)
-            progress[request_id] = done
-            if done >= seq.num_prompt_tokens:
+            progress[request_id] = min(seq.num_cached_tokens + seq.num_scheduled_tokens, seq.num_prompt_tokens)
+            if progress[request_id] >= seq.num_prompt_tokens:
                 del self._saving[request_id]
         metadata = KVConnectorMetadata(self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save, progress)
         self._reqs_to_recv, self._reqs_to_send, self._reqs_to_save = {}, {}, {}
         return metadata
 
     def request_finished(self, seq) -> tuple[bool, dict | None]:
+        """(whether the engine must keep the request's blocks for readers, the params a decode instance needs).
+        Only a prefill that ran to its token (length or stop) hands over; an aborted one frees its blocks."""
         self._saving.pop(seq.request_id, None)
         params = seq.kv_transfer_params
-        if not params or not params.get("do_remote_decode") or seq.finish_reason not in ("length", "stop"):
-            return False, None  # only a prefill that ran to its token hands over; an abort ends here
-        block_ids = list(seq.block_table[: _cdiv(seq.num_prompt_tokens, self.block_size)])
-        self._reqs_to_send[seq.request_id] = block_ids
+        if not (params and params.get("do_remote_decode")) or seq.finish_reason not in ("length", "stop"):
+            return False, None
+        blocks = list(seq.block_table[: self._prompt_blocks(seq)])
+        self._reqs_to_send[seq.request_id] = blocks
+        return True, self._decode_params(seq.request_id, blocks)
+
+    def _decode_params(self, request_id: str, blocks: list[int]) -> dict:
+        """Where a decode instance reads this prefill's blocks from: the kv_transfer_params wire dict the proxy
+        carries to it (nixl_connector.py:159-168, disagg_proxy.py:57-71)."""
         kv = self.kv_transfer
-        return True, {
-            "do_remote_prefill": True,
-            "do_remote_decode": False,
-            "remote_request_id": seq.request_id,
-            "remote_engine_id": kv.engine_id,
-            "remote_block_ids": block_ids,
-            "remote_host": kv.kv_ip,
-            "remote_port": kv.kv_port,
-            "tp_size": self.tp_size,
-        }
+        where = {"remote_engine_id": kv.engine_id, "remote_host": kv.kv_ip, "remote_port": kv.kv_port,
+                 "tp_size": self.tp_size}
+        return {"do_remote_prefill": True, "do_remote_decode": False, "remote_request_id": request_id,
+                "remote_block_ids": blocks, **where}
 
 
 @dataclass(slots=True)
@@ -308,8 +347,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self.transport = None
         self.node = node_id()
         self._lock = threading.Lock()  # guards the maps below that both threads touch
-        self._reqs_to_send: dict[str, float] = {}  # request -> deadline for its readers
-        self._notified: dict[str, list] = {}  # request -> [notifications, readers, first seen]
+        self._holds = Holds()  # producer: handed-over blocks kept for their readers; under the lock
         self._saves: dict[str, _Save] = {}  # producer: requests pushed layer by layer
         self._saved: dict[str, dict] = {}  # decode: request -> {producer rank: landed ok}, may precede the wait
         self._saved_seen: dict[str, float] = {}  # request -> when its first landing word came; under the lock
@@ -411,12 +449,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             with self._lock:
                 for request_id in metadata.reqs_to_send:
                     save = self._saves.get(request_id)
-                    if save is not None:
+                    if save is not None:  # pushed: it finishes once its copies land, not by readers
                         save.handed_over = True
                         finishing.append(request_id)
-                        continue
-                    self._reqs_to_send[request_id] = deadline
-                    self._release_if_read(request_id)
+                    elif self._holds.hold(request_id, deadline):  # every reader reported before the hand-over
+                        self._finished.finished_sending.add(request_id)
             if finishing:
                 ready = self.transport.ready_marker()
                 for request_id in finishing:
@@ -464,31 +501,37 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         """Saves are ordered after their layers on the GPU and awaited on the transfer thread: nothing to do."""
 
     def get_finished(self) -> KVConnectorOutput:
+        """What finished since the last call: the transfer thread fills the output as loads land and readers
+        report; here held blocks past the abort timeout are given back, and the output is handed to the engine."""
+        self._mark_swaps_passed()
+        timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+        now = monotonic()
+        with self._lock:
+            for request_id in self._holds.expire(now):
+                logger.warning("freeing the KV blocks of %s, which no decode instance read in %.0f s",
+                               request_id, timeout)
+                self._finished.finished_sending.add(request_id)
+                self._finished.expired_sending.add(request_id)
+            self._holds.forget_strays(now, timeout)
+            out, self._finished = self._finished, KVConnectorOutput()
+        return out
+
+    def _mark_swaps_passed(self):
+        """Every store and push the engine thread queued naming a replaced mapping is on a stream by now: the
+        engine stream's event here is what the mapping's close waits for."""
         with self._lock:
             swapped = [r for r in self._retired if not r.passed]
-        if swapped:
-            # Every store and push this thread queued naming a replaced mapping was queued before this point.
-            marker = self.transport.ready_marker()
-            with self._lock:
-                for retired in swapped:
-                    retired.marker, retired.passed = marker, True
-        now = monotonic()
-        timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
+        if not swapped:
+            return
+        marker = self.transport.ready_marker()
         with self._lock:
-            for request_id, deadline in list(self._reqs_to_send.items()):
-                if deadline < now:  # a copy is one-sided, so the producer cannot see one in flight: the timeout is long
-                    logger.warning("freeing the KV blocks of %s, which no decode instance read in %.0f s",
-                                   request_id, timeout)
-                    self._release(request_id)
-                    self._finished.expired_sending.add(request_id)
-            for request_id, (_, _, seen) in list(self._notified.items()):
-                if request_id not in self._reqs_to_send and seen + timeout < now:
-                    del self._notified[request_id]  # read here but never handed over: not this engine's
-            finished, self._finished = self._finished, KVConnectorOutput()
-        return finished
+            for retired in swapped:
+                retired.marker, retired.passed = marker, True
 
     def shutdown(self):
-        if self._context.closed:
+        """Stops the transfer thread -- which waits for the copies in flight before it closes any peer mapping --
+        then the wake-up descriptor and the sockets. A second call does nothing."""
+        if self._wake < 0:
             return
         if self._thread is not None:
             self._put(None)
@@ -496,18 +539,6 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         wake, self._wake = self._wake, -1
         os.close(wake)
         self._context.term()
-
-    def _release(self, request_id: str):
-        """Lock held. The engine frees the blocks once every rank reported them."""
-        if self._reqs_to_send.pop(request_id, None) is not None:
-            self._notified.pop(request_id, None)
-            self._finished.finished_sending.add(request_id)
-
-    def _release_if_read(self, request_id: str):
-        """Lock held."""
-        entry = self._notified.get(request_id)
-        if entry is not None and entry[0] >= entry[1]:
-            self._release(request_id)
 
     def _heads(self, req) -> int:
         return split_heads(self.num_heads, self.tp_size, req.remote_tp_size)
@@ -814,17 +845,6 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         except zmq.Again:
             logger.warning("a KV handshake went unanswered: its peer is not reading")
 
-    def _reply(self, sock, key) -> bytes:
-        """A peer's handshake reply, answering handshakes addressed to this rank meanwhile."""
-        deadline = monotonic() + HANDSHAKE_TIMEOUT
-        while True:
-            if sock.poll(timeout=2):
-                return sock.recv()
-            if self._server is not None:
-                self._serve(answer_only=True)
-            if monotonic() > deadline:
-                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake")
-
     def _count(self, message: str):
         try:
             request_id, readers = message.rsplit(":", 1)
@@ -833,9 +853,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             logger.warning("ignoring a malformed KV notification %r", message)
             return
         with self._lock:
-            entry = self._notified.setdefault(request_id, [0, readers, monotonic()])
-            entry[0] += 1
-            self._release_if_read(request_id)
+            if self._holds.reported(request_id, readers, monotonic()):
+                self._finished.finished_sending.add(request_id)
 
     # Pull: plan the step's loads, launch them (small ones together), then poll each launch once per pass.
 
@@ -1370,44 +1389,52 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         remote_engine_id accepts whichever engine answers; `fresh` asks again even if one is mapped, to see a
         restart (for a load that names no engine id)."""
         key = (req.remote_host, req.remote_port + remote_rank)
-        remote = self._remotes.get(key)
-        if remote is not None and fresh:
-            if self._ask(key)["engine_id"] == remote.engine_id:
-                return remote
-        elif remote is not None and (remote.engine_id == req.remote_engine_id or not req.remote_engine_id):
-            return remote
-        if remote is not None:
-            self._retire(key, remote)  # restarted since: ask afresh
-        sock = self._context.socket(zmq.DEALER)
-        keep = False
+        known = self._remotes.get(key)
+        if known is not None:
+            if fresh:
+                still = self._ask(key)["engine_id"] == known.engine_id
+            else:
+                still = not req.remote_engine_id or known.engine_id == req.remote_engine_id
+            if still:
+                return known
+            self._retire(key, known)  # the peer restarted under a new engine id: ask afresh
+        sock = self._dealer(key)
         try:
-            sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
-            sock.connect(f"tcp://{key[0]}:{key[1]}")
-            sock.send(json.dumps({"op": "handshake"}).encode())
-            reply = json.loads(self._reply(sock, key))
-            if not reply["ok"]:
-                raise RuntimeError(reply["error"])
-            if req.remote_engine_id and reply["engine_id"] != req.remote_engine_id:
-                raise RuntimeError(f"{key[0]}:{key[1]} is engine {reply['engine_id']}, not {req.remote_engine_id}")
-            if reply["tp_size"] != req.remote_tp_size:
-                raise RuntimeError(f"{key[0]}:{key[1]} runs tp_size {reply['tp_size']}, not {req.remote_tp_size}")
-            if reply["layout"] != json.loads(json.dumps(self.layout)):
-                raise RuntimeError(
-                    f"{key[0]}:{key[1]} lays its KV cache out as {reply['layout']}, this engine as {self.layout}; "
-                    "serve the same model, dtype and block size"
-                )
-            if reply.get("node") != self.node:
-                raise RuntimeError(f"{key[0]}:{key[1]} runs on another node; CUDA IPC needs both on one node")
-            table = self.transport.open(reply["exported"])
-            remote = _Remote(reply["engine_id"], reply["tp_size"], reply["num_blocks"], reply["exported"], table, sock)
-            self._remotes[key] = remote
-            with self._lock:
-                self._mapped[key] = (remote.engine_id, remote.table, remote.num_blocks)
-            keep = True
-            return remote
-        finally:
-            if not keep:
-                sock.close()
+            reply = self._round_trip(sock, key)
+            problem = _peer_mismatch(reply, key, req, self.layout, self.node)
+            if problem:
+                raise RuntimeError(problem)
+            remote = _Remote(reply["engine_id"], reply["tp_size"], reply["num_blocks"], reply["exported"],
+                             self.transport.open(reply["exported"]), sock)
+        except BaseException:
+            sock.close()
+            raise
+        self._remotes[key] = remote  # its socket stays open for notifications
+        with self._lock:
+            self._mapped[key] = (remote.engine_id, remote.table, remote.num_blocks)
+        return remote
+
+    def _dealer(self, key):
+        sock = self._context.socket(zmq.DEALER)
+        sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
+        sock.connect(f"tcp://{key[0]}:{key[1]}")
+        return sock
+
+    def _round_trip(self, sock, key) -> dict:
+        """Sends a handshake and returns the peer's accepted reply. While waiting, handshakes addressed to this rank
+        are answered (the peer may be waiting on this rank at the same time, which would otherwise hold both until
+        the timeout)."""
+        sock.send(json.dumps({"op": "handshake"}).encode())
+        deadline = monotonic() + HANDSHAKE_TIMEOUT
+        while not sock.poll(timeout=2):
+            if self._server is not None:
+                self._serve(answer_only=True)
+            if monotonic() > deadline:
+                raise ConnectionError(f"{key[0]}:{key[1]} did not answer the handshake")
+        reply = json.loads(sock.recv())
+        if not reply.get("ok"):
+            raise RuntimeError(reply.get("error", "handshake refused"))
+        return reply
 
     def _retire(self, key, remote: _Remote):
         """Drops a peer rank that restarted under a new engine id. Its old mapping stays open until nothing queued
@@ -1448,14 +1475,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
 
     def _ask(self, key) -> dict:
         """One handshake round trip on a socket of its own, for its reply only."""
-        sock = self._context.socket(zmq.DEALER)
+        sock = self._dealer(key)
         try:
-            sock.rcvtimeo = sock.sndtimeo = int(HANDSHAKE_TIMEOUT * 1000)
-            sock.connect(f"tcp://{key[0]}:{key[1]}")
-            sock.send(json.dumps({"op": "handshake"}).encode())
-            reply = json.loads(self._reply(sock, key))
+            return self._round_trip(sock, key)
         finally:
             sock.close()
-        if not reply.get("ok"):
-            raise RuntimeError(reply.get("error", "handshake refused"))
-        return reply
