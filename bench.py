@@ -1083,9 +1083,11 @@ def run_store(args) -> None:
         targets = [[PushTarget.of(c.transpose(2, 3)[0], c.transpose(2, 3)[1], peer_slots)] for c in peer_caches]
         torch.cuda.synchronize(peer)
 
-    from lean_vllm_b200._native import STORE_SERIAL
+    from lean_vllm_b200._native import STORE_LSU, STORE_SERIAL
 
-    store_flags = STORE_SERIAL if args.serial else 0
+    store_flags = (STORE_SERIAL if args.serial else 0) | (STORE_LSU if args.store_engine == "vector" else 0)
+    store_flags |= (args.store_stages << 8) | ((args.store_tpc.bit_length() - 1 if args.store_tpc else 0) << 12)
+    store_flags |= args.ctas_per_sm << 16
 
     def ours():
         for layer in range(layers):
@@ -1186,7 +1188,10 @@ def run_store(args) -> None:
         "config": {"workload": "qwen3-8b-kv/store-8192-token-step", "layers": layers, "tokens": tokens,
                    "shape": "8 KV heads x 128, block 256, HND",
                    "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None,
-                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)"},
+                   "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)",
+                   "engine": args.store_engine, "stages": args.store_stages or "default",
+                   "tokens_per_stage": args.store_tpc or "default",
+                   "ctas_per_sm": args.ctas_per_sm or "default"},
         "roofline": roofline,
         "ms_per_step_eager": round(ms_eager, 4),
         "timing": "CUDA graph of the step's 36 store launches, replayed; ms_per_step_eager issues them one by one",
@@ -1586,23 +1591,241 @@ def run_copy_engine(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+REFERENCE_PATH = os.path.join(ROOT, "baseline", "_ref")  # the reference, pip-installed here (git-ignored)
+REFERENCE_SECONDS = 180.0  # the reference worker leg's timed budget: its per-step sample shrinks to fit it
+
+
+def host_rank_caches(spec: Workload, tp: int, num_blocks: int, seed: int | None):
+    """One side's caches on the host, per rank (torch CPU bf16, HND or latents): rank r holds heads
+    [r*H/tp, (r+1)*H/tp), latents whole. With a seed every block gets distinct contents (a seeded random block
+    pattern, stamped with the layer and block index); without one, zeros."""
+    import torch
+
+    ranks = []
+    g = torch.Generator().manual_seed(seed or 0)
+    for rank in range(tp):
+        layers = []
+        for layer in range(spec.layers):
+            shape = ((1, num_blocks, spec.block, spec.head_dim) if spec.mla else
+                     (2, num_blocks, spec.kv_heads // tp, spec.block, spec.head_dim))
+            t = torch.zeros(shape, dtype=torch.bfloat16)
+            if seed is not None:
+                words = t.view(torch.int16)
+                pattern = torch.randint(-(1 << 15), 1 << 15, (shape[0], 1, *shape[2:]), generator=g,
+                                        dtype=torch.int16)
+                words.copy_(pattern.expand_as(words))
+                stamp = words.reshape(shape[0], num_blocks, -1)
+                stamp[:, :, 0] = torch.arange(num_blocks, dtype=torch.int16)
+                stamp[:, :, 1] = layer * 16 + rank
+            layers.append(t)
+        ranks.append(layers)
+    return ranks
+
+
+def reference_worker_leg(spec: Workload, reqs, producers, consumers, steps: int, warmup: int) -> dict:
+    """The reference's own transfer path, unmodified: lean-vLLM's NixlConnectorWorker (imported from the pip-installed
+    reference in baseline/_ref) as every prefill and decode rank in this process, over host caches, with NIXL
+    replaced by the memmove agent the reference's CPU tests describe (oracle/memmove_agent.py). A step hands every
+    request over on the producer ranks and loads it on the decode ranks (start_load_kv, then get_finished until all
+    have landed), as tests/test_nixl_connector.py:33-115 drives them. Returns the leg's numbers, or why it could not
+    run."""
+    import socket
+    from dataclasses import dataclass as plain_dataclass
+
+    if not os.path.isdir(os.path.join(REFERENCE_PATH, "lean_vllm")):
+        return {"unavailable": f"the reference is not installed in {os.path.relpath(REFERENCE_PATH, ROOT)}"}
+    if REFERENCE_PATH not in sys.path:
+        sys.path.insert(0, REFERENCE_PATH)
+    try:
+        from lean_vllm.kv_transfer import KVConnectorMetadata, KVTransferConfig, ReqToRecv
+        from lean_vllm.kv_transfer import nixl_connector
+    except Exception as error:  # noqa: BLE001
+        return {"unavailable": f"importing the reference failed: {type(error).__name__}: {error}"}
+    from oracle.memmove_agent import MemmoveAgent
+
+    nixl_connector.make_agent = MemmoveAgent
+
+    @plain_dataclass
+    class Cfg:
+        kv_transfer: object
+        tensor_parallel_size: int
+        kvcache_block_size: int
+        kv_cache_layout: str = "HND"
+
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    if port + spec.prefill_tp > 65535:
+        port -= 64
+    prefill_ranks, decode_ranks = [], []
+    try:
+        for rank, layers in enumerate(producers):
+            kv = KVTransferConfig(kv_role="kv_producer", kv_port=port, engine_id="ref-prefill")
+            worker = nixl_connector.NixlConnectorWorker(Cfg(kv, spec.prefill_tp, spec.block), rank)
+            worker.register_kv_caches(layers)
+            prefill_ranks.append(worker)
+        for rank, layers in enumerate(consumers):
+            kv = KVTransferConfig(kv_role="kv_consumer", kv_port=port + 64, engine_id="ref-decode")
+            worker = nixl_connector.NixlConnectorWorker(Cfg(kv, spec.decode_tp, spec.block), rank)
+            worker.register_kv_caches(layers)
+            decode_ranks.append(worker)
+
+        def step(tag: str, sample) -> tuple[float, int]:
+            sends = {f"{tag}-{i}": [int(b) for b in s] for i, (s, _) in enumerate(sample)}
+            recvs = {f"{tag}-{i}": ReqToRecv([int(b) for b in d], [int(b) for b in s], f"{tag}-{i}", "ref-prefill",
+                                             "127.0.0.1", port, spec.prefill_tp) for i, (s, d) in enumerate(sample)}
+            for worker in prefill_ranks:
+                worker.start_load_kv(KVConnectorMetadata(reqs_to_send=sends))
+            started = time.perf_counter()
+            for worker in decode_ranks:
+                worker.start_load_kv(KVConnectorMetadata(reqs_to_recv=recvs))
+            nbytes, waiting = 0, [set(recvs) for _ in decode_ranks]
+            deadline = time.monotonic() + 1800
+            while any(waiting) and time.monotonic() < deadline:
+                for left, worker in zip(waiting, decode_ranks):
+                    out = worker.get_finished()
+                    if out.failed_recving:
+                        raise RuntimeError(f"reference loads failed: {sorted(out.failed_recving)[:3]}")
+                    for request_id in out.finished_recving:
+                        nbytes += out.recv_stats[request_id].num_bytes
+                    left -= out.finished_recving
+                if any(waiting):
+                    time.sleep(1e-3)
+            elapsed = time.perf_counter() - started
+            if any(waiting):
+                raise RuntimeError("reference loads did not finish")
+            left, deadline = set(sends), time.monotonic() + 60  # held blocks released once every reader reported
+            while left and time.monotonic() < deadline:
+                for worker in prefill_ranks:
+                    left -= worker.get_finished().finished_sending
+                time.sleep(1e-3)
+            return elapsed, nbytes
+
+        for k in range(min(warmup, 1)):  # the first handshake; nothing else warms up
+            step(f"warm{k}", reqs[:1])
+        # A full step on the whole workload if the timed steps fit the budget, else the largest prefix that does.
+        probe_s, probe_bytes = step("probe", reqs[: max(1, len(reqs) // 8)])
+        per_byte = probe_s / max(probe_bytes, 1)
+        total = sum(request_bytes(len(s), spec) for s, _ in reqs)
+        sample = reqs
+        if per_byte * total * steps > REFERENCE_SECONDS:
+            budget = REFERENCE_SECONDS / steps / per_byte
+            sample, acc = [], 0
+            for s, d in reqs:
+                acc += request_bytes(len(s), spec)
+                if acc > budget and sample:
+                    break
+                sample.append((s, d))
+        times, moved = [], 0
+        for k in range(steps):
+            seconds, moved = step(f"s{k}", sample)
+            times.append(seconds)
+        seconds = float(np.median(times))
+        gbs = moved / seconds / 1e9
+        # The decode caches hold the producer's blocks (rank 0's share of the last request of the sample).
+        import torch
+
+        s_ids, d_ids = sample[-1]
+        heads = spec.kv_heads // spec.decode_tp if not spec.mla else None
+        landed = consumers[0][0][:, list(d_ids)]
+        sent = producers[0][0][:, list(s_ids)]
+        if heads is not None and spec.prefill_tp == 1:
+            sent = sent[:, :, :heads]
+        # Bit patterns, not values: random words include bf16 NaNs, which compare unequal to themselves.
+        correct = bool(torch.equal(landed.view(torch.int16), sent.view(torch.int16))) if spec.prefill_tp == 1 else None
+        return {
+            "value": round(gbs, 3), "unit": "GB/s", "kind": "reference",
+            "ms_per_step": round(seconds * 1e3, 3), "steps": steps,
+            "cores": spec.decode_tp,
+            "sample": (f"{len(sample)} of the workload's {len(reqs)} requests per step ({moved / 1e9:.2f} GB)"
+                       + ("" if len(sample) == len(reqs) else f", cut to fit {REFERENCE_SECONDS:.0f} s of timed steps")),
+            "same_config": len(sample) == len(reqs),
+            "path": ("lean_vllm.kv_transfer.nixl_connector.NixlConnectorWorker (the installed reference, unmodified): "
+                     f"{spec.prefill_tp} prefill + {spec.decode_tp} decode ranks in one process, one transfer thread "
+                     "each; NIXL replaced by the reference tests' memmove agent (one memmove per descriptor row)"),
+            "correct": correct,
+        }
+    except Exception as error:  # noqa: BLE001 - the arm reports what stopped it rather than no line at all
+        return {"unavailable": f"the reference worker leg failed: {type(error).__name__}: {error}"}
+    finally:
+        for worker in prefill_ranks + decode_ranks:
+            worker.shutdown()
+
+
+def port_leg(spec: Workload, reqs, producers, consumers, steps: int, threads: int) -> dict:
+    """The same loads by the C restatement of the reference's path (oracle/kvx_oracle.c: block_descs rows for both
+    sides, one memmove per row, rows split over `threads` host threads), on the same host caches."""
+    from oracle import c_oracle
+    from oracle.kv_oracle import Region, head_shares, lcm_heads
+
+    import torch
+
+    def regions(layers):
+        out = []
+        for t in layers:
+            for part in t:
+                head = part.stride(1) * 2 if t.dim() == 5 else 0
+                out.append(Region(part.data_ptr(), part.stride(0) * 2, head))
+        return out
+
+    c_oracle.lib()
+    src_regions = [regions(layers) for layers in producers]
+    dst_regions = [regions(layers) for layers in consumers]
+    heads = spec.kv_heads or lcm_heads(spec.decode_tp, spec.prefill_tp)
+    times, moved = [], 0
+    for _ in range(max(steps, 1)):
+        started, moved = time.perf_counter(), 0
+        for s_ids, d_ids in reqs:
+            for rank in range(spec.decode_tp):
+                for i, share in enumerate(head_shares(rank, spec.decode_tp, spec.prefill_tp, heads)):
+                    d_addr, d_len = c_oracle.block_descs(dst_regions[rank], d_ids, share.local_head, share.num_heads,
+                                                         i == 0)
+                    s_addr, _ = c_oracle.block_descs(src_regions[share.remote_rank], s_ids, share.remote_head,
+                                                     share.num_heads, i == 0)
+                    moved += c_oracle.read(d_addr, s_addr, d_len, threads)
+        times.append(time.perf_counter() - started)
+    seconds = float(np.median(times))
+    return {"value": round(moved / seconds / 1e9, 3), "unit": "GB/s", "kind": "port", "cores": threads,
+            "ms_per_step": round(seconds * 1e3, 3), "steps": max(steps, 1),
+            "sample": f"all {len(reqs)} requests per step ({moved / 1e9:.2f} GB) on the same host caches",
+            "path": "C restatement of block_descs + one memmove per row, rows split over every host thread"}
+
+
 def run_reference(args) -> None:
-    """The reference arm: the reference's CPU transfer path (C restatement in oracle/, all host threads)."""
+    """The reference arm, on the box's host cores: the reference's own NixlConnectorWorker pair (the primary value,
+    kind "reference") and the C restatement beside it (kind "port"), on the same host caches of the workload -- the
+    whole workload when host RAM allows. Rank 0 alone runs; other ranks exit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import psutil
+
     spec = WORKLOADS[args.workload]
     lengths, reqs, num_blocks = workload(args.seed, args.requests, spec)
-    cpu_seconds = max(2.0, min(args.cpu_seconds, 40.0 / max(args.steps + args.warmup, 1)))
-    for _ in range(args.warmup):
-        cpu_baseline(reqs, spec, seconds=0.5)
-    results = [cpu_baseline(reqs, spec, seconds=cpu_seconds) for _ in range(max(args.steps, 1))]
-    gbs = float(np.median([r["value"] for r in results]))
-    base = results[0]
+    layer_bytes = (num_blocks * spec.block * spec.head_dim * 2 * (1 if spec.mla else 2 * spec.kv_heads))
+    need = 2 * spec.layers * layer_bytes  # both sides; the ranks of a side split one side's bytes
+    available = psutil.virtual_memory().available
+    ram_note = f"{need / 1e9:.1f} GB of host caches, {available / 1e9:.1f} GB available"
+    if need > 0.6 * available:  # the largest prefix of the workload whose caches fit comfortably
+        n = len(reqs)
+        while n > 1:
+            n -= max(1, n // 8)
+            _, reqs, num_blocks = workload(args.seed, n, spec)
+            layer_bytes = (num_blocks * spec.block * spec.head_dim * 2 * (1 if spec.mla else 2 * spec.kv_heads))
+            if 2 * spec.layers * layer_bytes <= 0.6 * available:
+                break
+        ram_note += f": cut to the first {len(reqs)} requests"
+    producers = host_rank_caches(spec, spec.prefill_tp, num_blocks, seed=args.seed + 1)
+    consumers = host_rank_caches(spec, spec.decode_tp, num_blocks, seed=None)
+    threads = len(os.sched_getaffinity(0))
+    legs = {"reference": reference_worker_leg(spec, reqs, producers, consumers, max(args.steps, 1), args.warmup),
+            "port": port_leg(spec, reqs, producers, consumers, min(max(args.steps, 1), 5), threads)}
+    primary = legs["reference"] if "value" in legs["reference"] else legs["port"]
+    gbs = primary["value"]
     line = {
         "metric": METRIC,
         "impl": "reference",
-        "value": round(gbs, 3),
+        "value": gbs,
         "unit": "GB/s",
         "n_gpus": args.gpus,
         "steps": args.steps,
@@ -1612,20 +1835,20 @@ def run_reference(args) -> None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic: bf16-sized host caches, seeded shuffled block tables",
-        # The same workload our arm names at this N (so the two lines compare), timed on a bounded sample of it.
+        "data": "synthetic: seeded bf16 host caches (distinct per block), seeded shuffled block tables",
+        # The same workload our arm names at this N, so the two lines compare.
         "config": {"workload": (f"{spec.name}/loopback-1gpu" if args.gpus == 1 else
                                 f"{spec.name}/{args.gpus // spec.group_size}x-tp{spec.prefill_tp}to{spec.decode_tp}"),
                    "shape": spec.describe(),
                    "requests_per_step": len(reqs),
                    "prompt_lengths": f"{spec.lengths[0]} [{spec.lengths[1]}, {spec.lengths[2]}], seed {args.seed}",
-                   "mode": args.mode,
-                   "timed_sample": base["sample"],
-                   "path": "the reference's CPU transfer path: block_descs rows and one memmove per row (the NIXL "
-                           "READ its tests fake), restated in C, rows split over every host thread"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": base["cores"], "kind": "port",
-                         "sample": base["sample"]},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                   "mode": "pull",
+                   "host_ram": ram_note,
+                   "host_cpus": os.cpu_count()},
+        "legs": legs,
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": primary["cores"], "kind": primary["kind"],
+                         "sample": primary["sample"]},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -1653,6 +1876,10 @@ def main(argv=None):
                    help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
     p.add_argument("--store", action="store_true", help="measure the per-token cache store (and fused push)")
     p.add_argument("--serial", action="store_true", help="with --store: plain launches (KVX_STORE_SERIAL)")
+    p.add_argument("--store-engine", choices=["bulk", "vector"], default="bulk",
+                   help="with --store: the bulk-copy store (default where it applies) or the vector one")
+    p.add_argument("--store-stages", type=int, default=0, help="with --store: the bulk-copy store's ring depth")
+    p.add_argument("--store-tpc", type=int, default=0, help="with --store: tokens per bulk-copy stage (power of 2)")
     p.add_argument("--fused", action="store_true",
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals at 1-64 requests/s")

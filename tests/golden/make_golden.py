@@ -14,16 +14,12 @@ not have the reference; tests there read only these files.
 
 from __future__ import annotations
 
-import ctypes
 import hashlib
 import json
 import os
 import socket
 import sys
-import threading
-from collections import defaultdict
 from dataclasses import dataclass
-from itertools import count
 from time import monotonic, sleep
 
 import numpy as np
@@ -43,80 +39,8 @@ from lean_vllm.kv_transfer import (  # noqa: E402
 )
 from lean_vllm.kv_transfer.nixl_connector import NixlConnectorWorker, Region, block_descs, head_shares  # noqa: E402
 
-
-class MemmoveAgent:
-    """The NIXL agent surface NixlConnectorWorker calls, over host memory in this process."""
-
-    registry: dict[str, "MemmoveAgent"] = {}
-
-    def __init__(self, name: str):
-        self.name = name
-        self.memory: list[tuple[int, int]] = []
-        self.peers: set[str] = set()
-        self.pending: dict[int, tuple] = {}
-        self.inbox: dict[str, list[bytes]] = defaultdict(list)
-        self.mutex = threading.Lock()
-        self.ids = count()
-        MemmoveAgent.registry[name] = self
-
-    def get_reg_descs(self, memory, mem_type):
-        return [(addr, size) for addr, size, _, _ in memory]
-
-    def register_memory(self, descs):
-        self.memory.extend(descs)
-
-    def deregister_memory(self, descs):
-        self.memory = [d for d in self.memory if d not in descs]
-
-    def get_agent_metadata(self) -> bytes:
-        return self.name.encode()
-
-    def add_remote_agent(self, metadata: bytes) -> str:
-        self.peers.add(metadata.decode())
-        return metadata.decode()
-
-    def remove_remote_agent(self, name: str):
-        self.peers.discard(name)
-
-    def get_xfer_descs(self, rows, mem_type):
-        return np.asarray(rows)
-
-    def _inside(self, agent: "MemmoveAgent", rows) -> bool:
-        return all(any(lo <= a and a + n <= lo + size for lo, size in agent.memory) for a, n, _ in rows.tolist())
-
-    def initialize_xfer(self, op, local, remote, peer_name, notification):
-        peer = MemmoveAgent.registry[peer_name]
-        if op != "READ" or len(local) != len(remote) or not (self._inside(self, local) and self._inside(peer, remote)):
-            raise RuntimeError("bad transfer")
-        handle = next(self.ids)
-        self.pending[handle] = (local, remote, peer, notification)
-        return handle
-
-    def transfer(self, handle) -> str:
-        local, remote, _, _ = self.pending[handle]
-        for (dst, n, _), (src, _, _) in zip(local.tolist(), remote.tolist()):
-            ctypes.memmove(dst, src, n)
-        return "PROC"
-
-    def check_xfer_state(self, handle) -> str:
-        _, _, peer, notification = self.pending[handle]
-        peer.deliver(self.name, notification)
-        return "DONE"
-
-    def release_xfer_handle(self, handle):
-        self.pending.pop(handle, None)
-
-    def send_notif(self, peer_name: str, message: bytes):
-        MemmoveAgent.registry[peer_name].deliver(self.name, message)
-
-    def deliver(self, sender: str, message: bytes):
-        with self.mutex:
-            self.inbox[sender].append(message)
-
-    def get_new_notifs(self):
-        with self.mutex:
-            out, self.inbox = dict(self.inbox), defaultdict(list)
-        return out
+sys.path.insert(0, os.path.join(HERE, "..", ".."))
+from oracle.memmove_agent import MemmoveAgent  # noqa: E402  (the NIXL stand-in the reference's tests describe)
 
 
 nixl_connector.make_agent = MemmoveAgent

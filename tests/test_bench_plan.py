@@ -162,3 +162,28 @@ def test_the_command_line_parses_every_mode():
     for flag in ("--relay", "--staged", "--store", "--poisson", "--layerwise", "--copy-engine", "--step-exchange",
                  "--impl", "--peer-device", "--serial"):
         assert flag in out.getvalue(), flag
+
+
+@pytest.mark.parametrize("name", ["pair", "hetero", "mla"])
+def test_the_reference_arm_s_legs_land_the_same_bytes(name):
+    """bench.py's reference arm on tiny caches: the reference's own NixlConnectorWorker ranks (installed in
+    baseline/_ref, NIXL replaced by the memmove agent) and the C restatement each move every request's blocks, with
+    the reference's byte count, and the decode caches they leave are the same."""
+    import os
+
+    if not os.path.isdir(os.path.join(bench.REFERENCE_PATH, "lean_vllm")):
+        pytest.skip("the reference is not installed in baseline/_ref")
+    spec = tiny(bench.WORKLOADS[name])
+    _, reqs, num_blocks = bench.workload(0, None, spec)
+    producers = bench.host_rank_caches(spec, spec.prefill_tp, num_blocks, seed=1)
+    by_reference = bench.host_rank_caches(spec, spec.decode_tp, num_blocks, seed=None)
+    by_port = bench.host_rank_caches(spec, spec.decode_tp, num_blocks, seed=None)
+    ref = bench.reference_worker_leg(spec, reqs, producers, by_reference, steps=1, warmup=1)
+    port = bench.port_leg(spec, reqs, producers, by_port, steps=1, threads=2)
+    assert "value" in ref, ref
+    assert ref["kind"] == "reference" and port["kind"] == "port" and ref["same_config"]
+    import torch
+
+    for ref_rank, port_rank in zip(by_reference, by_port):
+        for x, y in zip(ref_rank, port_rank):
+            assert torch.equal(x.view(torch.int16), y.view(torch.int16))  # bit patterns: NaN words compare too
