@@ -626,7 +626,9 @@ def run_gpu(args) -> None:
     # e2e: the same loads through the connector's public API.
     e2e_ms, e2e_bytes = None, 0
     if args.steps and not args.no_e2e and not peer_mode:
+        e2e_launches0 = transport.launch_count()
         e2e_ms, e2e_bytes = e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo)
+        e2e_launches = transport.launch_count() - e2e_launches0
         e = torch.tensor([e2e_ms, float(e2e_bytes)], device=device, dtype=torch.float64)
         if world > 1:
             gathered = [torch.zeros_like(e) for _ in range(world)]
@@ -640,6 +642,14 @@ def run_gpu(args) -> None:
     if world > 1:
         dist.all_reduce(ok_t, op=dist.ReduceOp.MAX)
     clock_summary = clocks.summary()
+    # One GPU: the per-token store (a12) and the layer-wise push beside a prefill (a13), each in a child process of
+    # its own once this run's caches are freed, so this line carries them from the same run.
+    extras = {}
+    if loopback and not peer_mode and not args.no_extras and rank == 0:
+        src = dst = mine = None  # the caches: the children need the memory
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        extras = measure_extras(args)
 
     if rank == 0:
         ms_per_step = max_ms / args.steps
@@ -728,10 +738,13 @@ def run_gpu(args) -> None:
                            "ms_per_step": round(e2e_ms, 4),
                            "h2d_bytes_per_step": ids_bytes, "d2h_bytes_per_step": 0,
                            "bytes_reported_by_connector": e2e_bytes,
+                           "kvx_launches_per_step": round(e2e_launches / (1 + max(args.steps // 2, 2)), 1),
+                           "batch_bytes": int(os.environ.get("LEAN_VLLM_KVX_BATCH_BYTES", str(64 << 20))),
                            "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
                                     "get_finished() until every load finished_recving; one kvx launch per load, "
                                     "block ids carried in the launch, the transfer thread woken by a doorbell when "
                                     "each copy lands")}
+        line.update(extras)
         if loopback and not peer_mode and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(reqs, spec, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -740,6 +753,47 @@ def run_gpu(args) -> None:
         for blob in opened:
             transport.close_mapping(blob)
         dist.destroy_process_group()
+
+
+def child_line(argv: list[str], timeout: float = 600.0) -> dict:
+    """The JSON line a child run of this script prints, or why there is none."""
+    try:
+        run = subprocess.run([sys.executable, os.path.abspath(__file__), *argv], capture_output=True, text=True,
+                             timeout=timeout, cwd=ROOT)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"bench.py {' '.join(argv)} ran past {timeout:.0f} s"}
+    lines = [ln for ln in run.stdout.splitlines() if ln.startswith("{")]
+    if run.returncode or not lines:
+        return {"unavailable": f"bench.py {' '.join(argv)} exited {run.returncode}: {run.stderr.strip()[-300:]}"}
+    return json.loads(lines[-1])
+
+
+def measure_extras(args) -> dict:
+    """The store and the layer-wise push, measured by child runs of this script on the same GPU."""
+    out = {}
+    store = child_line(["--store", "--steps", str(max(args.steps, 10)), "--warmup", str(max(args.warmup, 3)),
+                        "--seed", str(args.seed)])
+    if "unavailable" in store:
+        out["store"] = store
+    else:
+        out["store"] = {"metric": store["metric"], "value": store["value"], "unit": store["unit"],
+                        "ms_per_step": store["ms_per_step"], "us_per_launch": round(store["ms_per_step"] / 36 * 1e3, 2),
+                        "roofline": store["roofline"], "frac_of_same_bytes_copy": store["frac_of_same_bytes_copy"],
+                        "correct": store["correct"], "clocks": store["clocks"],
+                        "workload": "36 kvx_store launches of an 8192-token Qwen3-8B prefill step, graph-replayed",
+                        "command": f"python bench.py --store --steps {max(args.steps, 10)} --warmup "
+                                   f"{max(args.warmup, 3)}"}
+    layerwise = child_line(["--layerwise", "--steps", "3", "--warmup", "1", "--seed", str(args.seed)])
+    if "unavailable" in layerwise:
+        out["layerwise"] = layerwise
+    else:
+        out["layerwise"] = {"metric": layerwise["metric"], "exposed_fraction": layerwise["value"],
+                            "ms_compute_alone": layerwise["ms_compute_alone"],
+                            "ms_until_last_byte_landed": layerwise["ms_until_last_byte_landed"],
+                            "prefill_tflops": layerwise["prefill_tflops"], "correct": layerwise["correct"],
+                            "workload": layerwise["config"]["workload"],
+                            "command": "python bench.py --layerwise --steps 3 --warmup 1"}
+    return out
 
 
 def e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo):
@@ -1083,11 +1137,9 @@ def run_store(args) -> None:
         targets = [[PushTarget.of(c.transpose(2, 3)[0], c.transpose(2, 3)[1], peer_slots)] for c in peer_caches]
         torch.cuda.synchronize(peer)
 
-    from lean_vllm_b200._native import STORE_LSU, STORE_SERIAL
+    from lean_vllm_b200._native import STORE_SERIAL
 
-    store_flags = (STORE_SERIAL if args.serial else 0) | (STORE_LSU if args.store_engine == "vector" else 0)
-    store_flags |= (args.store_stages << 8) | ((args.store_tpc.bit_length() - 1 if args.store_tpc else 0) << 12)
-    store_flags |= args.ctas_per_sm << 16
+    store_flags = (STORE_SERIAL if args.serial else 0) | (args.ctas_per_sm << 16)
 
     def ours():
         for layer in range(layers):
@@ -1189,8 +1241,6 @@ def run_store(args) -> None:
                    "shape": "8 KV heads x 128, block 256, HND",
                    "push": f"cuda:{args.peer_device}" if args.peer_device is not None else None,
                    "launch": "plain" if args.serial else "programmatic (overlaps the previous store's drain)",
-                   "engine": args.store_engine, "stages": args.store_stages or "default",
-                   "tokens_per_stage": args.store_tpc or "default",
                    "ctas_per_sm": args.ctas_per_sm or "default"},
         "roofline": roofline,
         "ms_per_step_eager": round(ms_eager, 4),
@@ -1869,6 +1919,8 @@ def main(argv=None):
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the connector end-to-end timing")
+    p.add_argument("--no-extras", action="store_true",
+                   help="N=1: skip the store and layer-wise push measurements added to the line")
     p.add_argument("--kv-port", type=int, default=24600, help="first handshake port of the e2e connectors")
     p.add_argument("--peer-device", type=int, default=None,
                    help="N=1 only: put the destination cache on this GPU (one process, peer access over NVLink)")
@@ -1876,10 +1928,6 @@ def main(argv=None):
                    help="measure the per-layer push beside a synthetic prefill (exposed transfer time)")
     p.add_argument("--store", action="store_true", help="measure the per-token cache store (and fused push)")
     p.add_argument("--serial", action="store_true", help="with --store: plain launches (KVX_STORE_SERIAL)")
-    p.add_argument("--store-engine", choices=["bulk", "vector"], default="bulk",
-                   help="with --store: the bulk-copy store (default where it applies) or the vector one")
-    p.add_argument("--store-stages", type=int, default=0, help="with --store: the bulk-copy store's ring depth")
-    p.add_argument("--store-tpc", type=int, default=0, help="with --store: tokens per bulk-copy stage (power of 2)")
     p.add_argument("--fused", action="store_true",
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals at 1-64 requests/s")

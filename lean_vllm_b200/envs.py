@@ -21,6 +21,9 @@ environment_variables: dict[str, Callable[[], Any]] = {
     # prefill the two are within run-to-run noise (0.5-0.9 % exposed), so the simpler one is the default.
     "LEAN_VLLM_KVX_FUSED_ASYNC": lambda: os.getenv("LEAN_VLLM_KVX_FUSED_ASYNC", "0").strip().lower()
     not in ("", "0", "false"),
+    # Loads planned in one pass of the transfer thread share one copy launch until they add up to this many bytes
+    # (the first load of a pass that finds the device idle launches at once, for its latency).
+    "LEAN_VLLM_KVX_BATCH_BYTES": lambda: int(os.getenv("LEAN_VLLM_KVX_BATCH_BYTES", str(64 << 20))),
     # SMs a per-layer save's copy may use while the prefill computes (0: every SM).
     "LEAN_VLLM_KVX_SAVE_SMS": lambda: int(os.getenv("LEAN_VLLM_KVX_SAVE_SMS", "16")),
 }

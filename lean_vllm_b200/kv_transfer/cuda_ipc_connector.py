@@ -50,7 +50,6 @@ HANDSHAKE_TIMEOUT = 5.0  # ZMQ never refuses a connect; an absent producer is on
 IDLE_WAIT = 0.01  # the transfer thread's longest sleep: deadlines are checked at least this often
 BELL_WAIT = 0.001  # its sleep with copies in flight whose completion rings its doorbell (a safety net only)
 BUSY_WAIT = 0.0002  # and with copies in flight on a transport without a doorbell, which it must poll
-BATCH_BYTES = 64 << 20  # loads planned in one pass share a launch until they add up to this much
 RELAY_WAIT = 60.0  # seconds a relayed load waits for its peer decode ranks' parts before it fails
 
 
@@ -910,7 +909,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 batch.append((load, tables, jobs, ready))
                 # Launch as soon as the batch is big enough to keep the GPU busy while the next loads are planned;
                 # only small loads share a launch.
-                if sum(entry[0].num_bytes for entry in batch) >= BATCH_BYTES:
+                if sum(entry[0].num_bytes for entry in batch) >= envs.LEAN_VLLM_KVX_BATCH_BYTES:
                     self._post_loads(batch)
                     batch.clear()
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving

@@ -265,3 +265,53 @@ def test_a_peers_only_store_writes_the_peers_and_not_the_local_cache():
     mapped = np.where(s >= 0, table[np.clip(s, 0, None) // 256].astype(np.int64) * 256 + s % 256, -1)
     oracle_store(bits(key), bits(value), ev[0], ev[1], mapped)
     assert np.array_equal(bits(peer), expected)
+
+
+@pytest.mark.parametrize("tokens, heads, dim, block, layout, strided", [
+    (8192, 8, 128, 256, "HND", False),  # a Qwen3-8B prefill step: full stages of 8 tokens
+    (777, 8, 128, 256, "HND", False),   # a last stage with 1 token
+    (300, 4, 128, 64, "NHD", False),    # NHD: a token's heads together, one bulk store per row
+    (513, 2, 64, 16, "HND", True),      # rows strided across tokens (a fused qkv): one load per token
+    (5, 8, 128, 256, "HND", False),     # fewer tokens than SMs
+])
+def test_the_store_matches_the_oracle_across_shapes(tokens, heads, dim, block, layout, strided):
+    """The store on a Qwen3-8B prefill step, ragged token counts, NHD, rows strided across tokens and fewer tokens
+    than SMs, each against the oracle's store on a host copy: padding slots skipped, everything else in place, the
+    status word clear."""
+    g = torch.Generator(device="cuda").manual_seed(tokens + heads)
+    if strided:
+        qkv = torch.randn(tokens, 3 * heads, dim, generator=g, device="cuda").to(torch.bfloat16)
+        key, value = qkv[:, heads : 2 * heads], qkv[:, 2 * heads :]
+    else:
+        key = torch.randn(tokens, heads, dim, generator=g, device="cuda").to(torch.bfloat16)
+        value = torch.randn(tokens, heads, dim, generator=g, device="cuda").to(torch.bfloat16)
+    blocks = -(-tokens // block) + 3
+    shape = (2, blocks, heads, block, dim) if layout == "HND" else (2, blocks, block, heads, dim)
+    cache = torch.randn(*shape, generator=g, device="cuda").to(torch.bfloat16)
+    slots = torch.randperm(blocks * block, generator=g, device="cuda")[:tokens]
+    slots[::13] = -1
+    expected = bits(cache).copy()
+    ev = expected.swapaxes(2, 3) if layout == "HND" else expected
+    oracle_store(bits(key.contiguous()), bits(value.contiguous()), ev[0], ev[1], slots.cpu().numpy())
+    view = cache.transpose(2, 3) if layout == "HND" else cache
+    word = transport.StatusWord()
+    store_kvcache(key, value, view[0], view[1], slots, status=word.address)
+    torch.cuda.synchronize()
+    assert word.bits() == 0
+    word.close()
+    assert np.array_equal(bits(cache), expected)
+
+
+def test_a_prefill_step_of_latents_stores_like_the_oracle():
+    from oracle.kv_oracle import store_latents as oracle_latents
+
+    g = torch.Generator(device="cuda").manual_seed(17)
+    latent = torch.randn(2049, 576, generator=g, device="cuda").to(torch.bfloat16)
+    cache = torch.randn(1, 40, 64, 576, generator=g, device="cuda").to(torch.bfloat16)
+    slots = torch.randperm(40 * 64, generator=g, device="cuda")[:2049]
+    slots[7::101] = -1
+    expected = bits(cache).copy()
+    oracle_latents(bits(latent), expected[0], slots.cpu().numpy())
+    store_latents(latent, cache[0], slots)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(cache), expected)
