@@ -299,11 +299,6 @@ def plan(spec: Workload, role: Role, reqs, mode: str):
 RELAY_CHUNKS = 8  # request chunks a relayed step is pipelined over
 
 
-def relay_chunk_count(n_requests: int) -> int:
-    """How many request chunks a relayed step has: every rank takes one barrier per chunk, so all must agree."""
-    return len(range(0, n_requests, max(1, -(-n_requests // RELAY_CHUNKS))))
-
-
 def plan_relay(spec: Workload, role: Role, reqs):
     """A decode rank's relayed latent load (LEAN_VLLM_KVX_RELAY): (peers, its own part of every request's blocks
     from the prefill rank, the other decode ranks' parts from them). Parts are contiguous 1/decode_tp slices of each
@@ -522,23 +517,39 @@ def run_gpu(args) -> None:
     sid = stream.cuda_stream
     peer_stream = torch.cuda.Stream(device=launch_device)  # relayed: the copies from peer decode ranks
 
+    # Relayed: one interprocess event per chunk on each decode rank, recorded once its own part of the chunk has
+    # landed; its peers' second stream waits on it (on the GPU) before pulling that part from it. The host only
+    # agrees that every rank recorded this step's events before any wait is enqueued -- it never waits for a copy.
+    chunk_events, peer_events = [], []
+    if relay:
+        if role.side == "decode":
+            chunk_events = [torch.cuda.Event(interprocess=True) for _ in relay_chunks]
+        handles = [None] * world
+        dist.all_gather_object(handles, (role.group, role.side, role.tp_rank,
+                                         [e.ipc_handle() for e in chunk_events]), group=gloo)
+        if role.side == "decode":
+            peer_events = [[torch.cuda.Event.from_ipc_handle(launch_device, h) for h in hs]
+                           for g, side, r, hs in handles if g == role.group and side == "decode" and r != role.tp_rank]
+
     def step():
         if not relay:
             if jobs:
                 transport.copy(caches, jobs, sid, copy_flags)
             return
-        # Pipelined by chunks of requests: a chunk's parts go from the peers (second stream) once every decode
-        # rank's own part of it landed (host barrier), while the next chunk's own parts come from the prefill rank.
-        chunks = relay_chunks or [([], [])] * relay_chunk_count(len(reqs))
-        for c in range(len(chunks) + 1):
-            if c:
-                stream.synchronize()
-                dist.barrier(group=gloo)
-            if c < len(chunks) and chunks[c][0]:
-                transport.copy(caches, chunks[c][0], sid, copy_flags)
-            if c and chunks[c - 1][1]:
-                transport.copy(caches, chunks[c - 1][1], peer_stream.cuda_stream, copy_flags)
+        # Pipelined by chunks of requests: every own part goes out from the prefill rank on the first stream, each
+        # followed by its event; a chunk's parts from the peers go on the second stream once their events passed.
+        for (own, _), event in zip(relay_chunks, chunk_events):
+            if own:
+                transport.copy(caches, own, sid, copy_flags)
+            event.record(stream)
+        dist.barrier(group=gloo)  # every decode rank has recorded this step's events
+        for c, (_, others) in enumerate(relay_chunks):
+            for events in peer_events:
+                peer_stream.wait_event(events[c])
+            if others:
+                transport.copy(caches, others, peer_stream.cuda_stream, copy_flags)
         stream.wait_stream(peer_stream)  # the step ends when both streams have
+        dist.barrier(group=gloo)  # every wait is enqueued before any rank records the events again
 
     def barrier():
         torch.cuda.synchronize()
@@ -743,7 +754,9 @@ def run_gpu(args) -> None:
                            "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
                                     "get_finished() until every load finished_recving; one kvx launch per load, "
                                     "block ids carried in the launch, the transfer thread woken by a doorbell when "
-                                    "each copy lands")}
+                                    "each copy lands; each transfer's result read from its status word in mapped "
+                                    "host memory (written by the device only on failure), so no device-to-host "
+                                    "copy is made")}
         line.update(extras)
         if loopback and not peer_mode and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(reqs, spec, seconds=args.cpu_seconds)
