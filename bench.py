@@ -599,16 +599,19 @@ def run_gpu(args) -> None:
     # Correctness over every byte the step moved: every block of every request, each decode rank's heads against
     # the producer rank that holds them. One GPU: the blocks compared outright. N GPUs: per-(layer, part, block)
     # digests of each share computed on both sides and compared.
-    ok = True
     all_src = np.concatenate([s for s, _ in reqs])
     all_dst = np.concatenate([d for _, d in reqs])
-    if loopback:
-        s_index = torch.as_tensor(all_src, dtype=torch.long, device=src[0].device)
-        d_index = torch.as_tensor(all_dst, dtype=torch.long, device=dst[0].device)
-        for a, b in zip(src, dst):
-            ok &= bool(torch.equal(a.index_select(1, s_index), b.index_select(1, d_index).to(a.device)))
-        checked = int(len(all_src) * len(src))
-    elif world > 1:
+
+    def verify() -> tuple[bool, int]:
+        ok = True
+        if loopback:
+            s_index = torch.as_tensor(all_src, dtype=torch.long, device=src[0].device)
+            d_index = torch.as_tensor(all_dst, dtype=torch.long, device=dst[0].device)
+            for a, b in zip(src, dst):
+                ok &= bool(torch.equal(a.index_select(1, s_index), b.index_select(1, d_index).to(a.device)))
+            return ok, int(len(all_src) * len(src))
+        if world == 1:
+            return ok, 0
         mine_digests = {}
         if role.side == "decode":
             for i, sh in enumerate(head_shares(role.tp_rank, spec.decode_tp, spec.prefill_tp, heads)):
@@ -631,15 +634,23 @@ def run_gpu(args) -> None:
             want = {k: v for g, side, d in every if g == group and side == "prefill" for k, v in d.items()}
             ok &= bool(got) and got.keys() == want.keys() and all(torch.equal(got[k], want[k]) for k in got)
             checked += sum(v.shape[0] * v.shape[2] for v in got.values())
-    else:
-        checked = 0
+        return ok, checked
+
+    ok, checked = verify()
 
     # e2e: the same loads through the connector's public API.
     e2e_ms, e2e_bytes = None, 0
+    e2e_ok = None
     if args.steps and not args.no_e2e and not peer_mode:
+        # The decode caches start from zeros, so the check after these loads sees what the connector moved.
+        if dst is not None:
+            for layer in dst:
+                layer.zero_()
+            torch.cuda.synchronize(dst[0].device)
         e2e_launches0 = transport.launch_count()
         e2e_ms, e2e_bytes = e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo)
         e2e_launches = transport.launch_count() - e2e_launches0
+        e2e_ok, _ = verify()
         e = torch.tensor([e2e_ms, float(e2e_bytes)], device=device, dtype=torch.float64)
         if world > 1:
             gathered = [torch.zeros_like(e) for _ in range(world)]
@@ -649,7 +660,8 @@ def run_gpu(args) -> None:
             e_all = e.cpu().numpy()[None]
         e2e_ms, e2e_bytes = float(e_all[:, 0].max()), int(e_all[:, 1].sum())
 
-    ok_t = torch.tensor([0.0 if ok else 1.0], device=device, dtype=torch.float64)
+    ok_t = torch.tensor([0.0 if ok else 1.0, 0.0 if e2e_ok in (True, None) else 1.0], device=device,
+                        dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ok_t, op=dist.ReduceOp.MAX)
     clock_summary = clocks.summary()
@@ -738,7 +750,7 @@ def run_gpu(args) -> None:
             "roofline": roofline,
             "gpu_launches": total_launches,
             "clocks": clock_summary,
-            "correct": bool(ok_t.item() == 0.0),
+            "correct": bool(ok_t[0].item() == 0.0),
             "correct_covers": (f"every moved block of every request ({checked} (layer, block) pairs"
                                + (": compared outright)" if loopback else
                                   ": per-(layer, part, block) digests of each head share on both sides)")),
@@ -750,7 +762,10 @@ def run_gpu(args) -> None:
                            "h2d_bytes_per_step": ids_bytes, "d2h_bytes_per_step": 0,
                            "bytes_reported_by_connector": e2e_bytes,
                            "kvx_launches_per_step": round(e2e_launches / (1 + max(args.steps // 2, 2)), 1),
-                           "batch_bytes": int(os.environ.get("LEAN_VLLM_KVX_BATCH_BYTES", str(64 << 20))),
+                           "correct": bool(ok_t[1].item() == 0.0),
+                           "correct_covers": "every moved block again, checked after these loads into zeroed "
+                                             "decode caches",
+                           "batch_bytes": envs.LEAN_VLLM_KVX_BATCH_BYTES,
                            "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
                                     "get_finished() until every load finished_recving; one kvx launch per load, "
                                     "block ids carried in the launch, the transfer thread woken by a doorbell when "
@@ -766,6 +781,9 @@ def run_gpu(args) -> None:
         for blob in opened:
             transport.close_mapping(blob)
         dist.destroy_process_group()
+
+
+from lean_vllm_b200 import envs  # noqa: E402
 
 
 def child_line(argv: list[str], timeout: float = 600.0) -> dict:

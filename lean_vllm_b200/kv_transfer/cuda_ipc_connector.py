@@ -5,7 +5,8 @@ half, the kv_transfer_params it returns, the handshake on kv_port + rank, the he
 tensor-parallel sizes, reader counting and the release/expiry rules are the reference's. What changes is below the
 worker: instead of registering memory with a NIXL agent and posting one-sided READs, each rank exports its cache
 through CUDA IPC in the handshake reply, maps the producer ranks' caches, and posts one kvx kernel launch per load
-(the loads of one step, planned together, share launches up to 64 MB), which gathers the shares' blocks from every
+(a load finding none of the rank's copies in flight launches at once; behind copies in flight, the loads planned in
+one pass share launches of up to 2 GiB), which gathers the shares' blocks from every
 producer rank's HBM over NVLink and scatters them into its own blocks.
 The launch waits on the stream for the load's ready event (no host synchronisation); a native watcher rings an
 eventfd once the copy's event completes, and the transfer thread sleeps on that, its ZMQ socket and its work queue
@@ -907,13 +908,18 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 return
             if jobs:
                 batch.append((load, tables, jobs, ready))
-                # Launch as soon as the batch is big enough to keep the GPU busy while the next loads are planned;
-                # only small loads share a launch.
-                if sum(entry[0].num_bytes for entry in batch) >= envs.LEAN_VLLM_KVX_BATCH_BYTES:
+                # A load that finds none of this rank's copies in flight launches at once: its latency is the
+                # device's alone. Behind copies in flight, loads share launches of up to BATCH_BYTES: fewer launches
+                # leave fewer ramps and tails between them, and the device stays busy while later loads are planned.
+                if (sum(entry[0].num_bytes for entry in batch) >= envs.LEAN_VLLM_KVX_BATCH_BYTES
+                        or not self._copies_in_flight()):
                     self._post_loads(batch)
                     batch.clear()
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
             self._fail(load, error)
+
+    def _copies_in_flight(self) -> bool:
+        return any(load.transfer is not None and not load.transfer.done for load in self._loads.values())
 
     def _job_bytes(self, remote: _Remote, job: CopyJob) -> int:
         """What the job moves: the reference's descriptor-length sum (nixl_connector.py:421). The bytes of one block
@@ -1456,16 +1462,14 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             close = False
             try:
                 if entry.fences is None:
-                    entry.fences = []
-                    for stream in ({}, {"save": True}, {"relay": True}):
-                        entry.fences.append(self.transport.post([], [], entry.marker, **stream))
+                    entry.fences = list(self.transport.fences(entry.marker))
                     continue
                 if not all(self.transport.done(fence) for fence in entry.fences):
                     continue
                 close = True
             except Exception as error:  # noqa: BLE001 - a mapping kept open is harmless; one closed early is not
                 logger.warning("keeping a replaced KV mapping open: %s", error)
-            for fence in entry.fences:
+            for fence in entry.fences or []:  # none when the transport refused to post them
                 self.transport.release(fence)
             if close:
                 self.transport.close(entry.remote.exported)

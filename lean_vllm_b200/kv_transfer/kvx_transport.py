@@ -35,7 +35,10 @@ class KvxTransport:
         # A per-layer save runs beside the prefill's kernels: hold it to a few SMs.
         self.save_flags = _native.flags(engine, sm_budget=min(max(envs.LEAN_VLLM_KVX_SAVE_SMS, 0), 255))
         with torch.cuda.device(self.device):
-            self.stream = torch.cuda.Stream(device=self.device)
+            # Loads alternate between two streams: each writes its own blocks, so a launch may start while the one
+            # before it drains, and a launch's tail no longer leaves SMs idle between consecutive loads.
+            self.load_streams = [torch.cuda.Stream(device=self.device), torch.cuda.Stream(device=self.device)]
+            self._lane = 0
             # Per-layer saves go first when SMs free up between the prefill's kernels.
             self.save_stream = torch.cuda.Stream(device=self.device, priority=-10)
             # A relayed load's copy from peer decode ranks runs beside the next loads' copies from the producer.
@@ -103,13 +106,28 @@ class KvxTransport:
         restricts every cache to one layer's regions. A push of a save (`save`) runs on the high-priority save
         stream, in order with the save's earlier pushes (a block pushed again must land after its older copy);
         `flags` holds a per-layer push to its SM budget. A relayed load's copy from its peers (`relay`) runs on a
-        stream of its own, beside later loads' copies from the producer."""
+        stream of its own, beside later loads' copies from the producer. Other loads alternate between the two load
+        streams."""
         event = ready.cuda_event if ready is not None else 0
-        stream = self.save_stream if save else self.relay_stream if relay else self.stream
+        if save or relay:
+            stream = self.save_stream if save else self.relay_stream
+        else:
+            stream = self.load_streams[self._lane]
+            self._lane ^= 1
+        return self._post_on(stream, tables, jobs, event, layer, flags)
+
+    def _post_on(self, stream, tables, jobs, event, layer=None, flags=None) -> transport.Transfer:
         xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags)
         self.doorbell.ring_after(stream.cuda_stream)
         return xfer
+
+    def fences(self, ready) -> list:
+        """One empty transfer after `ready` on every stream this transport copies on: once all have completed,
+        nothing queued before `ready` on any of them still reads or writes a peer's memory."""
+        event = ready.cuda_event if ready is not None else 0
+        return [self._post_on(s, [], [], event)
+                for s in (*self.load_streams, self.save_stream, self.relay_stream)]
 
     def fence(self, ready) -> transport.Transfer:
         """A transfer of nothing that completes once `ready` has: what a save whose layers were all stored fused

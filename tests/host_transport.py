@@ -120,6 +120,10 @@ class HostTransport:
         self.pending[handle] = [1]  # done on the second poll
         return handle
 
+    def fences(self, ready):
+        """An empty post per stream the GPU transport copies on (two load streams, save, relay)."""
+        return [self.post([], [], ready) for _ in range(4)]
+
     def fence(self, ready):
         """Host stores are synchronous: a handle that completes like a post's, copying nothing."""
         handle = next(self.ids)

@@ -227,7 +227,7 @@ def test_a_restarted_producer_is_asked_afresh_and_the_old_mapping_closed(sides):
     assert transport.opened == 1 and not consumers[0]._retired
     (exported, posts_by_then), = transport.closed
     assert exported["spans"] == [list(span) for span in first[0].transport.spans]  # the first producer's
-    assert transport.posts[posts_by_then - 3 : posts_by_then] == [(None, 0)] * 3  # a fence on every stream first
+    assert transport.posts[posts_by_then - 4 : posts_by_then] == [(None, 0)] * 4  # a fence on every stream first
     assert torch.equal(consumers[0].kv_caches[0][:, 1], rank_cache(full_cache(2, False), 0, 1)[:, 4])
 
 
