@@ -1401,6 +1401,9 @@ def run_poisson(args) -> None:
                                 "mean_ms": round(float(np.mean(latency)), 3),
                                 # the connector's own stats: from posting the copy to seeing it landed
                                 "p50_posted_to_landed_ms": round(float(np.percentile(in_flight, 50)), 3),
+                                # the host path around the copy: start_load_kv to posting, and landing to the
+                                # get_finished that reports it
+                                "p50_host_ms": round(float(np.percentile(np.subtract(latency, in_flight), 50)), 3),
                                 "offered_gb_per_s": round(moved / float(arrivals[-1]) / 1e9, 2),
                                 "moved_gb_per_s": round(moved / wall / 1e9, 2), "bytes": moved,
                                 "mean_prompt_tokens": int(lengths.mean())})

@@ -911,8 +911,9 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 # A load that finds none of this rank's copies in flight launches at once: its latency is the
                 # device's alone. Behind copies in flight, loads share launches of up to BATCH_BYTES: fewer launches
                 # leave fewer ramps and tails between them, and the device stays busy while later loads are planned.
+                # A relayed load launches at once too: its peers wait for its part to land before they copy theirs.
                 if (sum(entry[0].num_bytes for entry in batch) >= envs.LEAN_VLLM_KVX_BATCH_BYTES
-                        or not self._copies_in_flight()):
+                        or load.relay is not None or not self._copies_in_flight()):
                     self._post_loads(batch)
                     batch.clear()
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
