@@ -296,7 +296,7 @@ def plan(spec: Workload, role: Role, reqs, mode: str):
     return peers, jobs
 
 
-RELAY_CHUNKS = 8  # request chunks a relayed step is pipelined over
+RELAY_CHUNKS = 8  # request chunks a relayed step is pipelined over (--relay-chunks)
 
 
 def plan_relay(spec: Workload, role: Role, reqs):
@@ -492,7 +492,7 @@ def run_gpu(args) -> None:
     relay_jobs = []
     relay_chunks = []  # (own-part jobs, peer-part jobs) per chunk of the step's requests
     if relay and role.side == "decode":
-        chunk = max(1, -(-len(reqs) // RELAY_CHUNKS))
+        chunk = max(1, -(-len(reqs) // (args.relay_chunks or RELAY_CHUNKS)))
         for first in range(0, len(reqs), chunk):
             peers, own, others = plan_relay(spec, role, reqs[first : first + chunk])
             relay_chunks.append((own, others))
@@ -742,6 +742,7 @@ def run_gpu(args) -> None:
                 "payload_bytes_per_step": int(step_bytes_total),
                 "groups": groups,
                 "mode": "loopback" if loopback else args.mode + (" relayed" if relay else ""),
+                "relay_chunks": (args.relay_chunks or RELAY_CHUNKS) if relay else None,
                 "engine": args.engine,
                 "parallelism": ("1 GPU" if loopback else
                                 f"{groups} independent prefill TP{spec.prefill_tp} -> decode TP{spec.decode_tp} groups"),
@@ -1966,6 +1967,7 @@ def main(argv=None):
                    help="with --layerwise: each layer stores new rows through store_kv, which pushes them too")
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals at 1-64 requests/s")
     p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
+    p.add_argument("--relay-chunks", type=int, default=0, help="with --relay: request chunks per step (0: 8)")
     p.add_argument("--relay", action="store_true",
                    help="MLA workload: each decode rank pulls its part from the prefill rank, the rest from its peers")
     p.add_argument("--copy-engine", action="store_true",
