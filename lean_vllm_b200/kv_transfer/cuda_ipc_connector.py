@@ -52,6 +52,7 @@ IDLE_WAIT = 0.01  # the transfer thread's longest sleep: deadlines are checked a
 BELL_WAIT = 0.001  # its sleep with copies in flight whose completion rings its doorbell (a safety net only)
 BUSY_WAIT = 0.0002  # and with copies in flight on a transport without a doorbell, which it must poll
 RELAY_WAIT = 60.0  # seconds a relayed load waits for its peer decode ranks' parts before it fails
+RELAY_RING = 64  # slots of a decode rank's ring of relay events (kvx_transport.RELAY_RING)
 
 
 def _cdiv(a: int, b: int) -> int:
@@ -229,6 +230,7 @@ class _Remote:
     table: object  # the transport's view of the peer rank's cache, mapped into this process
     sock: object  # DEALER kept open for notifications
     per_block: dict = field(default_factory=dict)  # (share, latents) -> bytes one block of a load moves
+    ring: list = field(default_factory=list)  # a peer decode rank's relay events, opened here (relayed loads)
 
 
 @dataclass(slots=True)
@@ -262,6 +264,10 @@ class _Relay:
     parts: list  # (first, end) block positions of each decode rank's part
     transfer: _Batch | None = None  # the copy of the peers' parts
     waiting_since: float = field(default_factory=monotonic)
+    ready: object = None  # the load's ready event: the peers' copy writes the same freshly allocated blocks
+    own_done: bool = False  # this rank's own part has landed (or it had none)
+    copied: bool = False  # the copy of the peers' parts has landed (or there was nothing to copy)
+    peer_failed: bool = False  # a peer's part failed or never came: the load fails once nothing of it is in flight
 
 
 @dataclass(slots=True)
@@ -270,6 +276,7 @@ class _Load:
 
     req: ReqToRecv
     transfer: _Batch | None = None
+    request_id: str = ""
     notify: list = field(default_factory=list)  # (remote key, message, rank) to send once the bytes have landed
     unnotified: set = field(default_factory=set)  # producer ranks no notification has reached
     started: float = field(default_factory=monotonic)
@@ -368,6 +375,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
         self._relays: dict[str, _Load] = {}  # transfer thread only: loads past their own part, waiting for peers'
         self._parts: dict[str, dict] = {}  # request -> {decode rank: its part landed}; under the lock
+        self._part_slots: dict[str, dict] = {}  # request -> {decode rank: ring slot marking its part, -1: none}
+        self._ring_next = 0  # the next slot of this rank's relay ring (transfer thread only)
         self._parts_seen: dict[str, float] = {}  # request -> when its first part message came (transfer thread)
         self._block_maps: dict[tuple, object] = {}  # decode instance -> local block id -> its block id (engine thread)
         self._map_updates: list = []  # (instance, local ids, remote ids or None) for the engine thread to apply
@@ -539,6 +548,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         wake, self._wake = self._wake, -1
         os.close(wake)
         self._context.term()
+
+    def _relaying(self) -> bool:
+        """Latent-only loads on a decode instance of several ranks are relayed (LEAN_VLLM_KVX_RELAY)."""
+        return self.relay and self.tp_size > 1 and self.num_heads == 0
 
     def _heads(self, req) -> int:
         return split_heads(self.num_heads, self.tp_size, req.remote_tp_size)
@@ -816,10 +829,13 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if request_id is not None:
                 self._connect(request_id)
             return
-        if op == "part":
-            request = str(message.get("request"))
+        if op == "part":  # a peer decode rank posted its part (its ring slot), or its part landed (ok or not)
+            request, rank = str(message.get("request")), int(message.get("rank", -1))
             with self._lock:
-                self._parts.setdefault(request, {})[int(message.get("rank", -1))] = bool(message.get("ok"))
+                if "slot" in message:
+                    self._part_slots.setdefault(request, {})[rank] = int(message["slot"])
+                if "ok" in message:
+                    self._parts.setdefault(request, {})[rank] = bool(message["ok"])
             self._parts_seen.setdefault(request, monotonic())
             return
         if op == "saved":
@@ -838,6 +854,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 "exported": self.transport.exported,
                 "node": self.node,
             }
+            if self._relaying():
+                reply["relay_ring"] = self.transport.relay_ring()
         else:
             reply = {"ok": False, "error": f"unknown op {op!r}"}
         try:
@@ -863,15 +881,15 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         if getattr(req, "pushed", False):
             self._start_wait(request_id, req)
             return
-        load = self._loads[request_id] = _Load(req)
+        load = self._loads[request_id] = _Load(req, request_id=request_id)
         try:
             heads = self._heads(req)
             shares: list[Share] = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
             load.unnotified = {share.remote_rank for share in shares}
-            if self.relay and self.tp_size > 1 and self.num_heads == 0:
+            if self._relaying():
                 # Latents are whole on every decode rank: this rank pulls its part from the prefill rank and the
                 # others' parts from them, so each byte crosses the prefill GPU's links once.
-                load.relay = _Relay(relay_parts(len(req.local_block_ids), self.tp_size))
+                load.relay = _Relay(relay_parts(len(req.local_block_ids), self.tp_size), ready=ready)
                 for peer in range(self.tp_size):
                     if peer != self.rank:
                         self._handshake(self._peer_req(), peer)
@@ -902,9 +920,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 load.notify.append((key, message, share.remote_rank))
                 load.num_bytes += nbytes
             load.started = monotonic()
-            if not jobs and load.relay is not None:
+            if not jobs and load.relay is not None:  # an empty part: nothing to mark, nothing to land
                 del self._loads[request_id]
-                self._part_landed(request_id, load)  # an empty part: straight to the peers' parts
+                self._relay_posted(load, -1)
+                self._relay_landed(load)
                 return
             if jobs:
                 batch.append((load, tables, jobs, ready))
@@ -961,14 +980,20 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                         index[id(table)] = len(tables)
                     jobs.append(CopyJob(index[id(table)], 0, job.src_block_ids, job.dst_block_ids, job.src_first_head,
                                         job.dst_first_head, job.num_heads, job.latents))
+            relayed = [load for load, *_ in entries if load.relay is not None]
+            slot = None
+            if relayed:  # the launch is marked in this rank's ring, so the peers' copies of its part wait on the GPU
+                slot, self._ring_next = self._ring_next, (self._ring_next + 1) % RELAY_RING
             try:
-                shared = _Batch(self.transport.post(tables, jobs, entries[0][3]), len(entries))
+                shared = _Batch(self.transport.post(tables, jobs, entries[0][3], mark=slot), len(entries))
             except Exception as error:  # noqa: BLE001 - refused when posted: these loads fail, producers hear now
                 for load, *_ in entries:
                     self._fail(load, error)
                 continue
             for load, *_ in entries:
                 load.transfer = shared
+            for load in relayed:
+                self._relay_posted(load, slot)
 
     def _poll(self):
         notes: dict[tuple, list] = {}  # producer rank -> the notifications of every load this pass finished
@@ -990,8 +1015,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     continue
                 self._fail(load, RuntimeError(f"finishing the load failed: {error}"), in_flight=True)
             del self._loads[request_id]
-            if load.relay is not None and not load.failed:
-                self._part_landed(request_id, load)
+            if load.relay is not None and request_id in self._relays:
+                self._relay_landed(load)  # the rest of the load is _poll_relays'
                 continue
             self._finish_load(request_id, load)
 
@@ -1035,6 +1060,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._send_part(request_id, False)  # the peers' loads fail too, and prefill as this one does
             with self._lock:
                 self._parts.pop(request_id, None)
+                self._part_slots.pop(request_id, None)
             self._parts_seen.pop(request_id, None)
         with self._lock:
             if load.failed:
@@ -1057,14 +1083,28 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._send((kv.kv_ip, kv.kv_port + peer), {"op": "part", "request": request_id, "rank": self.rank,
                                                              "ok": ok})
 
-    def _part_landed(self, request_id: str, load: _Load):
-        self._send_part(request_id, True)
+    def _relay_posted(self, load: _Load, slot: int):
+        """Own part launched (marked with `slot` of this rank's ring; -1: nothing to wait for): the peers may queue
+        their copies of it now, and this load is _poll_relays' from here on."""
+        kv = self.kv_transfer
+        for peer in range(self.tp_size):
+            if peer != self.rank:
+                self._send((kv.kv_ip, kv.kv_port + peer), {"op": "part", "request": load.request_id,
+                                                             "rank": self.rank, "slot": slot})
         load.relay.waiting_since = monotonic()
-        self._relays[request_id] = load
+        self._relays[load.request_id] = load
+
+    def _relay_landed(self, load: _Load):
+        """Own part landed: the peers learn whether their copies of it hold the producer's bytes."""
+        load.relay.own_done = True
+        self._send_part(load.request_id, not load.failed)
 
     def _poll_relays(self):
+        """Relayed loads past their own part's launch. The copy of the peers' parts is queued as soon as every peer
+        has said where its part's launch is marked (its ring slot), and waits for those marks and for the load's
+        ready event on the GPU. The load ends once its own part and that copy have landed and every peer has said
+        its part landed; any failure fails it on every rank, once nothing of it is still in flight."""
         timeout = RELAY_WAIT
-        kv = self.kv_transfer
         now = monotonic()
         for request_id, seen in list(self._parts_seen.items()):
             # Parts for a load this rank finished (or never had) long ago: nobody will read them.
@@ -1072,40 +1112,27 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 del self._parts_seen[request_id]
                 with self._lock:
                     self._parts.pop(request_id, None)
+                    self._part_slots.pop(request_id, None)
+        peers = [r for r in range(self.tp_size) if r != self.rank]
         for request_id, load in list(self._relays.items()):
             relay = load.relay
-            if relay.transfer is None:
-                with self._lock:
-                    got = dict(self._parts.get(request_id, {}))
-                peers = [r for r in range(self.tp_size) if r != self.rank]
-                if any(got.get(r) is False for r in peers):
-                    load.failed = True
-                    logger.warning("a peer decode rank could not load its part of %s, so it prefills here",
-                                   load.req.remote_request_id)
-                elif all(r in got for r in peers):
-                    tables, jobs = [], []
-                    local = list(load.req.local_block_ids)
-                    for r in peers:
-                        first, end = relay.parts[r]
-                        if end > first:
-                            tables.append(self._remotes[(kv.kv_ip, kv.kv_port + r)].table)
-                            jobs.append(CopyJob(len(tables), 0, local[first:end], local[first:end], 0, 0, 0, True))
-                    if jobs:
-                        try:
-                            # Its own part landed after the load's ready event, so the blocks are free to write.
-                            relay.transfer = _Batch(self.transport.post(tables, jobs, None, relay=True), 1)
-                            continue
-                        except Exception as error:  # noqa: BLE001
-                            logger.warning("copying the peers' parts of %s failed: %s", load.req.remote_request_id,
-                                           error)
-                            load.failed = True
-                elif relay.waiting_since + timeout < monotonic():
-                    load.failed = True
+            with self._lock:
+                landed = dict(self._parts.get(request_id, {}))
+                slots = dict(self._part_slots.get(request_id, {}))
+            # A peer's failure is kept apart from this rank's own: its own part still lands and notifies the
+            # producer, and the load fails when it ends.
+            if any(landed.get(r) is False for r in peers) and not relay.peer_failed:
+                relay.peer_failed = True
+                logger.warning("a peer decode rank could not load its part of %s, so it prefills here",
+                               load.req.remote_request_id)
+            if relay.transfer is None and not relay.copied and not load.failed and not relay.peer_failed:
+                if all(r in slots for r in peers):
+                    self._copy_peer_parts(load, slots)
+                elif relay.waiting_since + timeout < now:
+                    relay.peer_failed = True
                     logger.warning("the peer decode ranks never reported their parts of %s",
                                    load.req.remote_request_id)
-                else:
-                    continue
-            else:
+            if relay.transfer is not None:
                 try:
                     if not self.transport.done(relay.transfer.xfer):
                         continue
@@ -1115,8 +1142,46 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     load.failed = True
                 self.transport.release(relay.transfer.xfer)
                 relay.transfer = None
+                relay.copied = True
+            if not relay.own_done:
+                continue  # its own copy may still write the blocks
+            healthy = not load.failed and not relay.peer_failed
+            if healthy and not relay.copied:
+                continue
+            if healthy and not all(landed.get(r) is True for r in peers):
+                if relay.waiting_since + timeout >= now:
+                    continue
+                relay.peer_failed = True
+                logger.warning("the peer decode ranks never said their parts of %s landed",
+                               load.req.remote_request_id)
+            load.failed = load.failed or relay.peer_failed
             del self._relays[request_id]
             self._finish_load(request_id, load)
+
+    def _copy_peer_parts(self, load: _Load, slots: dict):
+        """Queues the copy of every peer's part from its cache into this rank's blocks, after the peers' ring marks
+        and the load's ready event."""
+        kv = self.kv_transfer
+        relay = load.relay
+        tables, jobs, marks = [], [], []
+        local = list(load.req.local_block_ids)
+        for r, slot in sorted(slots.items()):
+            first, end = relay.parts[r]
+            if end <= first:
+                continue
+            remote = self._remotes[(kv.kv_ip, kv.kv_port + r)]
+            tables.append(remote.table)
+            jobs.append(CopyJob(len(tables), 0, local[first:end], local[first:end], 0, 0, 0, True))
+            if slot >= 0 and remote.ring:
+                marks.append(remote.ring[slot])
+        if not jobs:
+            relay.copied = True
+            return
+        try:
+            relay.transfer = _Batch(self.transport.post(tables, jobs, relay.ready, relay=True, after=marks), 1)
+        except Exception as error:  # noqa: BLE001
+            logger.warning("copying the peers' parts of %s failed: %s", load.req.remote_request_id, error)
+            load.failed = True
 
     def _send(self, key, message: dict):
         remote = self._remotes.get(key)
@@ -1138,9 +1203,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
     def _fail(self, load: _Load, error: Exception, in_flight: bool = False):
         req = load.req
         if load.relay is not None and not load.failed:
-            request_id = next((rid for rid, entry in self._loads.items() if entry is load), None)
-            if request_id is not None:
-                self._send_part(request_id, False)
+            self._send_part(load.request_id, False)
         if not load.failed:
             logger.warning("loading the KV of %s from %s:%d failed, so it prefills here: %s",
                            req.remote_request_id, req.remote_host, req.remote_port, error)
@@ -1412,6 +1475,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 raise RuntimeError(problem)
             remote = _Remote(reply["engine_id"], reply["tp_size"], reply["num_blocks"], reply["exported"],
                              self.transport.open(reply["exported"]), sock)
+            if reply.get("relay_ring") and self._relaying():
+                remote.ring = self.transport.open_ring(reply["relay_ring"])
         except BaseException:
             sock.close()
             raise

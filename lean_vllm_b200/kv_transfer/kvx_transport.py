@@ -18,6 +18,11 @@ from lean_vllm_b200.kv_transfer import transport
 from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
 
 ENGINES = {"auto": _native.ENGINE_AUTO, "lsu": _native.ENGINE_LSU, "tma": _native.ENGINE_TMA}
+RELAY_RING = 64  # interprocess events a decode rank marks its relayed parts with, reused in turn
+
+# This process's own ring events by IPC handle: a peer rank in the same process uses them directly (CUDA cannot
+# open an IPC handle in the process that exported it).
+_OWN_RING_EVENTS: dict[str, object] = {}
 
 
 class KvxTransport:
@@ -62,6 +67,27 @@ class KvxTransport:
             "pid": os.getpid(),
         }
 
+    def relay_ring(self) -> list[str]:
+        """IPC handles (hex) of this rank's ring of interprocess events, created on first use: a relayed load's own
+        part is marked with one (post's `mark`), and the peer decode ranks' copies of that part wait on it."""
+        if getattr(self, "_ring", None) is None:
+            with torch.cuda.device(self.device):
+                self._ring = [torch.cuda.Event(interprocess=True) for _ in range(RELAY_RING)]
+                self._ring_handles = [e.ipc_handle().hex() for e in self._ring]
+            for handle, event in zip(self._ring_handles, self._ring):
+                _OWN_RING_EVENTS[handle] = event
+        return self._ring_handles
+
+    def open_ring(self, handles: list[str]) -> list:
+        """A peer rank's ring events, opened once (or used directly when the peer lives in this process)."""
+        out = []
+        for handle in handles:
+            event = _OWN_RING_EVENTS.get(handle)
+            if event is None:
+                event = torch.cuda.Event.from_ipc_handle(self.device, bytes.fromhex(handle))
+            out.append(event)
+        return out
+
     def split_sms(self):
         """Relayed loads: copies from the producer and from peer decode ranks run at once on two streams, so each
         is held to half the SMs (a TMA copy CTA fills most of an SM's shared memory; a few dozen SMs already keep
@@ -101,20 +127,27 @@ class KvxTransport:
         return transport.job_bytes(self._caches(self.local, tables, layer), jobs)
 
     def post(self, tables: list[CacheTable], jobs: list[CopyJob], ready, layer=None,
-             flags: int | None = None, save: bool = False, relay: bool = False) -> transport.Transfer:
+             flags: int | None = None, save: bool = False, relay: bool = False, mark: int | None = None,
+             after: list | None = None) -> transport.Transfer:
         """One launch for all jobs, after `ready`, on a side stream. `layer` = (first region, region count)
         restricts every cache to one layer's regions. A push of a save (`save`) runs on the high-priority save
         stream, in order with the save's earlier pushes (a block pushed again must land after its older copy);
         `flags` holds a per-layer push to its SM budget. A relayed load's copy from its peers (`relay`) runs on a
         stream of its own, beside later loads' copies from the producer. Other loads alternate between the two load
-        streams."""
+        streams. `after`: events (a peer's ring) the launch also waits for; `mark`: the slot of this rank's ring
+        recorded after the launch, for peers to wait on."""
         event = ready.cuda_event if ready is not None else 0
         if save or relay:
             stream = self.save_stream if save else self.relay_stream
         else:
             stream = self.load_streams[self._lane]
             self._lane ^= 1
-        return self._post_on(stream, tables, jobs, event, layer, flags)
+        for peer_event in after or ():
+            stream.wait_event(peer_event)
+        xfer = self._post_on(stream, tables, jobs, event, layer, flags)
+        if mark is not None:
+            self._ring[mark].record(stream)
+        return xfer
 
     def _post_on(self, stream, tables, jobs, event, layer=None, flags=None) -> transport.Transfer:
         xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,

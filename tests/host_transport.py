@@ -110,7 +110,14 @@ class HostTransport:
     def job_bytes(self, tables, jobs, layer=None):
         return sum(n for (_, n), _ in self._pairs(tables, jobs, layer))
 
-    def post(self, tables, jobs, ready, layer=None, flags=None, save=False, relay=False):
+    def relay_ring(self):
+        return [f"ring-{id(self)}-{slot}" for slot in range(64)]
+
+    def open_ring(self, handles):
+        return list(handles)
+
+    def post(self, tables, jobs, ready, layer=None, flags=None, save=False, relay=False, mark=None, after=None):
+        """Host copies land when posted, so a mark needs no event and a wait on one is already satisfied."""
         if HostTransport.fail == "posted":
             raise RuntimeError("the transport refused the copy")
         for (dst, n), (src, _) in list(self._pairs(tables, jobs, layer)):

@@ -91,6 +91,28 @@ def test_the_load_waits_on_the_gpu_for_the_step_that_still_writes_its_blocks(sid
     assert torch.equal(cache[:, 0].cpu(), prefill[:, 4])
 
 
+@pytest.mark.parametrize("decode_tp", [2, 4])
+def test_relayed_latents_land_what_the_reference_s_pull_lands_on_the_gpu(sides, golden, monkeypatch, decode_tp):
+    """LEAN_VLLM_KVX_RELAY on one GPU: each decode rank pulls its part of the latent pages from the producer, marks
+    that launch in its ring of events and tells its peers at once; each peer's copy of the part waits on the mark on
+    the GPU. Two loads in a row (the second reuses the ring) land the reference's result bit for bit."""
+    monkeypatch.setenv("LEAN_VLLM_KVX_RELAY", "1")
+    _, arrays = golden
+    producers = sides.make("kv_producer", 1, full_cache(0, True))
+    consumers = sides.make("kv_consumer", decode_tp, full_cache(1, True), engine_id="decode")
+    for tag in ("1", "2"):
+        for producer in producers:
+            producer.start_load_kv(KVConnectorMetadata(reqs_to_send={f"p-{tag}": [7, 2, 9]}))
+        for consumer in consumers:
+            consumer.start_load_kv(KVConnectorMetadata(reqs_to_recv={f"d-{tag}": recv(
+                producers, [0, 5, 3], [7, 2, 9], remote_request_id=f"p-{tag}")}))
+        outputs = [wait_for(c) for c in consumers]
+        assert KVOutputAggregator(decode_tp).aggregate(outputs).finished_recving == {f"d-{tag}"}
+        for consumer in consumers:  # latents are whole on every decode rank
+            assert np.array_equal(bits(consumer.kv_caches[0].cpu()), arrays["small_lat_tp1to2"])
+        assert KVOutputAggregator(1).aggregate([wait_for(p) for p in producers]).finished_sending == {f"p-{tag}"}
+
+
 def test_a_copy_that_gave_up_fails_its_load_alone_and_the_next_load_lands(sides, golden):
     """The first load's launch is made to look stuck: the bounded-wait self-test writes "gave up" (1) into that
     launch's own status word, as a copy whose bytes did not all land would. That load fails (the engine prefills
