@@ -142,6 +142,8 @@ class KvxTransport:
         else:
             stream = self.load_streams[self._lane]
             self._lane ^= 1
+        if mark is not None:
+            self.relay_ring()  # before the launch: a mark must never fail after the copy went out
         for peer_event in after or ():
             stream.wait_event(peer_event)
         xfer = self._post_on(stream, tables, jobs, event, layer, flags)
