@@ -108,3 +108,21 @@ def test_part_messages_nobody_reads_are_dropped_after_the_wait(sides, monkeypatc
     while "never-here" in worker._parts and monotonic() < deadline:
         sleep(0.02)
     assert "never-here" not in worker._parts and not worker._parts_seen
+
+
+def test_a_peer_s_slot_that_comes_before_this_rank_starts_the_load_is_kept(sides, golden):
+    """Decode rank 1 starts, posts its part and announces its ring slot well before rank 0 even gets the load: rank 0
+    still finds the slot when it starts, copies rank 1's part, and both land the reference's result."""
+    from time import sleep
+
+    _, arrays = golden
+    producers = sides.make("kv_producer", 1, full_cache(0, True))
+    consumers = sides.make("kv_consumer", 2, full_cache(1, True), engine_id="decode")
+    producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={"p-1": list(REMOTE)}))
+    consumers[1].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, list(LOCAL), list(REMOTE))}))
+    sleep(0.3)  # rank 1's slot and landed messages are waiting at rank 0
+    consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={"d-1": recv(producers, list(LOCAL), list(REMOTE))}))
+    recved = KVOutputAggregator(2).aggregate([wait_for(c) for c in consumers])
+    assert recved.finished_recving == {"d-1"}
+    assert np.array_equal(bits(full_of([c.kv_caches[0] for c in consumers], True)), arrays["small_lat_tp1to2"])
+    assert KVOutputAggregator(1).aggregate([wait_for(p) for p in producers]).finished_sending == {"p-1"}
