@@ -39,6 +39,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from lean_vllm_b200 import envs  # noqa: E402  (settings only: no torch, no library load)
+
 METRIC = "KV transfer GB/s & ms per 8k-token request"
 BYTES_8K_REQUEST = 32 * 36 * 2 * 8 * 256 * 128 * 2  # 1,207,959,552: 32 blocks x 36 layers x K/V x 512 KiB
 NVLINK_GBS = 900.0  # NVLink 5, per direction per GPU (nominal): the north star's link peak, the N >= 2 denominator
@@ -782,9 +784,6 @@ def run_gpu(args) -> None:
         for blob in opened:
             transport.close_mapping(blob)
         dist.destroy_process_group()
-
-
-from lean_vllm_b200 import envs  # noqa: E402
 
 
 def child_line(argv: list[str], timeout: float = 600.0) -> dict:
