@@ -1126,7 +1126,10 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 logger.warning("a peer decode rank could not load its part of %s, so it prefills here",
                                load.req.remote_request_id)
             if relay.transfer is None and not relay.copied and not load.failed and not relay.peer_failed:
-                if all(r in slots for r in peers):
+                # A peer whose ring is not open here (in this process on another GPU) is copied from once its part
+                # landed; the others as soon as their launches are marked.
+                if all(r in slots for r in peers) and all(self._peer_ring(r) or landed.get(r) is True
+                                                          or relay.parts[r][1] <= relay.parts[r][0] for r in peers):
                     self._copy_peer_parts(load, slots)
                 elif relay.waiting_since + timeout < now:
                     relay.peer_failed = True
@@ -1157,6 +1160,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             load.failed = load.failed or relay.peer_failed
             del self._relays[request_id]
             self._finish_load(request_id, load)
+
+    def _peer_ring(self, rank: int) -> list:
+        kv = self.kv_transfer
+        remote = self._remotes.get((kv.kv_ip, kv.kv_port + rank))
+        return remote.ring if remote is not None else []
 
     def _copy_peer_parts(self, load: _Load, slots: dict):
         """Queues the copy of every peer's part from its cache into this rank's blocks, after the peers' ring marks

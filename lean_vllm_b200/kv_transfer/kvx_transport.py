@@ -20,9 +20,9 @@ from lean_vllm_b200.kv_transfer.transport import CacheTable, CopyJob
 ENGINES = {"auto": _native.ENGINE_AUTO, "lsu": _native.ENGINE_LSU, "tma": _native.ENGINE_TMA}
 RELAY_RING = 64  # interprocess events a decode rank marks its relayed parts with, reused in turn
 
-# This process's own ring events by IPC handle: a peer rank in the same process uses them directly (CUDA cannot
-# open an IPC handle in the process that exported it).
-_OWN_RING_EVENTS: dict[str, object] = {}
+# This process's own ring events by IPC handle, with their device: a peer rank in the same process on the same GPU
+# uses them directly (CUDA cannot open an IPC handle in the process that exported it).
+_OWN_RING_EVENTS: dict[str, tuple] = {}
 
 
 class KvxTransport:
@@ -75,17 +75,22 @@ class KvxTransport:
                 self._ring = [torch.cuda.Event(interprocess=True) for _ in range(RELAY_RING)]
                 self._ring_handles = [e.ipc_handle().hex() for e in self._ring]
             for handle, event in zip(self._ring_handles, self._ring):
-                _OWN_RING_EVENTS[handle] = event
+                _OWN_RING_EVENTS[handle] = (event, self.device.index)
         return self._ring_handles
 
     def open_ring(self, handles: list[str]) -> list:
-        """A peer rank's ring events, opened once (or used directly when the peer lives in this process)."""
+        """A peer rank's ring events, opened once -- or used directly when the peer lives in this process on this
+        GPU. A peer in this process on another GPU gets no ring (an empty list): a stream waiting on such an event
+        object crashed the process on this pool's B200s, so its parts are copied once it says they landed."""
         out = []
         for handle in handles:
-            event = _OWN_RING_EVENTS.get(handle)
-            if event is None:
-                event = torch.cuda.Event.from_ipc_handle(self.device, bytes.fromhex(handle))
-            out.append(event)
+            own = _OWN_RING_EVENTS.get(handle)
+            if own is None:
+                out.append(torch.cuda.Event.from_ipc_handle(self.device, bytes.fromhex(handle)))
+            elif own[1] == self.device.index:
+                out.append(own[0])
+            else:
+                return []
         return out
 
     def split_sms(self):

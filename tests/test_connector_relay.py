@@ -126,3 +126,16 @@ def test_a_peer_s_slot_that_comes_before_this_rank_starts_the_load_is_kept(sides
     assert recved.finished_recving == {"d-1"}
     assert np.array_equal(bits(full_of([c.kv_caches[0] for c in consumers], True)), arrays["small_lat_tp1to2"])
     assert KVOutputAggregator(1).aggregate([wait_for(p) for p in producers]).finished_sending == {"p-1"}
+
+
+def test_a_peer_without_an_open_ring_is_copied_from_once_its_part_landed(sides, golden, monkeypatch):
+    """A peer decode rank in this process on another GPU gets no ring (its event objects are not waited on across
+    GPUs in one process): this rank copies its part once it said the part landed, and the load lands the reference's
+    result all the same."""
+    _, arrays = golden
+    monkeypatch.setattr(HostTransport, "open_ring", lambda self, handles: [])
+    producers = sides.make("kv_producer", 1, full_cache(0, True))
+    consumers = sides.make("kv_consumer", 2, full_cache(1, True), engine_id="decode")
+    sent, recved = load(producers, consumers)
+    assert recved.finished_recving == {"d-1"} and sent.finished_sending == {"p-1"}
+    assert np.array_equal(bits(full_of([c.kv_caches[0] for c in consumers], True)), arrays["small_lat_tp1to2"])
