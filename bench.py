@@ -1315,6 +1315,11 @@ def run_poisson(args) -> None:
         gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=600))
     pool = 1024  # blocks per side: 38.7 GB
     rates = [float(r) for r in args.rates.split(",")]
+    # The decode loop below stands in for an engine calling get_finished as often as it can: it sleeps 20 us between
+    # calls, and a 1 us timer slack (this process only; Linux's default is 50 us) keeps each sleep near that.
+    import ctypes
+
+    ctypes.CDLL(None, use_errno=True).prctl(29, 1000, 0, 0, 0)  # PR_SET_TIMERSLACK, in ns
 
     @dataclass
     class WorkerConfig:
@@ -1357,7 +1362,7 @@ def run_poisson(args) -> None:
         warm_up()
         for rate in rates:
             rng = np.random.default_rng(int(rate * 1000) + args.seed)
-            n = int(min(max(rate * args.poisson_seconds, 8), 400))
+            n = int(min(max(rate * args.poisson_seconds, 24), 400))  # 24 at least: a p50 worth reading
             lengths = np.clip(np.exp(rng.normal(np.log(2048), 1.0, size=n)), 128, 32768).astype(np.int64)
             arrivals = np.cumsum(rng.exponential(1.0 / rate, size=n))
             blocks = [math.ceil(int(x) / spec.block) for x in lengths]
@@ -1394,7 +1399,7 @@ def run_poisson(args) -> None:
                         in_flight.append(out.recv_stats[rid].seconds * 1e3)
                         moved += out.recv_stats[rid].num_bytes
                         free.extend(local)
-                    time.sleep(50e-6)
+                    time.sleep(20e-6)
                 wall = time.perf_counter() - t0
                 results.append({"rate_req_per_s": rate, "requests": n, "p50_ms": round(float(np.percentile(latency, 50)), 3),
                                 "p99_ms": round(float(np.percentile(latency, 99)), 3),
@@ -1430,7 +1435,8 @@ def run_poisson(args) -> None:
                 "config": {"workload": f"{spec.name}/{'loopback-1gpu' if world == 1 else 'pair'} poisson",
                            "pairs": len(pairs),
                            "prompt_lengths": "log-normal, median 2048, sigma 1.0, clipped [128, 32768]",
-                           "decode_pool_blocks": pool},
+                           "decode_pool_blocks": pool, "get_finished_poll_us": 20,
+                           "inline_loads": bool(envs.LEAN_VLLM_KVX_INLINE_LOADS)},
                 "rates": pairs[0]}
         if len(pairs) > 1:  # every pair runs the same seeded arrivals at once: the spread shows any interference
             line["p50_ms_by_pair"] = {str(row["rate_req_per_s"]): [p[i]["p50_ms"] for p in pairs]

@@ -26,6 +26,11 @@ environment_variables: dict[str, Callable[[], Any]] = {
     # latency). 2 GiB: on one B200, 64 Qwen3-8B-shaped loads went from 64 launches to 17 and their end-to-end rate
     # from 0.944 to 0.967 of the device-timed copy.
     "LEAN_VLLM_KVX_BATCH_BYTES": lambda: int(os.getenv("LEAN_VLLM_KVX_BATCH_BYTES", str(2 << 30))),
+    # 1 (default): when none of a decode rank's copies is in flight, start_load_kv launches the step's first load
+    # itself if its producer ranks are already mapped, instead of waking the transfer thread to do it; the thread
+    # still plans every other load, polls the copy and notifies the producers. 0: every load goes to the thread.
+    "LEAN_VLLM_KVX_INLINE_LOADS": lambda: os.getenv("LEAN_VLLM_KVX_INLINE_LOADS", "1").strip().lower()
+    not in ("", "0", "false"),
     # SMs a per-layer save's copy may use while the prefill computes (0: every SM).
     "LEAN_VLLM_KVX_SAVE_SMS": lambda: int(os.getenv("LEAN_VLLM_KVX_SAVE_SMS", "16")),
 }

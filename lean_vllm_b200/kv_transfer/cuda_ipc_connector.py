@@ -283,6 +283,7 @@ class _Load:
     num_bytes: int = 0
     failed: bool = False
     relay: _Relay | None = None
+    reported: bool = False  # launched by the engine thread, which saw it land and reported it (under the lock)
 
 
 @dataclass(slots=True)
@@ -368,9 +369,11 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._server = None
         self._deferred: list = []  # messages that came while a handshake wait answered handshakes only
         self._remotes: dict[tuple[str, int], _Remote] = {}  # transfer thread only
-        self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table, blocks) of _remotes; locked
+        self._mapped: dict[tuple[str, int], tuple] = {}  # key -> (engine id, table, blocks, _Remote); locked
+        self._launches_in_flight = 0  # load launches (either thread's) not yet seen landed; under the lock
         self._retired: list[_Retired] = []  # replaced mappings not yet closed; both threads, under the lock
         self._loads: dict[str, _Load] = {}  # transfer thread only
+        self._inline: dict[str, _Load] = {}  # engine thread only: the loads it launched, until one side reports them
         self._waits: dict[str, _Wait] = {}  # transfer thread only
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
         self._relays: dict[str, _Load] = {}  # transfer thread only: loads past their own part, waiting for peers'
@@ -471,7 +474,81 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             # Freshly allocated blocks may still be written by a step in flight; the copy waits for it on the GPU.
             # One queue item for the step's loads: the transfer thread plans them in one pass, so they share launches.
             ready = self.transport.ready_marker()
-            self._put(("loads", ready, list(metadata.reqs_to_recv.items())))
+            loads = list(metadata.reqs_to_recv.items())
+            if self._post_here(*loads[0], ready):
+                loads = loads[1:]
+            if loads:
+                self._put(("loads", ready, loads))
+
+    def _post_here(self, request_id: str, req: ReqToRecv, ready) -> bool:
+        """Launches one load from the engine thread when none of this rank's copies is in flight and every producer
+        rank it reads is mapped with the engine id it names: its copy starts without waiting for the transfer thread
+        to wake. The thread then polls it and notifies the producers as for its own loads. Anything else -- a pushed
+        or relayed load, a producer not yet mapped, an empty share, a bad block id, a refused launch -- returns False
+        and the load goes to the thread, which plans it from the start (and fails it, if it must)."""
+        if not envs.LEAN_VLLM_KVX_INLINE_LOADS or getattr(req, "pushed", False) or self._relaying():
+            return False
+        try:
+            heads = self._heads(req)
+            shares: list[Share] = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
+            keys = [(req.remote_host, req.remote_port + share.remote_rank) for share in shares]
+            with self._lock:
+                if self._launches_in_flight:
+                    return False
+                # Read under the lock: a mapping _retire drops after this stays open until this engine thread has
+                # polled again (get_finished) and every transport stream has run past that poll.
+                remotes = [self._mapped.get(key) for key in keys]
+            if not all(m is not None and (not req.remote_engine_id or m[0] == req.remote_engine_id) for m in remotes):
+                return False
+            load = _Load(req, request_id=request_id)
+            jobs, tables = [], []
+            for i, (share, key, mapped) in enumerate(zip(shares, keys, remotes)):
+                job = CopyJob(len(tables) + 1, 0, req.remote_block_ids, req.local_block_ids, share.remote_head,
+                              share.local_head, share.num_heads, i == 0)
+                nbytes = self._job_bytes(mapped[3], job)
+                if nbytes == 0:
+                    return False
+                readers = readers_of(share.remote_rank, req.remote_tp_size, self.tp_size, heads)
+                tables.append(mapped[1])
+                jobs.append(job)
+                load.notify.append((key, f"{req.remote_request_id}:{readers}", share.remote_rank))
+                load.unnotified.add(share.remote_rank)
+                load.num_bytes += nbytes
+            if not jobs:
+                return False
+            load.started = monotonic()
+            load.transfer = _Batch(self.transport.post(tables, jobs, ready), 1)
+        except Exception:  # noqa: BLE001 - the transfer thread plans it again and reports what is wrong
+            return False
+        with self._lock:
+            self._launches_in_flight += 1
+        self._inline[request_id] = load
+        self._put(("posted", request_id, load))
+        return True
+
+    def _finish_inline(self):
+        """Engine thread, in get_finished: a load it launched whose copy has landed is reported here and now, without
+        waiting for the transfer thread to wake (under a busy engine that can take a GIL switch interval). The
+        thread still notifies its producers and lets the launch go; it lets it go under the lock, so the query here
+        never meets a released transfer. A copy that failed is left to the thread."""
+        with self._lock:
+            for request_id, load in list(self._inline.items()):
+                shared = load.transfer
+                if shared is None or shared.done or load.failed:  # the thread has taken it from here
+                    del self._inline[request_id]
+                    continue
+                try:
+                    landed = self.transport.done(shared.xfer)
+                except Exception:  # noqa: BLE001 - its own failure: the thread fails the load
+                    del self._inline[request_id]
+                    continue
+                if landed:
+                    del self._inline[request_id]
+                    self._mark_landed(shared, locked=True)
+                    load.reported = True
+                    self._finished.finished_recving.add(request_id)
+                    self._finished.recv_stats[request_id] = KVTransferStats(monotonic() - load.started,
+                                                                            load.num_bytes)
 
     def save_kv_layer(self, layer_index: int):
         """Pushes layer `layer_index` of every request being saved whose decode ranks are mapped -- the blocks this
@@ -513,6 +590,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         """What finished since the last call: the transfer thread fills the output as loads land and readers
         report; here held blocks past the abort timeout are given back, and the output is handed to the engine."""
         self._mark_swaps_passed()
+        if self._inline:
+            self._finish_inline()
         timeout = envs.LEAN_VLLM_KV_ABORT_REQUEST_TIMEOUT
         now = monotonic()
         with self._lock:
@@ -701,12 +780,17 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                     except queue.Empty:
                         break
                 if None in items:
+                    for item in items:  # copies the engine thread launched: _close waits for them to land
+                        if item is not None and item[0] == "posted":
+                            self._loads[item[1]] = item[2]
                     return
                 batch: list = []
                 for item in items:
                     if item[0] == "loads":
                         for request_id, req in item[2]:
                             self._guarded(self._start, request_id, req, item[1], batch)
+                    elif item[0] == "posted":  # launched by the engine thread (_post_here): polled from here on
+                        self._loads[item[1]] = item[2]
                     elif item[0] == "connect":
                         self._guarded(self._connect, item[1])
                     elif item[0] == "finish":
@@ -938,8 +1022,18 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         except Exception as error:  # noqa: BLE001 - every failure of a load becomes failed_recving
             self._fail(load, error)
 
+    def _mark_landed(self, shared: _Batch, locked: bool = False):
+        """The one place a launch is marked landed: the in-flight count drops once, whichever thread saw it."""
+        if not locked:
+            with self._lock:
+                return self._mark_landed(shared, locked=True)
+        if not shared.done:
+            shared.done = True
+            self._launches_in_flight -= 1
+
     def _copies_in_flight(self) -> bool:
-        return any(load.transfer is not None and not load.transfer.done for load in self._loads.values())
+        with self._lock:
+            return self._launches_in_flight > 0
 
     def _job_bytes(self, remote: _Remote, job: CopyJob) -> int:
         """What the job moves: the reference's descriptor-length sum (nixl_connector.py:421). The bytes of one block
@@ -990,6 +1084,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 for load, *_ in entries:
                     self._fail(load, error)
                 continue
+            with self._lock:
+                self._launches_in_flight += 1
             for load, *_ in entries:
                 load.transfer = shared
             for load in relayed:
@@ -1029,10 +1125,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         if not shared.done and id(shared) not in queried:
             queried.add(id(shared))
             try:
-                shared.done = self.transport.done(shared.xfer)
+                landed = self.transport.done(shared.xfer)
             except Exception as error:  # noqa: BLE001 - this launch's own failure (its status word, or CUDA)
-                shared.done = True
+                landed = True
                 shared.error = shared.error or error
+            if landed:
+                self._mark_landed(shared)
         if not shared.done:
             return False
         if shared.error is not None:
@@ -1040,7 +1138,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         load.transfer = None
         shared.refs -= 1
         if shared.refs == 0:
-            self.transport.release(shared.xfer)
+            with self._lock:  # the engine thread may be asking about it (_finish_inline)
+                self.transport.release(shared.xfer)
         if not load.failed:
             for key, message, remote_rank in load.notify:
                 notes.setdefault(key, []).append(message)
@@ -1063,6 +1162,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 self._part_slots.pop(request_id, None)
             self._parts_seen.pop(request_id, None)
         with self._lock:
+            if load.reported:  # the engine thread saw it land and reported it
+                return
             if load.failed:
                 self._finished.failed_recving.add(request_id)
             else:
@@ -1490,7 +1591,7 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             raise
         self._remotes[key] = remote  # its socket stays open for notifications
         with self._lock:
-            self._mapped[key] = (remote.engine_id, remote.table, remote.num_blocks)
+            self._mapped[key] = (remote.engine_id, remote.table, remote.num_blocks, remote)
         return remote
 
     def _dealer(self, key):
