@@ -186,6 +186,13 @@ int kvx_store(const void *key, const void *value, int64_t key_stride, int64_t va
 int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
                  void *wait_event, void *stream, kvx_xfer_t *out);
 
+/* kvx_transfer ordered after everything queued so far on `after_stream` (a cudaStream_t as void*; 0 is the legacy
+ * default stream): an event this library keeps per device is recorded there and waited for on `stream`, so the
+ * caller needs no event of its own. The reference's ready event (nixl_connector.py:266), for a caller that posts
+ * the transfer on the thread that runs the engine's stream. */
+int kvx_transfer_after(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
+                       void *after_stream, void *stream, kvx_xfer_t *out);
+
 /* KVX_OK once the transfer's copies have landed, KVX_PENDING while in flight, <0 on failure: KVX_ERR_CUDA if the
  * launch failed, KVX_ERR_DEVICE if one of ITS copies gave up a bounded wait (bit 1 of its own status word, read from
  * host memory once the transfer's event has completed: no copy, no stream). A failure elsewhere on the device fails

@@ -142,6 +142,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                    ctypes.POINTER(StoreDest), ctypes.c_int, _P, ctypes.c_int, _P], ctypes.c_int),
     "kvx_transfer": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int, ctypes.c_int, _P, _P,
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "kvx_transfer_after": ([ctypes.POINTER(Cache), ctypes.c_int, ctypes.POINTER(Job), ctypes.c_int, ctypes.c_int, _P,
+                            _P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "kvx_check_xfer": ([_P], ctypes.c_int),
     "kvx_release_xfer": ([_P], ctypes.c_int),
     "kvx_xfer_status": ([_P, ctypes.POINTER(_P)], ctypes.c_int),

@@ -879,6 +879,19 @@ struct Bell {
     std::vector<std::pair<cudaEvent_t, int>> pending;  // (event, device), guarded by mu
     bool stop = false;
     std::thread watcher;
+
+    // A doorbell its owner never closed (a process leaving on an exception) is stopped when the registry goes at
+    // exit: destroying a thread that can still be joined would end the process with std::terminate.
+    ~Bell() {
+        if (!watcher.joinable()) return;
+        {
+            std::lock_guard<std::mutex> lock(mu);
+            stop = true;
+        }
+        cv.notify_one();
+        watcher.join();
+        if (fd >= 0) close(fd);
+    }
 };
 
 void watch(Bell *bell) {
@@ -1343,6 +1356,27 @@ int kvx_transfer(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int
     }
     *out = reinterpret_cast<kvx_xfer_t>(new Xfer{done, device, status});
     return KVX_OK;
+}
+
+// One event per device for kvx_transfer_after: recorded on the caller's stream and waited for on the copy stream
+// under one lock, so every wait captures its own record (a wait is bound to the record before it, not to later ones).
+std::mutex g_after_mu;
+std::map<int, cudaEvent_t> g_after_events;
+
+int kvx_transfer_after(const kvx_cache *caches, int n_caches, const kvx_job *jobs, int n_jobs, int flags,
+                       void *after_stream, void *stream, kvx_xfer_t *out) {
+    if (!out) return fail(KVX_ERR_INVALID, "null pointer");
+    *out = nullptr;
+    int device;
+    KVX_CUDA(cudaGetDevice(&device));
+    {
+        std::lock_guard<std::mutex> lock(g_after_mu);
+        cudaEvent_t &after = g_after_events[device];
+        if (!after) KVX_CUDA(cudaEventCreateWithFlags(&after, cudaEventDisableTiming));
+        KVX_CUDA(cudaEventRecord(after, static_cast<cudaStream_t>(after_stream)));
+        KVX_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), after, 0));
+    }
+    return kvx_transfer(caches, n_caches, jobs, n_jobs, flags, nullptr, stream, out);
 }
 
 int kvx_check_xfer(kvx_xfer_t xfer) {

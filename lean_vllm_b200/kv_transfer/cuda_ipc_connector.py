@@ -374,6 +374,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._retired: list[_Retired] = []  # replaced mappings not yet closed; both threads, under the lock
         self._loads: dict[str, _Load] = {}  # transfer thread only
         self._inline: dict[str, _Load] = {}  # engine thread only: the loads it launched, until one side reports them
+        self._share_plans: dict[int, list] = {}  # producer TP size -> [(Share, readers)] (engine thread)
+        self.inline_loads = envs.LEAN_VLLM_KVX_INLINE_LOADS
         self._waits: dict[str, _Wait] = {}  # transfer thread only
         self._pushes: list = []  # (transfer, [saves]) in flight; both threads, under the lock
         self._relays: dict[str, _Load] = {}  # transfer thread only: loads past their own part, waiting for peers'
@@ -473,25 +475,23 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         if metadata.reqs_to_recv:
             # Freshly allocated blocks may still be written by a step in flight; the copy waits for it on the GPU.
             # One queue item for the step's loads: the transfer thread plans them in one pass, so they share launches.
-            ready = self.transport.ready_marker()
             loads = list(metadata.reqs_to_recv.items())
-            if self._post_here(*loads[0], ready):
+            if self._post_here(*loads[0]):
                 loads = loads[1:]
             if loads:
-                self._put(("loads", ready, loads))
+                self._put(("loads", self.transport.ready_marker(), loads))
 
-    def _post_here(self, request_id: str, req: ReqToRecv, ready) -> bool:
+    def _post_here(self, request_id: str, req: ReqToRecv) -> bool:
         """Launches one load from the engine thread when none of this rank's copies is in flight and every producer
         rank it reads is mapped with the engine id it names: its copy starts without waiting for the transfer thread
         to wake. The thread then polls it and notifies the producers as for its own loads. Anything else -- a pushed
         or relayed load, a producer not yet mapped, an empty share, a bad block id, a refused launch -- returns False
         and the load goes to the thread, which plans it from the start (and fails it, if it must)."""
-        if not envs.LEAN_VLLM_KVX_INLINE_LOADS or getattr(req, "pushed", False) or self._relaying():
+        if not self.inline_loads or getattr(req, "pushed", False) or self._relaying():
             return False
         try:
-            heads = self._heads(req)
-            shares: list[Share] = head_shares(self.rank, self.tp_size, req.remote_tp_size, heads)
-            keys = [(req.remote_host, req.remote_port + share.remote_rank) for share in shares]
+            shares = self._share_plan(req.remote_tp_size)
+            keys = [(req.remote_host, req.remote_port + share.remote_rank) for share, _ in shares]
             with self._lock:
                 if self._launches_in_flight:
                     return False
@@ -502,13 +502,12 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
                 return False
             load = _Load(req, request_id=request_id)
             jobs, tables = [], []
-            for i, (share, key, mapped) in enumerate(zip(shares, keys, remotes)):
+            for i, ((share, readers), key, mapped) in enumerate(zip(shares, keys, remotes)):
                 job = CopyJob(len(tables) + 1, 0, req.remote_block_ids, req.local_block_ids, share.remote_head,
                               share.local_head, share.num_heads, i == 0)
                 nbytes = self._job_bytes(mapped[3], job)
                 if nbytes == 0:
                     return False
-                readers = readers_of(share.remote_rank, req.remote_tp_size, self.tp_size, heads)
                 tables.append(mapped[1])
                 jobs.append(job)
                 load.notify.append((key, f"{req.remote_request_id}:{readers}", share.remote_rank))
@@ -517,7 +516,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             if not jobs:
                 return False
             load.started = monotonic()
-            load.transfer = _Batch(self.transport.post(tables, jobs, ready), 1)
+            # After the engine's stream as it stands (this is the engine thread): no ready event to create.
+            load.transfer = _Batch(self.transport.post(tables, jobs, None, engine_order=True), 1)
         except Exception:  # noqa: BLE001 - the transfer thread plans it again and reports what is wrong
             return False
         with self._lock:
@@ -525,6 +525,17 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
         self._inline[request_id] = load
         self._put(("posted", request_id, load))
         return True
+
+    def _share_plan(self, remote_tp: int) -> list:
+        """This rank's shares of a producer instance of `remote_tp` ranks, each with its reader count (the
+        notification's), computed once per producer TP size: both depend on nothing else."""
+        plan = self._share_plans.get(remote_tp)
+        if plan is None:
+            heads = split_heads(self.num_heads, self.tp_size, remote_tp)
+            plan = self._share_plans[remote_tp] = [
+                (share, readers_of(share.remote_rank, remote_tp, self.tp_size, heads))
+                for share in head_shares(self.rank, self.tp_size, remote_tp, heads)]
+        return plan
 
     def _finish_inline(self):
         """Engine thread, in get_finished: a load it launched whose copy has landed is reported here and now, without

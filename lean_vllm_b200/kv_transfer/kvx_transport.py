@@ -133,14 +133,16 @@ class KvxTransport:
 
     def post(self, tables: list[CacheTable], jobs: list[CopyJob], ready, layer=None,
              flags: int | None = None, save: bool = False, relay: bool = False, mark: int | None = None,
-             after: list | None = None) -> transport.Transfer:
+             after: list | None = None, engine_order: bool = False) -> transport.Transfer:
         """One launch for all jobs, after `ready`, on a side stream. `layer` = (first region, region count)
         restricts every cache to one layer's regions. A push of a save (`save`) runs on the high-priority save
         stream, in order with the save's earlier pushes (a block pushed again must land after its older copy);
         `flags` holds a per-layer push to its SM budget. A relayed load's copy from its peers (`relay`) runs on a
         stream of its own, beside later loads' copies from the producer. Other loads alternate between the two load
         streams. `after`: events (a peer's ring) the launch also waits for; `mark`: the slot of this rank's ring
-        recorded after the launch, for peers to wait on."""
+        recorded after the launch, for peers to wait on. `engine_order` (with `ready` None): the launch waits for
+        everything queued so far on the calling thread's current stream, through the library's own event -- what a
+        ready_marker would give, without creating one."""
         event = ready.cuda_event if ready is not None else 0
         if save or relay:
             stream = self.save_stream if save else self.relay_stream
@@ -151,14 +153,15 @@ class KvxTransport:
             self.relay_ring()  # before the launch: a mark must never fail after the copy went out
         for peer_event in after or ():
             stream.wait_event(peer_event)
-        xfer = self._post_on(stream, tables, jobs, event, layer, flags)
+        engine = torch._C._cuda_getCurrentRawStream(self.device.index) if engine_order else None
+        xfer = self._post_on(stream, tables, jobs, event, layer, flags, engine)
         if mark is not None:
             self._ring[mark].record(stream)
         return xfer
 
-    def _post_on(self, stream, tables, jobs, event, layer=None, flags=None) -> transport.Transfer:
+    def _post_on(self, stream, tables, jobs, event, layer=None, flags=None, after_stream=None) -> transport.Transfer:
         xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
-                                  self.flags if flags is None else flags)
+                                  self.flags if flags is None else flags, after_stream)
         self.doorbell.ring_after(stream.cuda_stream)
         return xfer
 

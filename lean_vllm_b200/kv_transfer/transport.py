@@ -90,8 +90,23 @@ class CopyJob:
     latents: bool = False
 
 
+_CACHE_ARRAYS: dict[tuple, tuple] = {}  # ids of a list of tables -> (the tables, their kvx_cache array)
+
+
+def _cache_array(caches: list[CacheTable]):
+    """The kvx_cache array of a list of tables, built once per list of the same (long-lived) tables: the entry
+    holds the tables, so their ids cannot be reused while it exists."""
+    key = tuple(map(id, caches))
+    entry = _CACHE_ARRAYS.get(key)
+    if entry is None or any(a is not b for a, b in zip(entry[0], caches)):
+        if len(_CACHE_ARRAYS) >= 256:
+            _CACHE_ARRAYS.clear()
+        entry = _CACHE_ARRAYS[key] = (tuple(caches), (Cache * max(len(caches), 1))(*[c.struct() for c in caches]))
+    return entry[1]
+
+
 def _marshal(caches: list[CacheTable], jobs: list[CopyJob]):
-    cache_array = (Cache * max(len(caches), 1))(*[c.struct() for c in caches])
+    cache_array = _cache_array(caches)
     keep = [cache_array]
     job_array = (Job * max(len(jobs), 1))()
     for k, job in enumerate(jobs):
@@ -177,12 +192,17 @@ class Transfer:
 
 
 def transfer(caches: list[CacheTable], jobs: list[CopyJob], stream: int, wait_event: int = 0,
-             flags: int = 0) -> Transfer:
-    """Waits (on the stream) for `wait_event`, launches the copy, records completion."""
+             flags: int = 0, after_stream: int | None = None) -> Transfer:
+    """Waits (on the stream) for `wait_event` -- or, given `after_stream`, for everything queued on that stream so
+    far (kvx_transfer_after; 0 is the legacy default stream) -- launches the copy, records completion."""
     cache_array, job_array, _keep = _marshal(caches, jobs)
     out = ctypes.c_void_p()
-    check(lib().kvx_transfer(cache_array, len(caches), job_array, len(jobs), flags, wait_event or None,
-                             stream or None, ctypes.byref(out)))
+    if after_stream is None:
+        check(lib().kvx_transfer(cache_array, len(caches), job_array, len(jobs), flags, wait_event or None,
+                                 stream or None, ctypes.byref(out)))
+    else:
+        check(lib().kvx_transfer_after(cache_array, len(caches), job_array, len(jobs), flags, after_stream or None,
+                                       stream or None, ctypes.byref(out)))
     return Transfer(out.value)
 
 

@@ -116,7 +116,8 @@ class HostTransport:
     def open_ring(self, handles):
         return list(handles)
 
-    def post(self, tables, jobs, ready, layer=None, flags=None, save=False, relay=False, mark=None, after=None):
+    def post(self, tables, jobs, ready, layer=None, flags=None, save=False, relay=False, mark=None, after=None,
+             engine_order=False):
         """Host copies land when posted, so a mark needs no event and a wait on one is already satisfied."""
         if HostTransport.fail == "posted":
             raise RuntimeError("the transport refused the copy")

@@ -113,6 +113,22 @@ def test_a_doorbell_opens_and_closes_without_a_device():
     b.close()
 
 
+def test_a_process_that_leaves_a_doorbell_open_still_exits_cleanly():
+    """A process that ends on an exception before its connector shut down leaves its doorbell open: the library
+    stops the doorbell's watcher at exit rather than abort (std::terminate on a joinable thread)."""
+    if not os.path.exists(_native.LIB_PATH):
+        pytest.skip("libkvx.so is not built here")
+    import subprocess
+    import sys
+
+    code = ("from lean_vllm_b200.kv_transfer.transport import Doorbell\n"
+            "bells = [Doorbell(), Doorbell()]\n"
+            "raise SystemExit(3)\n")
+    done = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert done.returncode == 3, done.stderr[-2000:]
+    assert "terminate" not in done.stderr
+
+
 def test_the_wait_selftest_checks_its_limit_before_launching():
     if not os.path.exists(_native.LIB_PATH):
         pytest.skip("libkvx.so is not built here")

@@ -264,6 +264,38 @@ def test_a_transfer_waits_for_its_ready_event_and_reports_completion():
         assert bool((d[:, [0, 1, 2, 5, 6, 7]] == 1.0).all())
 
 
+@pytest.mark.parametrize("on_default_stream", [False, True])
+def test_a_transfer_after_a_stream_waits_for_what_was_queued_there(on_default_stream):
+    """kvx_transfer_after: no ready event from the caller; the library's own event, recorded on the engine's stream,
+    orders the copy after the writes queued there -- on a stream of the engine's or the legacy default stream (0),
+    and again for a second transfer reusing the same event while the first still waits."""
+    src = _qwen_like(8, 2, seed=6)
+    dst = [torch.zeros_like(s) for s in src]
+    side = torch.cuda.Stream()
+    engine = torch.cuda.default_stream() if on_default_stream else torch.cuda.Stream()
+    caches = [CacheTable.from_tensors(src), CacheTable.from_tensors(dst)]
+    with torch.cuda.stream(engine):
+        torch.cuda._sleep(20_000_000)  # the "step in flight" that still owns dst's blocks
+        for d in dst:
+            d.fill_(1.0)  # ... and writes them after the sleep
+        first = transport.transfer(caches, [CopyJob(0, 1, [1, 2], [3, 4], 0, 0, 8)], side.cuda_stream,
+                                   after_stream=engine.cuda_stream)
+        torch.cuda._sleep(20_000_000)
+        for d in dst:
+            d[:, [6]] = 2.0
+        second = transport.transfer(caches, [CopyJob(0, 1, [5], [6], 0, 0, 8)], side.cuda_stream,
+                                    after_stream=engine.cuda_stream)
+    while not (first.done() and second.done()):
+        pass
+    first.release()
+    second.release()
+    torch.cuda.synchronize()
+    for s, d in zip(src, dst):
+        assert torch.equal(d[:, [3, 4]], s[:, [1, 2]])
+        assert torch.equal(d[:, [6]], s[:, [5]])
+        assert bool((d[:, [0, 1, 2, 5, 7]] == 1.0).all())
+
+
 def test_a_doorbell_rings_once_the_stream_work_before_it_ends():
     """kvx_doorbell_ring_after: the eventfd turns readable only after the copy queued before the ring landed."""
     import select
