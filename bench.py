@@ -770,11 +770,12 @@ def run_gpu(args) -> None:
                                              "decode caches",
                            "batch_bytes": envs.LEAN_VLLM_KVX_BATCH_BYTES,
                            "path": (f"CudaIpcConnectorWorker.start_load_kv({len(reqs)} ReqToRecv from host lists) -> "
-                                    "get_finished() until every load finished_recving; one kvx launch per load, "
-                                    "block ids carried in the launch, the transfer thread woken by a doorbell when "
-                                    "each copy lands; each transfer's result read from its status word in mapped "
-                                    "host memory (written by the device only on failure), so no device-to-host "
-                                    "copy is made")}
+                                    "get_finished() until every load finished_recving; the first load launched "
+                                    "by start_load_kv itself, the rest planned by the transfer thread into "
+                                    "launches of up to batch_bytes on two alternating streams, block ids carried "
+                                    "in each launch; the thread woken by a doorbell when a copy lands; each "
+                                    "transfer's result read from its status word in mapped host memory (written "
+                                    "by the device only on failure), so no device-to-host copy is made")}
         line.update(extras)
         if loopback and not peer_mode and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(reqs, spec, seconds=args.cpu_seconds)

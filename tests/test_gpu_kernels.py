@@ -152,6 +152,34 @@ def test_more_jobs_and_blocks_than_one_launch_holds():
         assert torch.equal(big[layer], expect[2][layer])
 
 
+@pytest.mark.parametrize("layers, n_jobs, blocks_per_job", [(40, 8, 16), (41, 8, 16), (40, 9, 14), (40, 8, 17)])
+@pytest.mark.parametrize("engine", ["lsu", "tma"])
+def test_launches_at_and_past_the_compact_parameter_block_match_torch_indexing(layers, n_jobs, blocks_per_job,
+                                                                             engine):
+    """A launch that fits the compact parameter block (8 jobs, 160 region slots, 256 block ids) goes out with it;
+    one region, job or id more and it takes the full block. Both sides of each limit land what torch indexing of the
+    source says, and leave every other block alone."""
+    rng = np.random.default_rng(layers * 100 + n_jobs * 10 + blocks_per_job)
+    num_blocks = n_jobs * blocks_per_job + 4
+    g = torch.Generator(device="cuda").manual_seed(9)
+    src = [torch.randn(2, num_blocks, 2, 16, 64, generator=g, device="cuda").to(torch.bfloat16) for _ in range(layers)]
+    dst = [torch.randn(2, num_blocks, 2, 16, 64, generator=g, device="cuda").to(torch.bfloat16) for _ in range(layers)]
+    before = [d.clone() for d in dst]
+    src_order, dst_order = rng.permutation(num_blocks), rng.permutation(num_blocks)
+    b = blocks_per_job
+    fixed = [([int(x) for x in src_order[j * b : (j + 1) * b]], [int(x) for x in dst_order[j * b : (j + 1) * b]])
+             for j in range(n_jobs)]  # each job its own destinations
+    jobs = [CopyJob(1, 0, s_ids, d_ids, 0, 0, 2) for s_ids, d_ids in fixed]
+    caches = [CacheTable.from_tensors(dst), CacheTable.from_tensors(src)]
+    transport.copy(caches, jobs, torch.cuda.current_stream().cuda_stream, ENGINES[engine])
+    torch.cuda.synchronize()
+    for s_layer, d_layer, old in zip(src, dst, before):
+        expected = old.clone()
+        for s_ids, d_ids in fixed:
+            expected[:, d_ids] = s_layer[:, s_ids]
+        assert torch.equal(d_layer, expected)
+
+
 def test_out_of_range_blocks_and_heads_raise_before_any_launch():
     src = [torch.zeros(2, 4, 2, 16, 8, device="cuda", dtype=torch.bfloat16)]
     dst = [torch.zeros(2, 4, 2, 16, 8, device="cuda", dtype=torch.bfloat16)]
