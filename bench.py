@@ -434,6 +434,8 @@ def run_gpu(args) -> None:
     engine = {"auto": ENGINE_AUTO, "lsu": ENGINE_LSU, "tma": ENGINE_TMA}[args.engine]
     # Relayed: the copies from the prefill rank and from the peers run at once on two streams, half the SMs each.
     relay_sms = torch.cuda.get_device_properties(local_rank).multi_processor_count // 2 if args.relay else 0
+    if args.relay and args.relay_sms >= 0:  # an explicit SM budget per relay stream (0: every SM)
+        relay_sms = args.relay_sms
     copy_flags = flags(engine, args.tile_bytes, args.ctas_per_sm, relay_sms)
     lengths, reqs, num_blocks = workload(args.seed, args.requests, spec)
     step_blocks = sum(len(s) for s, _ in reqs)
@@ -745,7 +747,9 @@ def run_gpu(args) -> None:
                 "groups": groups,
                 "mode": "loopback" if loopback else args.mode + (" relayed" if relay else ""),
                 "relay_chunks": (args.relay_chunks or RELAY_CHUNKS) if relay else None,
+                "relay_sms_per_stream": (relay_sms or "all") if relay else None,
                 "engine": args.engine,
+                "tile_bytes": args.tile_bytes or "default", "ctas_per_sm": args.ctas_per_sm or "default",
                 "parallelism": ("1 GPU" if loopback else
                                 f"{groups} independent prefill TP{spec.prefill_tp} -> decode TP{spec.decode_tp} groups"),
                 "l2": f"no flush: each step moves {step_bytes_total / 1e9:.1f} GB, far beyond the 126 MB L2",
@@ -1974,6 +1978,8 @@ def main(argv=None):
     p.add_argument("--poisson", action="store_true", help="latency under Poisson arrivals at 1-64 requests/s")
     p.add_argument("--staged", action="store_true", help="the pack -> push -> scatter path, stage by stage")
     p.add_argument("--relay-chunks", type=int, default=0, help="with --relay: request chunks per step (0: 8)")
+    p.add_argument("--relay-sms", type=int, default=-1,
+                   help="with --relay: SMs each of the two copy streams may use (default half; 0: every SM)")
     p.add_argument("--relay", action="store_true",
                    help="MLA workload: each decode rank pulls its part from the prefill rank, the rest from its peers")
     p.add_argument("--copy-engine", action="store_true",
