@@ -655,7 +655,7 @@ def run_gpu(args) -> None:
         e2e_ms, e2e_bytes = e2e_connector(args, spec, world, rank, role, src, dst, reqs, gloo)
         e2e_launches = transport.launch_count() - e2e_launches0
         e2e_ok, _ = verify()
-        e = torch.tensor([e2e_ms, float(e2e_bytes)], device=device, dtype=torch.float64)
+        e = torch.tensor([e2e_ms, float(e2e_bytes), float(e2e_launches)], device=device, dtype=torch.float64)
         if world > 1:
             gathered = [torch.zeros_like(e) for _ in range(world)]
             dist.all_gather(gathered, e)
@@ -663,6 +663,7 @@ def run_gpu(args) -> None:
         else:
             e_all = e.cpu().numpy()[None]
         e2e_ms, e2e_bytes = float(e_all[:, 0].max()), int(e_all[:, 1].sum())
+        e2e_launches = int(e_all[:, 2].sum())  # every rank's (a pull's producers launch none)
 
     ok_t = torch.tensor([0.0 if ok else 1.0, 0.0 if e2e_ok in (True, None) else 1.0], device=device,
                         dtype=torch.float64)
