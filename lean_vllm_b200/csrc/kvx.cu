@@ -494,13 +494,13 @@ constexpr int kStoreUnroll = 4;  // tokens each thread loads before it stores an
 // flight before it stores any, so every dependent load is one round trip per batch, not per token.
 //
 // Launched with programmatic stream serialization (unless flags ask for a plain launch): the grid may be scheduled
-// while the kernel before it on the stream drains, waits for that kernel's completion and memory (griddepcontrol.
-// wait) before reading anything, then lets the next such launch start (launch_dependents). Per-layer stores thus
-// overlap each other's launch and ramp; with an ordinary kernel before or after, ordering is the plain stream's.
+// while the kernel before it on the stream drains; it lets the next such launch start at once (launch_dependents),
+// decodes its positions from the parameters, and waits for the previous kernel's completion and memory
+// (griddepcontrol.wait) before it reads any row, slot or block map. Per-layer stores thus overlap each other's
+// launch, ramp and set-up; with an ordinary kernel before or after, ordering is the plain stream's.
 template <int VEC, bool FAST>
 __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __grid_constant__ StoreParams p) {
     using V = Vec<VEC>;
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t vecs = (uint32_t)p.head_bytes / VEC;  // per (token, head) row
     const uint32_t parts = p.value ? 2u : 1u;
@@ -524,6 +524,9 @@ __global__ void __launch_bounds__(kStoreThreads, 5) kvx_store_kernel(const __gri
         const bool peers_only = p.peers_only != 0;
         const void *slots0 = p.dests[0].slots;
         const bool wide0 = p.dests[0].slot_bytes == 8;
+        // Everything above reads only this launch's parameters, so it runs while the kernel before it drains; rows,
+        // slots and block maps are read only once that kernel has completed and its memory is visible.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         for (uint32_t t0 = blockIdx.x * tpp + lane_token; t0 < n; t0 += token_step * kStoreUnroll) {
             typename V::T data[kStoreUnroll];
             int32_t first[kStoreUnroll];
