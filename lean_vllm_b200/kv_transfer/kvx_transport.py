@@ -160,6 +160,11 @@ class KvxTransport:
         return xfer
 
     def _post_on(self, stream, tables, jobs, event, layer=None, flags=None, after_stream=None) -> transport.Transfer:
+        if torch.cuda.current_device() != self.device.index:
+            # A launch goes to the calling thread's current device: an engine thread that posts for a rank whose
+            # cache sits on another GPU (several ranks in one process) launches on the cache's device.
+            with torch.cuda.device(self.device):
+                return self._post_on(stream, tables, jobs, event, layer, flags, after_stream)
         xfer = transport.transfer(self._caches(self.local, tables, layer), jobs, stream.cuda_stream, event,
                                   self.flags if flags is None else flags, after_stream)
         self.doorbell.ring_after(stream.cuda_stream)

@@ -270,3 +270,46 @@ def test_a_relayed_latent_load_between_processes(golden, monkeypatch, decode_tp)
         proc.join(timeout=60)
         if proc.is_alive():
             proc.kill()
+
+
+@pytest.mark.multigpu
+def test_a_load_the_engine_thread_launches_for_a_cache_on_another_gpu_lands(golden, monkeypatch):
+    """Two ranks in one process: the producer's cache on cuda:0, the decode rank's on cuda:1, the calling thread's
+    current device cuda:0. Once the producer is mapped, start_load_kv launches the next load itself -- on the decode
+    cache's device, ordered after that device's current stream -- and it lands the reference's bytes."""
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import threading
+
+    from lean_vllm_b200.kv_transfer.kvx_transport import KvxTransport
+
+    _, arrays = golden
+    torch.cuda.set_device(0)
+    posting = []
+    original = KvxTransport.post
+
+    def post(self, *args, **kwargs):
+        if self.device.index == 1 and not kwargs.get("save"):
+            posting.append(threading.current_thread().name)
+        return original(self, *args, **kwargs)
+
+    monkeypatch.setattr(KvxTransport, "post", post)
+    producers_side, consumers_side = Sides("cuda:0"), Sides("cuda:1")
+    try:
+        producers = producers_side.make("kv_producer", 1, full_cache(0, False))
+        consumers = consumers_side.make("kv_consumer", 1, full_cache(1, False), engine_id="decode")
+        before = consumers[0].kv_caches[0].clone()
+        for request_id, local, remote in (("warm", [1], [4]), ("p-1", [0, 5, 3], [7, 2, 9])):
+            producers[0].start_load_kv(KVConnectorMetadata(reqs_to_send={request_id: list(remote)}))
+            consumers[0].start_load_kv(KVConnectorMetadata(reqs_to_recv={
+                f"d-{request_id}": recv(producers, list(local), list(remote), remote_request_id=request_id)}))
+            assert wait_for(consumers[0]).finished_recving == {f"d-{request_id}"}
+            assert wait_for(producers[0]).finished_sending == {request_id}
+            if request_id == "warm":
+                consumers[0].kv_caches[0].copy_(before)  # the fixture's state before its load
+        assert posting[0].startswith("kvx-ipc-") and posting[-1] == threading.current_thread().name
+        assert torch.cuda.current_device() == 0
+        assert np.array_equal(bits(consumers[0].kv_caches[0]), arrays["small_kv_tp1to1"])
+    finally:
+        consumers_side.close()
+        producers_side.close()
