@@ -518,7 +518,8 @@ class CudaIpcConnectorWorker(KVConnectorWorker):
             load.started = monotonic()
             # After the engine's stream as it stands (this is the engine thread): no ready event to create.
             load.transfer = _Batch(self.transport.post(tables, jobs, None, engine_order=True), 1)
-        except Exception:  # noqa: BLE001 - the transfer thread plans it again and reports what is wrong
+        except Exception as error:  # noqa: BLE001 - the transfer thread plans it again and reports what is wrong
+            logger.debug("load %s goes to the transfer thread: %s", request_id, error)
             return False
         with self._lock:
             self._launches_in_flight += 1
