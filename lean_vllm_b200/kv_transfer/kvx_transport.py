@@ -146,6 +146,10 @@ class KvxTransport:
         event = ready.cuda_event if ready is not None else 0
         if save or relay:
             stream = self.save_stream if save else self.relay_stream
+        elif mark is not None:
+            # A relayed load's own part: one stream for all of them, so with the peers' copies on the relay stream
+            # two copies run at once, each on its half of the SMs (split_sms), as in the device-timed relay.
+            stream = self.load_streams[0]
         else:
             stream = self.load_streams[self._lane]
             self._lane ^= 1
